@@ -1,0 +1,87 @@
+"""ctypes binding of liblrk's C ABI (include/lrk.h).
+
+This is the same surface a non-Python host (cgo, JNI, N-API) would bind.
+Pointers are passed as integers (e.g. ``tensor.data_ptr()``), streams as the
+integer value of a ``cudaStream_t`` (``torch.cuda.current_stream().cuda_stream``).
+Every entry point returns an lrk_status; :func:`check` raises on failure.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+from . import LIBRARY_PATH
+
+OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE = 0, 1, 2, 3, 4
+F32, F64, F16, BF16 = 0, 1, 2, 3
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int
+F = ctypes.c_float
+D = ctypes.c_double
+SIZE = ctypes.c_size_t
+
+
+class Segment(ctypes.Structure):
+    """lrk_segment (include/lrk.h)."""
+    _fields_ = [("keys", P), ("values", P), ("positions", P), ("source_row", I64), ("length", I64),
+                ("destination_row", I64), ("logical_position", I64)]
+
+
+SIGNATURES = {
+    "lrk_last_error": (ctypes.c_char_p, []),
+    "lrk_version": (I32, []),
+    "lrk_dtype_size": (I32, [I32]),
+    "lrk_temporal_probabilities": (I32, [P, I32, P, P, P, P, P, I64, I64, I64, F, P]),
+    "lrk_temporal_risk": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, F, P]),
+    "lrk_pool": (I32, [P, I64, P, I64, I64, I64, P, P]),
+    "lrk_decision_risk": (I32, [P, P, I32, P, P, I64, I64, I64, D, F, P, P]),
+    "lrk_append": (I32, [P, P, P, I64, P, P, P, I64, I64, I64, I32, I64, P, P, P, P, P, P]),
+    "lrk_compact": (I32, [P, P, P, I64, I64, I32, P, I64, P, P, P, P]),
+    "lrk_merge": (I32, [P, P, P, I64, P, P, I64, P, I64, I64, I32, P, P, P, P]),
+    "lrk_pack": (I32, [P, P, P, I64, I64, I32, P, P, I64, I64, P, P, P]),
+    "lrk_batch_append": (I32, [ctypes.POINTER(Segment), I64, P, P, I64, I32, P, P, P, I64, P]),
+    "lrk_append_flattened": (I32, [P, I64, P, I64, I64, I64, I32, P, P, P, I64, P]),
+    "lrk_compact_flattened": (I32, [P, P, I64, I64, I32, P, I64, P, P, P]),
+    "lrk_refine_workspace_bytes": (SIZE, [I64, I64]),
+    "lrk_refine": (I32, [P, P, I64, P, P, I64, I64, P, SIZE, P, P, P, P, P]),
+    "lrk_topk_workspace_bytes": (SIZE, [I64]),
+    "lrk_topk_smallest": (I32, [P, I64, I64, P, SIZE, P, P, P]),
+    "lrk_register_host": (I32, [P, SIZE]),
+    "lrk_unregister_host": (I32, [P]),
+}
+
+_library = None
+
+
+def library(path: str | Path | None = None) -> ctypes.CDLL:
+    """Load liblrk.so once and declare every entry point's types."""
+    global _library
+    if _library is None or path is not None:
+        lib = ctypes.CDLL(str(path or LIBRARY_PATH))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            function = getattr(lib, name)
+            function.restype = restype
+            function.argtypes = argtypes
+        if path is not None:
+            return lib
+        _library = lib
+    return _library
+
+
+class LrkError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"liblrk status {status}: {message}")
+        self.status = status
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise LrkError(status, library().lrk_last_error().decode(errors="replace"))
+
+
+def dtype_code(torch_dtype) -> int:
+    import torch
+
+    return {torch.float32: F32, torch.float64: F64, torch.float16: F16, torch.bfloat16: BF16}[torch_dtype]

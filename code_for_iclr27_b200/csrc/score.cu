@@ -1,0 +1,497 @@
+// Scoring kernels of liblrk: temporal probabilities, temporal risk, Pool7 and
+// the legacy single-query decision risk.  Compiled with --fmad=false, and the
+// order-sensitive arithmetic is written with explicit round-to-nearest
+// intrinsics, so every value matches the reference operator bit for bit:
+//
+// * A softmax row's denominator and value projection are sums.  The
+//   reference (csrc/scoring.cu:32-66) forms them as 256 per-thread sequential
+//   sums over positions t, t+256, t+512, ... followed by a 256-wide tree
+//   (csrc/scoring.cu:15-30).  Here the same 256 "lanes" and the same tree are
+//   kept, but the row is read from HBM once: it is staged in shared memory and
+//   every element-wise step (scale/round/mask, exp, divide, product) runs on all
+//   threads in parallel, so only the 256 cheap sequential add chains remain.
+// * Max and min reductions are order-free and use warp shuffles.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace lrk {
+namespace {
+
+constexpr int kLanes = 256;  // the reference's reduction width
+
+template <typename T> struct Logit;
+template <> struct Logit<float> {
+  static __device__ __forceinline__ float scaled(float x, float scale) { return __fmul_rn(x, scale); }
+  static __device__ __forceinline__ float load(const float *p) { return __ldcs(p); }
+};
+template <> struct Logit<__nv_bfloat16> {
+  static __device__ __forceinline__ float scaled(float x, float scale) {
+    return __bfloat162float(__float2bfloat16_rn(__fmul_rn(x, scale)));
+  }
+  static __device__ __forceinline__ float load(const __nv_bfloat16 *p) {
+    return __bfloat162float(__ushort_as_bfloat16(__ldcs(reinterpret_cast<const unsigned short *>(p))));
+  }
+};
+template <> struct Logit<__half> {
+  static __device__ __forceinline__ float scaled(float x, float scale) {
+    return __half2float(__float2half_rn(__fmul_rn(x, scale)));
+  }
+  static __device__ __forceinline__ float load(const __half *p) {
+    return __half2float(__ushort_as_half(__ldcs(reinterpret_cast<const unsigned short *>(p))));
+  }
+};
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block max over all threads (order-free).  `scratch` holds >= 32 floats.
+template <int NT>
+__device__ float block_max(float v, float *scratch) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = threadIdx.x < NT / 32 ? scratch[threadIdx.x] : -INFINITY;
+  if (threadIdx.x < 32) r = warp_max(r);
+  if (threadIdx.x == 0) scratch[0] = r;
+  __syncthreads();
+  r = scratch[0];
+  __syncthreads();
+  return r;
+}
+
+// Sum of per-lane partials with the reference's 256-wide pairwise tree:
+// partial[t] += partial[t + s] for s = 128, 64, ..., 1.  Lanes are threads
+// 0..255; all NT threads must call.  `tree` holds 256 floats.
+template <int NT>
+__device__ float tree_sum(float partial, float *tree) {
+  if (threadIdx.x < kLanes) tree[threadIdx.x] = partial;
+  __syncthreads();
+#pragma unroll
+  for (int s = kLanes / 2; s >= 32; s >>= 1) {
+    if (threadIdx.x < s) tree[threadIdx.x] = __fadd_rn(tree[threadIdx.x], tree[threadIdx.x + s]);
+    __syncthreads();
+  }
+  float result = 0.0f;
+  if (threadIdx.x < 32) {
+    float value = tree[threadIdx.x];
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const float other = __shfl_down_sync(0xffffffffu, value, s);
+      if (threadIdx.x < s) value = __fadd_rn(value, other);
+    }
+    if (threadIdx.x == 0) tree[0] = value;
+  }
+  __syncthreads();
+  result = tree[0];
+  __syncthreads();
+  return result;
+}
+
+// Sequential per-lane sum over buffer[t], buffer[t + 256], ... (lane t).
+__device__ __forceinline__ float lane_chain(const float *buffer, int length) {
+  float sum = 0.0f;
+  int p = threadIdx.x;
+#pragma unroll 8
+  for (; p < length; p += kLanes) sum = __fadd_rn(sum, buffer[p]);
+  return sum;
+}
+
+// One CTA per (query, group) row with the whole row staged in shared memory.
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT) probabilities_staged(
+    const T *__restrict__ logits, const float *__restrict__ projected_values,
+    const int64_t *__restrict__ query_positions, const float *__restrict__ key_positions,
+    float *__restrict__ probabilities, float *__restrict__ output_projection, int groups, int length,
+    float scale) {
+  extern __shared__ float row_buffer[];
+  __shared__ float scratch[kLanes];
+  const int64_t row = blockIdx.x;
+  const int group = static_cast<int>(row % groups);
+  const int64_t query = row / groups;
+  const float query_position = static_cast<float>(query_positions[query]);
+  const T *in = logits + row * length;
+  float *out = probabilities + row * length;
+  const float *pv = projected_values + static_cast<int64_t>(group) * length;
+
+  // A: scale, round to the logit dtype, causal mask; row max.
+  float maximum = -INFINITY;
+  for (int p = threadIdx.x; p < length; p += NT) {
+    const float rounded = Logit<T>::scaled(Logit<T>::load(in + p), scale);
+    const float value = key_positions[p] <= query_position ? rounded : -INFINITY;
+    row_buffer[p] = value;
+    maximum = fmaxf(maximum, value);
+  }
+  maximum = block_max<NT>(maximum, scratch);
+
+  // B: weights.
+  for (int p = threadIdx.x; p < length; p += NT) row_buffer[p] = expf(__fsub_rn(row_buffer[p], maximum));
+  __syncthreads();
+  // C: denominator in the reference's lane order.
+  const float denominator = tree_sum<NT>(threadIdx.x < kLanes ? lane_chain(row_buffer, length) : 0.0f, scratch);
+
+  // D: normalise, write probabilities, stage products p * pv.
+  for (int p = threadIdx.x; p < length; p += NT) {
+    const float probability = __fdiv_rn(row_buffer[p], denominator);
+    __stcs(out + p, probability);
+    row_buffer[p] = __fmul_rn(probability, pv[p]);
+  }
+  __syncthreads();
+  // E: value projection in the reference's lane order.
+  const float projection = tree_sum<NT>(threadIdx.x < kLanes ? lane_chain(row_buffer, length) : 0.0f, scratch);
+  if (threadIdx.x == 0) output_projection[row] = projection;
+}
+
+// Rows too long for shared memory: the reference's three-pass structure with
+// the intermediate values recomputed from the logits instead of round-tripping
+// through the probability buffer (logits re-reads hit L2).
+template <typename T>
+__global__ void __launch_bounds__(kLanes) probabilities_streamed(
+    const T *__restrict__ logits, const float *__restrict__ projected_values,
+    const int64_t *__restrict__ query_positions, const float *__restrict__ key_positions,
+    float *__restrict__ probabilities, float *__restrict__ output_projection, int groups, int length,
+    float scale) {
+  __shared__ float scratch[kLanes];
+  const int64_t row = blockIdx.x;
+  const int group = static_cast<int>(row % groups);
+  const int64_t query = row / groups;
+  const float query_position = static_cast<float>(query_positions[query]);
+  const T *in = logits + row * length;
+  float *out = probabilities + row * length;
+  const float *pv = projected_values + static_cast<int64_t>(group) * length;
+  auto value_at = [&](int p) {
+    const float rounded = Logit<T>::scaled(Logit<T>::load(in + p), scale);
+    return key_positions[p] <= query_position ? rounded : -INFINITY;
+  };
+  float maximum = -INFINITY;
+  for (int p = threadIdx.x; p < length; p += kLanes) maximum = fmaxf(maximum, value_at(p));
+  maximum = block_max<kLanes>(maximum, scratch);
+  float sum = 0.0f;
+  for (int p = threadIdx.x; p < length; p += kLanes) sum = __fadd_rn(sum, expf(__fsub_rn(value_at(p), maximum)));
+  const float denominator = tree_sum<kLanes>(sum, scratch);
+  float projection = 0.0f;
+  for (int p = threadIdx.x; p < length; p += kLanes) {
+    const float probability = __fdiv_rn(expf(__fsub_rn(value_at(p), maximum)), denominator);
+    __stcs(out + p, probability);
+    projection = __fadd_rn(projection, __fmul_rn(probability, pv[p]));
+  }
+  projection = tree_sum<kLanes>(projection, scratch);
+  if (threadIdx.x == 0) output_projection[row] = projection;
+}
+
+__device__ __forceinline__ double softplus64(double value) {
+  return value > 20.0 ? value : log1p(exp(value));
+}
+
+// max(0, p*(m - c) - softplus(m) + softplus(c)) with c = m - drop
+// (csrc/scoring.cu:68-75), evaluated in the same operation order.
+__device__ __forceinline__ double risk64(double margin, double probability, double base_softplus, float drop) {
+  const double compared = __dsub_rn(margin, static_cast<double>(drop));
+  const double kl = __dadd_rn(__dsub_rn(__dmul_rn(probability, __dsub_rn(margin, compared)), base_softplus),
+                              softplus64(compared));
+  return fmax(0.0, kl);
+}
+
+// One warp row = 32 consecutive candidates; `split` query lanes per candidate
+// (blockDim.y), each taking queries lane, lane + split, ...  G <= MAXG keeps
+// the candidate's projected values in registers.
+template <int MAXG>
+__global__ void __launch_bounds__(1024) risk_kernel(
+    const float *__restrict__ probabilities, const float *__restrict__ output_projection,
+    const float *__restrict__ projected_values, const float *__restrict__ margin, float *__restrict__ result,
+    int window, int groups, int64_t length, int64_t first, int64_t count, float epsilon) {
+  __shared__ float minimums[32][33];
+  __shared__ float maximums[32][33];
+  __shared__ int bad[32][33];
+  const int lane = threadIdx.x;
+  const int split = blockDim.y;
+  const int64_t candidate = static_cast<int64_t>(blockIdx.x) * 32 + lane;
+  const int64_t position = first + candidate;
+  const bool active = candidate < count;
+  float minimum = INFINITY, maximum = -INFINITY;
+  int nonfinite = 0;
+  if (active) {
+    float pv[MAXG > 0 ? MAXG : 1];
+    if (MAXG > 0) {
+#pragma unroll
+      for (int g = 0; g < MAXG; ++g) pv[g] = g < groups ? projected_values[g * length + position] : 0.0f;
+    }
+#pragma unroll 2
+    for (int query = threadIdx.y; query < window; query += split) {
+      float drop = 0.0f;
+      const float *column = probabilities + static_cast<int64_t>(query) * groups * length + position;
+      const float *op = output_projection + static_cast<int64_t>(query) * groups;
+      if (MAXG > 0) {
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g) {
+          if (g < groups) {
+            const float probability = __ldcs(column + g * length);
+            const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
+            drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(pv[g], op[g])));
+          }
+        }
+      } else {
+        for (int g = 0; g < groups; ++g) {
+          const float probability = __ldcs(column + g * length);
+          const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
+          drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(projected_values[g * length + position], op[g])));
+        }
+      }
+      if (!isfinite(drop)) nonfinite = 1;
+      minimum = fminf(minimum, drop);
+      maximum = fmaxf(maximum, drop);
+    }
+  }
+  minimums[threadIdx.y][lane] = minimum;
+  maximums[threadIdx.y][lane] = maximum;
+  bad[threadIdx.y][lane] = nonfinite;
+  __syncthreads();
+  if (threadIdx.y == 0 && active) {
+    for (int y = 1; y < split; ++y) {
+      minimum = fminf(minimum, minimums[y][lane]);
+      maximum = fmaxf(maximum, maximums[y][lane]);
+      nonfinite |= bad[y][lane];
+    }
+    if (nonfinite) {
+      result[candidate] = NAN;
+    } else {
+      const double m = static_cast<double>(margin[0]);
+      const double probability = 1.0 / (1.0 + exp(-m));
+      const double base = softplus64(m);
+      result[candidate] = static_cast<float>(fmax(risk64(m, probability, base, minimum),
+                                                  risk64(m, probability, base, maximum)));
+    }
+  }
+}
+
+// Pool: out[i] = max of scores over [i - w/2, i + w/2] clipped to i's segment.
+__global__ void pool_kernel(const float *__restrict__ scores, int64_t n, const int64_t *__restrict__ bounds,
+                            int64_t segments, int half, float *__restrict__ out) {
+  for (int64_t segment = blockIdx.y; segment < segments; segment += gridDim.y) {
+    const int64_t begin = lmax(0, bounds[segment]);
+    const int64_t end = lmin(n, bounds[segment + 1]);
+    for (int64_t i = begin + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < end;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      float value = -INFINITY;
+      const int64_t lo = lmax(begin, i - half), hi = lmin(end - 1, i + half);
+      for (int64_t j = lo; j <= hi; ++j) value = fmaxf(value, scores[j]);
+      out[i] = value;
+    }
+  }
+}
+
+template <typename T> __device__ __forceinline__ float to_float(T v);
+template <> __device__ __forceinline__ float to_float(float v) { return v; }
+template <> __device__ __forceinline__ float to_float(double v) { return static_cast<float>(v); }
+template <> __device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+__device__ double stable_sigmoid(double value) {
+  if (value >= 0.0) return 1.0 / (1.0 + exp(-value));
+  const double e = exp(value);
+  return e / (1.0 + e);
+}
+__device__ double stable_softplus(double value) {
+  if (value > 20.0) return __dadd_rn(value, log1p(exp(-value)));
+  return log1p(exp(value));
+}
+
+// Legacy decision risk (csrc/cache_legacy.cu:81-135): 256 threads per
+// candidate, term index t, t + 256, ... over (group, channel), then a tree.
+template <typename T>
+__global__ void __launch_bounds__(kLanes) decision_risk_kernel(
+    float *__restrict__ scores, const float *__restrict__ probabilities, const T *__restrict__ values,
+    const float *__restrict__ head_outputs, const float *__restrict__ gradients, int groups, int64_t candidates,
+    int dimension, double base_margin, float epsilon) {
+  __shared__ float tree[kLanes];
+  const int64_t candidate = blockIdx.x;
+  float partial = 0.0f;
+  const int terms = groups * dimension;
+  for (int index = threadIdx.x; index < terms; index += kLanes) {
+    const int group = index / dimension;
+    const int channel = index % dimension;
+    const float alpha = probabilities[group * candidates + candidate];
+    const float denominator = fmaxf(__fsub_rn(1.0f, alpha), epsilon);
+    const float value = to_float(values[candidate * dimension + channel]);
+    const float local_delta =
+        __fmul_rn(__fdiv_rn(alpha, denominator), __fsub_rn(value, head_outputs[group * dimension + channel]));
+    partial = __fadd_rn(partial, __fmul_rn(gradients[group * dimension + channel], local_delta));
+  }
+  const float total = tree_sum<kLanes>(partial, tree);
+  if (threadIdx.x == 0) {
+    const double compared = __dsub_rn(base_margin, static_cast<double>(total));
+    const double probability = stable_sigmoid(base_margin);
+    double kl = __dadd_rn(__dsub_rn(__dmul_rn(probability, __dsub_rn(base_margin, compared)),
+                                    stable_softplus(base_margin)),
+                          stable_softplus(compared));
+    if (kl < 0.0) kl = 0.0;
+    scores[candidate] = static_cast<float>(kl);
+  }
+}
+
+// Largest row kept whole in shared memory (floats), leaving room for scratch.
+constexpr int kMaxStagedLength = 56 * 1024;
+
+template <typename T, int NT>
+int launch_probabilities_staged(const T *logits, const float *pv, const int64_t *qpos, const float *kpos,
+                                float *probs, float *op, int64_t rows, int groups, int length, float scale,
+                                cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(length) * sizeof(float);
+  auto kernel = probabilities_staged<T, NT>;
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kMaxStagedLength * sizeof(float)));
+    if (e != cudaSuccess) {
+      set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      return LRK_ERR_CUDA;
+    }
+  }
+  kernel<<<static_cast<unsigned>(rows), NT, bytes, stream>>>(logits, pv, qpos, kpos, probs, op, groups, length,
+                                                            scale);
+  return launch_status("lrk_temporal_probabilities");
+}
+
+template <typename T>
+int launch_probabilities(const void *logits, const float *pv, const int64_t *qpos, const float *kpos,
+                         float *probs, float *op, int64_t rows, int groups, int length, float scale,
+                         cudaStream_t stream) {
+  const T *in = static_cast<const T *>(logits);
+  if (length <= kMaxStagedLength) {
+    if (length <= 8192)
+      return launch_probabilities_staged<T, 256>(in, pv, qpos, kpos, probs, op, rows, groups, length, scale, stream);
+    return launch_probabilities_staged<T, 1024>(in, pv, qpos, kpos, probs, op, rows, groups, length, scale, stream);
+  }
+  probabilities_streamed<T><<<static_cast<unsigned>(rows), kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op,
+                                                                                groups, length, scale);
+  return launch_status("lrk_temporal_probabilities");
+}
+
+}  // namespace
+}  // namespace lrk
+
+using namespace lrk;
+
+extern "C" int lrk_temporal_probabilities(const void *logits, int logits_dtype, const float *projected_values,
+                                          const int64_t *query_positions, const float *key_positions,
+                                          float *probabilities, float *output_projection, int64_t window,
+                                          int64_t groups, int64_t length, float scale, lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(window > 0 && groups > 0 && length > 0, "Empty attention dimensions");
+  LRK_REQUIRE(length <= INT32_MAX && groups <= INT32_MAX && window * groups <= INT32_MAX, "attention too large");
+  LRK_REQUIRE(logits && projected_values && query_positions && key_positions && probabilities && output_projection,
+              "null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t rows = window * groups;
+  switch (logits_dtype) {
+    case LRK_BF16:
+      return launch_probabilities<__nv_bfloat16>(logits, projected_values, query_positions, key_positions,
+                                                 probabilities, output_projection, rows, static_cast<int>(groups),
+                                                 static_cast<int>(length), scale, s);
+    case LRK_F16:
+      return launch_probabilities<__half>(logits, projected_values, query_positions, key_positions, probabilities,
+                                          output_projection, rows, static_cast<int>(groups),
+                                          static_cast<int>(length), scale, s);
+    case LRK_F32:
+      return launch_probabilities<float>(logits, projected_values, query_positions, key_positions, probabilities,
+                                         output_projection, rows, static_cast<int>(groups),
+                                         static_cast<int>(length), scale, s);
+    default:
+      return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
+  }
+}
+
+extern "C" int lrk_temporal_risk(const float *probabilities, const float *output_projection,
+                                 const float *projected_values, const float *margin, float *scores, int64_t window,
+                                 int64_t groups, int64_t length, int64_t first, int64_t last, float epsilon,
+                                 lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(window > 0 && groups > 0 && first >= 0 && last > first && last <= length && epsilon > 0,
+              "Invalid risk interval");
+  LRK_REQUIRE(window <= INT32_MAX && groups <= INT32_MAX, "risk too large");
+  LRK_REQUIRE(probabilities && output_projection && projected_values && margin && scores, "null pointer");
+  const int64_t count = last - first;
+  const int64_t blocks = ceil_div(count, 32);
+  LRK_REQUIRE(blocks <= INT32_MAX, "too many candidates");
+  const int sms = sm_count();
+  int split = 8;
+  if (blocks < 2 * sms) split = 16;
+  if (blocks < sms) split = 32;
+  split = static_cast<int>(std::min<int64_t>(split, std::max<int64_t>(1, window)));
+  dim3 block(32, split);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int g = static_cast<int>(groups);
+  if (g <= 4)
+    risk_kernel<4><<<static_cast<unsigned>(blocks), block, 0, s>>>(probabilities, output_projection, projected_values,
+                                                                    margin, scores, static_cast<int>(window), g,
+                                                                    length, first, count, epsilon);
+  else if (g <= 8)
+    risk_kernel<8><<<static_cast<unsigned>(blocks), block, 0, s>>>(probabilities, output_projection, projected_values,
+                                                                    margin, scores, static_cast<int>(window), g,
+                                                                    length, first, count, epsilon);
+  else
+    risk_kernel<0><<<static_cast<unsigned>(blocks), block, 0, s>>>(probabilities, output_projection, projected_values,
+                                                                    margin, scores, static_cast<int>(window), g,
+                                                                    length, first, count, epsilon);
+  return launch_status("lrk_temporal_risk");
+}
+
+extern "C" int lrk_pool(const float *scores, int64_t n, const int64_t *bounds, int64_t segments,
+                        int64_t maximum_count, int64_t width, float *out, lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(width > 0 && width % 2 == 1 && maximum_count > 0, "Invalid pool configuration");
+  LRK_REQUIRE(segments >= 1 && n >= 0, "Invalid pool layout");
+  if (n == 0) return LRK_OK;
+  LRK_REQUIRE(scores && bounds && out, "null pointer");
+  const int threads = 256;
+  const int64_t tiles = std::max<int64_t>(1, std::min<int64_t>(ceil_div(maximum_count, threads), 65535));
+  dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min<int64_t>(segments, 65535)));
+  const int half = static_cast<int>(std::min<int64_t>(width / 2, INT32_MAX));
+  pool_kernel<<<grid, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(scores, n, bounds, segments, half, out);
+  return launch_status("lrk_pool");
+}
+
+extern "C" int lrk_decision_risk(const float *probabilities, const void *values, int values_dtype,
+                                 const float *head_outputs, const float *gradients, int64_t groups,
+                                 int64_t candidates, int64_t dimension, double base_margin, float epsilon,
+                                 float *scores, lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(groups >= 0 && candidates >= 0 && dimension >= 0, "invalid sizes");
+  LRK_REQUIRE(epsilon > 0.0f && epsilon < 1.0f, "denominator_epsilon must be in (0,1)");
+  if (candidates == 0) return LRK_OK;
+  LRK_REQUIRE(groups * dimension <= INT32_MAX && candidates <= INT32_MAX, "too large");
+  LRK_REQUIRE(probabilities && values && head_outputs && gradients && scores, "null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(candidates);
+  const int g = static_cast<int>(groups), d = static_cast<int>(dimension);
+  switch (values_dtype) {
+    case LRK_F32:
+      decision_risk_kernel<float><<<grid, kLanes, 0, s>>>(scores, probabilities, static_cast<const float *>(values),
+                                                          head_outputs, gradients, g, candidates, d, base_margin,
+                                                          epsilon);
+      break;
+    case LRK_F64:
+      decision_risk_kernel<double><<<grid, kLanes, 0, s>>>(scores, probabilities, static_cast<const double *>(values),
+                                                           head_outputs, gradients, g, candidates, d, base_margin,
+                                                           epsilon);
+      break;
+    case LRK_F16:
+      decision_risk_kernel<__half><<<grid, kLanes, 0, s>>>(scores, probabilities, static_cast<const __half *>(values),
+                                                           head_outputs, gradients, g, candidates, d, base_margin,
+                                                           epsilon);
+      break;
+    case LRK_BF16:
+      decision_risk_kernel<__nv_bfloat16><<<grid, kLanes, 0, s>>>(
+          scores, probabilities, static_cast<const __nv_bfloat16 *>(values), head_outputs, gradients, g, candidates,
+          d, base_margin, epsilon);
+      break;
+    default:
+      return fail(LRK_ERR_UNSUPPORTED, "unsupported values dtype");
+  }
+  return launch_status("lrk_decision_risk");
+}

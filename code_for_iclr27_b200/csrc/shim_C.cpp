@@ -1,0 +1,335 @@
+// lazy_recall._C, backed by liblrk.
+//
+// The eight operators keep the reference's positional signatures
+// (csrc/bindings.cpp:20-29), its argument checks and messages (TORCH_CHECK ->
+// RuntimeError), its output allocation (torch::empty on the input's device,
+// through the caching allocator) and its stream (the current CUDA stream).
+// Two operators are added for the selection step: refine and topk_smallest.
+#include <vector>
+
+#include "shim_common.h"
+
+using lrk_shim::check_status;
+using lrk_shim::current_stream;
+using lrk_shim::dtype_code;
+
+namespace {
+
+void check_cuda(const torch::Tensor &tensor, const torch::Tensor &reference) {
+  TORCH_CHECK(tensor.is_cuda() && tensor.is_contiguous(), "Expected contiguous CUDA tensor");
+  TORCH_CHECK(tensor.device() == reference.device(), "CUDA devices differ");
+}
+
+void check_recall_tensor(const torch::Tensor &tensor, const torch::Tensor &reference) {
+  TORCH_CHECK(tensor.is_cuda() && tensor.is_contiguous(), "Expected contiguous CUDA tensor");
+  TORCH_CHECK(tensor.device() == reference.device(), "Recall devices differ");
+}
+
+void check_cache(const torch::Tensor &keys, const torch::Tensor &values, const torch::Tensor &positions) {
+  for (const auto &tensor : {keys, values, positions}) check_cuda(tensor, keys);
+  TORCH_CHECK(keys.dim() == 2 && keys.size(1) > 0 && keys.sizes() == values.sizes() &&
+                  keys.scalar_type() == values.scalar_type(),
+              "Invalid KV layout");
+  TORCH_CHECK(positions.scalar_type() == at::kFloat && positions.numel() == keys.size(0), "Invalid positions");
+}
+
+// csrc/scoring.cu:205-233
+std::vector<torch::Tensor> temporal_probabilities(torch::Tensor logits, torch::Tensor projected_values,
+                                                  torch::Tensor query_positions, torch::Tensor key_positions,
+                                                  double scale) {
+  check_cuda(logits, logits);
+  check_cuda(projected_values, logits);
+  check_cuda(query_positions, logits);
+  check_cuda(key_positions, logits);
+  TORCH_CHECK(logits.dim() == 3, "logits must be [window, groups, positions]");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat || logits.scalar_type() == at::kHalf ||
+                  logits.scalar_type() == at::kBFloat16,
+              "Only FP32/FP16/BF16 scores are supported");
+  const int64_t window = logits.size(0), groups = logits.size(1), length = logits.size(2);
+  TORCH_CHECK(window > 0 && groups > 0 && length > 0, "Empty attention dimensions");
+  TORCH_CHECK(projected_values.scalar_type() == at::kFloat && projected_values.dim() == 2 &&
+                  projected_values.size(0) == groups && projected_values.size(1) == length,
+              "Invalid projected values");
+  TORCH_CHECK(query_positions.scalar_type() == at::kLong && query_positions.numel() == window,
+              "Invalid query positions");
+  TORCH_CHECK(key_positions.scalar_type() == at::kFloat && key_positions.numel() == length, "Invalid key positions");
+  c10::cuda::CUDAGuard guard(logits.device());
+  auto probabilities = torch::empty(logits.sizes(), logits.options().dtype(at::kFloat));
+  auto output = torch::empty({window, groups}, probabilities.options());
+  check_status(lrk_temporal_probabilities(logits.data_ptr(), dtype_code(logits.scalar_type()),
+                                          projected_values.data_ptr<float>(), query_positions.data_ptr<int64_t>(),
+                                          key_positions.data_ptr<float>(), probabilities.data_ptr<float>(),
+                                          output.data_ptr<float>(), window, groups, length,
+                                          static_cast<float>(scale), current_stream()));
+  return {probabilities, output};
+}
+
+// csrc/scoring.cu:235-255
+torch::Tensor temporal_risk(torch::Tensor probabilities, torch::Tensor output_projection,
+                            torch::Tensor projected_values, torch::Tensor margin, int64_t first, int64_t last,
+                            double epsilon) {
+  for (const auto &tensor : {probabilities, output_projection, projected_values, margin}) {
+    check_cuda(tensor, probabilities);
+    TORCH_CHECK(tensor.scalar_type() == at::kFloat, "Risk inputs must be float32");
+  }
+  TORCH_CHECK(probabilities.dim() == 3, "Invalid probability dimensions");
+  const int64_t window = probabilities.size(0), groups = probabilities.size(1), length = probabilities.size(2);
+  TORCH_CHECK(window > 0 && groups > 0 && first >= 0 && last > first && last <= length && epsilon > 0,
+              "Invalid risk interval");
+  TORCH_CHECK(margin.numel() == 1 && output_projection.numel() == window * groups &&
+                  projected_values.numel() == groups * length,
+              "Risk shapes differ");
+  c10::cuda::CUDAGuard guard(probabilities.device());
+  auto result = torch::empty({last - first}, probabilities.options());
+  check_status(lrk_temporal_risk(probabilities.data_ptr<float>(), output_projection.data_ptr<float>(),
+                                 projected_values.data_ptr<float>(), margin.data_ptr<float>(),
+                                 result.data_ptr<float>(), window, groups, length, first, last,
+                                 static_cast<float>(epsilon), current_stream()));
+  return result;
+}
+
+// csrc/scoring.cu:264-292
+std::vector<torch::Tensor> append(torch::Tensor keys, torch::Tensor values, torch::Tensor positions,
+                                  torch::Tensor new_keys, torch::Tensor new_values, torch::Tensor cumulative,
+                                  int64_t logical_start, int64_t maximum_length) {
+  check_cache(keys, values, positions);
+  for (const auto &tensor : {new_keys, new_values, cumulative}) check_cuda(tensor, keys);
+  TORCH_CHECK(new_keys.dim() == 4 && new_keys.size(0) == 1 && new_keys.sizes() == new_values.sizes() &&
+                  new_keys.scalar_type() == keys.scalar_type() && new_values.scalar_type() == keys.scalar_type(),
+              "Invalid appended KV");
+  const int64_t heads = new_keys.size(1), added = new_keys.size(2), dimension = keys.size(1);
+  TORCH_CHECK(heads > 0 && added > 0 && new_keys.size(3) == dimension && maximum_length >= 0,
+              "Invalid appended shape");
+  TORCH_CHECK(cumulative.scalar_type() == at::kInt && cumulative.numel() == heads + 1, "Invalid cumulative lengths");
+  c10::cuda::CUDAGuard guard(keys.device());
+  const int64_t rows = keys.size(0) + heads * added;
+  auto output_keys = torch::empty({rows, dimension}, keys.options());
+  auto output_values = torch::empty_like(output_keys);
+  auto output_positions = torch::empty({rows, 1}, positions.options());
+  auto output_cumulative = torch::empty_like(cumulative);
+  auto output_lengths = torch::empty({heads}, cumulative.options());
+  check_status(lrk_append(keys.data_ptr(), values.data_ptr(), positions.data_ptr<float>(), keys.size(0),
+                          new_keys.data_ptr(), new_values.data_ptr(), cumulative.data_ptr<int32_t>(), heads, added,
+                          dimension, dtype_code(keys.scalar_type()), logical_start, output_keys.data_ptr(),
+                          output_values.data_ptr(), output_positions.data_ptr<float>(),
+                          output_cumulative.data_ptr<int32_t>(), output_lengths.data_ptr<int32_t>(),
+                          current_stream()));
+  return {output_keys, output_values, output_positions, output_cumulative, output_lengths};
+}
+
+// csrc/scoring.cu:294-314
+std::vector<torch::Tensor> compact(torch::Tensor keys, torch::Tensor values, torch::Tensor positions,
+                                   torch::Tensor removed) {
+  check_cache(keys, values, positions);
+  check_cuda(removed, keys);
+  TORCH_CHECK(removed.scalar_type() == at::kLong && removed.dim() == 1 && removed.numel() <= keys.size(0),
+              "Invalid removals");
+  c10::cuda::CUDAGuard guard(keys.device());
+  const int64_t rows = keys.size(0) - removed.numel(), dimension = keys.size(1);
+  auto output_keys = torch::empty({rows, dimension}, keys.options());
+  auto output_values = torch::empty_like(output_keys);
+  auto output_positions = torch::empty({rows, 1}, positions.options());
+  if (rows > 0) {
+    check_status(lrk_compact(keys.data_ptr(), values.data_ptr(), positions.data_ptr<float>(), keys.size(0),
+                             dimension, dtype_code(keys.scalar_type()), removed.data_ptr<int64_t>(), removed.numel(),
+                             output_keys.data_ptr(), output_values.data_ptr(), output_positions.data_ptr<float>(),
+                             current_stream()));
+  }
+  return {output_keys, output_values, output_positions};
+}
+
+// csrc/scoring.cu:316-329
+torch::Tensor pool(torch::Tensor scores, torch::Tensor bounds, int64_t maximum_count, int64_t width) {
+  check_cuda(scores, scores);
+  check_cuda(bounds, scores);
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.dim() == 1 && bounds.scalar_type() == at::kLong &&
+                  bounds.dim() == 1 && bounds.numel() >= 2,
+              "Invalid pool layout");
+  TORCH_CHECK(width > 0 && width % 2 == 1 && maximum_count > 0, "Invalid pool configuration");
+  c10::cuda::CUDAGuard guard(scores.device());
+  auto output = torch::empty_like(scores);
+  check_status(lrk_pool(scores.data_ptr<float>(), scores.numel(), bounds.data_ptr<int64_t>(), bounds.numel() - 1,
+                        maximum_count, width, output.data_ptr<float>(), current_stream()));
+  return output;
+}
+
+// csrc/recall.cu:54-84
+std::vector<torch::Tensor> merge(torch::Tensor keys, torch::Tensor values, torch::Tensor positions,
+                                 torch::Tensor recalled, torch::Tensor recalled_positions, torch::Tensor mapping) {
+  for (const auto &tensor : {keys, values, positions, recalled, recalled_positions, mapping})
+    check_recall_tensor(tensor, keys);
+  TORCH_CHECK(keys.dim() == 2 && keys.size(1) > 0 && keys.sizes() == values.sizes(), "Invalid K/V shape");
+  TORCH_CHECK(recalled.dim() == 3 && recalled.size(1) == 2 && recalled.size(2) == keys.size(1),
+              "Invalid recalled shape");
+  TORCH_CHECK(keys.scalar_type() == values.scalar_type() && keys.scalar_type() == recalled.scalar_type(),
+              "K/V dtypes differ");
+  TORCH_CHECK(positions.scalar_type() == at::kFloat && recalled_positions.scalar_type() == at::kFloat &&
+                  positions.numel() == keys.size(0) && recalled_positions.numel() == recalled.size(0),
+              "Invalid positions");
+  TORCH_CHECK(mapping.dim() == 1 && mapping.scalar_type() == at::kLong, "Mapping must be int64");
+  c10::cuda::CUDAGuard guard(keys.device());
+  const auto rows = mapping.numel();
+  const auto dimension = keys.size(1);
+  auto output_keys = torch::empty({rows, dimension}, keys.options());
+  auto output_values = torch::empty_like(output_keys);
+  auto output_positions = torch::empty({rows, 1}, positions.options());
+  if (rows) {
+    check_status(lrk_merge(keys.data_ptr(), values.data_ptr(), positions.data_ptr<float>(), keys.size(0),
+                           recalled.data_ptr(), recalled_positions.data_ptr<float>(), recalled.size(0),
+                           mapping.data_ptr<int64_t>(), rows, dimension, dtype_code(keys.scalar_type()),
+                           output_keys.data_ptr(), output_values.data_ptr(), output_positions.data_ptr<float>(),
+                           current_stream()));
+  }
+  return {output_keys, output_values, output_positions};
+}
+
+// csrc/recall.cu:86-111
+void pack(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor indices,
+          torch::Tensor heads, int64_t layer, torch::Tensor payload, torch::Tensor metadata) {
+  for (const auto &tensor : {keys, values, positions, indices, heads, payload, metadata})
+    check_recall_tensor(tensor, keys);
+  TORCH_CHECK(keys.dim() == 2 && keys.size(1) > 0 && keys.sizes() == values.sizes(), "Invalid K/V shape");
+  TORCH_CHECK(keys.scalar_type() == values.scalar_type() && keys.scalar_type() == payload.scalar_type(),
+              "Dtype mismatch");
+  TORCH_CHECK(indices.dim() == 1 && indices.scalar_type() == at::kLong && heads.sizes() == indices.sizes() &&
+                  heads.scalar_type() == at::kLong,
+              "Invalid gather indices");
+  const auto rows = indices.numel();
+  const auto dimension = keys.size(1);
+  TORCH_CHECK(payload.dim() == 3 && payload.size(0) == rows && payload.size(1) == 2 && payload.size(2) == dimension,
+              "Invalid payload buffer");
+  TORCH_CHECK(positions.numel() == keys.size(0) && positions.scalar_type() == at::kFloat, "Invalid positions");
+  TORCH_CHECK(metadata.dim() == 2 && metadata.size(0) == rows && metadata.size(1) == 3 &&
+                  metadata.scalar_type() == at::kLong,
+              "Invalid identity buffer");
+  c10::cuda::CUDAGuard guard(keys.device());
+  if (!rows) return;
+  check_status(lrk_pack(keys.data_ptr(), values.data_ptr(), positions.data_ptr<float>(), keys.size(0), dimension,
+                        dtype_code(keys.scalar_type()), indices.data_ptr<int64_t>(), heads.data_ptr<int64_t>(), rows,
+                        layer, payload.data_ptr(), metadata.data_ptr<int64_t>(), current_stream()));
+}
+
+// csrc/batch_append.cu:36-94.  The descriptor table stays on the host and
+// reaches the kernel as a launch parameter: no pageable copy, no sync.
+std::vector<torch::Tensor> batch_append(std::vector<torch::Tensor> keys, std::vector<torch::Tensor> values,
+                                        std::vector<torch::Tensor> positions, torch::Tensor new_keys,
+                                        torch::Tensor new_values, std::vector<std::vector<int64_t>> lengths,
+                                        std::vector<int64_t> logical_positions) {
+  TORCH_CHECK(new_keys.is_cuda() && new_keys.is_contiguous() && new_values.is_contiguous(),
+              "Contiguous CUDA states required");
+  TORCH_CHECK(new_keys.dim() == 4 && new_keys.size(2) == 1 && new_keys.size(3) > 0,
+              "Only batched one-token append is supported");
+  TORCH_CHECK(new_keys.sizes() == new_values.sizes() && new_keys.scalar_type() == new_values.scalar_type() &&
+                  new_keys.device() == new_values.device(),
+              "New K/V mismatch");
+  const int64_t requests = new_keys.size(0), heads = new_keys.size(1), dimension = new_keys.size(3);
+  TORCH_CHECK(requests > 0 && heads > 0 && static_cast<int64_t>(keys.size()) == requests &&
+                  static_cast<int64_t>(values.size()) == requests &&
+                  static_cast<int64_t>(positions.size()) == requests &&
+                  static_cast<int64_t>(lengths.size()) == requests &&
+                  static_cast<int64_t>(logical_positions.size()) == requests,
+              "Request metadata mismatch");
+  c10::cuda::CUDAGuard guard(new_keys.device());
+  std::vector<lrk_segment> segments(static_cast<size_t>(requests * heads));
+  int64_t destination = 0;
+  for (int64_t request = 0; request < requests; ++request) {
+    TORCH_CHECK(keys[request].is_cuda() && keys[request].is_contiguous() && values[request].is_contiguous() &&
+                    positions[request].is_contiguous(),
+                "Contiguous CUDA cache required");
+    TORCH_CHECK(keys[request].device() == new_keys.device() && values[request].device() == new_keys.device() &&
+                    positions[request].device() == new_keys.device(),
+                "Cache devices differ");
+    TORCH_CHECK(keys[request].dim() == 2 && keys[request].size(1) == dimension &&
+                    keys[request].sizes() == values[request].sizes() &&
+                    keys[request].scalar_type() == new_keys.scalar_type() &&
+                    values[request].scalar_type() == new_keys.scalar_type(),
+                "Cache K/V mismatch");
+    TORCH_CHECK(positions[request].scalar_type() == at::kFloat &&
+                    positions[request].numel() == keys[request].size(0) &&
+                    static_cast<int64_t>(lengths[request].size()) == heads && logical_positions[request] >= 0 &&
+                    logical_positions[request] < (1 << 24),
+                "Invalid positions or head metadata");
+    int64_t source = 0;
+    for (int64_t head = 0; head < heads; ++head) {
+      const int64_t length = lengths[request][head];
+      TORCH_CHECK(length >= 0 && source + length <= keys[request].size(0), "Invalid head length");
+      lrk_segment &segment = segments[static_cast<size_t>(request * heads + head)];
+      segment.keys = keys[request].data_ptr();
+      segment.values = values[request].data_ptr();
+      segment.positions = positions[request].data_ptr<float>();
+      segment.source_row = source;
+      segment.length = length;
+      segment.destination_row = destination;
+      segment.logical_position = logical_positions[request];
+      source += length;
+      destination += length + 1;
+    }
+    TORCH_CHECK(source == keys[request].size(0), "Head lengths do not cover cache rows");
+  }
+  auto output_keys = torch::empty({destination, dimension}, new_keys.options());
+  auto output_values = torch::empty_like(output_keys);
+  auto output_positions = torch::empty({destination, 1}, new_keys.options().dtype(torch::kFloat));
+  check_status(lrk_batch_append(segments.data(), static_cast<int64_t>(segments.size()), new_keys.data_ptr(),
+                                new_values.data_ptr(), dimension, dtype_code(new_keys.scalar_type()),
+                                output_keys.data_ptr(), output_values.data_ptr(), output_positions.data_ptr<float>(),
+                                destination, current_stream()));
+  return {output_keys, output_values, output_positions};
+}
+
+// Selection (selection.py:52-88): raw/pooled [n] f32; ends, position_starts
+// [segments] i64 on the same device.  Returns (values f32 [count], segment ids
+// i64 [count], positions i64 [count], stats i64 [2]) on the device.
+std::vector<torch::Tensor> refine(torch::Tensor raw, torch::Tensor pooled, torch::Tensor ends,
+                                  torch::Tensor position_starts, int64_t count) {
+  for (const auto &tensor : {raw, pooled, ends, position_starts}) check_cuda(tensor, raw);
+  TORCH_CHECK(raw.scalar_type() == at::kFloat && pooled.scalar_type() == at::kFloat && raw.dim() == 1 &&
+                  pooled.sizes() == raw.sizes(),
+              "Refine scores must be matching 1-D float32 tensors");
+  TORCH_CHECK(ends.scalar_type() == at::kLong && position_starts.scalar_type() == at::kLong && ends.dim() == 1 &&
+                  ends.numel() >= 1 && position_starts.sizes() == ends.sizes(),
+              "Invalid segment bounds");
+  TORCH_CHECK(count >= 0 && count <= raw.numel(), "Invalid selection count");
+  c10::cuda::CUDAGuard guard(raw.device());
+  const int64_t n = raw.numel(), segments = ends.numel();
+  auto values = torch::empty({count}, raw.options());
+  auto segment_ids = torch::empty({count}, ends.options());
+  auto positions = torch::empty({count}, ends.options());
+  auto stats = torch::empty({2}, ends.options());
+  const size_t bytes = lrk_refine_workspace_bytes(n, segments);
+  auto workspace = torch::empty({static_cast<int64_t>(bytes)}, raw.options().dtype(at::kByte));
+  check_status(lrk_refine(raw.data_ptr<float>(), pooled.data_ptr<float>(), n, ends.data_ptr<int64_t>(),
+                          position_starts.data_ptr<int64_t>(), segments, count, workspace.data_ptr(), bytes,
+                          values.data_ptr<float>(), segment_ids.data_ptr<int64_t>(), positions.data_ptr<int64_t>(),
+                          stats.data_ptr<int64_t>(), current_stream()));
+  return {values, segment_ids, positions, stats};
+}
+
+// torch.topk(x, k, largest=False, sorted=True) for a 1-D float32 CUDA tensor.
+std::vector<torch::Tensor> topk_smallest(torch::Tensor x, int64_t k) {
+  check_cuda(x, x);
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.dim() == 1, "topk_smallest expects a 1-D float32 tensor");
+  TORCH_CHECK(k >= 0 && k <= x.numel(), "selected index k out of range");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto values = torch::empty({k}, x.options());
+  auto indices = torch::empty({k}, x.options().dtype(at::kLong));
+  const size_t bytes = lrk_topk_workspace_bytes(x.numel());
+  auto workspace = torch::empty({static_cast<int64_t>(bytes)}, x.options().dtype(at::kByte));
+  check_status(lrk_topk_smallest(x.data_ptr<float>(), x.numel(), k, workspace.data_ptr(), bytes,
+                                 values.data_ptr<float>(), indices.data_ptr<int64_t>(), current_stream()));
+  return {values, indices};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
+  module.def("temporal_probabilities", &temporal_probabilities);
+  module.def("temporal_risk", &temporal_risk);
+  module.def("append", &append);
+  module.def("compact", &compact);
+  module.def("pool", &pool);
+  module.def("merge", &merge);
+  module.def("pack", &pack);
+  module.def("batch_append", &batch_append);
+  module.def("refine", &refine);
+  module.def("topk_smallest", &topk_smallest);
+}

@@ -1,0 +1,110 @@
+"""Drop-in replacement for LazyRecall's selection step on the GPU.
+
+refine_arrays(allocation, refinement, count) keeps the signature, checks and
+return value of selection.py:52-88 in the reference: a rank-slot queue
+(ArrayReferences) plus the number of changed identities and changed heads.
+The body -- global bottom-`count` of raw scores, per-head quotas, per-head
+bottom-quota of pooled scores and the transplant of those picks into the
+raw-score slots -- runs as one sequence of liblrk kernels (_C.refine) with a
+single device-to-host copy of the finished queue at the end.  Tie handling
+reproduces torch.topk(largest=False, sorted=True) on CUDA, which is what the
+reference calls.
+
+Integration: a caller that wants the reference's own ArrayReferences class
+passes it as ``references_type``; by default the equivalent class below is
+returned.
+"""
+from __future__ import annotations
+
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import operators
+
+
+@dataclass(order=True, frozen=True)
+class KVReference:
+    """One queued identity: its raw score, layer, KV head and head-local row."""
+    score: float
+    layer: int
+    head: int
+    position: int
+
+
+class ArrayReferences(Sequence):
+    """Column-store queue of KV identities in eviction order.
+
+    Same interface as the reference's queue type: ``scores``, ``segments``,
+    ``positions`` (one entry per queue slot), ``coordinates`` (segment ->
+    (layer, head)), slicing, item access as :class:`KVReference` and
+    :meth:`groups` ((layer, head) -> sorted positions)."""
+
+    def __init__(self, scores, segments, positions, coordinates):
+        self.scores = np.asarray(scores)
+        self.segments = np.asarray(segments, dtype=np.int64)
+        self.positions = np.asarray(positions, dtype=np.int64)
+        self.coordinates = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)
+        if not len(self.scores) == len(self.segments) == len(self.positions):
+            raise ValueError("Queue column lengths differ")
+
+    def __len__(self):
+        return int(self.positions.shape[0])
+
+    def __getitem__(self, index):
+        if isinstance(index, slice):
+            return type(self)(self.scores[index], self.segments[index], self.positions[index], self.coordinates)
+        layer, head = self.coordinates[self.segments[index]]
+        return KVReference(float(self.scores[index]), int(layer), int(head), int(self.positions[index]))
+
+    def groups(self):
+        """(layer, head) -> ascending positions queued for that head."""
+        result = {}
+        if not len(self):
+            return result
+        for segment in np.unique(self.segments):
+            layer, head = self.coordinates[segment]
+            result[(int(layer), int(head))] = np.sort(self.positions[self.segments == segment])
+        return result
+
+
+def refine_arrays(allocation, refinement, count, references_type=None):
+    """GPU refine_arrays (selection.py:52-88).  ``allocation`` and
+    ``refinement`` are score tables with ``scores`` (1-D float32 CUDA tensor),
+    ``segments`` (objects with layer, head, position_start, count) and
+    ``cumulative_ends``.  Returns (references, changed, changed_heads)."""
+    import torch
+
+    make = references_type or ArrayReferences
+    if allocation.segments != refinement.segments or allocation.cumulative_ends != refinement.cumulative_ends:
+        raise ValueError("Allocation and refinement layouts differ")
+    coordinates = [(segment.layer, segment.head) for segment in allocation.segments]
+    if len(set(coordinates)) != len(coordinates):
+        raise ValueError("Each physical head must have exactly one score segment")
+    count = min(max(0, int(count)), allocation.scores.numel())
+    if not count:
+        return make([], [], [], coordinates), 0, 0
+    ends = np.asarray(allocation.cumulative_ends, dtype=np.int64)
+    starts = np.concatenate(([0], ends[:-1]))
+    if ends[-1] != allocation.scores.numel() or any(
+            end - start != segment.count for start, end, segment in zip(starts, ends, allocation.segments)):
+        raise ValueError("Invalid segment bounds")
+    raw = allocation.scores
+    if not raw.is_cuda:
+        raise RuntimeError("refine_arrays runs on CUDA score tables only")
+    device = raw.device
+    ends_device = torch.as_tensor(ends, device=device)
+    position_starts = torch.as_tensor([segment.position_start for segment in allocation.segments],
+                                      dtype=torch.int64, device=device)
+    values, segment_ids, positions, stats = operators().refine(
+        raw.float().contiguous(), refinement.scores.float().contiguous(), ends_device, position_starts, count)
+    packed = torch.cat([segment_ids, positions, stats]).cpu().numpy()
+    values = values.cpu().numpy()
+    changed, changed_heads = int(packed[2 * count]), int(packed[2 * count + 1])
+    return make(values, packed[:count], packed[count:2 * count], coordinates), changed, changed_heads
+
+
+def allocation_preserving_references(allocation_table, refinement_table, count, references_type=None):
+    """scoring.py:356-361 without the timing wrapper: refine_arrays' result."""
+    return refine_arrays(allocation_table, refinement_table, count, references_type)

@@ -1,0 +1,210 @@
+/*
+ * lrk.h — C ABI of liblrk, the sm_100a KV-management kernels behind the
+ * LazyRecall operator modules (lazy_recall._C, lazy_recall._legacy_C,
+ * lazy_recall._host).
+ *
+ * Every entry point takes plain device pointers, element counts and the CUDA
+ * stream to launch on; none allocates device memory, synchronises the stream
+ * or touches torch.  Each returns LRK_OK (0) or an error code, and on error
+ * lrk_last_error() gives a message for the calling thread.  Arguments are
+ * validated on the host before anything is launched; device code additionally
+ * skips (never performs) an access whose index falls outside the sizes given
+ * here, so inconsistent metadata cannot read or write out of bounds.
+ *
+ * Reference citations name the operator each entry point replaces, by the
+ * file path inside the reference project (wrnwwrnw/code_for_iclr27).
+ */
+#ifndef LRK_H
+#define LRK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; a null value means the legacy default stream. */
+typedef struct CUstream_st *lrk_stream_t;
+
+enum lrk_status {
+  LRK_OK = 0,
+  LRK_ERR_INVALID = 1,     /* an argument was rejected before any launch */
+  LRK_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  LRK_ERR_UNSUPPORTED = 3, /* dtype / size combination not implemented */
+  LRK_ERR_WORKSPACE = 4    /* the caller's workspace is too small */
+};
+
+/* Element types, as the reference's AT_DISPATCH_FLOATING_TYPES_AND2(Half, BFloat16). */
+enum lrk_dtype { LRK_F32 = 0, LRK_F64 = 1, LRK_F16 = 2, LRK_BF16 = 3 };
+
+/* Message for the last failed call on this host thread ("" if none). */
+const char *lrk_last_error(void);
+/* 100 * major + minor of this library. */
+int lrk_version(void);
+/* Size in bytes of one element of an lrk_dtype, or 0 for an unknown code. */
+int lrk_dtype_size(int dtype);
+
+/* ---------------------------------------------------------------- scoring */
+
+/* Masked causal softmax of one query chunk + value projection.
+ * Replaces _C.temporal_probabilities (csrc/scoring.cu:205-233, kernel :32-66;
+ * bound at csrc/bindings.cpp:21).
+ * logits [window, groups, length] of logits_dtype (F32/F16/BF16);
+ * projected_values [groups, length] f32; query_positions [window] i64;
+ * key_positions [length] f32 -> probabilities [window, groups, length] f32,
+ * output_projection [window, groups] f32.  Each scaled logit is rounded to
+ * logits_dtype before the softmax, exactly as the reference. */
+int lrk_temporal_probabilities(const void *logits, int logits_dtype, const float *projected_values,
+                               const int64_t *query_positions, const float *key_positions,
+                               float *probabilities, float *output_projection, int64_t window,
+                               int64_t groups, int64_t length, float scale, lrk_stream_t stream);
+
+/* Temporal decision risk of candidates [first, last) of one head.
+ * Replaces _C.temporal_risk (csrc/scoring.cu:235-255, kernel :68-128; bound at
+ * csrc/bindings.cpp:22).  margin is a device pointer to one f32.
+ * scores [last - first] f32. */
+int lrk_temporal_risk(const float *probabilities, const float *output_projection,
+                      const float *projected_values, const float *margin, float *scores,
+                      int64_t window, int64_t groups, int64_t length, int64_t first, int64_t last,
+                      float epsilon, lrk_stream_t stream);
+
+/* Per-segment sliding max of odd width (Pool7).
+ * Replaces _C.pool (csrc/scoring.cu:316-329, kernel :190-203; bound at
+ * csrc/bindings.cpp:25).  scores [n] f32, bounds [segments + 1] i64 (device).
+ * maximum_count is validated (> 0) like the reference; every position of every
+ * segment is written whatever its value. */
+int lrk_pool(const float *scores, int64_t n, const int64_t *bounds, int64_t segments,
+             int64_t maximum_count, int64_t width, float *out, lrk_stream_t stream);
+
+/* Frozen single-query decision-risk scores (legacy v0 scorer).
+ * Replaces _legacy_C.decision_risk_scores (csrc/cache_legacy.cu:244-302,
+ * kernel :81-135).  probabilities [groups, candidates] f32; values
+ * [candidates, dimension] of values_dtype; head_outputs, gradients
+ * [groups, dimension] f32 -> scores [candidates] f32. */
+int lrk_decision_risk(const float *probabilities, const void *values, int values_dtype,
+                      const float *head_outputs, const float *gradients, int64_t groups,
+                      int64_t candidates, int64_t dimension, double base_margin, float epsilon,
+                      float *scores, lrk_stream_t stream);
+
+/* ------------------------------------------------- cache data movement */
+
+/* Append `added` rows to each head segment of a packed layer.
+ * Replaces _C.append (csrc/scoring.cu:264-292, kernel :130-162; bound at
+ * csrc/bindings.cpp:23).  keys/values [rows, dimension], positions [rows];
+ * new_keys/new_values [heads, added, dimension]; cumulative [heads + 1] i32
+ * (device) -> out_* [rows + heads * added, ...], out_cumulative [heads + 1],
+ * out_lengths [heads] (i32).  New rows get position float(logical_start + i). */
+int lrk_append(const void *keys, const void *values, const float *positions, int64_t rows,
+               const void *new_keys, const void *new_values, const int32_t *cumulative,
+               int64_t heads, int64_t added, int64_t dimension, int dtype, int64_t logical_start,
+               void *out_keys, void *out_values, float *out_positions, int32_t *out_cumulative,
+               int32_t *out_lengths, lrk_stream_t stream);
+
+/* Drop sorted, unique row indices from packed K/V/positions.
+ * Replaces _C.compact (csrc/scoring.cu:294-314, kernel :164-188; bound at
+ * csrc/bindings.cpp:24).  removed [removed_count] i64 sorted ascending ->
+ * out_* [rows - removed_count, ...]. */
+int lrk_compact(const void *keys, const void *values, const float *positions, int64_t rows,
+                int64_t dimension, int dtype, const int64_t *removed, int64_t removed_count,
+                void *out_keys, void *out_values, float *out_positions, lrk_stream_t stream);
+
+/* Two-source gather of recalled rows into a layer.
+ * Replaces _C.merge (csrc/recall.cu:54-84, kernel :7-28; bound at
+ * csrc/bindings.cpp:26).  recalled [recalled_rows, 2, dimension] (K then V);
+ * mapping [out_rows] i64: m >= 0 takes existing row m, m < 0 takes recalled
+ * row -m-1. */
+int lrk_merge(const void *keys, const void *values, const float *positions, int64_t rows,
+              const void *recalled, const float *recalled_positions, int64_t recalled_rows,
+              const int64_t *mapping, int64_t out_rows, int64_t dimension, int dtype,
+              void *out_keys, void *out_values, float *out_positions, lrk_stream_t stream);
+
+/* Gather evicted rows into an archive payload.
+ * Replaces _C.pack (csrc/recall.cu:86-111, kernel :30-47; bound at
+ * csrc/bindings.cpp:27).  payload [count, 2, dimension], metadata [count, 3]
+ * i64 = (layer, heads[i], int64(positions[indices[i]])). */
+int lrk_pack(const void *keys, const void *values, const float *positions, int64_t rows,
+             int64_t dimension, int dtype, const int64_t *indices, const int64_t *heads,
+             int64_t count, int64_t layer, void *payload, int64_t *metadata, lrk_stream_t stream);
+
+/* One (request, head) segment of a static-batch append.  Same fields, in the
+ * same order, as the reference's 7-wide descriptor rows
+ * (csrc/batch_append.cu:179-186). */
+typedef struct lrk_segment {
+  const void *keys;         /* request's packed K [*, dimension] (device) */
+  const void *values;       /* request's packed V */
+  const float *positions;   /* request's positions */
+  int64_t source_row;       /* first row of this head in the request's cache */
+  int64_t length;           /* rows of this head before the append */
+  int64_t destination_row;  /* first row of this head in the output */
+  int64_t logical_position; /* position value of the appended token */
+} lrk_segment;
+
+/* Multi-request one-token append into one packed output.
+ * Replaces _C.batch_append (csrc/batch_append.cu:36-94, kernel :8-34; bound at
+ * csrc/bindings.cpp:28).  segments is a HOST array (request-major, head-minor);
+ * it is passed to the kernels by value, so no descriptor copy or device
+ * allocation happens.  new_keys/new_values [segment_count, dimension]. */
+int lrk_batch_append(const lrk_segment *segments, int64_t segment_count, const void *new_keys,
+                     const void *new_values, int64_t dimension, int dtype, void *out_keys,
+                     void *out_values, float *out_positions, int64_t out_rows,
+                     lrk_stream_t stream);
+
+/* Append new_length states per head to one flattened cache tensor.
+ * Replaces _legacy_C.append_flattened_cache (csrc/cache_legacy.cu:145-197,
+ * kernel :13-40).  states [total_heads, new_length, dimension]; head_lens
+ * [total_heads], cu_head_lens [total_heads + 1] i32 (device). */
+int lrk_append_flattened(const void *cache, int64_t rows, const void *states, int64_t total_heads,
+                         int64_t new_length, int64_t dimension, int dtype, const int32_t *head_lens,
+                         const int32_t *cu_head_lens, void *out, int64_t out_rows,
+                         lrk_stream_t stream);
+
+/* Gather kept rows of K and V.
+ * Replaces _legacy_C.compact_flattened_kv (csrc/cache_legacy.cu:199-242,
+ * kernel :42-61). */
+int lrk_compact_flattened(const void *keys, const void *values, int64_t rows, int64_t dimension,
+                          int dtype, const int64_t *keep, int64_t keep_count, void *out_keys,
+                          void *out_values, lrk_stream_t stream);
+
+/* ------------------------------------------------------------ selection */
+
+/* Workspace bytes lrk_refine needs for n scores in `segments` segments. */
+size_t lrk_refine_workspace_bytes(int64_t n, int64_t segments);
+
+/* Allocation-preserving refinement: the global bottom-`count` of raw scores,
+ * per-segment quotas, each segment's bottom-quota of pooled scores, and the
+ * transplant of those refined positions into the raw-score slots.
+ * Replaces the torch.topk + numpy body of refine_arrays
+ * (src/lazy_recall/selection.py:52-88, transplant :42-49); the ordering
+ * reproduces torch.topk(largest=False, sorted=True) on CUDA, ties included.
+ * raw, pooled [n] f32; segment_ends, position_starts [segments] i64 (device).
+ * Outputs (device): values [count] f32 (raw scores, ascending),
+ * segment_ids [count] i64, positions [count] i64, stats [2] i64 =
+ * (changed identities, changed heads). */
+int lrk_refine(const float *raw, const float *pooled, int64_t n, const int64_t *segment_ends,
+               const int64_t *position_starts, int64_t segments, int64_t count, void *workspace,
+               size_t workspace_bytes, float *values, int64_t *segment_ids, int64_t *positions,
+               int64_t *stats, lrk_stream_t stream);
+
+/* Workspace bytes lrk_topk_smallest needs for n scores. */
+size_t lrk_topk_workspace_bytes(int64_t n);
+
+/* torch.topk(x, k, largest=False, sorted=True) of one 1-D f32 slice, with the
+ * same choice and order of tied elements as PyTorch's CUDA implementation.
+ * values [k] f32, indices [k] i64 (device). */
+int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
+                      size_t workspace_bytes, float *values, int64_t *indices, lrk_stream_t stream);
+
+/* ------------------------------------------------------------------ host */
+
+/* Page-lock a host range for async DMA (cudaHostRegisterDefault).
+ * Replaces _host.register_host (csrc/host.cpp:5-8). */
+int lrk_register_host(void *address, size_t bytes);
+/* Replaces _host.unregister_host (csrc/host.cpp:10-13). */
+int lrk_unregister_host(void *address);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LRK_H */
