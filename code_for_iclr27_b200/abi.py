@@ -29,6 +29,12 @@ class Segment(ctypes.Structure):
                 ("destination_row", I64), ("logical_position", I64)]
 
 
+class ScoreSegment(ctypes.Structure):
+    """lrk_score_segment (include/lrk.h)."""
+    _fields_ = [("logits", P), ("projected_values", P), ("projected_stride", I64), ("key_positions", P),
+                ("length", I64), ("first", I64), ("last", I64), ("scores", P)]
+
+
 SIGNATURES = {
     "lrk_last_error": (ctypes.c_char_p, []),
     "lrk_version": (I32, []),
@@ -36,6 +42,8 @@ SIGNATURES = {
     "lrk_temporal_probabilities": (I32, [P, I32, P, P, P, P, P, I64, I64, I64, F, P]),
     "lrk_temporal_risk": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, F, P]),
     "lrk_pool": (I32, [P, I64, P, I64, I64, I64, P, P]),
+    "lrk_temporal_scores_workspace_bytes": (SIZE, [I64, I64, I64]),
+    "lrk_temporal_scores": (I32, [ctypes.POINTER(ScoreSegment), I64, I32, P, I64, I64, F, P, F, P, SIZE, P]),
     "lrk_decision_risk": (I32, [P, P, I32, P, P, I64, I64, I64, D, F, P, P]),
     "lrk_append": (I32, [P, P, P, I64, P, P, P, I64, I64, I64, I32, I64, P, P, P, P, P, P]),
     "lrk_compact": (I32, [P, P, P, I64, I64, I32, P, I64, P, P, P, P]),

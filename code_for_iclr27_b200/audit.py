@@ -1,0 +1,147 @@
+"""One LazyRecall audit pass on the GPU: score -> pool -> select -> evict.
+
+Mirrors the KV side of LazyController.run_audit (controller.py:140-160):
+compute_score_table (scoring.py:198-308) with temporal_head_scores'
+GPU branch (scoring.py:152-195), pool_score_table (scoring.py:322-335),
+refine_arrays (selection.py:52-88) and the eviction of the immediate prefix
+(controller.py:154-158 -> cache.remove_positions).  The model-side inputs of
+an audit -- per-layer query history [W, query_heads, D], query positions
+[W], and the per-layer margin gradient projected to the head inputs
+[query_heads, D] -- are passed in.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import List
+
+import numpy as np
+
+from . import operators
+from .selection import ArrayReferences, refine_arrays
+
+
+@dataclass(frozen=True)
+class ScoreSegment:
+    """One physical head's candidate range (_core/scoring.py:198-203)."""
+    layer: int
+    head: int
+    position_start: int
+    count: int
+
+
+@dataclass
+class ScoreTable:
+    scores: "object"
+    segments: List[ScoreSegment]
+    cumulative_ends: List[int]
+
+
+def temporal_head_scores(queries, query_positions, keys, key_positions, values, candidate_start, candidate_end,
+                         margin_gradient, base_margin, denominator_epsilon, query_chunk_size):
+    """scoring.py:152-195 on the new operators: pv = g V^T, then per chunk of
+    queries bf16 logits = Q K^T, temporal_probabilities, temporal_risk, and a
+    running maximum."""
+    import torch
+
+    C = operators()
+    projected_values = torch.matmul(margin_gradient.float(), values.float().transpose(0, 1)).contiguous()
+    key_positions = key_positions.to(dtype=torch.float32).contiguous()
+    query_positions = query_positions.to(dtype=torch.int64).contiguous()
+    margin = base_margin.to(device=keys.device, dtype=torch.float32).reshape(1).contiguous()
+    bytes_per_query = queries.shape[1] * keys.shape[0] * (keys.element_size() + 4)
+    chunk_size = min(query_chunk_size, max(1, (64 * 1024 ** 2) // bytes_per_query))
+    result = None
+    for start in range(0, queries.shape[0], chunk_size):
+        end = min(start + chunk_size, queries.shape[0])
+        logits = torch.matmul(queries[start:end].to(keys.dtype), keys.transpose(0, 1))
+        probabilities, output_projection = C.temporal_probabilities(
+            logits.contiguous(), projected_values, query_positions[start:end], key_positions,
+            1.0 / math.sqrt(keys.shape[-1]))
+        scores = C.temporal_risk(probabilities, output_projection, projected_values, margin, candidate_start,
+                                 candidate_end, denominator_epsilon)
+        result = scores if result is None else torch.maximum(result, scores)
+    return result
+
+
+def score_table(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
+                denominator_epsilon=1e-6, query_chunk_size=250) -> ScoreTable:
+    """compute_score_table (scoring.py:198-308): every eligible generation row
+    of every (layer, KV head), prompt protected, the last protect_recent rows
+    protected.  queries[layer] [W, query_heads, D]; gradients[layer]
+    [query_heads, D] float32."""
+    import torch
+
+    parts, segments, ends, running = [], [], [], 0
+    for layer_index, layer in enumerate(cache.layers):
+        heads = len(layer.head_lens)
+        groups = queries[layer_index].shape[1] // heads
+        bounds = layer.bounds()
+        positions = layer.positions.reshape(-1)
+        for head in range(heads):
+            start, end = int(bounds[head]), int(bounds[head + 1])
+            candidate_start = int(layer.prompt_lens[head])
+            candidate_end = max(candidate_start, end - start - protect_recent)
+            if candidate_end <= candidate_start:
+                continue
+            mapped = queries[layer_index][:, head * groups:(head + 1) * groups]
+            scores = temporal_head_scores(mapped, query_positions, layer.keys[start:end], positions[start:end],
+                                          layer.values[start:end], candidate_start, candidate_end,
+                                          gradients[layer_index][head * groups:(head + 1) * groups], base_margin,
+                                          denominator_epsilon, query_chunk_size)
+            count = candidate_end - candidate_start
+            parts.append(scores)
+            segments.append(ScoreSegment(layer_index, head, candidate_start, count))
+            running += count
+            ends.append(running)
+    if not parts:
+        raise RuntimeError("No eligible KV remains after prompt/recent protection")
+    return ScoreTable(torch.cat(parts), segments, ends)
+
+
+def pool_table(table: ScoreTable, kernel_size: int = 7) -> ScoreTable:
+    """pool_score_table (scoring.py:322-335)."""
+    import torch
+
+    bounds = torch.tensor([0] + table.cumulative_ends, dtype=torch.int64, device=table.scores.device)
+    pooled = operators().pool(table.scores.contiguous(), bounds, max(s.count for s in table.segments), kernel_size)
+    return ScoreTable(pooled, list(table.segments), list(table.cumulative_ends))
+
+
+@dataclass
+class AuditResult:
+    table: ScoreTable
+    references: ArrayReferences
+    changed: int
+    changed_heads: int
+    evicted: int
+
+
+def audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
+               protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250, pool_kernel=7) -> AuditResult:
+    """Score, pool, select immediate + queued references, evict the immediate
+    prefix.  Returns the queue (references[immediate:] is the lazy queue)."""
+    table = score_table(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                        denominator_epsilon, query_chunk_size)
+    pooled = pool_table(table, pool_kernel)
+    references, changed, changed_heads = refine_arrays(table, pooled, immediate + queued)
+    if len(references) < immediate:
+        raise RuntimeError("Not enough unprotected candidates to enforce the budget")
+    removals = {key: value for key, value in references[:immediate].groups().items()}
+    evicted = cache.remove_positions(removals) if removals else 0
+    return AuditResult(table, references, changed, changed_heads, evicted)
+
+
+def evict_prefix(cache, queue: ArrayReferences, removed_at_audit: dict, count: int):
+    """Lazy eviction (controller.py:57-70): pop `count` queued references,
+    shifting their audit-time positions by the rows already removed from the
+    same head since the audit.  Returns (remaining queue, updated removed map)."""
+    removals, updates = {}, {}
+    for segment, positions in queue[:count].groups().items():
+        removed = np.asarray(removed_at_audit.get(segment, ()), dtype=np.int64)
+        removals[segment] = positions - np.searchsorted(removed, positions)
+        updates[segment] = np.union1d(removed, positions)
+    cache.remove_positions(removals)
+    removed_at_audit = dict(removed_at_audit)
+    removed_at_audit.update(updates)
+    return queue[count:], removed_at_audit

@@ -7,10 +7,10 @@
 //   PyTorch's radix select uses; the k chosen elements are the k smallest by
 //   (key, index).
 // * Output order is (key, index) -- PyTorch's stable sorts -- except for
-//   slices shorter than 100000 elements with 2 <= k <= 32, where PyTorch
-//   sorts the gathered elements (keys below the k-th in index order, then
-//   the k-th key's ties in index order) with an unstable 32-wide bitonic
-//   network; that network is replayed here exactly.
+//   2 <= k <= 32, where PyTorch sorts the gathered elements (keys below the
+//   k-th in index order, then the k-th key's ties in index order) with an
+//   unstable 32-wide bitonic network; that network is replayed here exactly.
+//   This holds at every slice length (checked against torch 2.11 on B200).
 //
 // Machinery: a stable LSD radix sort of (64-bit key, 32-bit payload) pairs in
 // 8-bit digits.  Each pass is a per-tile digit histogram, one exclusive scan
@@ -28,7 +28,6 @@ namespace {
 constexpr int kSortThreads = 256;
 constexpr int kSortRounds = 16;
 constexpr int kSortTile = kSortThreads * kSortRounds;  // elements per scatter tile
-constexpr int64_t kTopkSortThreshold = 100000;     // PyTorch: 1-D slices this long are fully sorted
 constexpr int kBitonicMax = 32;
 constexpr int kMaxSharedSegments = 4096;
 
@@ -278,8 +277,8 @@ __global__ void global_bitonic_kernel(uint32_t *values, int k, const float *scor
   if (threadIdx.x == 0 && blockIdx.x == 0) bitonic_replay(values, k, scores);
 }
 
-// Per-segment fix-up: segments shorter than the sort threshold whose quota
-// is in [2, 32].  One thread per segment.
+// Per-segment fix-up: segments whose quota is in [2, 32].  One thread per
+// segment.
 __global__ void segment_bitonic_kernel(uint32_t *sorted_values, const int64_t *__restrict__ ends, int64_t segments,
                                        const uint32_t *__restrict__ quota, const float *scores) {
   const int64_t s = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -287,7 +286,7 @@ __global__ void segment_bitonic_kernel(uint32_t *sorted_values, const int64_t *_
   const int64_t start = s == 0 ? 0 : ends[s - 1];
   const int64_t length = ends[s] - start;
   const uint32_t q = quota[s];
-  if (length < kTopkSortThreshold && q >= 2 && q <= kBitonicMax && q <= length)
+  if (q >= 2 && q <= kBitonicMax && q <= length)
     bitonic_replay(sorted_values + start, q, scores);
 }
 
@@ -473,7 +472,7 @@ extern "C" int lrk_refine(const float *raw, const float *pooled, int64_t n, cons
   const int raw_at = radix_sort(l.raw_sort, n, 32, s, status);
   if (status != LRK_OK) return status;
   uint32_t *picked = l.raw_sort.values[raw_at];
-  if (n < kTopkSortThreshold && count >= 2 && count <= kBitonicMax) global_bitonic_kernel<<<1, 1, 0, s>>>(picked, static_cast<int>(count), raw);
+  if (count >= 2 && count <= kBitonicMax) global_bitonic_kernel<<<1, 1, 0, s>>>(picked, static_cast<int>(count), raw);
   picks_kernel<<<grid_for(count), 256, 0, s>>>(picked, count, raw, segment_ends, segments, values, segment_ids,
                                                l.quota, l.mark, l.pick_sort.keys[0], l.pick_sort.values[0]);
   if ((status = launch_status("refine picks")) != LRK_OK) return status;
@@ -531,7 +530,7 @@ extern "C" int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *wor
   if (status != LRK_OK) return status;
   const int at = radix_sort(b, n, 32, s, status);
   if (status != LRK_OK) return status;
-  if (n < kTopkSortThreshold && k >= 2 && k <= kBitonicMax) global_bitonic_kernel<<<1, 1, 0, s>>>(b.values[at], static_cast<int>(k), x);
+  if (k >= 2 && k <= kBitonicMax) global_bitonic_kernel<<<1, 1, 0, s>>>(b.values[at], static_cast<int>(k), x);
   gather_topk_kernel<<<grid_for(k), 256, 0, s>>>(b.values[at], k, x, values, indices);
   return launch_status("topk gather");
 }

@@ -319,6 +319,68 @@ std::vector<torch::Tensor> topk_smallest(torch::Tensor x, int64_t k) {
   return {values, indices};
 }
 
+// Fused scoring of many (layer, head) segments from bf16/fp16/fp32 logits
+// (lrk_temporal_scores).  projected_values[i] may be a strided view (row
+// stride >= length, unit column stride).  Returns the concatenated scores of
+// all segments, in order -- the layout compute_score_table builds with
+// torch.cat (scoring.py:291).
+torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<torch::Tensor> projected_values,
+                              std::vector<torch::Tensor> key_positions, std::vector<int64_t> first,
+                              std::vector<int64_t> last, torch::Tensor query_positions, torch::Tensor margin,
+                              double scale, double epsilon) {
+  const size_t count = logits.size();
+  TORCH_CHECK(count > 0 && projected_values.size() == count && key_positions.size() == count &&
+                  first.size() == count && last.size() == count,
+              "Segment lists differ in length");
+  check_cuda(query_positions, logits[0]);
+  check_cuda(margin, logits[0]);
+  TORCH_CHECK(query_positions.scalar_type() == at::kLong && margin.scalar_type() == at::kFloat &&
+                  margin.numel() == 1,
+              "Invalid query positions or margin");
+  const auto dtype = logits[0].scalar_type();
+  TORCH_CHECK(dtype == at::kFloat || dtype == at::kHalf || dtype == at::kBFloat16,
+              "Only FP32/FP16/BF16 scores are supported");
+  const int64_t window = logits[0].size(0), groups = logits[0].size(1);
+  TORCH_CHECK(query_positions.numel() == window, "Invalid query positions");
+  c10::cuda::CUDAGuard guard(logits[0].device());
+  int64_t total = 0;
+  for (size_t i = 0; i < count; ++i) total += last[i] - first[i];
+  auto scores = torch::empty({total}, margin.options());
+  std::vector<lrk_score_segment> segments(count);
+  int64_t offset = 0;
+  for (size_t i = 0; i < count; ++i) {
+    check_cuda(logits[i], logits[0]);
+    TORCH_CHECK(logits[i].dim() == 3 && logits[i].size(0) == window && logits[i].size(1) == groups &&
+                    logits[i].scalar_type() == dtype,
+                "logits must be [window, groups, positions] of one dtype");
+    const int64_t length = logits[i].size(2);
+    const auto &pv = projected_values[i];
+    TORCH_CHECK(pv.is_cuda() && pv.device() == logits[0].device() && pv.scalar_type() == at::kFloat &&
+                    pv.dim() == 2 && pv.size(0) == groups && pv.size(1) == length && pv.stride(1) == 1,
+                "Invalid projected values");
+    check_cuda(key_positions[i], logits[0]);
+    TORCH_CHECK(key_positions[i].scalar_type() == at::kFloat && key_positions[i].numel() == length,
+                "Invalid key positions");
+    lrk_score_segment &s = segments[i];
+    s.logits = logits[i].data_ptr();
+    s.projected_values = pv.data_ptr<float>();
+    s.projected_stride = groups > 1 ? pv.stride(0) : length;
+    s.key_positions = key_positions[i].data_ptr<float>();
+    s.length = length;
+    s.first = first[i];
+    s.last = last[i];
+    s.scores = scores.data_ptr<float>() + offset;
+    offset += last[i] - first[i];
+  }
+  const size_t bytes = lrk_temporal_scores_workspace_bytes(static_cast<int64_t>(count), window, groups);
+  auto workspace = torch::empty({static_cast<int64_t>(bytes)}, margin.options().dtype(at::kByte));
+  check_status(lrk_temporal_scores(segments.data(), static_cast<int64_t>(count), dtype_code(dtype),
+                                   query_positions.data_ptr<int64_t>(), window, groups, static_cast<float>(scale),
+                                   margin.data_ptr<float>(), static_cast<float>(epsilon), workspace.data_ptr(), bytes,
+                                   current_stream()));
+  return scores;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -332,4 +394,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("batch_append", &batch_append);
   module.def("refine", &refine);
   module.def("topk_smallest", &topk_smallest);
+  module.def("temporal_scores", &temporal_scores);
 }

@@ -87,6 +87,33 @@ int lrk_decision_risk(const float *probabilities, const void *values, int values
                       int64_t candidates, int64_t dimension, double base_margin, float epsilon,
                       float *scores, lrk_stream_t stream);
 
+/* One (layer, KV head) segment of a fused scoring call. */
+typedef struct lrk_score_segment {
+  const void *logits;              /* [window, groups, length] of the call's logits dtype */
+  const float *projected_values;   /* row g at projected_values + g * projected_stride, [length] each */
+  int64_t projected_stride;        /* elements between the groups' projected-value rows (>= length) */
+  const float *key_positions;      /* [length] */
+  int64_t length;                  /* rows of this head */
+  int64_t first;                   /* candidate interval [first, last) */
+  int64_t last;
+  float *scores;                   /* [last - first] output */
+} lrk_score_segment;
+
+/* Workspace bytes for lrk_temporal_scores. */
+size_t lrk_temporal_scores_workspace_bytes(int64_t segments, int64_t window, int64_t groups);
+
+/* Temporal decision risk of every segment's candidates over all `window`
+ * queries, straight from logits: the composition temporal_probabilities ->
+ * temporal_risk -> running maximum over query chunks that
+ * src/lazy_recall/scoring.py:179-195 performs per head, without writing the
+ * probabilities.  Many heads per call (segments is a HOST array).  Agrees with
+ * the drop-in operators within 1e-5 relative (different summation order).
+ * No counterpart operator in the reference (new entry point). */
+int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype,
+                        const int64_t *query_positions, int64_t window, int64_t groups, float scale,
+                        const float *margin, float epsilon, void *workspace, size_t workspace_bytes,
+                        lrk_stream_t stream);
+
 /* ------------------------------------------------- cache data movement */
 
 /* Append `added` rows to each head segment of a packed layer.

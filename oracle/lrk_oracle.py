@@ -14,7 +14,6 @@ from __future__ import annotations
 import numpy as np
 
 LANES = 256
-TOPK_SORT_THRESHOLD = 100000  # torch CUDA topk fully sorts 1-D slices this long
 BITONIC_MAX = 32
 
 # --------------------------------------------------------------- dtypes
@@ -156,7 +155,7 @@ def temporal_head_scores_gpu_path(queries, query_positions, keys, key_positions,
         q = round_to(queries[start:end], kv_dtype)
         # Q K^T comes out of the GEMM in the KV dtype; the kernel then rounds
         # logit * scale to that dtype again.
-        logits = round_to(np.einsum("wgd,ld->wgl", q, keys).astype(np.float32), kv_dtype)
+        logits = round_to((q.reshape(-1, q.shape[-1]) @ keys.T).reshape(q.shape[0], q.shape[1], -1), kv_dtype)
         stored = f32_to_bf16(logits) if kv_dtype == "bf16" else logits
         probs, op = temporal_probabilities(stored, kv_dtype, pv, query_positions[start:end], key_positions, scale)
         scores = temporal_risk(probs, op, pv, np.float32(base_margin), candidate_start, candidate_end,
@@ -186,14 +185,14 @@ def temporal_head_scores_cpu_path(queries, query_positions, keys, key_positions,
     for start in range(0, queries.shape[0], query_chunk_size):
         end = min(start + query_chunk_size, queries.shape[0])
         q = round_to(queries[start:end], kv_dtype)
-        logits = round_to(np.einsum("wgd,ld->wgl", q, keys).astype(np.float32), kv_dtype)
+        logits = round_to((q.reshape(-1, q.shape[-1]) @ keys.T).reshape(q.shape[0], q.shape[1], -1), kv_dtype)
         logits = round_to((logits / sqrt_d).astype(np.float32), kv_dtype)
         causal = kpos[None, None, :] <= qpos_all[start:end].reshape(-1, 1, 1)
         logits = np.where(causal, logits, np.float32(-np.inf))
         shifted = logits - logits.max(axis=-1, keepdims=True)
         weights = np.exp(shifted).astype(np.float32)
         probs = (weights / weights.sum(axis=-1, keepdims=True)).astype(np.float32)
-        og = np.einsum("wgl,gl->wg", probs, pv).astype(np.float32)
+        og = (probs * pv[None]).sum(axis=-1, dtype=np.float32)
         cand = probs[:, :, candidate_start:candidate_end]
         ratio = cand / np.maximum(np.float32(1.0) - cand, np.float32(denominator_epsilon))
         drop = (ratio * (vg[None] - og[..., None])).sum(axis=1).astype(np.float32)
@@ -294,12 +293,15 @@ def merge(keys, values, positions, recalled, recalled_positions, mapping):
     """_C.merge -- csrc/recall.cu:7-28 (CPU twin cache.py:240-245)."""
     mapping = np.asarray(mapping, np.int64)
     positions = np.asarray(positions, np.float32).reshape(-1)
+    recalled_positions = np.asarray(recalled_positions, np.float32).reshape(-1)
+    k = np.empty((len(mapping),) + keys.shape[1:], keys.dtype)
+    v = np.empty_like(k)
+    p = np.empty(len(mapping), np.float32)
     existing = mapping >= 0
-    source = np.where(existing, mapping, -mapping - 1)
-    k = np.where(existing[:, None], keys[np.where(existing, source, 0)], recalled[np.where(existing, 0, source), 0])
-    v = np.where(existing[:, None], values[np.where(existing, source, 0)], recalled[np.where(existing, 0, source), 1])
-    p = np.where(existing, positions[np.where(existing, source, 0)],
-                 np.asarray(recalled_positions, np.float32)[np.where(existing, 0, source)])
+    k[existing], v[existing], p[existing] = keys[mapping[existing]], values[mapping[existing]], \
+        positions[mapping[existing]]
+    rows = -mapping[~existing] - 1
+    k[~existing], v[~existing], p[~existing] = recalled[rows, 0], recalled[rows, 1], recalled_positions[rows]
     return k, v, p.reshape(-1, 1)
 
 
@@ -323,8 +325,8 @@ def batch_append(keys_list, values_list, positions_list, new_keys, new_values, l
         p = np.asarray(p, np.float32).reshape(-1)
         source = 0
         for h, length in enumerate(lengths[r]):
-            k_parts += [k[source:source + length], new_keys[r, h]]
-            v_parts += [v[source:source + length], new_values[r, h]]
+            k_parts += [k[source:source + length], np.asarray(new_keys[r, h]).reshape(1, -1)]
+            v_parts += [v[source:source + length], np.asarray(new_values[r, h]).reshape(1, -1)]
             p_parts += [p[source:source + length], np.asarray([logical[r]], np.float32)]
             source += length
     return np.concatenate(k_parts), np.concatenate(v_parts), np.concatenate(p_parts).reshape(-1, 1)
@@ -402,15 +404,16 @@ def topk_smallest(x, k):
     environment.txt:1; used at selection.py:69 and :77).
 
     Chosen set: the k smallest by (radix key, index).  Order: (radix key,
-    index), except for slices shorter than 100000 with 2 <= k <= 32, where the
-    gathered order (below-kth keys by index, then kth-key ties by index) goes
-    through the bitonic network.  Returns (values, indices)."""
+    index), except for 2 <= k <= 32, where the gathered order (below-kth keys
+    by index, then kth-key ties by index) goes through the bitonic network --
+    at every slice length (measured against torch 2.11 on B200).
+    Returns (values, indices)."""
     x = np.asarray(x, np.float32)
     if k == 0:
         return x[:0].copy(), np.zeros(0, np.int64)
     keys = radix_key(x)
     order = np.lexsort((np.arange(len(x)), keys))[:k]
-    if len(x) < TOPK_SORT_THRESHOLD and 2 <= k <= BITONIC_MAX:
+    if 2 <= k <= BITONIC_MAX:
         kth = keys[order[-1]]
         below = np.sort(order[keys[order] < kth])
         ties = np.sort(order[keys[order] == kth])

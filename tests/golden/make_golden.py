@@ -237,7 +237,7 @@ def make_gpu(out: Path):
         keys, values = rn(rows, d, dtype=torch.bfloat16), rn(rows, d, dtype=torch.bfloat16)
         positions = torch.randperm(rows + 50, generator=g)[:rows].to(torch.float32).reshape(-1, 1).to(dev)
         new_keys, new_values = rn(1, heads, 2, d, dtype=torch.bfloat16), rn(1, heads, 2, d, dtype=torch.bfloat16)
-        out = ref.append(keys, values, positions, new_keys, new_values, cumulative, 12345, int(lengths.max()))
+        appended = ref.append(keys, values, positions, new_keys, new_values, cumulative, 12345, int(lengths.max()))
         removed = torch.randperm(rows, generator=g)[: rows // 3].sort().values.to(dev)
         compacted = ref.compact(keys, values, positions, removed)
         recalled = rn(9, 2, d, dtype=torch.bfloat16)
@@ -256,7 +256,7 @@ def make_gpu(out: Path):
                    p + "recalled_pos": bits(recalled_pos), p + "mapping": bits(mapping), p + "indices": bits(indices),
                    p + "heads": bits(head_ids), p + "payload": bits(payload), p + "metadata": bits(metadata)})
         for j, name in enumerate(["keys", "values", "positions", "cumulative", "lengths"]):
-            fx[p + "append_" + name] = bits(out[j])
+            fx[p + "append_" + name] = bits(appended[j])
         for j, name in enumerate(["keys", "values", "positions"]):
             fx[p + "compact_" + name] = bits(compacted[j])
             fx[p + "merge_" + name] = bits(merged[j])
@@ -307,13 +307,16 @@ def make_gpu(out: Path):
                "legacy_dgrads": bits(dgrads), "legacy_drisk": bits(drisk)})
 
     # torch.topk(largest=False, sorted=True) on CUDA with heavy ties.
+    # Inputs are stored as uint16 codes (x = code / 4) and indices as int32 to
+    # keep the fixture small; slices over 10^6 are checked live by the GPU tests.
     cases = [(40, 1), (40, 2), (40, 7), (40, 32), (40, 33), (300, 17), (300, 100), (300, 129), (5000, 4096),
              (5000, 31), (99999, 20), (99999, 5000), (100000, 20), (150000, 31), (150000, 70000)]
     for i, (n, k) in enumerate(cases):
-        x = (torch.randint(0, max(3, n // 50), (n,), generator=g).to(torch.float32) / 4).to(dev)
-        values_k, indices_k = torch.topk(x, k, largest=False, sorted=True)
-        fx.update({f"topk{i}_x": bits(x), f"topk{i}_k": np.asarray(k), f"topk{i}_values": bits(values_k),
-                   f"topk{i}_indices": bits(indices_k)})
+        codes = torch.randint(0, max(3, n // 50), (n,), generator=g)
+        x = (codes.to(torch.float32) / 4).to(dev)
+        _, indices_k = torch.topk(x, k, largest=False, sorted=True)
+        fx.update({f"topk{i}_codes": codes.numpy().astype(np.uint16), f"topk{i}_k": np.asarray(k),
+                   f"topk{i}_indices": indices_k.cpu().numpy().astype(np.int32)})
     np.savez_compressed(out, **fx)
     print(f"wrote {out} ({len(fx)} arrays)")
 

@@ -12,7 +12,7 @@ pytestmark = pytest.mark.gpu
 
 TOPK_CASES = [(1, 1), (40, 1), (40, 2), (40, 7), (40, 32), (40, 33), (40, 40), (300, 17), (300, 100), (300, 129),
               (5000, 4096), (5000, 4097), (5000, 31), (99999, 20), (99999, 5000), (100000, 20), (150000, 31),
-              (150000, 70000), (600000, 300000)]
+              (150000, 70000), (600000, 300000), (200000, 2), (1000000, 32), (1000000, 33), (4000000, 5)]
 
 
 @pytest.fixture(scope="module")
@@ -82,7 +82,8 @@ REFINE_CASES = [
     ([2226] * 32, 200, 40000),
     ([3, 1, 40, 17, 900, 5], 3, 500),
     ([40] * 30, 10, 300),          # quotas around 10: the bitonic path
-    ([120000, 10, 500], 20, 60000),  # one segment over the sort threshold
+    ([120000, 10, 500], 20, 60000),  # one long segment
+    ([150000, 64, 64], 40, 40),      # small quotas in a long segment
     ([7] * 3, 2, 21),
     ([1000] * 4, 5, 1),
 ]
