@@ -64,6 +64,9 @@ def parse_args():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--decode-steps", type=int, default=64)
     parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--scoring", choices=["fused", "dropin"], default="fused",
+                        help="fused: lrk_temporal_scores per layer; dropin: the reference's per-head composition of "
+                             "temporal_probabilities + temporal_risk")
     return parser.parse_args()
 
 
@@ -343,8 +346,20 @@ def main():
     timer = KernelTimer()
 
     def probability_bytes(logits, projected_values, query_positions, key_positions, scale):
+        # read logits, write probabilities, read projected values and key positions
         w, g, length = logits.shape
         return w * g * length * (logits.element_size() + 4) + g * length * 4 + length * 4
+
+    def fused_bytes(logits, projected_values, key_positions, first, last, query_positions, margin, scale, eps):
+        # the fused minimum: logits read once, projected values and key positions once, scores written
+        total = 0
+        for lg, f, l in zip(logits, first, last):
+            w, g, length = lg.shape
+            total += w * g * length * lg.element_size() + g * length * 4 + length * 4 + (l - f) * 4
+        return total
+
+    fused = args.scoring == "fused"
+    timed_name = "temporal_scores" if fused else "temporal_probabilities"
 
     from code_for_iclr27_b200 import kvcache as kvcache_module
     from code_for_iclr27_b200 import selection as selection_module
@@ -359,18 +374,18 @@ def main():
     route(lambda: counter)
 
     def one_pass():
-        return audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT)
+        return audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT, fused=fused)
 
     for _ in range(args.warmup):
         last = one_pass()
     barrier()
     # Timed region: K audit passes.
     counter.count = 0
-    wrapped = timer.wrap(C.temporal_probabilities, probability_bytes)
+    wrapped = timer.wrap(getattr(C, timed_name), fused_bytes if fused else probability_bytes)
 
     class Timed:
         def __getattr__(self, name):
-            if name == "temporal_probabilities":
+            if name == timed_name:
                 return wrapped
             return getattr(counter, name)
 
@@ -385,7 +400,7 @@ def main():
         end.record()
         barrier()
     elapsed_ms = start.elapsed_time(end)
-    launches = counter.count + len(timer.pairs)
+    launches = counter.count + len(timer.pairs) * (2 if fused else 1)
     for module, function in zip(patched, originals):
         module.operators = function
     local = torch.tensor([elapsed_ms], device=device)
@@ -425,7 +440,8 @@ def main():
     for _ in range(e2e_steps):
         device_queries = [q.to(device, non_blocking=True) for q in host_queries]
         device_gradients = [x.to(device, non_blocking=True) for x in host_gradients]
-        audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT)
+        audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT,
+                   fused=fused)
     e_end.record()
     barrier()
     e2e_ms = torch.tensor([e_start.elapsed_time(e_end)], device=device)
@@ -442,6 +458,7 @@ def main():
         "vs_baseline": None, "dtype": "f32", "impl": "ours",
         "data": "synthetic (seeded): bf16 K/V ~N(0,1), queries ~N(0,4), margin gradient ~N(0,1/D)",
         "config": {"workload": "configs[1] llama-3-8b single request, steady-state audit pass",
+                   "scoring": args.scoring,
                    "layers": LAYERS, "kv_heads": HEADS, "gqa_group": GROUPS, "head_dim": DIM,
                    "prompt_rows_per_head": PROMPT, "generation_rows": RETAINED + IMMEDIATE, "budget": BUDGET,
                    "temporal_window": WINDOW, "selected_per_audit": IMMEDIATE + QUEUED, "evicted_per_audit": IMMEDIATE,
@@ -449,7 +466,7 @@ def main():
                    "parallelism": f"request-sharded x{world}" if world > 1 else "single request",
                    "l2": "no flush: 4.6 GB of K/V per request, larger than L2"},
         "decode_overhead_us": decode_us,
-        "roofline": {"kernel": "temporal_probabilities", "bound": "hbm", "achieved": achieved, "peak": peak,
+        "roofline": {"kernel": timed_name, "bound": "hbm", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
                      "share_of_step": kernel_ms / elapsed_ms, "traffic": None,
                      "bytes_per_launch": timer.bytes / max(1, len(timer.pairs)), "launches": len(timer.pairs)},

@@ -54,7 +54,10 @@ def temporal_head_scores(queries, query_positions, keys, key_positions, values, 
     result = None
     for start in range(0, queries.shape[0], chunk_size):
         end = min(start + chunk_size, queries.shape[0])
-        logits = torch.matmul(queries[start:end].to(keys.dtype), keys.transpose(0, 1))
+        # A contiguous [chunk, G, D] block folds into one [chunk*G, D] x [D, L]
+        # GEMM; the permuted query-history view of scoring.py:260-262 does not,
+        # and torch.matmul then runs `chunk` batched [G, D] x [D, L] products.
+        logits = torch.matmul(queries[start:end].to(keys.dtype).contiguous(), keys.transpose(0, 1))
         probabilities, output_projection = C.temporal_probabilities(
             logits.contiguous(), projected_values, query_positions[start:end], key_positions,
             1.0 / math.sqrt(keys.shape[-1]))
@@ -99,6 +102,54 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
     return ScoreTable(torch.cat(parts), segments, ends)
 
 
+def score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
+                      denominator_epsilon=1e-6) -> ScoreTable:
+    """compute_score_table with the fused scorer: per layer one projected-value
+    GEMM for all heads (g V^T, float32 like scoring.py:175), one bf16 Q K^T GEMM
+    per head (scoring.py:184), then one lrk_temporal_scores call over all of
+    the layer's heads -- the probabilities never reach HBM.  Same table as
+    score_table (within 1e-5 relative)."""
+    import torch
+
+    C = operators()
+    margin = base_margin.to(device=cache.layers[0].keys.device, dtype=torch.float32).reshape(1).contiguous()
+    qpos = query_positions.to(dtype=torch.int64).contiguous()
+    parts, segments, ends, running = [], [], [], 0
+    for layer_index, layer in enumerate(cache.layers):
+        heads = len(layer.head_lens)
+        layer_queries = queries[layer_index]
+        groups = layer_queries.shape[1] // heads
+        scale = 1.0 / math.sqrt(layer.keys.shape[-1])
+        bounds = layer.bounds()
+        positions = layer.positions.reshape(-1)
+        projected = torch.matmul(gradients[layer_index].float(), layer.values.float().transpose(0, 1))
+        window, dim = layer_queries.shape[0], layer_queries.shape[-1]
+        # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
+        per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1).contiguous()
+        logits, pvs, kpos, firsts, lasts = [], [], [], [], []
+        for head in range(heads):
+            start, end = int(bounds[head]), int(bounds[head + 1])
+            candidate_start = int(layer.prompt_lens[head])
+            candidate_end = max(candidate_start, end - start - protect_recent)
+            if candidate_end <= candidate_start:
+                continue
+            head_logits = torch.matmul(per_head[head].view(window * groups, dim), layer.keys[start:end].transpose(0, 1))
+            logits.append(head_logits.view(window, groups, end - start))
+            pvs.append(projected[head * groups:(head + 1) * groups, start:end])
+            kpos.append(positions[start:end])
+            firsts.append(candidate_start)
+            lasts.append(candidate_end)
+            segments.append(ScoreSegment(layer_index, head, candidate_start, candidate_end - candidate_start))
+            running += candidate_end - candidate_start
+            ends.append(running)
+        if logits:
+            parts.append(C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, scale,
+                                           denominator_epsilon))
+    if not parts:
+        raise RuntimeError("No eligible KV remains after prompt/recent protection")
+    return ScoreTable(torch.cat(parts), segments, ends)
+
+
 def pool_table(table: ScoreTable, kernel_size: int = 7) -> ScoreTable:
     """pool_score_table (scoring.py:322-335)."""
     import torch
@@ -118,11 +169,18 @@ class AuditResult:
 
 
 def audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
-               protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250, pool_kernel=7) -> AuditResult:
+               protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250, pool_kernel=7,
+               fused=True) -> AuditResult:
     """Score, pool, select immediate + queued references, evict the immediate
-    prefix.  Returns the queue (references[immediate:] is the lazy queue)."""
-    table = score_table(cache, queries, query_positions, gradients, base_margin, protect_recent,
-                        denominator_epsilon, query_chunk_size)
+    prefix.  Returns the queue (references[immediate:] is the lazy queue).
+    fused=False scores through the drop-in operators exactly as the reference
+    composes them (bit-identical scores); fused=True uses lrk_temporal_scores."""
+    if fused:
+        table = score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                                  denominator_epsilon)
+    else:
+        table = score_table(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                            denominator_epsilon, query_chunk_size)
     pooled = pool_table(table, pool_kernel)
     references, changed, changed_heads = refine_arrays(table, pooled, immediate + queued)
     if len(references) < immediate:

@@ -37,7 +37,7 @@ CUDA_SOURCES = {
     # Same no-contraction rule as the reference scoring build (setup.py:15-16).
     "score.cu": ["--fmad=false"],
     "select.cu": [],
-    "fused.cu": [],
+    "fused.cu": ["--fmad=false"],
 }
 MODULES = {"_C": "shim_C.cpp", "_legacy_C": "shim_legacy_C.cpp", "_host": "shim_host.cpp"}
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"

@@ -1,0 +1,195 @@
+// Softmax row statistics in the reference operator's exact arithmetic.
+//
+// For one (query, group) row of logits the reference (csrc/scoring.cu:32-66)
+// computes x = dtype(float(logit) * scale), masked to -inf where the key's
+// position exceeds the query's; the row max; 256 per-thread sequential sums
+// of expf(x - max) over positions t, t+256, ... folded by a pairwise tree
+// (csrc/scoring.cu:15-30) into the denominator; p = w / denominator; and the
+// same lane-order sum of p * projected_value.  Every kernel here reproduces
+// those operations and their order exactly (the including file is compiled
+// with --fmad=false, and order-sensitive steps use _rn intrinsics), so the
+// max, denominator, projection and probabilities are bit-identical.
+//
+// The work is arranged for B200: one CTA per row, the row read from HBM once
+// with 16-byte vector loads and staged in shared memory in the logits dtype
+// (x is exact in that dtype), then the two reduction passes run from shared
+// memory.  bf16 rows up to 116k positions fit (3 CTAs per SM at 35k); longer
+// rows recompute x from the logits (L2-resident) in each pass.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace lrk {
+namespace rows {
+
+constexpr int kLanes = 256;  // the reference's reduction width; one thread per lane
+constexpr int kStageBytes = 220 * 1024;
+
+template <typename T> struct Dtype;
+template <> struct Dtype<__nv_bfloat16> {
+  static constexpr int kPerVec = 8;
+  using Bits = unsigned short;
+  static __device__ __forceinline__ float to_float(Bits b) { return __uint_as_float(static_cast<uint32_t>(b) << 16); }
+  static __device__ __forceinline__ Bits round(float x, float scale) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(__fmul_rn(x, scale)));
+  }
+};
+template <> struct Dtype<__half> {
+  static constexpr int kPerVec = 8;
+  using Bits = unsigned short;
+  static __device__ __forceinline__ float to_float(Bits b) { return __half2float(__ushort_as_half(b)); }
+  static __device__ __forceinline__ Bits round(float x, float scale) {
+    return __half_as_ushort(__float2half_rn(__fmul_rn(x, scale)));
+  }
+};
+template <> struct Dtype<float> {
+  static constexpr int kPerVec = 4;
+  using Bits = uint32_t;
+  static __device__ __forceinline__ float to_float(Bits b) { return __uint_as_float(b); }
+  static __device__ __forceinline__ Bits round(float x, float scale) { return __float_as_uint(__fmul_rn(x, scale)); }
+};
+
+// -inf in each dtype's bit pattern.
+template <typename T> __device__ __forceinline__ typename Dtype<T>::Bits minus_infinity();
+template <> __device__ __forceinline__ unsigned short minus_infinity<__nv_bfloat16>() { return 0xff80u; }
+template <> __device__ __forceinline__ unsigned short minus_infinity<__half>() { return 0xfc00u; }
+template <> __device__ __forceinline__ uint32_t minus_infinity<float>() { return 0xff800000u; }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block max (order-free); scratch holds >= 32 floats.
+__device__ __forceinline__ float block_max(float v, float *scratch) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = threadIdx.x < kLanes / 32 ? scratch[threadIdx.x] : -INFINITY;
+  if (threadIdx.x < 32) r = warp_max(r);
+  if (threadIdx.x == 0) scratch[0] = r;
+  __syncthreads();
+  r = scratch[0];
+  __syncthreads();
+  return r;
+}
+
+// The reference's 256-wide pairwise tree: partial[t] += partial[t + s] for
+// s = 128 .. 1.  tree holds 256 floats.
+__device__ __forceinline__ float tree_sum(float partial, float *tree) {
+  tree[threadIdx.x] = partial;
+  __syncthreads();
+#pragma unroll
+  for (int s = kLanes / 2; s >= 32; s >>= 1) {
+    if (threadIdx.x < s) tree[threadIdx.x] = __fadd_rn(tree[threadIdx.x], tree[threadIdx.x + s]);
+    __syncthreads();
+  }
+  if (threadIdx.x < 32) {
+    float value = tree[threadIdx.x];
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) {
+      const float other = __shfl_down_sync(0xffffffffu, value, s);
+      if (threadIdx.x < s) value = __fadd_rn(value, other);
+    }
+    if (threadIdx.x == 0) tree[0] = value;
+  }
+  __syncthreads();
+  const float result = tree[0];
+  __syncthreads();
+  return result;
+}
+
+struct RowResult {
+  float maximum, denominator, projection;
+};
+
+// Statistics of one row (all 256 threads call).  probabilities_out, when not
+// null, receives every probability (the drop-in operator's output).
+// `stage` is dynamic shared memory of at least staged_bytes<T>(length) when
+// STAGED, unused otherwise.
+template <typename T, bool STAGED>
+__device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const float *__restrict__ key_positions,
+                                    float query_position, const float *__restrict__ projected_values, float scale,
+                                    float *__restrict__ probabilities_out, unsigned char *stage, float *scratch) {
+  using D = Dtype<T>;
+  using Bits = typename D::Bits;
+  constexpr int V = D::kPerVec;
+  const Bits *in = reinterpret_cast<const Bits *>(row);
+  // Element index of the first 16-byte boundary of this row, and the shared
+  // offset that puts that element on a 16-byte boundary of the stage too.
+  const int64_t lead = lmin(length, static_cast<int64_t>(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) /
+                                                        sizeof(Bits)));
+  const int pad = static_cast<int>((V - lead % V) % V);
+  Bits *x_stage = reinterpret_cast<Bits *>(stage) + pad;
+  const Bits neg_inf = minus_infinity<T>();
+  auto value_bits = [&](int64_t p, Bits raw) -> Bits {
+    return __ldg(key_positions + p) <= query_position ? D::round(D::to_float(raw), scale) : neg_inf;
+  };
+
+  // Pass A: scale, round, mask; row max; stage the row.
+  float local_max = -INFINITY;
+  if (STAGED) {
+    for (int64_t p = threadIdx.x; p < lead; p += kLanes) {
+      const Bits b = value_bits(p, __ldg(in + p));
+      x_stage[p] = b;
+      local_max = fmaxf(local_max, D::to_float(b));
+    }
+    const int64_t vectors = (length - lead) / V;
+    const uint4 *body = reinterpret_cast<const uint4 *>(in + lead);
+    uint4 *stage_body = reinterpret_cast<uint4 *>(x_stage + lead);
+#pragma unroll 4
+    for (int64_t v = threadIdx.x; v < vectors; v += kLanes) {
+      uint4 raw = __ldcs(body + v);
+      Bits *lanes = reinterpret_cast<Bits *>(&raw);
+      const int64_t p0 = lead + v * V;
+#pragma unroll
+      for (int j = 0; j < V; ++j) {
+        lanes[j] = value_bits(p0 + j, lanes[j]);
+        local_max = fmaxf(local_max, D::to_float(lanes[j]));
+      }
+      stage_body[v] = raw;
+    }
+    for (int64_t p = lead + vectors * V + threadIdx.x; p < length; p += kLanes) {
+      const Bits b = value_bits(p, __ldg(in + p));
+      x_stage[p] = b;
+      local_max = fmaxf(local_max, D::to_float(b));
+    }
+  } else {
+    for (int64_t p = threadIdx.x; p < length; p += kLanes)
+      local_max = fmaxf(local_max, D::to_float(value_bits(p, __ldg(in + p))));
+  }
+  const float maximum = block_max(local_max, scratch);
+
+  auto x_at = [&](int64_t p) -> float {
+    return STAGED ? D::to_float(x_stage[p]) : D::to_float(value_bits(p, __ldg(in + p)));
+  };
+
+  // Pass B: denominator, lane t summing positions t, t + 256, ... in order.
+  float sum = 0.0f;
+#pragma unroll 4
+  for (int64_t p = threadIdx.x; p < length; p += kLanes) sum = __fadd_rn(sum, expf(__fsub_rn(x_at(p), maximum)));
+  const float denominator = tree_sum(sum, scratch);
+
+  // Pass C: probabilities (optionally stored) and the value projection.
+  float projection = 0.0f;
+#pragma unroll 4
+  for (int64_t p = threadIdx.x; p < length; p += kLanes) {
+    const float probability = __fdiv_rn(expf(__fsub_rn(x_at(p), maximum)), denominator);
+    if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
+    projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(projected_values + p)));
+  }
+  projection = tree_sum(projection, scratch);
+  return {maximum, denominator, projection};
+}
+
+template <typename T>
+__host__ __device__ constexpr int64_t staged_bytes(int64_t length) {
+  return (length + 16) * static_cast<int64_t>(sizeof(typename Dtype<T>::Bits));
+}
+
+}  // namespace rows
+}  // namespace lrk

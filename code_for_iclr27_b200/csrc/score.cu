@@ -17,172 +17,30 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "rows.cuh"
 
 namespace lrk {
 namespace {
 
-constexpr int kLanes = 256;  // the reference's reduction width
+constexpr int kLanes = rows::kLanes;  // the reference's reduction width
 
-template <typename T> struct Logit;
-template <> struct Logit<float> {
-  static __device__ __forceinline__ float scaled(float x, float scale) { return __fmul_rn(x, scale); }
-  static __device__ __forceinline__ float load(const float *p) { return __ldcs(p); }
-};
-template <> struct Logit<__nv_bfloat16> {
-  static __device__ __forceinline__ float scaled(float x, float scale) {
-    return __bfloat162float(__float2bfloat16_rn(__fmul_rn(x, scale)));
-  }
-  static __device__ __forceinline__ float load(const __nv_bfloat16 *p) {
-    return __bfloat162float(__ushort_as_bfloat16(__ldcs(reinterpret_cast<const unsigned short *>(p))));
-  }
-};
-template <> struct Logit<__half> {
-  static __device__ __forceinline__ float scaled(float x, float scale) {
-    return __half2float(__float2half_rn(__fmul_rn(x, scale)));
-  }
-  static __device__ __forceinline__ float load(const __half *p) {
-    return __half2float(__ushort_as_half(__ldcs(reinterpret_cast<const unsigned short *>(p))));
-  }
-};
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// Block max over all threads (order-free).  `scratch` holds >= 32 floats.
-template <int NT>
-__device__ float block_max(float v, float *scratch) {
-  v = warp_max(v);
-  if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = threadIdx.x < NT / 32 ? scratch[threadIdx.x] : -INFINITY;
-  if (threadIdx.x < 32) r = warp_max(r);
-  if (threadIdx.x == 0) scratch[0] = r;
-  __syncthreads();
-  r = scratch[0];
-  __syncthreads();
-  return r;
-}
-
-// Sum of per-lane partials with the reference's 256-wide pairwise tree:
-// partial[t] += partial[t + s] for s = 128, 64, ..., 1.  Lanes are threads
-// 0..255; all NT threads must call.  `tree` holds 256 floats.
-template <int NT>
-__device__ float tree_sum(float partial, float *tree) {
-  if (threadIdx.x < kLanes) tree[threadIdx.x] = partial;
-  __syncthreads();
-#pragma unroll
-  for (int s = kLanes / 2; s >= 32; s >>= 1) {
-    if (threadIdx.x < s) tree[threadIdx.x] = __fadd_rn(tree[threadIdx.x], tree[threadIdx.x + s]);
-    __syncthreads();
-  }
-  float result = 0.0f;
-  if (threadIdx.x < 32) {
-    float value = tree[threadIdx.x];
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) {
-      const float other = __shfl_down_sync(0xffffffffu, value, s);
-      if (threadIdx.x < s) value = __fadd_rn(value, other);
-    }
-    if (threadIdx.x == 0) tree[0] = value;
-  }
-  __syncthreads();
-  result = tree[0];
-  __syncthreads();
-  return result;
-}
-
-// Sequential per-lane sum over buffer[t], buffer[t + 256], ... (lane t).
-__device__ __forceinline__ float lane_chain(const float *buffer, int length) {
-  float sum = 0.0f;
-  int p = threadIdx.x;
-#pragma unroll 8
-  for (; p < length; p += kLanes) sum = __fadd_rn(sum, buffer[p]);
-  return sum;
-}
-
-// One CTA per (query, group) row with the whole row staged in shared memory.
-template <typename T, int NT>
-__global__ void __launch_bounds__(NT) probabilities_staged(
+// One CTA per (query, group) row (csrc/scoring.cu:32-66): rows::row_statistics
+// writes the row's probabilities and returns its value projection.
+template <typename T, bool STAGED>
+__global__ void __launch_bounds__(kLanes) probabilities_kernel(
     const T *__restrict__ logits, const float *__restrict__ projected_values,
     const int64_t *__restrict__ query_positions, const float *__restrict__ key_positions,
-    float *__restrict__ probabilities, float *__restrict__ output_projection, int groups, int length,
+    float *__restrict__ probabilities, float *__restrict__ output_projection, int groups, int64_t length,
     float scale) {
-  extern __shared__ float row_buffer[];
+  extern __shared__ __align__(16) unsigned char stage[];
   __shared__ float scratch[kLanes];
   const int64_t row = blockIdx.x;
   const int group = static_cast<int>(row % groups);
   const int64_t query = row / groups;
-  const float query_position = static_cast<float>(query_positions[query]);
-  const T *in = logits + row * length;
-  float *out = probabilities + row * length;
-  const float *pv = projected_values + static_cast<int64_t>(group) * length;
-
-  // A: scale, round to the logit dtype, causal mask; row max.
-  float maximum = -INFINITY;
-  for (int p = threadIdx.x; p < length; p += NT) {
-    const float rounded = Logit<T>::scaled(Logit<T>::load(in + p), scale);
-    const float value = key_positions[p] <= query_position ? rounded : -INFINITY;
-    row_buffer[p] = value;
-    maximum = fmaxf(maximum, value);
-  }
-  maximum = block_max<NT>(maximum, scratch);
-
-  // B: weights.
-  for (int p = threadIdx.x; p < length; p += NT) row_buffer[p] = expf(__fsub_rn(row_buffer[p], maximum));
-  __syncthreads();
-  // C: denominator in the reference's lane order.
-  const float denominator = tree_sum<NT>(threadIdx.x < kLanes ? lane_chain(row_buffer, length) : 0.0f, scratch);
-
-  // D: normalise, write probabilities, stage products p * pv.
-  for (int p = threadIdx.x; p < length; p += NT) {
-    const float probability = __fdiv_rn(row_buffer[p], denominator);
-    __stcs(out + p, probability);
-    row_buffer[p] = __fmul_rn(probability, pv[p]);
-  }
-  __syncthreads();
-  // E: value projection in the reference's lane order.
-  const float projection = tree_sum<NT>(threadIdx.x < kLanes ? lane_chain(row_buffer, length) : 0.0f, scratch);
-  if (threadIdx.x == 0) output_projection[row] = projection;
-}
-
-// Rows too long for shared memory: the reference's three-pass structure with
-// the intermediate values recomputed from the logits instead of round-tripping
-// through the probability buffer (logits re-reads hit L2).
-template <typename T>
-__global__ void __launch_bounds__(kLanes) probabilities_streamed(
-    const T *__restrict__ logits, const float *__restrict__ projected_values,
-    const int64_t *__restrict__ query_positions, const float *__restrict__ key_positions,
-    float *__restrict__ probabilities, float *__restrict__ output_projection, int groups, int length,
-    float scale) {
-  __shared__ float scratch[kLanes];
-  const int64_t row = blockIdx.x;
-  const int group = static_cast<int>(row % groups);
-  const int64_t query = row / groups;
-  const float query_position = static_cast<float>(query_positions[query]);
-  const T *in = logits + row * length;
-  float *out = probabilities + row * length;
-  const float *pv = projected_values + static_cast<int64_t>(group) * length;
-  auto value_at = [&](int p) {
-    const float rounded = Logit<T>::scaled(Logit<T>::load(in + p), scale);
-    return key_positions[p] <= query_position ? rounded : -INFINITY;
-  };
-  float maximum = -INFINITY;
-  for (int p = threadIdx.x; p < length; p += kLanes) maximum = fmaxf(maximum, value_at(p));
-  maximum = block_max<kLanes>(maximum, scratch);
-  float sum = 0.0f;
-  for (int p = threadIdx.x; p < length; p += kLanes) sum = __fadd_rn(sum, expf(__fsub_rn(value_at(p), maximum)));
-  const float denominator = tree_sum<kLanes>(sum, scratch);
-  float projection = 0.0f;
-  for (int p = threadIdx.x; p < length; p += kLanes) {
-    const float probability = __fdiv_rn(expf(__fsub_rn(value_at(p), maximum)), denominator);
-    __stcs(out + p, probability);
-    projection = __fadd_rn(projection, __fmul_rn(probability, pv[p]));
-  }
-  projection = tree_sum<kLanes>(projection, scratch);
-  if (threadIdx.x == 0) output_projection[row] = projection;
+  const rows::RowResult result = rows::row_statistics<T, STAGED>(
+      logits + row * length, length, key_positions, static_cast<float>(query_positions[query]),
+      projected_values + static_cast<int64_t>(group) * length, scale, probabilities + row * length, stage, scratch);
+  if (threadIdx.x == 0) output_projection[row] = result.projection;
 }
 
 __device__ __forceinline__ double softplus64(double value) {
@@ -323,7 +181,7 @@ __global__ void __launch_bounds__(kLanes) decision_risk_kernel(
         __fmul_rn(__fdiv_rn(alpha, denominator), __fsub_rn(value, head_outputs[group * dimension + channel]));
     partial = __fadd_rn(partial, __fmul_rn(gradients[group * dimension + channel], local_delta));
   }
-  const float total = tree_sum<kLanes>(partial, tree);
+  const float total = rows::tree_sum(partial, tree);
   if (threadIdx.x == 0) {
     const double compared = __dsub_rn(base_margin, static_cast<double>(total));
     const double probability = stable_sigmoid(base_margin);
@@ -335,40 +193,23 @@ __global__ void __launch_bounds__(kLanes) decision_risk_kernel(
   }
 }
 
-// Largest row kept whole in shared memory (floats), leaving room for scratch.
-constexpr int kMaxStagedLength = 56 * 1024;
-
-template <typename T, int NT>
-int launch_probabilities_staged(const T *logits, const float *pv, const int64_t *qpos, const float *kpos,
-                                float *probs, float *op, int64_t rows, int groups, int length, float scale,
-                                cudaStream_t stream) {
-  const size_t bytes = static_cast<size_t>(length) * sizeof(float);
-  auto kernel = probabilities_staged<T, NT>;
-  if (bytes > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(kMaxStagedLength * sizeof(float)));
-    if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute: %s", cudaGetErrorString(e));
-      return LRK_ERR_CUDA;
-    }
-  }
-  kernel<<<static_cast<unsigned>(rows), NT, bytes, stream>>>(logits, pv, qpos, kpos, probs, op, groups, length,
-                                                            scale);
-  return launch_status("lrk_temporal_probabilities");
-}
-
 template <typename T>
-int launch_probabilities(const void *logits, const float *pv, const int64_t *qpos, const float *kpos,
-                         float *probs, float *op, int64_t rows, int groups, int length, float scale,
-                         cudaStream_t stream) {
+int launch_probabilities(const void *logits, const float *pv, const int64_t *qpos, const float *kpos, float *probs,
+                         float *op, int64_t rows, int groups, int64_t length, float scale, cudaStream_t stream) {
   const T *in = static_cast<const T *>(logits);
-  if (length <= kMaxStagedLength) {
-    if (length <= 8192)
-      return launch_probabilities_staged<T, 256>(in, pv, qpos, kpos, probs, op, rows, groups, length, scale, stream);
-    return launch_probabilities_staged<T, 1024>(in, pv, qpos, kpos, probs, op, rows, groups, length, scale, stream);
+  const int64_t bytes = rows::staged_bytes<T>(length);
+  if (bytes <= rows::kStageBytes) {
+    auto kernel = probabilities_kernel<T, true>;
+    if (bytes > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::kStageBytes);
+      if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+    }
+    kernel<<<static_cast<unsigned>(rows), kLanes, static_cast<size_t>(bytes), stream>>>(in, pv, qpos, kpos, probs, op,
+                                                                                       groups, length, scale);
+  } else {
+    probabilities_kernel<T, false><<<static_cast<unsigned>(rows), kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op,
+                                                                                     groups, length, scale);
   }
-  probabilities_streamed<T><<<static_cast<unsigned>(rows), kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op,
-                                                                                groups, length, scale);
   return launch_status("lrk_temporal_probabilities");
 }
 
@@ -392,15 +233,13 @@ extern "C" int lrk_temporal_probabilities(const void *logits, int logits_dtype, 
     case LRK_BF16:
       return launch_probabilities<__nv_bfloat16>(logits, projected_values, query_positions, key_positions,
                                                  probabilities, output_projection, rows, static_cast<int>(groups),
-                                                 static_cast<int>(length), scale, s);
+                                                 length, scale, s);
     case LRK_F16:
       return launch_probabilities<__half>(logits, projected_values, query_positions, key_positions, probabilities,
-                                          output_projection, rows, static_cast<int>(groups),
-                                          static_cast<int>(length), scale, s);
+                                          output_projection, rows, static_cast<int>(groups), length, scale, s);
     case LRK_F32:
       return launch_probabilities<float>(logits, projected_values, query_positions, key_positions, probabilities,
-                                         output_projection, rows, static_cast<int>(groups),
-                                         static_cast<int>(length), scale, s);
+                                         output_projection, rows, static_cast<int>(groups), length, scale, s);
     default:
       return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
   }

@@ -1,0 +1,84 @@
+"""Single-kernel workloads at configs[1] shape, for profiling one operator.
+
+    python -m code_for_iclr27_b200.profile_cases CASE [--iters N]
+
+CASE is one of:
+  scores         lrk_temporal_scores over one layer (8 heads x [250, 4, 34880]
+                 bf16 logits, 558 MB, larger than L2)
+  probabilities  temporal_probabilities on one query chunk [79, 4, 35026]
+  risk           temporal_risk over 2226 candidates of that chunk
+  compact        compaction of one layer (279k rows of D=128 bf16) removing 64 rows
+  append         one-token append to one layer
+  refine         selection over 502k scores in 256 segments
+Inputs are seeded and generated on the device; each iteration launches the
+operator once.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+
+LAYER_ROWS = 8 * 34880
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine"])
+    parser.add_argument("--iters", type=int, default=3)
+    args = parser.parse_args(argv)
+
+    import torch
+
+    from . import operators
+
+    C = operators()
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(0)
+    if args.case == "scores":
+        length, window, groups = 34880, 250, 4
+        logits = [(torch.randn(window, groups, length, generator=g, device=dev) * 2 * math.sqrt(128)).to(torch.bfloat16)
+                  for _ in range(8)]
+        pv = [torch.randn(groups, length, generator=g, device=dev) for _ in range(8)]
+        kpos = [torch.arange(length, dtype=torch.float32, device=dev) for _ in range(8)]
+        qpos = torch.arange(length - window, length, dtype=torch.int64, device=dev)
+        margin = torch.tensor([1.0], device=dev)
+        run = lambda: C.temporal_scores(logits, pv, kpos, [32768] * 8, [length - 32] * 8, qpos, margin,
+                                        1 / math.sqrt(128), 1e-6)
+    elif args.case in ("probabilities", "risk"):
+        window, groups, length = 79, 4, 35026
+        logits = (torch.randn(window, groups, length, generator=g, device=dev) * 2 * math.sqrt(128)).to(torch.bfloat16)
+        pv = torch.rand(groups, length, generator=g, device=dev)
+        qpos = torch.arange(length - window, length, dtype=torch.int64, device=dev)
+        kpos = torch.arange(length, dtype=torch.float32, device=dev)
+        if args.case == "probabilities":
+            run = lambda: C.temporal_probabilities(logits, pv, qpos, kpos, 1 / math.sqrt(128))
+        else:
+            probs, op = C.temporal_probabilities(logits, pv, qpos, kpos, 1 / math.sqrt(128))
+            margin = torch.tensor([1.0], device=dev)
+            run = lambda: C.temporal_risk(probs, op, pv, margin, length - 2258, length - 32, 1e-6)
+    elif args.case in ("compact", "append"):
+        keys = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
+        values = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
+        positions = torch.arange(LAYER_ROWS, dtype=torch.float32, device=dev).reshape(-1, 1)
+        if args.case == "compact":
+            removed = torch.randperm(LAYER_ROWS, generator=g, device=dev)[:64].sort().values
+            run = lambda: C.compact(keys, values, positions, removed)
+        else:
+            cumulative = torch.arange(0, LAYER_ROWS + 1, 34880, dtype=torch.int32, device=dev)
+            new = torch.randn(1, 8, 1, 128, generator=g, device=dev).to(torch.bfloat16)
+            run = lambda: C.append(keys, values, positions, new, new, cumulative, 40000, 34880)
+    else:
+        n = 256 * 1962
+        raw = torch.rand(n, generator=g, device=dev)
+        bounds = torch.arange(0, n + 1, 1962, dtype=torch.int64, device=dev)
+        pooled = C.pool(raw, bounds, 1962, 7)
+        starts = torch.zeros(256, dtype=torch.int64, device=dev)
+        run = lambda: C.refine(raw, pooled, bounds[1:].contiguous(), starts, 64512)
+    for _ in range(args.iters):
+        run()
+    torch.cuda.synchronize()
+    print(f"{args.case}: {args.iters} iterations ok")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+"""GPU parity of the fused scorer (lrk_temporal_scores / _C.temporal_scores).
+
+Reference semantics: for one head, temporal_probabilities + temporal_risk over
+all queries (scoring.py:179-195; per-chunk maxima equal the all-query risk).
+The fused path sums in a different order, so scores must agree with the
+drop-in operators -- which are bit-identical to the reference kernels -- and
+with the oracle within 1e-5 relative.  The absolute floor is 1e-6 of the
+largest score of the call: scores near zero (a drop close to 0) carry the
+absolute, not the relative, error of the probability sums."""
+import math
+
+import numpy as np
+import pytest
+
+from oracle import lrk_oracle as O
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-5
+
+
+def assert_scores_close(actual, expected):
+    actual = np.asarray(actual, np.float64)
+    expected = np.asarray(expected, np.float64)
+    assert actual.shape == expected.shape
+    assert (np.isnan(actual) == np.isnan(expected)).all(), "NaN pattern differs"
+    ok = ~np.isnan(expected)
+    if not ok.any():
+        return
+    floor = 1e-6 * np.abs(expected[ok]).max()
+    error = np.abs(actual[ok] - expected[ok])
+    bound = RTOL * np.abs(expected[ok]) + floor
+    worst = np.argmax(error - bound)
+    assert (error <= bound).all(), (f"max excess at {worst}: {actual[ok][worst]} vs {expected[ok][worst]}, "
+                                    f"max rel {np.max(error / np.maximum(np.abs(expected[ok]), 1e-300))}")
+
+
+@pytest.fixture(scope="module")
+def C(cuda):
+    from code_for_iclr27_b200 import operators
+
+    return operators()
+
+
+def make_head(g, device, window, groups, length, dtype, masked_queries=0):
+    import torch
+
+    logits = (torch.randn(window, groups, length, generator=g) * 2 * math.sqrt(128)).to(dtype).to(device)
+    pv = torch.randn(groups, length, generator=g).to(device)
+    kpos = torch.arange(length, dtype=torch.float32).to(device)
+    qpos = torch.arange(length - window - 1, length - 1, dtype=torch.int64).to(device)
+    if masked_queries:
+        qpos[:masked_queries] = -1  # every key masked for these queries
+    return logits, pv, kpos, qpos
+
+
+def dropin_scores(C, logits, pv, kpos, qpos, margin, first, last, scale, chunk=79):
+    import torch
+
+    result = None
+    for start in range(0, logits.shape[0], chunk):
+        end = min(start + chunk, logits.shape[0])
+        probs, op = C.temporal_probabilities(logits[start:end].contiguous(), pv, qpos[start:end].contiguous(), kpos,
+                                             scale)
+        s = C.temporal_risk(probs, op, pv, margin, first, last, 1e-6)
+        result = s if result is None else torch.maximum(result, s)
+    return result
+
+
+CASES = [
+    ("bf16", 250, 4, 4096, 0, 4064),
+    ("bf16", 250, 4, 35026, 32768, 34994),
+    ("bf16", 79, 8, 3000, 100, 2900),
+    ("f16", 30, 4, 1027, 5, 1020),
+    ("f32", 17, 2, 513, 0, 513),
+    ("bf16", 6, 1, 70001, 60000, 70000),
+]
+
+
+@pytest.mark.parametrize("dtype_name,window,groups,length,first,last", CASES)
+def test_fused_matches_dropin_and_oracle(C, cuda, dtype_name, window, groups, length, first, last):
+    import torch
+
+    dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dtype_name]
+    g = torch.Generator().manual_seed(length + window)
+    logits, pv, kpos, qpos = make_head(g, cuda, window, groups, length, dtype)
+    margin = torch.tensor([0.7], device=cuda)
+    scale = 1.0 / math.sqrt(128)
+    fused = C.temporal_scores([logits], [pv], [kpos], [first], [last], qpos, margin, scale, 1e-6)
+    reference = dropin_scores(C, logits, pv, kpos, qpos, margin, first, last, scale)
+    assert_scores_close(fused.cpu().numpy(), reference.cpu().numpy())
+    if length <= 5000:
+        raw = logits.detach().cpu()
+        raw = raw.view(torch.int16).numpy().view(np.uint16) if dtype == torch.bfloat16 else raw.numpy()
+        probs, op = O.temporal_probabilities(raw, dtype_name, pv.cpu().numpy(), qpos.cpu().numpy(),
+                                             kpos.cpu().numpy(), np.float32(scale))
+        expect = O.temporal_risk(probs, op, pv.cpu().numpy(), np.float32(0.7), first, last, 1e-6)
+        assert_scores_close(fused.cpu().numpy(), expect)
+
+
+def test_fused_many_segments_strided_and_masked(C, cuda):
+    """100 segments (three launches), projected values as strided views of one
+    layer-wide matrix, some queries with every key masked (NaN scores)."""
+    import torch
+
+    g = torch.Generator().manual_seed(5)
+    groups, window = 4, 40
+    lengths = torch.randint(50, 700, (100,), generator=g).tolist()
+    total = sum(lengths)
+    projected = torch.randn(8 * groups, total + 3, generator=g).to(cuda)
+    logits, pvs, kpos, firsts, lasts = [], [], [], [], []
+    margin = torch.tensor([1.1], device=cuda)
+    start = 0
+    for i, length in enumerate(lengths):
+        lg, _, kp, _ = make_head(g, cuda, window, groups, length, torch.bfloat16)
+        head = i % 8
+        logits.append(lg)
+        pvs.append(projected[head * groups:(head + 1) * groups, start:start + length])
+        kpos.append(kp)
+        firsts.append(length // 5)
+        lasts.append(length - 3)
+        start += length
+    # one query-position vector is shared by every segment of a call
+    qpos = torch.arange(window, dtype=torch.int64, device=cuda) + 10 ** 6
+    expected = [dropin_scores(C, lg, pv.contiguous(), kp, qpos, margin, f, l, 0.125)
+                for lg, pv, kp, f, l in zip(logits, pvs, kpos, firsts, lasts)]
+    fused = C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, 0.125, 1e-6)
+    assert_scores_close(fused.cpu().numpy(), torch.cat(expected).cpu().numpy())
+    # A query with every key masked makes the whole head NaN, as in the reference.
+    masked_qpos = qpos.clone()
+    masked_qpos[3] = -5
+    fused = C.temporal_scores(logits[:2], pvs[:2], kpos[:2], firsts[:2], lasts[:2], masked_qpos, margin, 0.125, 1e-6)
+    assert torch.isnan(fused).all()
+
+
+def test_fused_through_c_abi(cuda):
+    import torch
+
+    from code_for_iclr27_b200 import abi, operators
+
+    g = torch.Generator().manual_seed(9)
+    logits, pv, kpos, qpos = make_head(g, cuda, 50, 4, 2000, torch.bfloat16)
+    margin = torch.tensor([0.5], device=cuda)
+    out = torch.empty(1900, device=cuda)
+    segments = (abi.ScoreSegment * 1)()
+    segments[0] = abi.ScoreSegment(logits.data_ptr(), pv.data_ptr(), 2000, kpos.data_ptr(), 2000, 100, 2000,
+                                   out.data_ptr())
+    lib = abi.library()
+    size = lib.lrk_temporal_scores_workspace_bytes(1, 50, 4)
+    workspace = torch.empty(size, dtype=torch.uint8, device=cuda)
+    abi.check(lib.lrk_temporal_scores(segments, 1, abi.BF16, qpos.data_ptr(), 50, 4, 0.125, margin.data_ptr(), 1e-6,
+                                      workspace.data_ptr(), size, torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    expected = dropin_scores(operators(), logits, pv, kpos, qpos, margin, 100, 2000, 0.125)
+    assert_scores_close(out.cpu().numpy(), expected.cpu().numpy())
+    assert lib.lrk_temporal_scores(segments, 1, abi.BF16, qpos.data_ptr(), 50, 4, 0.125, margin.data_ptr(), 1e-6,
+                                   workspace.data_ptr(), 8, 0) == abi.ERR_WORKSPACE
+
+
+def test_audit_tables_agree(cuda):
+    """The audit driver's fused score table equals its drop-in score table."""
+    import torch
+
+    from code_for_iclr27_b200.audit import score_table, score_table_fused
+    from code_for_iclr27_b200.kvcache import PackedCache
+
+    g = torch.Generator().manual_seed(2)
+    cache = PackedCache()
+    layers, heads, groups, dim, window = 2, 4, 4, 64, 30
+    for layer in range(layers):
+        lens = torch.randint(200, 600, (heads,), generator=g).tolist()
+        rows = sum(lens)
+        keys = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(cuda)
+        values = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(cuda)
+        positions = torch.cat([torch.arange(n, dtype=torch.float32) for n in lens]).to(cuda)
+        cache.add_layer(keys, values, positions, lens, [40, 0, 100, 10])
+    queries = [(torch.randn(window, heads * groups, dim, generator=g) * 2).to(torch.bfloat16).to(cuda)
+               for _ in range(layers)]
+    grads = [torch.randn(heads * groups, dim, generator=g).to(cuda) / 8 for _ in range(layers)]
+    qpos = torch.arange(570, 570 + window, dtype=torch.int64, device=cuda)
+    margin = torch.tensor(0.9, device=cuda)
+    a = score_table(cache, queries, qpos, grads, margin, query_chunk_size=7)
+    b = score_table_fused(cache, queries, qpos, grads, margin)
+    assert a.segments == b.segments and a.cumulative_ends == b.cumulative_ends
+    assert_scores_close(b.scores.cpu().numpy(), a.scores.cpu().numpy())
