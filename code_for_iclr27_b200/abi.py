@@ -14,6 +14,7 @@ from . import LIBRARY_PATH
 
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE = 0, 1, 2, 3, 4
 F32, F64, F16, BF16 = 0, 1, 2, 3
+STATIC_SCORE_ROWS = 262144  # LRK_STATIC_SCORE_ROWS in include/lrk.h
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -44,6 +45,7 @@ SIGNATURES = {
     "lrk_pool": (I32, [P, I64, P, I64, I64, I64, P, P]),
     "lrk_temporal_scores_workspace_bytes": (SIZE, [I64, I64, I64]),
     "lrk_temporal_scores": (I32, [ctypes.POINTER(ScoreSegment), I64, I32, P, I64, I64, F, P, F, P, SIZE, P]),
+    "lrk_temporal_scores_static": (I32, [ctypes.POINTER(ScoreSegment), I64, I32, P, I64, I64, F, P, F, P]),
     "lrk_decision_risk": (I32, [P, P, I32, P, P, I64, I64, I64, D, F, P, P]),
     "lrk_append": (I32, [P, P, P, I64, P, P, P, I64, I64, I64, I32, I64, P, P, P, P, P, P]),
     "lrk_compact": (I32, [P, P, P, I64, I64, I32, P, I64, P, P, P, P]),

@@ -27,6 +27,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "rows.cuh"
@@ -186,6 +187,70 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
   return LRK_OK;
 }
 
+// Scratch of lrk_temporal_scores_static: the per-row statistics of up to
+// LRK_STATIC_SCORE_ROWS rows.  Every device that loads liblrk holds one copy
+// until the process exits.  Host code must not pass this name to a kernel (on
+// the host it is a stand-in, not a device address); static_scratch() looks up
+// the device address once per device.
+__device__ __align__(256) float3 g_static_row_stats[LRK_STATIC_SCORE_ROWS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+float3 *g_static_address[kMaxDevices] = {};
+
+// Device address of g_static_row_stats on the current device (looked up with
+// cudaGetSymbolAddress on the first call for that device).
+int static_scratch(float3 **address) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+  if (device < 0 || device >= kMaxDevices) return fail(LRK_ERR_UNSUPPORTED, "device index out of range");
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_address[device] == nullptr) {
+    void *found = nullptr;
+    e = cudaGetSymbolAddress(&found, g_static_row_stats);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      set_error("cudaGetSymbolAddress(g_static_row_stats): %s", cudaGetErrorString(e));
+      return LRK_ERR_CUDA;
+    }
+    g_static_address[device] = static_cast<float3 *>(found);
+  }
+  *address = g_static_address[device];
+  return LRK_OK;
+}
+
+int check_score_call(const lrk_score_segment *segments, int64_t count, int64_t window, int64_t groups,
+                     float epsilon, const int64_t *query_positions, const float *margin) {
+  LRK_REQUIRE(count >= 0 && window > 0 && groups > 0 && epsilon > 0, "invalid score sizes");
+  LRK_REQUIRE(groups <= kMaxGroups, "fused scoring supports at most 8 query heads per KV head");
+  LRK_REQUIRE(window <= 65535 && window * groups * static_cast<int64_t>(sizeof(float4)) <= 200 * 1024,
+              "window * groups too large for one CTA's statistics");
+  if (count == 0) return LRK_OK;
+  LRK_REQUIRE(segments && query_positions && margin, "null pointer");
+  for (int64_t s = 0; s < count; ++s) {
+    const lrk_score_segment &seg = segments[s];
+    LRK_REQUIRE(seg.logits && seg.projected_values && seg.key_positions && seg.scores, "null segment pointer");
+    LRK_REQUIRE(seg.length > 0 && seg.first >= 0 && seg.last > seg.first && seg.last <= seg.length,
+                "Invalid risk interval");
+    LRK_REQUIRE(seg.projected_stride >= seg.length, "projected_stride shorter than the segment");
+  }
+  return LRK_OK;
+}
+
+int dispatch_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype, const int64_t *qpos,
+                    int64_t window, int64_t groups, float scale, const float *margin, float epsilon, float3 *stats,
+                    lrk_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int w = static_cast<int>(window), g = static_cast<int>(groups);
+  switch (logits_dtype) {
+    case LRK_BF16: return launch_scores<__nv_bfloat16>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
+    case LRK_F16: return launch_scores<__half>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
+    case LRK_F32: return launch_scores<float>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
+    default: return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
+  }
+}
+
 }  // namespace
 }  // namespace lrk
 
@@ -201,28 +266,31 @@ extern "C" int lrk_temporal_scores(const lrk_score_segment *segments, int64_t co
                                    const float *margin, float epsilon, void *workspace, size_t workspace_bytes,
                                    lrk_stream_t stream) {
   clear_error();
-  LRK_REQUIRE(count >= 0 && window > 0 && groups > 0 && epsilon > 0, "invalid score sizes");
-  LRK_REQUIRE(groups <= kMaxGroups, "fused scoring supports at most 8 query heads per KV head");
-  LRK_REQUIRE(window <= 65535 && window * groups * static_cast<int64_t>(sizeof(float4)) <= 200 * 1024,
-              "window * groups too large for one CTA's statistics");
-  if (count == 0) return LRK_OK;
-  LRK_REQUIRE(segments && query_positions && margin, "null pointer");
-  for (int64_t s = 0; s < count; ++s) {
-    const lrk_score_segment &seg = segments[s];
-    LRK_REQUIRE(seg.logits && seg.projected_values && seg.key_positions && seg.scores, "null segment pointer");
-    LRK_REQUIRE(seg.length > 0 && seg.first >= 0 && seg.last > seg.first && seg.last <= seg.length,
-                "Invalid risk interval");
-    LRK_REQUIRE(seg.projected_stride >= seg.length, "projected_stride shorter than the segment");
-  }
+  int status = check_score_call(segments, count, window, groups, epsilon, query_positions, margin);
+  if (status != LRK_OK || count == 0) return status;
   const size_t need = lrk_temporal_scores_workspace_bytes(count, window, groups);
   if (workspace == nullptr || workspace_bytes < need) return fail(LRK_ERR_WORKSPACE, "score workspace too small");
   float3 *stats = reinterpret_cast<float3 *>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t{15});
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const int w = static_cast<int>(window), g = static_cast<int>(groups);
-  switch (logits_dtype) {
-    case LRK_BF16: return launch_scores<__nv_bfloat16>(segments, count, query_positions, w, g, scale, margin, epsilon, stats, s);
-    case LRK_F16: return launch_scores<__half>(segments, count, query_positions, w, g, scale, margin, epsilon, stats, s);
-    case LRK_F32: return launch_scores<float>(segments, count, query_positions, w, g, scale, margin, epsilon, stats, s);
-    default: return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
+  return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
+                         stream);
+}
+
+extern "C" int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count, int logits_dtype,
+                                          const int64_t *query_positions, int64_t window, int64_t groups,
+                                          float scale, const float *margin, float epsilon, lrk_stream_t stream) {
+  clear_error();
+  int status = check_score_call(segments, count, window, groups, epsilon, query_positions, margin);
+  if (status != LRK_OK || count == 0) return status;
+  if (count * window * groups > LRK_STATIC_SCORE_ROWS) {
+    set_error("lrk_temporal_scores_static: %lld segments x %lld queries x %lld groups exceeds the static scratch of "
+              "%d row statistics (LRK_STATIC_SCORE_ROWS); split the call or use lrk_temporal_scores",
+              static_cast<long long>(count), static_cast<long long>(window), static_cast<long long>(groups),
+              LRK_STATIC_SCORE_ROWS);
+    return LRK_ERR_INVALID;
   }
+  float3 *stats = nullptr;
+  status = static_scratch(&stats);
+  if (status != LRK_OK) return status;
+  return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
+                         stream);
 }

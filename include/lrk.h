@@ -114,6 +114,30 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
                         const float *margin, float epsilon, void *workspace, size_t workspace_bytes,
                         lrk_stream_t stream);
 
+/* Largest segments x window x groups one lrk_temporal_scores_static call takes
+ * (one configs[1] audit: 256 heads x 250 queries x 4 groups = 256000). */
+#define LRK_STATIC_SCORE_ROWS 262144
+
+/* lrk_temporal_scores without a workspace argument, for callers that cannot
+ * allocate device memory: a host whose device memory is all handed out by
+ * another allocator (an inference engine that reserves the GPU's memory up
+ * front and forbids further cudaMalloc), or a plain C host (cgo, JNI) with no
+ * device allocator of its own.  It allocates nothing: its scratch is a
+ * file-scope device array of LRK_STATIC_SCORE_ROWS row statistics (3 MiB),
+ * which every GPU that loads liblrk holds until the process exits.  Calls with
+ * segments x window x groups above LRK_STATIC_SCORE_ROWS are rejected with
+ * LRK_ERR_INVALID before anything is launched.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that
+ * first call before any stream capture on that device.  All calls share the
+ * one array: calls whose work overlaps on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller.  Nothing in the array
+ * needs clearing between calls: each call writes every entry it reads first.
+ * Same results as lrk_temporal_scores.
+ * No counterpart in the reference (new entry point). */
+int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count, int logits_dtype,
+                               const int64_t *query_positions, int64_t window, int64_t groups, float scale,
+                               const float *margin, float epsilon, lrk_stream_t stream);
+
 /* ------------------------------------------------- cache data movement */
 
 /* Append `added` rows to each head segment of a packed layer.
