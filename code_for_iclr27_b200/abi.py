@@ -33,7 +33,7 @@ class Segment(ctypes.Structure):
 class ScoreSegment(ctypes.Structure):
     """lrk_score_segment (include/lrk.h)."""
     _fields_ = [("logits", P), ("projected_values", P), ("projected_stride", I64), ("key_positions", P),
-                ("length", I64), ("first", I64), ("last", I64), ("scores", P)]
+                ("length", I64), ("first", I64), ("last", I64), ("scores", P), ("logits_stride", I64)]
 
 
 SIGNATURES = {
@@ -58,6 +58,9 @@ SIGNATURES = {
     "lrk_refine": (I32, [P, P, I64, P, P, I64, I64, P, SIZE, P, P, P, P, P]),
     "lrk_topk_workspace_bytes": (SIZE, [I64]),
     "lrk_topk_smallest": (I32, [P, I64, I64, P, SIZE, P, P, P]),
+    "lrk_gather_rows": (I32, [P, I64, I64, P, I64, P, P]),
+    "lrk_project_values": (I32, [P, I32, I64, I64, P, P, I64, I64, P, P]),
+    "lrk_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "lrk_register_host": (I32, [P, SIZE]),
     "lrk_unregister_host": (I32, [P]),
 }

@@ -102,13 +102,28 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
     return ScoreTable(torch.cat(parts), segments, ends)
 
 
+def _aligned_keys(keys, start, end, multiple=8):
+    """Keys of one head extended to a multiple of 8 rows.  cuBLAS runs the
+    [W*G, D] x [D, L] logits GEMM about 5x faster when L is a multiple of 8
+    (B200: 20 vs 110 us at L ~ 35k); the extra columns are never read.  The
+    view reaches into the next head's rows, or is a zero-padded copy at the
+    end of the layer."""
+    import torch
+
+    padded = -(-(end - start) // multiple) * multiple
+    if start + padded <= keys.shape[0]:
+        return keys[start:start + padded]
+    return torch.cat([keys[start:end], keys.new_zeros(padded - (end - start), keys.shape[1])])
+
+
 def score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
                       denominator_epsilon=1e-6) -> ScoreTable:
-    """compute_score_table with the fused scorer: per layer one projected-value
-    GEMM for all heads (g V^T, float32 like scoring.py:175), one bf16 Q K^T GEMM
-    per head (scoring.py:184), then one lrk_temporal_scores call over all of
-    the layer's heads -- the probabilities never reach HBM.  Same table as
-    score_table (within 1e-5 relative)."""
+    """compute_score_table with the fused scorer.  Per layer: one
+    lrk_project_values call (g V^T for every head, scoring.py:175), one bf16
+    Q K^T GEMM per head (scoring.py:184), then one lrk_temporal_scores call
+    over all of the layer's heads -- the probabilities never reach HBM.  Given
+    the same logits and projected values, the scores are bit-identical to the
+    temporal_probabilities + temporal_risk composition."""
     import torch
 
     C = operators()
@@ -122,7 +137,8 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
         scale = 1.0 / math.sqrt(layer.keys.shape[-1])
         bounds = layer.bounds()
         positions = layer.positions.reshape(-1)
-        projected = torch.matmul(gradients[layer_index].float(), layer.values.float().transpose(0, 1))
+        projected = C.project_values(layer.values, gradients[layer_index].float().contiguous(), layer.cumulative,
+                                     groups)
         window, dim = layer_queries.shape[0], layer_queries.shape[-1]
         # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
         per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1).contiguous()
@@ -133,9 +149,10 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
             candidate_end = max(candidate_start, end - start - protect_recent)
             if candidate_end <= candidate_start:
                 continue
-            head_logits = torch.matmul(per_head[head].view(window * groups, dim), layer.keys[start:end].transpose(0, 1))
-            logits.append(head_logits.view(window, groups, end - start))
-            pvs.append(projected[head * groups:(head + 1) * groups, start:end])
+            keys = _aligned_keys(layer.keys, start, end)
+            head_logits = torch.matmul(per_head[head].view(window * groups, dim), keys.transpose(0, 1))
+            logits.append(head_logits.view(window, groups, keys.shape[0])[:, :, :end - start])
+            pvs.append(projected[:, start:end])
             kpos.append(positions[start:end])
             firsts.append(candidate_start)
             lasts.append(candidate_end)

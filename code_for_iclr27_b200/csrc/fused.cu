@@ -37,6 +37,7 @@ namespace {
 
 constexpr int kMaxScoreSegments = 48;
 constexpr int kRiskThreads = 256;
+constexpr int kQueryLanes = kRiskThreads / 32;
 constexpr int kMaxGroups = 8;
 
 struct ScoreTableParam {
@@ -44,24 +45,54 @@ struct ScoreTableParam {
   int count;
 };
 
-// stats[(segment * window * groups) + row] = (max, denominator, projection).
-template <typename T, bool STAGED>
+// One CTA per (segment, query, group) row: its exact statistics (rows.cuh).
+// stats[(segment * window + query) * groups + group] = (max, denominator, projection).
+template <typename T, int MODE>
 __global__ void __launch_bounds__(rows::kLanes) stats_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
                                                              int groups, float scale, float3 *__restrict__ stats,
                                                              int64_t segment_base, int64_t rows_per_segment) {
   extern __shared__ __align__(16) unsigned char stage[];
   __shared__ float scratch[rows::kLanes];
-  const int64_t row = blockIdx.x;  // query * groups + group
+  const int64_t row = blockIdx.x;
   const int si = blockIdx.y;
   const lrk_score_segment &seg = table.segment[si];
   const int group = static_cast<int>(row % groups);
-  const int64_t query = row / groups;
-  const rows::RowResult r = rows::row_statistics<T, STAGED>(
-      static_cast<const T *>(seg.logits) + row * seg.length, seg.length, seg.key_positions,
-      static_cast<float>(qpos[query]), seg.projected_values + group * seg.projected_stride, scale, nullptr, stage,
-      scratch);
+  const rows::RowResult r = rows::row_statistics<T, MODE>(
+      static_cast<const T *>(seg.logits) + row * seg.logits_stride, seg.length, seg.key_positions,
+      static_cast<float>(qpos[row / groups]), seg.projected_values + group * seg.projected_stride, scale, nullptr,
+      stage, scratch);
   if (threadIdx.x == 0)
     stats[(segment_base + si) * rows_per_segment + row] = make_float3(r.maximum, r.denominator, r.projection);
+}
+
+template <typename K>
+int allow_shared(K kernel, int64_t bytes) {
+  if (bytes <= 48 * 1024) return LRK_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  return e == cudaSuccess ? LRK_OK : fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+}
+
+template <typename T>
+int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int window, int groups, float scale,
+                 float3 *stats, int64_t s0, int64_t max_length, cudaStream_t stream) {
+  const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
+  const dim3 grid(static_cast<unsigned>(rows_per_segment), n);
+  const int mode = rows::choose_stage<T>(max_length);
+  const int64_t bytes = rows::staged_bytes<T>(mode, max_length);
+  int status = LRK_OK;
+  if (mode == rows::kWeights) {
+    if ((status = allow_shared(stats_kernel<T, rows::kWeights>, bytes)) != LRK_OK) return status;
+    stats_kernel<T, rows::kWeights><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, s0,
+                                                                           rows_per_segment);
+  } else if (mode == rows::kBits) {
+    if ((status = allow_shared(stats_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
+    stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, s0,
+                                                                        rows_per_segment);
+  } else {
+    stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, s0,
+                                                                      rows_per_segment);
+  }
+  return launch_status("lrk_temporal_scores statistics");
 }
 
 __device__ __forceinline__ double softplus64(double value) { return value > 20.0 ? value : log1p(exp(value)); }
@@ -74,6 +105,10 @@ __device__ __forceinline__ double risk64(double margin, double probability, doub
   return fmax(0.0, kl);
 }
 
+// A CTA covers 32 consecutive candidate columns (one warp row, 64-byte bf16
+// reads per logits row) with kQueryLanes query lanes: lane y walks queries
+// y, y + kQueryLanes, ...  The lanes' min / max / non-finite flags meet in
+// shared memory (min and max are order-free), then lane 0 computes the risk.
 template <typename T, int G>
 __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
                                                             int window, int groups, float scale,
@@ -82,45 +117,60 @@ __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam tabl
                                                             float epsilon) {
   using D = rows::Dtype<T>;
   extern __shared__ float4 shared_stats[];  // [window * groups] (max, denominator, projection, query position)
+  __shared__ float lane_min[kQueryLanes][33], lane_max[kQueryLanes][33];
+  __shared__ int lane_bad[kQueryLanes][33];
   const int si = blockIdx.y;
   const lrk_score_segment &seg = table.segment[si];
   const int ng = G > 0 ? G : groups;
-  for (int i = threadIdx.x; i < window * ng; i += kRiskThreads) {
+  const int tid = threadIdx.y * 32 + threadIdx.x;
+  for (int i = tid; i < window * ng; i += kRiskThreads) {
     const float3 st = stats[(segment_base + si) * window * ng + i];
     shared_stats[i] = make_float4(st.x, st.y, st.z, static_cast<float>(qpos[i / ng]));
   }
   __syncthreads();
   const int64_t count = seg.last - seg.first;
-  const int64_t candidate = static_cast<int64_t>(blockIdx.x) * kRiskThreads + threadIdx.x;
-  if (candidate >= count) return;
-  const int64_t column = seg.first + candidate;
-  const int64_t length = seg.length;
-  const float key_position = __ldg(seg.key_positions + column);
-  float pv[G > 0 ? G : kMaxGroups];
-#pragma unroll
-  for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g)
-    pv[g] = g < ng ? __ldg(seg.projected_values + g * seg.projected_stride + column) : 0.0f;
-  const typename D::Bits *base = static_cast<const typename D::Bits *>(seg.logits) + column;
+  const int64_t candidate = static_cast<int64_t>(blockIdx.x) * 32 + threadIdx.x;
+  const bool active = candidate < count;
   float minimum = INFINITY, maximum = -INFINITY;
-  bool nonfinite = false;
-#pragma unroll 4
-  for (int q = 0; q < window; ++q) {
-    float drop = 0.0f;
+  int nonfinite = 0;
+  if (active) {
+    const int64_t column = seg.first + candidate;
+    const int64_t stride = seg.logits_stride;
+    const float key_position = __ldg(seg.key_positions + column);
+    float pv[G > 0 ? G : kMaxGroups];
 #pragma unroll
-    for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g) {
-      if (g < ng) {
-        const float4 st = shared_stats[q * ng + g];
-        const float rounded = D::to_float(D::round(D::to_float(__ldg(base + (static_cast<int64_t>(q) * ng + g) * length)),
-                                                   scale));
-        const float x = key_position <= st.w ? rounded : -INFINITY;
-        const float probability = __fdiv_rn(expf(__fsub_rn(x, st.x)), st.y);
-        const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
-        drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(pv[g], st.z)));
+    for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g)
+      pv[g] = g < ng ? __ldg(seg.projected_values + g * seg.projected_stride + column) : 0.0f;
+    const typename D::Bits *base = static_cast<const typename D::Bits *>(seg.logits) + column;
+#pragma unroll 2
+    for (int q = threadIdx.y; q < window; q += kQueryLanes) {
+      float drop = 0.0f;
+#pragma unroll
+      for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g) {
+        if (g < ng) {
+          const float4 st = shared_stats[q * ng + g];
+          const float rounded = D::to_float(
+              D::round(D::to_float(__ldg(base + (static_cast<int64_t>(q) * ng + g) * stride)), scale));
+          const float x = key_position <= st.w ? rounded : -INFINITY;
+          const float probability = __fdiv_rn(expf(__fsub_rn(x, st.x)), st.y);
+          const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
+          drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(pv[g], st.z)));
+        }
       }
+      nonfinite |= !isfinite(drop);
+      minimum = fminf(minimum, drop);
+      maximum = fmaxf(maximum, drop);
     }
-    nonfinite |= !isfinite(drop);
-    minimum = fminf(minimum, drop);
-    maximum = fmaxf(maximum, drop);
+  }
+  lane_min[threadIdx.y][threadIdx.x] = minimum;
+  lane_max[threadIdx.y][threadIdx.x] = maximum;
+  lane_bad[threadIdx.y][threadIdx.x] = nonfinite;
+  __syncthreads();
+  if (threadIdx.y != 0 || !active) return;
+  for (int y = 1; y < kQueryLanes; ++y) {
+    minimum = fminf(minimum, lane_min[y][threadIdx.x]);
+    maximum = fmaxf(maximum, lane_max[y][threadIdx.x]);
+    nonfinite |= lane_bad[y][threadIdx.x];
   }
   float result;
   if (nonfinite) {
@@ -148,23 +198,11 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
     }
     int64_t max_length = 0;
     for (int i = 0; i < n; ++i) max_length = std::max<int64_t>(max_length, table.segment[i].length);
-    const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
-    const int64_t stage = rows::staged_bytes<T>(max_length);
-    const dim3 stats_grid(static_cast<unsigned>(rows_per_segment), n);
-    if (stage <= rows::kStageBytes) {
-      auto kernel = stats_kernel<T, true>;
-      if (stage > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::kStageBytes);
-        if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-      }
-      kernel<<<stats_grid, rows::kLanes, static_cast<size_t>(stage), stream>>>(table, qpos, groups, scale, stats, s0,
-                                                                               rows_per_segment);
-    } else {
-      stats_kernel<T, false><<<stats_grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, s0,
-                                                                       rows_per_segment);
-    }
+    int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, s0, max_length, stream);
+    if (status != LRK_OK) return status;
     const size_t shared = static_cast<size_t>(window) * groups * sizeof(float4);
-    const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, kRiskThreads))), n);
+    const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, 32))), n);
+    const dim3 block(32, kQueryLanes);
     if (shared > 48 * 1024) {
       auto set = [&](auto kernel) {
         return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
@@ -173,15 +211,15 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
       if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
     }
     if (groups == 4)
-      risk_kernel<T, 4><<<grid, kRiskThreads, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
+      risk_kernel<T, 4><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
                                                                  epsilon);
     else if (groups == 8)
-      risk_kernel<T, 8><<<grid, kRiskThreads, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
+      risk_kernel<T, 8><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
                                                                  epsilon);
     else
-      risk_kernel<T, 0><<<grid, kRiskThreads, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
+      risk_kernel<T, 0><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
                                                                  epsilon);
-    const int status = launch_status("lrk_temporal_scores");
+    status = launch_status("lrk_temporal_scores");
     if (status != LRK_OK) return status;
   }
   return LRK_OK;
@@ -234,6 +272,7 @@ int check_score_call(const lrk_score_segment *segments, int64_t count, int64_t w
     LRK_REQUIRE(seg.length > 0 && seg.first >= 0 && seg.last > seg.first && seg.last <= seg.length,
                 "Invalid risk interval");
     LRK_REQUIRE(seg.projected_stride >= seg.length, "projected_stride shorter than the segment");
+    LRK_REQUIRE(seg.logits_stride >= seg.length, "logits_stride shorter than the segment");
   }
   return LRK_OK;
 }

@@ -74,3 +74,17 @@ extern "C" int lrk_unregister_host(void *address) {
   }
   return LRK_OK;
 }
+
+extern "C" int lrk_host_device_pointer(void *host, void **device) {
+  lrk::clear_error();
+  if (host == nullptr || device == nullptr) return lrk::fail(LRK_ERR_INVALID, "null pointer");
+  cudaError_t status = cudaHostGetDevicePointer(device, host, 0);
+  if (status != cudaSuccess) {
+    cudaGetLastError();
+    *device = nullptr;
+    lrk::set_error("cudaHostGetDevicePointer: %s (register the memory with lrk_register_host first)",
+                   cudaGetErrorString(status));
+    return LRK_ERR_INVALID;
+  }
+  return LRK_OK;
+}

@@ -326,6 +326,24 @@ struct IndexPlan {
   }
 };
 
+// Plain row gather out of one table: dst row i <- src row indices[i].
+struct RowsPlan {
+  const char *src;
+  int64_t rows, row_bytes;
+  const int64_t *indices;
+  using Shared = NoShared;
+  __device__ void prologue(Shared &) const {}
+  template <int TR>
+  __device__ void fill(int64_t first, int nrows, RowSource *sources, Shared &) const {
+    for (int i = threadIdx.x; i < nrows; i += kThreads) {
+      const int64_t source = indices[first + i];
+      RowSource out{nullptr, nullptr, 0.0f};
+      if (source >= 0 && source < rows) out.k = src + source * row_bytes;
+      sources[i] = out;
+    }
+  }
+};
+
 // _C.batch_append: segments (request-major, head-minor) passed by value.
 constexpr int kMaxSegmentsPerLaunch = 64;
 
@@ -388,14 +406,19 @@ int launch_gather(const Plan &plan, GatherOut out, int vb, cudaStream_t stream, 
   const int64_t units = out.row_bytes / vb;
   if (units <= 0 || units > 1024) return fail(LRK_ERR_UNSUPPORTED, "row too wide for the gather engine");
   out.units.init(static_cast<uint32_t>(units));
+  // Tile height: 256 rows for narrow rows; 64 normally; 16 when 64-row tiles
+  // would leave SMs idle (small outputs such as an archive pack).
+  const int sms = sm_count();
   const bool narrow = out.row_bytes < 64;
-  const int64_t tile_rows = narrow ? 256 : 64;
+  const bool small = !narrow && ceil_div(out.rows, 64) < 2 * sms;
+  const int64_t tile_rows = narrow ? 256 : small ? 16 : 64;
   const int64_t tiles = ceil_div(out.rows, tile_rows);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, static_cast<int64_t>(sm_count()) * 16));
-#define LRK_GATHER_CASE(VB)                                                          \
-  case VB:                                                                           \
-    if (narrow) gather_kernel<VB, 256, Plan><<<grid, kThreads, 0, stream>>>(plan, out); \
-    else gather_kernel<VB, 64, Plan><<<grid, kThreads, 0, stream>>>(plan, out);      \
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, static_cast<int64_t>(sms) * 16));
+#define LRK_GATHER_CASE(VB)                                                              \
+  case VB:                                                                               \
+    if (narrow) gather_kernel<VB, 256, Plan><<<grid, kThreads, 0, stream>>>(plan, out);     \
+    else if (small) gather_kernel<VB, 16, Plan><<<grid, kThreads, 0, stream>>>(plan, out);  \
+    else gather_kernel<VB, 64, Plan><<<grid, kThreads, 0, stream>>>(plan, out);          \
     break;
   switch (vb) {
     LRK_GATHER_CASE(16)
@@ -582,4 +605,16 @@ extern "C" int lrk_batch_append(const lrk_segment *segments, int64_t segment_cou
     if (status != LRK_OK) return status;
   }
   return LRK_OK;
+}
+
+extern "C" int lrk_gather_rows(const void *src, int64_t src_rows, int64_t row_bytes, const int64_t *indices,
+                               int64_t count, void *dst, lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(src_rows >= 0 && row_bytes > 0 && count >= 0, "invalid gather sizes");
+  if (count == 0) return LRK_OK;
+  LRK_REQUIRE(src && indices && dst, "null pointer");
+  const int vb = pick_vector(row_bytes, {src, dst}, {});
+  RowsPlan plan{static_cast<const char *>(src), src_rows, row_bytes, indices};
+  GatherOut out{static_cast<char *>(dst), nullptr, nullptr, row_bytes, row_bytes, count, row_bytes, {}};
+  return launch_gather(plan, out, vb, reinterpret_cast<cudaStream_t>(stream), "lrk_gather_rows");
 }

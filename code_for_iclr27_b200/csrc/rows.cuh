@@ -10,11 +10,12 @@
 // with --fmad=false, and order-sensitive steps use _rn intrinsics), so the
 // max, denominator, projection and probabilities are bit-identical.
 //
-// The work is arranged for B200: one CTA per row, the row read from HBM once
-// with 16-byte vector loads and staged in shared memory in the logits dtype
-// (x is exact in that dtype), then the two reduction passes run from shared
-// memory.  bf16 rows up to 116k positions fit (3 CTAs per SM at 35k); longer
-// rows recompute x from the logits (L2-resident) in each pass.
+// The work is arranged for B200: one CTA of 256 threads (the 256 reference
+// lanes) per row; the row is read from HBM once with 16-byte loads and staged
+// in shared memory -- as fp32 weights for rows up to 18k positions (3 CTAs per
+// SM; the weights are computed once and reused by pass C), in the logits dtype
+// (exact) up to 110k bf16 positions -- and the reduction passes then run from
+// shared memory.  Longer rows recompute x from the logits in each pass.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -64,12 +65,13 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Block max (order-free); scratch holds >= 32 floats.
+// Block max over NT threads (order-free); scratch holds >= 32 floats.
+template <int NT = kLanes>
 __device__ __forceinline__ float block_max(float v, float *scratch) {
   v = warp_max(v);
   if ((threadIdx.x & 31) == 0) scratch[threadIdx.x >> 5] = v;
   __syncthreads();
-  float r = threadIdx.x < kLanes / 32 ? scratch[threadIdx.x] : -INFINITY;
+  float r = threadIdx.x < NT / 32 ? scratch[threadIdx.x] : -INFINITY;
   if (threadIdx.x < 32) r = warp_max(r);
   if (threadIdx.x == 0) scratch[0] = r;
   __syncthreads();
@@ -79,9 +81,10 @@ __device__ __forceinline__ float block_max(float v, float *scratch) {
 }
 
 // The reference's 256-wide pairwise tree: partial[t] += partial[t + s] for
-// s = 128 .. 1.  tree holds 256 floats.
+// s = 128 .. 1.  Lanes are threads 0..255; all threads of the CTA call.  tree
+// holds 256 floats.
 __device__ __forceinline__ float tree_sum(float partial, float *tree) {
-  tree[threadIdx.x] = partial;
+  if (threadIdx.x < kLanes) tree[threadIdx.x] = partial;
   __syncthreads();
 #pragma unroll
   for (int s = kLanes / 2; s >= 32; s >>= 1) {
@@ -107,11 +110,35 @@ struct RowResult {
   float maximum, denominator, projection;
 };
 
+// Layouts of a row between its passes (one CTA of 256 threads = the 256
+// reference lanes per row).
+enum Stage : int {
+  kStream = 0,   // nothing staged: x is recomputed from the logits in each pass
+  kBits = 1,     // x staged in the logits dtype (exact), expf recomputed in pass C
+  kWeights = 2,  // x staged as fp32 and overwritten by w = expf(x - max) in pass B
+};
+
+template <typename T>
+__host__ __device__ constexpr int64_t staged_bytes(int mode, int64_t length) {
+  return mode == kWeights ? (length + 8) * 4
+         : mode == kBits  ? (length + 16) * static_cast<int64_t>(sizeof(typename Dtype<T>::Bits))
+                          : 0;
+}
+
+// Rows up to this many fp32 weights (72 KB, 3 CTAs per SM) keep w.
+constexpr int64_t kWeightStageMax = 18 * 1024;
+
+template <typename T>
+inline int choose_stage(int64_t length) {
+  if (length <= kWeightStageMax) return kWeights;
+  if (staged_bytes<T>(kBits, length) <= kStageBytes) return kBits;
+  return kStream;
+}
+
 // Statistics of one row (all 256 threads call).  probabilities_out, when not
-// null, receives every probability (the drop-in operator's output).
-// `stage` is dynamic shared memory of at least staged_bytes<T>(length) when
-// STAGED, unused otherwise.
-template <typename T, bool STAGED>
+// null, receives every probability (the drop-in operator's output).  `stage`
+// is dynamic shared memory of staged_bytes<T>(MODE, length) bytes.
+template <typename T, int MODE>
 __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const float *__restrict__ key_positions,
                                     float query_position, const float *__restrict__ projected_values, float scale,
                                     float *__restrict__ probabilities_out, unsigned char *stage, float *scratch) {
@@ -119,12 +146,11 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
   using Bits = typename D::Bits;
   constexpr int V = D::kPerVec;
   const Bits *in = reinterpret_cast<const Bits *>(row);
-  // Element index of the first 16-byte boundary of this row, and the shared
-  // offset that puts that element on a 16-byte boundary of the stage too.
+  // First 16-byte boundary of the row, and the stage offsets that align it.
   const int64_t lead = lmin(length, static_cast<int64_t>(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) /
                                                         sizeof(Bits)));
-  const int pad = static_cast<int>((V - lead % V) % V);
-  Bits *x_stage = reinterpret_cast<Bits *>(stage) + pad;
+  Bits *x_bits = reinterpret_cast<Bits *>(stage) + (V - lead % V) % V;
+  float *x_float = reinterpret_cast<float *>(stage) + (4 - lead % 4) % 4;
   const Bits neg_inf = minus_infinity<T>();
   auto value_bits = [&](int64_t p, Bits raw) -> Bits {
     return __ldg(key_positions + p) <= query_position ? D::round(D::to_float(raw), scale) : neg_inf;
@@ -132,63 +158,68 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
 
   // Pass A: scale, round, mask; row max; stage the row.
   float local_max = -INFINITY;
-  if (STAGED) {
-    for (int64_t p = threadIdx.x; p < lead; p += kLanes) {
-      const Bits b = value_bits(p, __ldg(in + p));
-      x_stage[p] = b;
+  if (MODE == kStream) {
+    for (int64_t p = threadIdx.x; p < length; p += kLanes)
+      local_max = fmaxf(local_max, D::to_float(value_bits(p, __ldg(in + p))));
+  } else {
+    auto put = [&](int64_t p, Bits b) {
+      if (MODE == kBits) x_bits[p] = b; else x_float[p] = D::to_float(b);
       local_max = fmaxf(local_max, D::to_float(b));
-    }
+    };
+    for (int64_t p = threadIdx.x; p < lead; p += kLanes) put(p, value_bits(p, __ldg(in + p)));
     const int64_t vectors = (length - lead) / V;
     const uint4 *body = reinterpret_cast<const uint4 *>(in + lead);
-    uint4 *stage_body = reinterpret_cast<uint4 *>(x_stage + lead);
 #pragma unroll 4
     for (int64_t v = threadIdx.x; v < vectors; v += kLanes) {
       uint4 raw = __ldcs(body + v);
       Bits *lanes = reinterpret_cast<Bits *>(&raw);
       const int64_t p0 = lead + v * V;
+      float xs[V];
 #pragma unroll
       for (int j = 0; j < V; ++j) {
         lanes[j] = value_bits(p0 + j, lanes[j]);
-        local_max = fmaxf(local_max, D::to_float(lanes[j]));
+        xs[j] = D::to_float(lanes[j]);
+        local_max = fmaxf(local_max, xs[j]);
       }
-      stage_body[v] = raw;
+      if (MODE == kBits) {
+        reinterpret_cast<uint4 *>(x_bits + lead)[v] = raw;
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; j += 4)
+          *reinterpret_cast<float4 *>(x_float + p0 + j) = make_float4(xs[j], xs[j + 1], xs[j + 2], xs[j + 3]);
+      }
     }
-    for (int64_t p = lead + vectors * V + threadIdx.x; p < length; p += kLanes) {
-      const Bits b = value_bits(p, __ldg(in + p));
-      x_stage[p] = b;
-      local_max = fmaxf(local_max, D::to_float(b));
-    }
-  } else {
-    for (int64_t p = threadIdx.x; p < length; p += kLanes)
-      local_max = fmaxf(local_max, D::to_float(value_bits(p, __ldg(in + p))));
+    for (int64_t p = lead + vectors * V + threadIdx.x; p < length; p += kLanes) put(p, value_bits(p, __ldg(in + p)));
   }
   const float maximum = block_max(local_max, scratch);
 
   auto x_at = [&](int64_t p) -> float {
-    return STAGED ? D::to_float(x_stage[p]) : D::to_float(value_bits(p, __ldg(in + p)));
+    if (MODE == kBits) return D::to_float(x_bits[p]);
+    if (MODE == kWeights) return x_float[p];
+    return D::to_float(value_bits(p, __ldg(in + p)));
   };
 
   // Pass B: denominator, lane t summing positions t, t + 256, ... in order.
   float sum = 0.0f;
 #pragma unroll 4
-  for (int64_t p = threadIdx.x; p < length; p += kLanes) sum = __fadd_rn(sum, expf(__fsub_rn(x_at(p), maximum)));
+  for (int64_t p = threadIdx.x; p < length; p += kLanes) {
+    const float w = expf(__fsub_rn(x_at(p), maximum));
+    if (MODE == kWeights) x_float[p] = w;
+    sum = __fadd_rn(sum, w);
+  }
   const float denominator = tree_sum(sum, scratch);
 
   // Pass C: probabilities (optionally stored) and the value projection.
   float projection = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
   for (int64_t p = threadIdx.x; p < length; p += kLanes) {
-    const float probability = __fdiv_rn(expf(__fsub_rn(x_at(p), maximum)), denominator);
+    const float w = MODE == kWeights ? x_float[p] : expf(__fsub_rn(x_at(p), maximum));
+    const float probability = __fdiv_rn(w, denominator);
     if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
     projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(projected_values + p)));
   }
   projection = tree_sum(projection, scratch);
   return {maximum, denominator, projection};
-}
-
-template <typename T>
-__host__ __device__ constexpr int64_t staged_bytes(int64_t length) {
-  return (length + 16) * static_cast<int64_t>(sizeof(typename Dtype<T>::Bits));
 }
 
 }  // namespace rows

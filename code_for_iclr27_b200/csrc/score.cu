@@ -24,9 +24,9 @@ namespace {
 
 constexpr int kLanes = rows::kLanes;  // the reference's reduction width
 
-// One CTA per (query, group) row (csrc/scoring.cu:32-66): rows::row_statistics
-// writes the row's probabilities and returns its value projection.
-template <typename T, bool STAGED>
+// One CTA per (query, group) row (csrc/scoring.cu:32-66): the row's exact
+// statistics (rows.cuh), its probabilities written out, its value projection.
+template <typename T, int MODE>
 __global__ void __launch_bounds__(kLanes) probabilities_kernel(
     const T *__restrict__ logits, const float *__restrict__ projected_values,
     const int64_t *__restrict__ query_positions, const float *__restrict__ key_positions,
@@ -37,7 +37,7 @@ __global__ void __launch_bounds__(kLanes) probabilities_kernel(
   const int64_t row = blockIdx.x;
   const int group = static_cast<int>(row % groups);
   const int64_t query = row / groups;
-  const rows::RowResult result = rows::row_statistics<T, STAGED>(
+  const rows::RowResult result = rows::row_statistics<T, MODE>(
       logits + row * length, length, key_positions, static_cast<float>(query_positions[query]),
       projected_values + static_cast<int64_t>(group) * length, scale, probabilities + row * length, stage, scratch);
   if (threadIdx.x == 0) output_projection[row] = result.projection;
@@ -193,22 +193,32 @@ __global__ void __launch_bounds__(kLanes) decision_risk_kernel(
   }
 }
 
+template <typename K>
+int allow_shared(K kernel, int64_t bytes) {
+  if (bytes <= 48 * 1024) return LRK_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  return e == cudaSuccess ? LRK_OK : fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+}
+
 template <typename T>
 int launch_probabilities(const void *logits, const float *pv, const int64_t *qpos, const float *kpos, float *probs,
                          float *op, int64_t rows, int groups, int64_t length, float scale, cudaStream_t stream) {
   const T *in = static_cast<const T *>(logits);
-  const int64_t bytes = rows::staged_bytes<T>(length);
-  if (bytes <= rows::kStageBytes) {
-    auto kernel = probabilities_kernel<T, true>;
-    if (bytes > 48 * 1024) {
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::kStageBytes);
-      if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-    }
-    kernel<<<static_cast<unsigned>(rows), kLanes, static_cast<size_t>(bytes), stream>>>(in, pv, qpos, kpos, probs, op,
-                                                                                       groups, length, scale);
+  const int mode = rows::choose_stage<T>(length);
+  const int64_t bytes = rows::staged_bytes<T>(mode, length);
+  const unsigned grid = static_cast<unsigned>(rows);
+  int status = LRK_OK;
+  if (mode == rows::kWeights) {
+    if ((status = allow_shared(probabilities_kernel<T, rows::kWeights>, bytes)) != LRK_OK) return status;
+    probabilities_kernel<T, rows::kWeights><<<grid, kLanes, bytes, stream>>>(in, pv, qpos, kpos, probs, op, groups,
+                                                                             length, scale);
+  } else if (mode == rows::kBits) {
+    if ((status = allow_shared(probabilities_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
+    probabilities_kernel<T, rows::kBits><<<grid, kLanes, bytes, stream>>>(in, pv, qpos, kpos, probs, op, groups,
+                                                                          length, scale);
   } else {
-    probabilities_kernel<T, false><<<static_cast<unsigned>(rows), kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op,
-                                                                                     groups, length, scale);
+    probabilities_kernel<T, rows::kStream><<<grid, kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op, groups, length,
+                                                                        scale);
   }
   return launch_status("lrk_temporal_probabilities");
 }

@@ -349,11 +349,14 @@ torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<tor
   std::vector<lrk_score_segment> segments(count);
   int64_t offset = 0;
   for (size_t i = 0; i < count; ++i) {
-    check_cuda(logits[i], logits[0]);
-    TORCH_CHECK(logits[i].dim() == 3 && logits[i].size(0) == window && logits[i].size(1) == groups &&
-                    logits[i].scalar_type() == dtype,
+    const auto &lg = logits[i];
+    TORCH_CHECK(lg.is_cuda() && lg.device() == logits[0].device(), "Expected CUDA logits on one device");
+    TORCH_CHECK(lg.dim() == 3 && lg.size(0) == window && lg.size(1) == groups && lg.scalar_type() == dtype,
                 "logits must be [window, groups, positions] of one dtype");
-    const int64_t length = logits[i].size(2);
+    const int64_t length = lg.size(2);
+    // Rows may be padded: [window, groups, length] with a row stride >= length.
+    TORCH_CHECK(lg.stride(2) == 1 && lg.stride(1) >= length && lg.stride(0) == groups * lg.stride(1),
+                "logits rows must be unit-stride with a common row stride");
     const auto &pv = projected_values[i];
     TORCH_CHECK(pv.is_cuda() && pv.device() == logits[0].device() && pv.scalar_type() == at::kFloat &&
                     pv.dim() == 2 && pv.size(0) == groups && pv.size(1) == length && pv.stride(1) == 1,
@@ -370,6 +373,7 @@ torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<tor
     s.first = first[i];
     s.last = last[i];
     s.scores = scores.data_ptr<float>() + offset;
+    s.logits_stride = lg.stride(1);
     offset += last[i] - first[i];
   }
   const size_t bytes = lrk_temporal_scores_workspace_bytes(static_cast<int64_t>(count), window, groups);
@@ -379,6 +383,24 @@ torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<tor
                                    margin.data_ptr<float>(), static_cast<float>(epsilon), workspace.data_ptr(), bytes,
                                    current_stream()));
   return scores;
+}
+
+// Per-layer projected values [groups, rows] (lrk_project_values): each row of
+// the packed layer against its own head's margin gradients.
+torch::Tensor project_values(torch::Tensor values, torch::Tensor gradients, torch::Tensor cumulative, int64_t groups) {
+  check_cuda(values, values);
+  check_cuda(gradients, values);
+  check_cuda(cumulative, values);
+  TORCH_CHECK(values.dim() == 2 && gradients.dim() == 2 && gradients.size(1) == values.size(1) &&
+                  gradients.scalar_type() == at::kFloat && cumulative.scalar_type() == at::kInt && groups > 0 &&
+                  gradients.size(0) == (cumulative.numel() - 1) * groups,
+              "Invalid projection inputs");
+  c10::cuda::CUDAGuard guard(values.device());
+  auto out = torch::empty({groups, values.size(0)}, gradients.options());
+  check_status(lrk_project_values(values.data_ptr(), dtype_code(values.scalar_type()), values.size(0), values.size(1),
+                                  gradients.data_ptr<float>(), cumulative.data_ptr<int32_t>(), cumulative.numel() - 1,
+                                  groups, out.data_ptr<float>(), current_stream()));
+  return out;
 }
 
 }  // namespace
@@ -395,4 +417,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("refine", &refine);
   module.def("topk_smallest", &topk_smallest);
   module.def("temporal_scores", &temporal_scores);
+  module.def("project_values", &project_values);
 }

@@ -1,0 +1,121 @@
+"""Layer-group sharding of one request's eviction selection across ranks.
+
+When one request's cache is split by layers over several GPUs (each rank
+scores and compacts its own contiguous group of layers), the selection of
+refine_arrays (selection.py:52-88) still needs the request-wide bottom-`count`
+of raw scores.  The only data that crosses ranks is a few histograms:
+
+  1. Each rank maps its scores to order-preserving 32-bit keys (the map
+     PyTorch's radix select uses; NaN last).
+  2. Radix rounds of 12, 12 and 8 bits: every rank histograms the digit of
+     the keys still in play, the histograms are all-gathered (NCCL over
+     NVLink on GPUs, gloo on CPU), summed, and the bin holding the k-th key is
+     fixed.  After the rounds every rank knows the exact k-th key and how many
+     keys lie below it request-wide.
+  3. Ties at the k-th key are taken in global flat-index order (layer-major,
+     the order compute_score_table concatenates heads in, scoring.py:218-287),
+     which is torch.topk's choice: ranks own increasing index ranges, so each
+     rank takes the first ties it holds after the ties of lower ranks (one
+     all-gather of per-rank tie counts).
+
+The chosen set equals the single-GPU set exactly.  Queue prefixes (the
+immediate eviction and each lazy prefix of controller.py:57-70) are again
+"k smallest" questions over the chosen set and use the same rounds.
+Per-segment refinement (Pool7 quotas and transplant) is layer-local, so each
+rank finishes it on its own segments.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+import torch.distributed as dist
+
+DIGITS = (12, 12, 8)
+
+
+def radix_keys(scores: torch.Tensor) -> torch.Tensor:
+    """Order-preserving uint32 image of float32 scores, held in int64."""
+    bits = scores.float().contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    negative = (bits & 0x80000000) != 0
+    keys = torch.where(negative, bits ^ 0xFFFFFFFF, bits ^ 0x80000000)
+    return torch.where(torch.isnan(scores), torch.full_like(keys, 0xFFFFFFFF), keys)
+
+
+def _all_gather_counts(local: torch.Tensor, group) -> torch.Tensor:
+    world = dist.get_world_size(group)
+    gathered = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(gathered, local, group=group)
+    return torch.stack(gathered)
+
+
+@dataclass
+class Threshold:
+    key: int          # the k-th smallest key request-wide
+    below: int        # keys strictly below it, request-wide
+    ties_taken: int   # keys equal to it that belong to the chosen k
+
+
+def global_kth_key(keys: torch.Tensor, k: int, group=None, digits: Sequence[int] = DIGITS) -> Threshold:
+    """Exact k-th smallest (1 <= k <= total) of the union of every rank's keys,
+    found with one histogram all-gather per radix round."""
+    if sum(digits) != 32:
+        raise ValueError("digit widths must cover 32 bits")
+    prefix, done, need, below = 0, 0, int(k), 0
+    in_play = keys
+    for width in digits:
+        shift = 32 - done - width
+        digit = (in_play >> shift) & ((1 << width) - 1)
+        local = torch.bincount(digit, minlength=1 << width).to(torch.int64)
+        total = _all_gather_counts(local, group).sum(0)
+        cumulative = total.cumsum(0)
+        bin_index = int(torch.searchsorted(cumulative, torch.tensor([need], device=cumulative.device)).item())
+        if bin_index >= total.numel():
+            raise ValueError(f"k={k} exceeds the number of keys")
+        skipped = int(cumulative[bin_index].item() - total[bin_index].item())
+        below += skipped
+        need -= skipped
+        prefix = (prefix << width) | bin_index
+        done += width
+        in_play = in_play[digit == bin_index]
+    return Threshold(key=prefix, below=below, ties_taken=need)
+
+
+def select_smallest(scores: torch.Tensor, k: int, group=None, eligible: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Boolean mask of this rank's share of the request-wide k smallest
+    scores, ties broken by global flat index (ranks in index order).
+    `eligible` restricts the candidates (e.g. to already-chosen rows)."""
+    keys = radix_keys(scores)
+    if eligible is not None:
+        keys = torch.where(eligible, keys, torch.full_like(keys, 1 << 32))  # beyond every real key
+    if k <= 0:
+        return torch.zeros_like(keys, dtype=torch.bool)
+    real = keys < (1 << 32)
+    threshold = global_kth_key(keys[real], k, group)
+    below = keys < threshold.key
+    ties = keys == threshold.key
+    tie_counts = _all_gather_counts(ties.sum().reshape(1).to(torch.int64), group).reshape(-1)
+    rank = dist.get_rank(group)
+    before = int(tie_counts[:rank].sum().item())
+    take = max(0, min(threshold.ties_taken - before, int(tie_counts[rank].item())))
+    chosen = below.clone()
+    if take:
+        tie_index = torch.nonzero(ties, as_tuple=False).reshape(-1)[:take]
+        chosen[tie_index] = True
+    return chosen
+
+
+def queue_order(scores: torch.Tensor, chosen: torch.Tensor) -> torch.Tensor:
+    """Local indices of this rank's chosen rows in queue order: ascending
+    (key, index), the order of torch.topk(sorted=True) for more than 32 picks."""
+    index = torch.nonzero(chosen, as_tuple=False).reshape(-1)
+    keys = radix_keys(scores[index])
+    order = torch.argsort(keys * (index.numel() + 1) + torch.arange(index.numel(), device=keys.device), stable=True)
+    return index[order]
+
+
+def prefix_split(scores: torch.Tensor, chosen: torch.Tensor, prefix: int, group=None) -> torch.Tensor:
+    """Mask of this rank's chosen rows that fall in the first `prefix` slots of
+    the request-wide queue (an immediate or lazy eviction batch)."""
+    return select_smallest(scores, prefix, group, eligible=chosen)

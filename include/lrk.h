@@ -97,6 +97,7 @@ typedef struct lrk_score_segment {
   int64_t first;                   /* candidate interval [first, last) */
   int64_t last;
   float *scores;                   /* [last - first] output */
+  int64_t logits_stride;           /* elements between consecutive (query, group) rows of logits (>= length) */
 } lrk_score_segment;
 
 /* Workspace bytes for lrk_temporal_scores. */
@@ -137,6 +138,19 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
 int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count, int logits_dtype,
                                const int64_t *query_positions, int64_t window, int64_t groups, float scale,
                                const float *margin, float epsilon, lrk_stream_t stream);
+
+/* Projected values of one layer for the audit: out[g, r] = sum_d
+ * gradients[head(r) * groups + g, d] * float(values[r, d]) for every row r of
+ * the packed layer, head(r) the KV head whose segment (cumulative, int32
+ * [heads + 1], device) holds r -- each head's rows against its own query
+ * heads' margin gradients, the product src/lazy_recall/scoring.py:175 forms
+ * per head (float32 accumulation; the order of the 128-term dot product is
+ * this kernel's own).  values [rows, dimension] of values_dtype; gradients
+ * [heads * groups, dimension] f32; out [groups, rows] f32.  Reads V once.
+ * No counterpart operator in the reference (new entry point). */
+int lrk_project_values(const void *values, int values_dtype, int64_t rows, int64_t dimension,
+                       const float *gradients, const int32_t *cumulative, int64_t heads, int64_t groups,
+                       float *out, lrk_stream_t stream);
 
 /* ------------------------------------------------- cache data movement */
 
@@ -246,6 +260,17 @@ size_t lrk_topk_workspace_bytes(int64_t n);
 int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
                       size_t workspace_bytes, float *values, int64_t *indices, lrk_stream_t stream);
 
+/* Gather rows of one table: dst row i = src row indices[i] (row_bytes each);
+ * out-of-range indices leave their destination row unwritten.  src may be
+ * device memory or pinned host memory mapped for the device
+ * (lrk_host_device_pointer): the GPU then reads the recalled rows over the host
+ * link itself, with no CPU gather and no staging copy.  Replaces, for recall,
+ * the CPU worker's gather into a shared-memory result slot and the slot's
+ * cudaMemcpyAsync (src/lazy_recall/recall/cpu_worker.py:161-166,
+ * recall/transport.py:221-229); no counterpart operator in the reference. */
+int lrk_gather_rows(const void *src, int64_t src_rows, int64_t row_bytes, const int64_t *indices, int64_t count,
+                    void *dst, lrk_stream_t stream);
+
 /* ------------------------------------------------------------------ host */
 
 /* Page-lock a host range for async DMA (cudaHostRegisterDefault).
@@ -253,6 +278,10 @@ int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
 int lrk_register_host(void *address, size_t bytes);
 /* Replaces _host.unregister_host (csrc/host.cpp:10-13). */
 int lrk_unregister_host(void *address);
+/* Device address of registered (page-locked, mapped) host memory; fails with
+ * LRK_ERR_INVALID for memory that is not registered.  No counterpart in the
+ * reference. */
+int lrk_host_device_pointer(void *host, void **device);
 
 #ifdef __cplusplus
 }

@@ -73,6 +73,10 @@ CASES = [
     ("f16", 30, 4, 1027, 5, 1020),
     ("f32", 17, 2, 513, 0, 513),
     ("bf16", 6, 1, 70001, 60000, 70000),
+    ("bf16", 3, 2, 120001, 100, 120000),
+    ("f32", 4, 4, 60001, 59000, 60001),
+    ("bf16", 8, 4, 18432, 0, 18432),
+    ("bf16", 4, 4, 18433, 18000, 18433),
 ]
 
 
@@ -143,7 +147,7 @@ def test_fused_through_c_abi(cuda):
     out = torch.empty(1900, device=cuda)
     segments = (abi.ScoreSegment * 1)()
     segments[0] = abi.ScoreSegment(logits.data_ptr(), pv.data_ptr(), 2000, kpos.data_ptr(), 2000, 100, 2000,
-                                   out.data_ptr())
+                                   out.data_ptr(), 2000)
     lib = abi.library()
     size = lib.lrk_temporal_scores_workspace_bytes(1, 50, 4)
     workspace = torch.empty(size, dtype=torch.uint8, device=cuda)
@@ -182,3 +186,40 @@ def test_audit_tables_agree(cuda):
     b = score_table_fused(cache, queries, qpos, grads, margin)
     assert a.segments == b.segments and a.cumulative_ends == b.cumulative_ends
     assert_scores_close(b.scores.cpu().numpy(), a.scores.cpu().numpy())
+
+
+def test_fused_padded_logits_rows(C, cuda):
+    """Logits rows with a stride larger than the row (a GEMM over a padded key
+    block) score exactly like contiguous rows."""
+    import torch
+
+    g = torch.Generator().manual_seed(12)
+    logits, pv, kpos, qpos = make_head(g, cuda, 40, 4, 3001, torch.bfloat16)
+    padded = torch.zeros(40, 4, 3008, dtype=torch.bfloat16, device=cuda)
+    padded[:, :, :3001] = logits
+    margin = torch.tensor([0.9], device=cuda)
+    a = C.temporal_scores([logits], [pv], [kpos], [10], [2990], qpos, margin, 0.125, 1e-6)
+    b = C.temporal_scores([padded[:, :, :3001]], [pv], [kpos], [10], [2990], qpos, margin, 0.125, 1e-6)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("groups,dtype_name", [(4, "bf16"), (8, "bf16"), (1, "f32"), (2, "f16")])
+def test_project_values(C, cuda, groups, dtype_name):
+    """Per-head g V^T over a packed layer against a float64 reference."""
+    import torch
+
+    dtype = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[dtype_name]
+    g = torch.Generator().manual_seed(groups)
+    lengths = [300, 0, 1025, 77, 4000, 12, 999, 1]
+    heads, dim = len(lengths), 128
+    values = torch.randn(sum(lengths), dim, generator=g).to(dtype).to(cuda)
+    grads = torch.randn(heads * groups, dim, generator=g).to(cuda)
+    cumulative = torch.tensor(np.concatenate(([0], np.cumsum(lengths))), dtype=torch.int32, device=cuda)
+    out = C.project_values(values, grads, cumulative, groups)
+    v64, g64 = values.double().cpu(), grads.double().cpu()
+    start = 0
+    for h, n in enumerate(lengths):
+        expect = g64[h * groups:(h + 1) * groups] @ v64[start:start + n].T
+        np.testing.assert_allclose(out[:, start:start + n].double().cpu().numpy(), expect.numpy(), rtol=1e-5,
+                                   atol=1e-5)
+        start += n

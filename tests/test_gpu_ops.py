@@ -334,7 +334,8 @@ def test_pool(C, ref, cuda, width):
 
 PROB_CASES = [
     ("bf16", 6, 4, 1), ("bf16", 3, 4, 255), ("bf16", 2, 4, 256), ("bf16", 5, 4, 4099), ("f16", 4, 2, 8192),
-    ("f32", 3, 8, 1030), ("bf16", 4, 4, 35026), ("bf16", 2, 8, 60001),
+    ("f32", 3, 8, 1030), ("bf16", 4, 4, 35026), ("bf16", 2, 8, 60001), ("bf16", 1, 2, 120001), ("f32", 1, 2, 60001),
+    ("bf16", 3, 4, 18432), ("bf16", 3, 4, 18433), ("bf16", 1, 2, 112624), ("bf16", 1, 2, 112625),
 ]
 
 
@@ -410,3 +411,40 @@ def test_head_scores_end_to_end(C, cuda):
     expect = O.temporal_head_scores_gpu_path(q.numpy(), qpos.numpy(), O.bf16_to_f32(bits(k)), kpos.numpy(),
                                              O.bf16_to_f32(bits(v)), 10, 690, grad.numpy(), 0.9, 1e-6, 6)
     close(result.cpu().numpy(), expect, rtol=1e-4, atol=1e-6)
+
+
+# ---------------------------------------------------------------- recall
+
+
+def test_gather_rows_from_registered_host_pool(cuda):
+    """Recall rows fetched by the GPU straight from a registered host pool
+    (the archive layout [rows, 2, D] bf16, recall/cpu_worker.py:21-22)."""
+    import mmap
+
+    torch = torch_mod()
+    from code_for_iclr27_b200 import abi, host_operators
+
+    H = host_operators()
+    rows, d = 20000, 128
+    row_bytes = 2 * d * 2
+    buffer = mmap.mmap(-1, rows * row_bytes)  # page-aligned, like the transport's SharedMemory slots
+    pool = np.frombuffer(buffer, dtype=np.uint16).reshape(rows, 2, d)
+    pool[:] = np.random.default_rng(0).integers(0, 65535, size=pool.shape, dtype=np.uint16)
+    address = pool.__array_interface__["data"][0]
+    with pytest.raises(RuntimeError):
+        H.device_pointer(address)  # not registered yet: refused before any launch
+    H.register_host(address, rows * row_bytes)
+    try:
+        device = H.device_pointer(address)
+        chosen = np.random.default_rng(1).choice(rows, 256, replace=False)
+        indices = torch.from_numpy(chosen).to(cuda)
+        out = torch.empty(256, 2, d, dtype=torch.bfloat16, device=cuda)
+        stream = torch.cuda.current_stream().cuda_stream
+        abi.check(abi.library().lrk_gather_rows(device, rows, row_bytes, indices.data_ptr(), 256, out.data_ptr(),
+                                                stream))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(bits(out), pool[chosen])
+    finally:
+        H.unregister_host(address)
+        del pool
+        buffer.close()

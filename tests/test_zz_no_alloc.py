@@ -48,7 +48,7 @@ def make_call(seed, heads, window, groups, lengths, device):
         first, last = length // 4, length - 3
         out = torch.full((last - first,), -1.0, device=device)
         segments[h] = abi.ScoreSegment(logits.data_ptr(), pv.data_ptr(), length, kpos.data_ptr(), length, first, last,
-                                       out.data_ptr())
+                                       out.data_ptr(), length)
         tensors += [logits, pv, kpos]
         outputs.append(out)
     qpos = torch.arange(10 ** 6, 10 ** 6 + window, dtype=torch.int64, device=device)
