@@ -5,6 +5,10 @@
 // probability of a [window, groups, length] chunk, temporal_risk reads the
 // candidate columns back.  Here the probabilities never reach HBM:
 //
+//   visibility     one CTA per segment: when the segment's key positions
+//   kernel         are non-decreasing, each query's visible keys are a
+//                  prefix; its length replaces the per-key position compare
+//                  in the stats kernel (-1: compare positions).
 //   stats kernel   one CTA per (segment, query, group) row: the exact row
 //                  statistics of rows.cuh (max, denominator, value projection,
 //                  in the reference's operation order), written to a small
@@ -45,11 +49,47 @@ struct ScoreTableParam {
   int count;
 };
 
+constexpr int kVisibilityThreads = 1024;
+
+// One CTA per segment.  If key_positions[0 .. length) is non-decreasing (and
+// free of NaN), visible[(segment * window) + q] = the number of keys with
+// position <= the query's position (they are a prefix); otherwise -1.
+__global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTableParam table,
+                                                                        const int64_t *__restrict__ qpos, int window,
+                                                                        int32_t *__restrict__ visible,
+                                                                        int64_t segment_base) {
+  const lrk_score_segment &seg = table.segment[blockIdx.x];
+  const float *kpos = seg.key_positions;
+  const int64_t n = seg.length;
+  int ordered = 1;
+  for (int64_t p = threadIdx.x; p < n; p += kVisibilityThreads) {
+    const float here = __ldg(kpos + p);
+    if (!(here == here) || (p + 1 < n && !(here <= __ldg(kpos + p + 1)))) ordered = 0;
+  }
+  ordered = __syncthreads_and(ordered);
+  int32_t *out = visible + (segment_base + blockIdx.x) * window;
+  for (int q = threadIdx.x; q < window; q += kVisibilityThreads) {
+    int64_t count = -1;
+    if (ordered) {
+      const float position = static_cast<float>(qpos[q]);
+      int64_t lo = 0, hi = n;  // first key with position > the query's
+      while (lo < hi) {
+        const int64_t mid = (lo + hi) / 2;
+        if (__ldg(kpos + mid) <= position) lo = mid + 1; else hi = mid;
+      }
+      count = lo;
+    }
+    out[q] = static_cast<int32_t>(count);
+  }
+}
+
 // One CTA per (segment, query, group) row: its exact statistics (rows.cuh).
 // stats[(segment * window + query) * groups + group] = (max, denominator, projection).
+// visible may be null (every row compares key positions).
 template <typename T, int MODE>
 __global__ void __launch_bounds__(rows::kLanes) stats_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
                                                              int groups, float scale, float3 *__restrict__ stats,
+                                                             const int32_t *__restrict__ visible,
                                                              int64_t segment_base, int64_t rows_per_segment) {
   extern __shared__ __align__(16) unsigned char stage[];
   __shared__ float scratch[rows::kLanes];
@@ -57,10 +97,13 @@ __global__ void __launch_bounds__(rows::kLanes) stats_kernel(ScoreTableParam tab
   const int si = blockIdx.y;
   const lrk_score_segment &seg = table.segment[si];
   const int group = static_cast<int>(row % groups);
+  const int64_t query = row / groups;
+  const int64_t window = rows_per_segment / groups;
+  const rows::Visibility sees{seg.key_positions, static_cast<float>(qpos[query]),
+                              visible != nullptr ? visible[(segment_base + si) * window + query] : -1};
   const rows::RowResult r = rows::row_statistics<T, MODE>(
-      static_cast<const T *>(seg.logits) + row * seg.logits_stride, seg.length, seg.key_positions,
-      static_cast<float>(qpos[row / groups]), seg.projected_values + group * seg.projected_stride, scale, nullptr,
-      stage, scratch);
+      static_cast<const T *>(seg.logits) + row * seg.logits_stride, seg.length, sees,
+      seg.projected_values + group * seg.projected_stride, scale, nullptr, stage, scratch);
   if (threadIdx.x == 0)
     stats[(segment_base + si) * rows_per_segment + row] = make_float3(r.maximum, r.denominator, r.projection);
 }
@@ -74,7 +117,12 @@ int allow_shared(K kernel, int64_t bytes) {
 
 template <typename T>
 int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int window, int groups, float scale,
-                 float3 *stats, int64_t s0, int64_t max_length, cudaStream_t stream) {
+                 float3 *stats, int32_t *visible, int64_t s0, int64_t max_length, cudaStream_t stream) {
+  if (visible != nullptr) {
+    visibility_kernel<<<n, kVisibilityThreads, 0, stream>>>(table, qpos, window, visible, s0);
+    const int status = launch_status("lrk_temporal_scores visibility");
+    if (status != LRK_OK) return status;
+  }
   const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
   const dim3 grid(static_cast<unsigned>(rows_per_segment), n);
   const int mode = rows::choose_stage<T>(max_length);
@@ -82,15 +130,15 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
   int status = LRK_OK;
   if (mode == rows::kWeights) {
     if ((status = allow_shared(stats_kernel<T, rows::kWeights>, bytes)) != LRK_OK) return status;
-    stats_kernel<T, rows::kWeights><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, s0,
-                                                                           rows_per_segment);
+    stats_kernel<T, rows::kWeights><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
+                                                                           visible, s0, rows_per_segment);
   } else if (mode == rows::kBits) {
     if ((status = allow_shared(stats_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
-    stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, s0,
-                                                                        rows_per_segment);
+    stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, visible,
+                                                                        s0, rows_per_segment);
   } else {
-    stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, s0,
-                                                                      rows_per_segment);
+    stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, visible,
+                                                                      s0, rows_per_segment);
   }
   return launch_status("lrk_temporal_scores statistics");
 }
@@ -186,7 +234,8 @@ __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam tabl
 
 template <typename T>
 int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window, int groups,
-                  float scale, const float *margin, float epsilon, float3 *stats, cudaStream_t stream) {
+                  float scale, const float *margin, float epsilon, float3 *stats, int32_t *visible,
+                  cudaStream_t stream) {
   for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
     const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
     ScoreTableParam table;
@@ -198,7 +247,7 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
     }
     int64_t max_length = 0;
     for (int i = 0; i < n; ++i) max_length = std::max<int64_t>(max_length, table.segment[i].length);
-    int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, s0, max_length, stream);
+    int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, stream);
     if (status != LRK_OK) return status;
     const size_t shared = static_cast<size_t>(window) * groups * sizeof(float4);
     const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, 32))), n);
@@ -279,13 +328,14 @@ int check_score_call(const lrk_score_segment *segments, int64_t count, int64_t w
 
 int dispatch_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype, const int64_t *qpos,
                     int64_t window, int64_t groups, float scale, const float *margin, float epsilon, float3 *stats,
-                    lrk_stream_t stream) {
+                    int32_t *visible, lrk_stream_t stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int w = static_cast<int>(window), g = static_cast<int>(groups);
   switch (logits_dtype) {
-    case LRK_BF16: return launch_scores<__nv_bfloat16>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
-    case LRK_F16: return launch_scores<__half>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
-    case LRK_F32: return launch_scores<float>(segments, count, qpos, w, g, scale, margin, epsilon, stats, s);
+    case LRK_BF16:
+      return launch_scores<__nv_bfloat16>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, s);
+    case LRK_F16: return launch_scores<__half>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, s);
+    case LRK_F32: return launch_scores<float>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, s);
     default: return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
   }
 }
@@ -295,9 +345,12 @@ int dispatch_scores(const lrk_score_segment *segments, int64_t count, int logits
 
 using namespace lrk;
 
+// Workspace: the row statistics (float3 per row), then the visible-prefix
+// lengths (int32 per segment and query).
 extern "C" size_t lrk_temporal_scores_workspace_bytes(int64_t segments, int64_t window, int64_t groups) {
   if (segments < 0 || window < 0 || groups < 0) return 0;
-  return static_cast<size_t>(segments) * window * groups * sizeof(float3) + 256;
+  return static_cast<size_t>(segments) * window * groups * sizeof(float3) +
+         static_cast<size_t>(segments) * window * sizeof(int32_t) + 256;
 }
 
 extern "C" int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype,
@@ -310,8 +363,9 @@ extern "C" int lrk_temporal_scores(const lrk_score_segment *segments, int64_t co
   const size_t need = lrk_temporal_scores_workspace_bytes(count, window, groups);
   if (workspace == nullptr || workspace_bytes < need) return fail(LRK_ERR_WORKSPACE, "score workspace too small");
   float3 *stats = reinterpret_cast<float3 *>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t{15});
+  int32_t *visible = reinterpret_cast<int32_t *>(stats + count * window * groups);
   return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
-                         stream);
+                         visible, stream);
 }
 
 extern "C" int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count, int logits_dtype,
@@ -330,6 +384,7 @@ extern "C" int lrk_temporal_scores_static(const lrk_score_segment *segments, int
   float3 *stats = nullptr;
   status = static_scratch(&stats);
   if (status != LRK_OK) return status;
+  // No visible-prefix table here: every row compares key positions.
   return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
-                         stream);
+                         nullptr, stream);
 }

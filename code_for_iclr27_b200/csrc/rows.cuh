@@ -106,6 +106,42 @@ __device__ __forceinline__ float tree_sum(float partial, float *tree) {
   return result;
 }
 
+// Correctly rounded a / b for a row's probabilities, b = the row's
+// denominator (>= 1 when finite), a = an exp weight in [0, 1].  With the
+// correctly rounded reciprocal y = RN(1/b), q0 = RN(a y) is within 2 ulp of
+// a/b; one residual step q1 = RN(q0 + y RN(a - b q0)) makes it faithful (the
+// residual is exact in one FMA), and a second step is Markstein's theorem: if y
+// is within half an ulp of 1/b and q1 within one ulp of a/b, RN(q1 + y r1) is
+// RN(a/b) (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990; Muller et al.,
+// Handbook of Floating-Point Arithmetic, 2nd ed., 2018, section 4.7).  The
+// theorem needs every residual and quotient in the normal range, which
+// 1 <= b <= 2^32 and 2^-60 <= a <= 2^32 guarantee; other operands (0,
+// subnormal, NaN, inf) take the IEEE division itself.  Correct rounding is
+// unique, so the result equals __fdiv_rn bit for bit; lrk_check_division
+// tests that on the GPU.
+struct Divider {
+  float b, y;
+  bool fast;
+};
+
+__device__ __forceinline__ Divider make_divider(float denominator) {
+  Divider d;
+  d.b = denominator;
+  d.y = __frcp_rn(denominator);
+  d.fast = denominator >= 1.0f && denominator <= 4294967296.0f;  // false for NaN
+  return d;
+}
+
+__device__ __forceinline__ float divide(const Divider &d, float a) {
+  if (d.fast && a >= 8.673617379884035e-19f && a <= 4294967296.0f) {  // 2^-60, 2^32
+    float q = __fmul_rn(a, d.y);
+    q = __fmaf_rn(__fmaf_rn(-q, d.b, a), d.y, q);
+    return __fmaf_rn(__fmaf_rn(-q, d.b, a), d.y, q);
+  }
+  return __fdiv_rn(a, d.b);
+}
+
 struct RowResult {
   float maximum, denominator, projection;
 };
@@ -126,7 +162,10 @@ __host__ __device__ constexpr int64_t staged_bytes(int mode, int64_t length) {
 }
 
 // Rows up to this many fp32 weights (72 KB, 3 CTAs per SM) keep w.
-constexpr int64_t kWeightStageMax = 18 * 1024;
+#ifndef LRK_WEIGHT_STAGE_MAX
+#define LRK_WEIGHT_STAGE_MAX (18 * 1024)
+#endif
+constexpr int64_t kWeightStageMax = LRK_WEIGHT_STAGE_MAX;
 
 template <typename T>
 inline int choose_stage(int64_t length) {
@@ -135,16 +174,35 @@ inline int choose_stage(int64_t length) {
   return kStream;
 }
 
+// Which keys a row sees.  The reference masks key p when key_positions[p] >
+// query_position.  When the caller knows the visible keys form a prefix (key
+// positions non-decreasing, as in an append-only cache), `visible` is that
+// prefix's length and the mask is an index compare; visible < 0 compares
+// positions element by element.
+struct Visibility {
+  const float *key_positions;
+  float query_position;
+  int64_t visible;
+  __device__ __forceinline__ bool operator()(int64_t p) const {
+    return visible >= 0 ? p < visible : __ldg(key_positions + p) <= query_position;
+  }
+  // Every key of [p, p + n) is visible (index test only).
+  __device__ __forceinline__ bool all(int64_t p, int n) const { return visible >= 0 && p + n <= visible; }
+};
+
 // Statistics of one row (all 256 threads call).  probabilities_out, when not
 // null, receives every probability (the drop-in operator's output).  `stage`
-// is dynamic shared memory of staged_bytes<T>(MODE, length) bytes.
+// is dynamic shared memory of staged_bytes<T>(MODE, length) bytes.  Global
+// loads are issued in batches ahead of their use (kBatch vectors or elements
+// per thread), which hides their latency at 3 CTAs per SM.
 template <typename T, int MODE>
-__device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const float *__restrict__ key_positions,
-                                    float query_position, const float *__restrict__ projected_values, float scale,
+__device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const Visibility sees,
+                                    const float *__restrict__ projected_values, float scale,
                                     float *__restrict__ probabilities_out, unsigned char *stage, float *scratch) {
   using D = Dtype<T>;
   using Bits = typename D::Bits;
   constexpr int V = D::kPerVec;
+  constexpr int kBatch = 8;
   const Bits *in = reinterpret_cast<const Bits *>(row);
   // First 16-byte boundary of the row, and the stage offsets that align it.
   const int64_t lead = lmin(length, static_cast<int64_t>(((16 - (reinterpret_cast<uintptr_t>(row) & 15)) & 15) /
@@ -152,9 +210,7 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
   Bits *x_bits = reinterpret_cast<Bits *>(stage) + (V - lead % V) % V;
   float *x_float = reinterpret_cast<float *>(stage) + (4 - lead % 4) % 4;
   const Bits neg_inf = minus_infinity<T>();
-  auto value_bits = [&](int64_t p, Bits raw) -> Bits {
-    return __ldg(key_positions + p) <= query_position ? D::round(D::to_float(raw), scale) : neg_inf;
-  };
+  auto value_bits = [&](int64_t p, Bits raw) -> Bits { return sees(p) ? D::round(D::to_float(raw), scale) : neg_inf; };
 
   // Pass A: scale, round, mask; row max; stage the row.
   float local_max = -INFINITY;
@@ -169,15 +225,19 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
     for (int64_t p = threadIdx.x; p < lead; p += kLanes) put(p, value_bits(p, __ldg(in + p)));
     const int64_t vectors = (length - lead) / V;
     const uint4 *body = reinterpret_cast<const uint4 *>(in + lead);
-#pragma unroll 4
-    for (int64_t v = threadIdx.x; v < vectors; v += kLanes) {
-      uint4 raw = __ldcs(body + v);
+    auto vector = [&](int64_t v, uint4 raw) {
       Bits *lanes = reinterpret_cast<Bits *>(&raw);
       const int64_t p0 = lead + v * V;
       float xs[V];
+      if (sees.all(p0, V)) {
+#pragma unroll
+        for (int j = 0; j < V; ++j) lanes[j] = D::round(D::to_float(lanes[j]), scale);
+      } else {
+#pragma unroll
+        for (int j = 0; j < V; ++j) lanes[j] = value_bits(p0 + j, lanes[j]);
+      }
 #pragma unroll
       for (int j = 0; j < V; ++j) {
-        lanes[j] = value_bits(p0 + j, lanes[j]);
         xs[j] = D::to_float(lanes[j]);
         local_max = fmaxf(local_max, xs[j]);
       }
@@ -188,7 +248,16 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
         for (int j = 0; j < V; j += 4)
           *reinterpret_cast<float4 *>(x_float + p0 + j) = make_float4(xs[j], xs[j + 1], xs[j + 2], xs[j + 3]);
       }
+    };
+    int64_t v = threadIdx.x;
+    for (; v + (kBatch - 1) * kLanes < vectors; v += kBatch * kLanes) {
+      uint4 raw[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) raw[u] = __ldcs(body + v + u * kLanes);
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) vector(v + u * kLanes, raw[u]);
     }
+    for (; v < vectors; v += kLanes) vector(v, __ldcs(body + v));
     for (int64_t p = lead + vectors * V + threadIdx.x; p < length; p += kLanes) put(p, value_bits(p, __ldg(in + p)));
   }
   const float maximum = block_max(local_max, scratch);
@@ -210,14 +279,23 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
   const float denominator = tree_sum(sum, scratch);
 
   // Pass C: probabilities (optionally stored) and the value projection.
+  const Divider divider = make_divider(denominator);
   float projection = 0.0f;
-#pragma unroll 8
-  for (int64_t p = threadIdx.x; p < length; p += kLanes) {
+  auto element = [&](int64_t p, float value) {
     const float w = MODE == kWeights ? x_float[p] : expf(__fsub_rn(x_at(p), maximum));
-    const float probability = __fdiv_rn(w, denominator);
+    const float probability = divide(divider, w);
     if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
-    projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(projected_values + p)));
+    projection = __fadd_rn(projection, __fmul_rn(probability, value));
+  };
+  int64_t p = threadIdx.x;
+  for (; p + (kBatch - 1) * kLanes < length; p += kBatch * kLanes) {
+    float values[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) values[u] = __ldg(projected_values + p + u * kLanes);
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) element(p + u * kLanes, values[u]);
   }
+  for (; p < length; p += kLanes) element(p, __ldg(projected_values + p));
   projection = tree_sum(projection, scratch);
   return {maximum, denominator, projection};
 }

@@ -38,7 +38,7 @@ __global__ void __launch_bounds__(kLanes) probabilities_kernel(
   const int group = static_cast<int>(row % groups);
   const int64_t query = row / groups;
   const rows::RowResult result = rows::row_statistics<T, MODE>(
-      logits + row * length, length, key_positions, static_cast<float>(query_positions[query]),
+      logits + row * length, length, rows::Visibility{key_positions, static_cast<float>(query_positions[query]), -1},
       projected_values + static_cast<int64_t>(group) * length, scale, probabilities + row * length, stage, scratch);
   if (threadIdx.x == 0) output_projection[row] = result.projection;
 }
@@ -223,10 +223,46 @@ int launch_probabilities(const void *logits, const float *pv, const int64_t *qpo
   return launch_status("lrk_temporal_probabilities");
 }
 
+// rows::divide against __fdiv_rn over count pseudo-random (a, b) pairs: a any
+// float in [0, 1], b in [1, 2^32) with a random significand, plus every 1024th
+// a in [1/4, 1) and every 4096th b with a significand of trailing ones (the
+// hard cases of reciprocal rounding).  Counts the pairs whose bits differ.
+__global__ void divider_check_kernel(uint64_t count, uint64_t seed, unsigned long long *mismatches) {
+  unsigned long long local = 0;
+  for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    uint64_t x = (i + 1) * 0x9e3779b97f4a7c15ull ^ seed;
+    x ^= x >> 31;
+    x *= 0xbf58476d1ce4e5b9ull;
+    x ^= x >> 29;
+    x *= 0x94d049bb133111ebull;
+    x ^= x >> 32;
+    const uint32_t u = static_cast<uint32_t>(x), v = static_cast<uint32_t>(x >> 32);
+    float a = __uint_as_float(u % 0x3f800001u);
+    float b = __uint_as_float(0x3f800000u + (v % (32u << 23)));
+    if ((i & 1023) == 0) a = __uint_as_float((u & 0x007fffffu) | ((v & 1u) ? 0x3f000000u : 0x3e800000u));
+    if ((i & 4095) == 1) b = __uint_as_float((__float_as_uint(b) & 0xff800000u) | 0x007ff000u | (v & 0xfffu));
+    const rows::Divider divider = rows::make_divider(b);
+    if (__float_as_uint(rows::divide(divider, a)) != __float_as_uint(__fdiv_rn(a, b))) ++local;
+  }
+  if (local) atomicAdd(mismatches, local);
+}
+
 }  // namespace
 }  // namespace lrk
 
 using namespace lrk;
+
+// Test hook: number of (a, b) pairs out of `count` on which the row
+// statistics' division differs from IEEE division (expected 0).
+extern "C" int lrk_check_division(uint64_t count, uint64_t seed, unsigned long long *mismatches_device,
+                                  lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(mismatches_device != nullptr, "null pointer");
+  divider_check_kernel<<<sm_count() * 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(count, seed,
+                                                                                         mismatches_device);
+  return launch_status("lrk_check_division");
+}
 
 extern "C" int lrk_temporal_probabilities(const void *logits, int logits_dtype, const float *projected_values,
                                           const int64_t *query_positions, const float *key_positions,

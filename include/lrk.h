@@ -152,6 +152,13 @@ int lrk_project_values(const void *values, int values_dtype, int64_t rows, int64
                        const float *gradients, const int32_t *cumulative, int64_t heads, int64_t groups,
                        float *out, lrk_stream_t stream);
 
+/* Test hook: counts, into *mismatches_device (device, zeroed by the caller),
+ * the pairs among `count` pseudo-random (a, b) -- a in [0, 1], b in [1, 2^20],
+ * the row-statistics domain -- on which the scoring kernels' division differs
+ * in any bit from IEEE round-to-nearest division.  Expected 0.
+ * No counterpart in the reference. */
+int lrk_check_division(uint64_t count, uint64_t seed, unsigned long long *mismatches_device, lrk_stream_t stream);
+
 /* ------------------------------------------------- cache data movement */
 
 /* Append `added` rows to each head segment of a packed layer.

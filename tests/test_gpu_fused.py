@@ -101,6 +101,48 @@ def test_fused_matches_dropin_and_oracle(C, cuda, dtype_name, window, groups, le
         assert_scores_close(fused.cpu().numpy(), expect)
 
 
+KEY_LAYOUTS = ["sorted_ties", "shuffled", "sorted_nan", "sorted_inf", "descending"]
+
+
+@pytest.mark.parametrize("length", [3001, 20011])
+@pytest.mark.parametrize("layout", KEY_LAYOUTS)
+def test_fused_key_position_layouts(C, cuda, layout, length):
+    """Masks from every kind of key-position vector: non-decreasing ones take
+    the visible-prefix path, the others compare positions per key.  Queries sit
+    inside the key range, so each row sees a different prefix (some none).
+    The fused scores must equal the drop-in composition bit for bit."""
+    import torch
+
+    g = torch.Generator().manual_seed(KEY_LAYOUTS.index(layout) * 7919 + length)
+    window, groups, first, last = 37, 4, 7, length - 2
+    logits, pv, _, _ = make_head(g, cuda, window, groups, length, torch.bfloat16)
+    if layout == "sorted_ties":
+        kpos = torch.sort(torch.randint(0, length // 2, (length,), generator=g)).values.float()
+    elif layout == "shuffled":
+        kpos = torch.randperm(length, generator=g).float()
+    elif layout == "sorted_nan":
+        kpos = torch.arange(length, dtype=torch.float32)
+        kpos[length // 3] = float("nan")
+    elif layout == "sorted_inf":
+        kpos = torch.arange(length, dtype=torch.float32)
+        kpos[-5:] = float("inf")
+    else:
+        kpos = torch.arange(length, 0, -1, dtype=torch.float32)
+    kpos = kpos.to(cuda)
+    top = int(torch.nan_to_num(kpos, nan=0.0, posinf=0.0).max().item())
+    qpos = torch.randint(top // 3, top + 2, (window,), generator=g, dtype=torch.int64).to(cuda)
+    qpos[0] = -1  # a query that sees no key: the head's scores are NaN
+    margin = torch.tensor([0.9], device=cuda)
+    scale = 1.0 / math.sqrt(128)
+    for queries in (qpos, qpos[1:].contiguous()):
+        n = queries.shape[0]
+        lg = logits[-n:].contiguous()
+        fused = C.temporal_scores([lg], [pv], [kpos], [first], [last], queries, margin, scale, 1e-6).cpu()
+        expected = dropin_scores(C, lg, pv, kpos, queries, margin, first, last, scale).cpu()
+        assert torch.equal(torch.isnan(fused), torch.isnan(expected))
+        assert torch.equal(torch.nan_to_num(fused), torch.nan_to_num(expected))
+
+
 def test_fused_many_segments_strided_and_masked(C, cuda):
     """100 segments (three launches), projected values as strided views of one
     layer-wide matrix, some queries with every key masked (NaN scores)."""

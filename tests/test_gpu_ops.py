@@ -448,3 +448,17 @@ def test_gather_rows_from_registered_host_pool(cuda):
         H.unregister_host(address)
         del pool
         buffer.close()
+
+
+def test_row_division_is_ieee_division(cuda):
+    """The scoring kernels divide each exp weight by the row denominator with a
+    Markstein quotient correction; it must equal IEEE division bit for bit."""
+    torch = torch_mod()
+    from code_for_iclr27_b200 import abi
+
+    lib = abi.library()
+    counter = torch.zeros(1, dtype=torch.int64, device=cuda)
+    for seed in (1, 2):
+        abi.check(lib.lrk_check_division(1 << 28, seed, counter.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert int(counter.item()) == 0
