@@ -87,7 +87,7 @@ __global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTab
 // stats[(segment * window + query) * groups + group] = (max, denominator, projection).
 // visible may be null (every row compares key positions).
 template <typename T, int MODE>
-__global__ void __launch_bounds__(rows::kLanes) stats_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
+__global__ void __launch_bounds__(rows::kLanes, 3) stats_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
                                                              int groups, float scale, float3 *__restrict__ stats,
                                                              const int32_t *__restrict__ visible,
                                                              int64_t segment_base, int64_t rows_per_segment) {
@@ -125,7 +125,11 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
   }
   const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
   const dim3 grid(static_cast<unsigned>(rows_per_segment), n);
-  const int mode = rows::choose_stage<T>(max_length);
+  bool aligned_rows = true;  // every row of every segment on a 16-byte boundary
+  for (int i = 0; i < n; ++i)
+    aligned_rows = aligned_rows && aligned(table.segment[i].logits, 16) &&
+              (table.segment[i].logits_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  const int mode = rows::choose_stage<T>(max_length, aligned_rows);
   const int64_t bytes = rows::staged_bytes<T>(mode, max_length);
   int status = LRK_OK;
   if (mode == rows::kWeights) {
@@ -136,6 +140,12 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
     if ((status = allow_shared(stats_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
     stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, visible,
                                                                         s0, rows_per_segment);
+  } else if (mode == rows::kPacked) {
+    if constexpr (sizeof(T) == 2) {
+      if ((status = allow_shared(stats_kernel<T, rows::kPacked>, bytes)) != LRK_OK) return status;
+      stats_kernel<T, rows::kPacked><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
+                                                                            visible, s0, rows_per_segment);
+    }
   } else {
     stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, visible,
                                                                       s0, rows_per_segment);

@@ -152,13 +152,16 @@ enum Stage : int {
   kStream = 0,   // nothing staged: x is recomputed from the logits in each pass
   kBits = 1,     // x staged in the logits dtype (exact), expf recomputed in pass C
   kWeights = 2,  // x staged as fp32 and overwritten by w = expf(x - max) in pass B
+  kPacked = 3,   // kBits for 16-bit logits in 16-byte aligned rows, lane-major
+                 // (row_statistics_packed): 8 elements per lane per 16-byte
+                 // chunk, pairs of elements in float2 arithmetic
 };
 
 template <typename T>
 __host__ __device__ constexpr int64_t staged_bytes(int mode, int64_t length) {
-  return mode == kWeights ? (length + 8) * 4
-         : mode == kBits  ? (length + 16) * static_cast<int64_t>(sizeof(typename Dtype<T>::Bits))
-                          : 0;
+  return mode == kWeights                    ? (length + 8) * 4
+         : mode == kBits || mode == kPacked ? (length + 16) * static_cast<int64_t>(sizeof(typename Dtype<T>::Bits))
+                                             : 0;
 }
 
 // Rows up to this many fp32 weights (72 KB, 3 CTAs per SM) keep w.
@@ -167,10 +170,12 @@ __host__ __device__ constexpr int64_t staged_bytes(int mode, int64_t length) {
 #endif
 constexpr int64_t kWeightStageMax = LRK_WEIGHT_STAGE_MAX;
 
+// aligned: every row starts on a 16-byte boundary.
 template <typename T>
-inline int choose_stage(int64_t length) {
+inline int choose_stage(int64_t length, bool aligned) {
+  constexpr bool kSixteenBit = sizeof(typename Dtype<T>::Bits) == 2;
   if (length <= kWeightStageMax) return kWeights;
-  if (staged_bytes<T>(kBits, length) <= kStageBytes) return kBits;
+  if (staged_bytes<T>(kBits, length) <= kStageBytes) return kSixteenBit && aligned ? kPacked : kBits;
   return kStream;
 }
 
@@ -190,6 +195,12 @@ struct Visibility {
   __device__ __forceinline__ bool all(int64_t p, int n) const { return visible >= 0 && p + n <= visible; }
 };
 
+template <typename T>
+__device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t length, const Visibility sees,
+                                           const float *__restrict__ projected_values, float scale,
+                                           float *__restrict__ probabilities_out, unsigned char *stage,
+                                           float *scratch);
+
 // Statistics of one row (all 256 threads call).  probabilities_out, when not
 // null, receives every probability (the drop-in operator's output).  `stage`
 // is dynamic shared memory of staged_bytes<T>(MODE, length) bytes.  Global
@@ -199,6 +210,9 @@ template <typename T, int MODE>
 __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const Visibility sees,
                                     const float *__restrict__ projected_values, float scale,
                                     float *__restrict__ probabilities_out, unsigned char *stage, float *scratch) {
+  if constexpr (MODE == kPacked) {
+    return row_statistics_packed<T>(row, length, sees, projected_values, scale, probabilities_out, stage, scratch);
+  }
   using D = Dtype<T>;
   using Bits = typename D::Bits;
   constexpr int V = D::kPerVec;
@@ -296,6 +310,201 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
     for (int u = 0; u < kBatch; ++u) element(p + u * kLanes, values[u]);
   }
   for (; p < length; p += kLanes) element(p, __ldg(projected_values + p));
+  projection = tree_sum(projection, scratch);
+  return {maximum, denominator, projection};
+}
+
+// Pairs of 16-bit logits in one 32-bit word (low half = the earlier element).
+template <typename T> struct Packed;
+template <> struct Packed<__nv_bfloat16> {
+  static constexpr uint32_t kMinusInfinity = 0xff80ff80u;
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t round(float2 v) {  // two RN conversions
+    const __nv_bfloat162 r = __floats2bfloat162_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+  static __device__ __forceinline__ uint32_t max(uint32_t a, uint32_t b) {  // NaN loses, as in fmaxf
+    const __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                                     *reinterpret_cast<const __nv_bfloat162 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+};
+template <> struct Packed<__half> {
+  static constexpr uint32_t kMinusInfinity = 0xfc00fc00u;
+  static __device__ __forceinline__ float2 unpack(uint32_t w) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&w));
+  }
+  static __device__ __forceinline__ uint32_t round(float2 v) {
+    const __half2 r = __floats2half2_rn(v.x, v.y);
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+  static __device__ __forceinline__ uint32_t max(uint32_t a, uint32_t b) {
+    const __half2 r = __hmax2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+};
+
+// divide() on a pair sharing one denominator: the same residual steps with
+// float2 operations (q * (-b) + a is exactly a - q * b before its one rounding).
+__device__ __forceinline__ float2 divide2(const Divider &d, float2 a) {
+  const float2 y = make_float2(d.y, d.y), minus_b = make_float2(-d.b, -d.b);
+  float2 q = __fmul2_rn(a, y);
+  q = __ffma2_rn(__ffma2_rn(q, minus_b, a), y, q);
+  q = __ffma2_rn(__ffma2_rn(q, minus_b, a), y, q);
+  const bool fast = d.fast && a.x >= 8.673617379884035e-19f && a.x <= 4294967296.0f &&
+                    a.y >= 8.673617379884035e-19f && a.y <= 4294967296.0f;
+  if (!fast) q = make_float2(__fdiv_rn(a.x, d.b), __fdiv_rn(a.y, d.b));
+  return q;
+}
+
+// Word i of a 16-byte vector (i a compile-time constant after unrolling, so
+// the vector stays in registers).
+__device__ __forceinline__ uint32_t &word(uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+__device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Position of lane t's 16-byte chunk within a k-block: XOR-swizzled so that
+// both the transposing stores of pass A and the per-lane loads of passes B
+// and C touch 8 distinct bank groups per quarter-warp.
+__device__ __forceinline__ int chunk_slot(int lane) { return lane ^ ((lane >> 3) & 7); }
+
+// row_statistics for MODE == kPacked: 16-bit logits, row 16-byte aligned.
+// Stage layout: k-blocks of 8 x 256 elements; lane t's elements t + 256 k,
+// k = 8 kb .. 8 kb + 7, sit in order in chunk kb * 256 + chunk_slot(t).  The
+// last length % 2048 elements follow in row order.  Pass A reads 8 rows of
+// 16-byte vectors per thread (one 8 x 8 tile of lanes x k), rounds and masks
+// them in pairs, and transposes the tile with byte permutes; passes B and C
+// read one chunk per 8 elements of their lane.  Every element still takes the
+// reference's operations in the reference's order.
+template <typename T>
+__device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t length, const Visibility sees,
+                                           const float *__restrict__ projected_values, float scale,
+                                           float *__restrict__ probabilities_out, unsigned char *stage,
+                                           float *scratch) {
+  using P = Packed<T>;
+  using D = Dtype<T>;
+  constexpr int kBlock = 8 * kLanes;
+  const int64_t blocks = length / kBlock;
+  const int64_t body = blocks * kBlock;
+  uint4 *chunks = reinterpret_cast<uint4 *>(stage);
+  unsigned short *tail = reinterpret_cast<unsigned short *>(stage + body * 2);
+  const uint4 *in = reinterpret_cast<const uint4 *>(row);
+  const float2 scale2 = make_float2(scale, scale);
+  const unsigned short neg_inf = minus_infinity<T>();
+  uint32_t max_pair = P::kMinusInfinity;
+  float local_max = -INFINITY;
+
+  // dtype(x * scale), masked, for the 8 elements from p0 (one vector).
+  auto prepare = [&](int64_t p0, uint4 raw) -> uint4 {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) word(raw, i) = P::round(__fmul2_rn(P::unpack(word(raw, i)), scale2));
+    if (!sees.all(p0, 8)) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t keep = (sees(p0 + 2 * i) ? 0x0000ffffu : 0u) | (sees(p0 + 2 * i + 1) ? 0xffff0000u : 0u);
+        word(raw, i) = (word(raw, i) & keep) | (P::kMinusInfinity & ~keep);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) max_pair = P::max(max_pair, word(raw, i));
+    return raw;
+  };
+
+  // Pass A, k-blocks: thread item i = (kb, c) covers lanes 8c .. 8c + 7.
+  for (int64_t i = threadIdx.x; i < blocks * 32; i += kLanes) {
+    const int64_t kb = i >> 5;
+    const int c = static_cast<int>(i & 31);
+    uint4 raw[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) raw[m] = __ldcs(in + (kb * 8 + m) * 32 + c);
+#pragma unroll
+    for (int m = 0; m < 8; ++m) raw[m] = prepare((kb * 8 + m) * kLanes + c * 8, raw[m]);
+    uint4 *dst = chunks + kb * kLanes;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      uint32_t col[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) col[m] = word(raw[m], w);
+      const uint4 even = make_uint4(__byte_perm(col[0], col[1], 0x5410), __byte_perm(col[2], col[3], 0x5410),
+                                    __byte_perm(col[4], col[5], 0x5410), __byte_perm(col[6], col[7], 0x5410));
+      const uint4 odd = make_uint4(__byte_perm(col[0], col[1], 0x7632), __byte_perm(col[2], col[3], 0x7632),
+                                   __byte_perm(col[4], col[5], 0x7632), __byte_perm(col[6], col[7], 0x7632));
+      dst[chunk_slot(c * 8 + 2 * w)] = even;
+      dst[chunk_slot(c * 8 + 2 * w + 1)] = odd;
+    }
+  }
+  // Pass A, tail: whole vectors, then single elements, in row order.
+  const int64_t tail_vectors = (length - body) / 8;
+  for (int64_t v = threadIdx.x; v < tail_vectors; v += kLanes)
+    reinterpret_cast<uint4 *>(tail)[v] = prepare(body + v * 8, __ldcs(in + body / 8 + v));
+  for (int64_t p = body + tail_vectors * 8 + threadIdx.x; p < length; p += kLanes) {
+    const unsigned short raw = reinterpret_cast<const unsigned short *>(row)[p];
+    const unsigned short b = sees(p) ? D::round(D::to_float(raw), scale) : neg_inf;
+    tail[p - body] = b;
+    local_max = fmaxf(local_max, D::to_float(b));
+  }
+  const float2 pair_max = P::unpack(max_pair);
+  local_max = fmaxf(local_max, fmaxf(pair_max.x, pair_max.y));
+  const float maximum = block_max(local_max, scratch);
+
+  // Pass B: x - max as x + (-max) (the same IEEE operation), lane order.
+  const float2 minus_max = make_float2(-maximum, -maximum);
+  const int slot = chunk_slot(threadIdx.x);
+  float sum = 0.0f;
+  for (int64_t kb = 0; kb < blocks; ++kb) {
+    const uint4 chunk = chunks[kb * kLanes + slot];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float2 d = __fadd2_rn(P::unpack(word(chunk, v)), minus_max);
+      sum = __fadd_rn(sum, expf(d.x));
+      sum = __fadd_rn(sum, expf(d.y));
+    }
+  }
+  for (int64_t p = body + threadIdx.x; p < length; p += kLanes)
+    sum = __fadd_rn(sum, expf(__fsub_rn(D::to_float(tail[p - body]), maximum)));
+  const float denominator = tree_sum(sum, scratch);
+
+  // Pass C: probabilities and the value projection; the next chunk's
+  // projected values are loaded while this chunk computes.
+  const Divider divider = make_divider(denominator);
+  const float *values = projected_values + threadIdx.x;
+  float projection = 0.0f;
+  float next[8];
+  if (blocks > 0) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) next[m] = __ldg(values + m * kLanes);
+  }
+  for (int64_t kb = 0; kb < blocks; ++kb) {
+    float current[8];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) current[m] = next[m];
+    if (kb + 1 < blocks) {
+#pragma unroll
+      for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
+    }
+    const uint4 chunk = chunks[kb * kLanes + slot];
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const float2 d = __fadd2_rn(P::unpack(word(chunk, v)), minus_max);
+      const float2 probability = divide2(divider, make_float2(expf(d.x), expf(d.y)));
+      if (probabilities_out != nullptr) {
+        float *out = probabilities_out + threadIdx.x + (kb * 8 + 2 * v) * kLanes;
+        __stcs(out, probability.x);
+        __stcs(out + kLanes, probability.y);
+      }
+      const float2 product = __fmul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
+      projection = __fadd_rn(projection, product.x);
+      projection = __fadd_rn(projection, product.y);
+    }
+  }
+  for (int64_t p = body + threadIdx.x; p < length; p += kLanes) {
+    const float probability = divide(divider, expf(__fsub_rn(D::to_float(tail[p - body]), maximum)));
+    if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
+    projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(projected_values + p)));
+  }
   projection = tree_sum(projection, scratch);
   return {maximum, denominator, projection};
 }

@@ -204,7 +204,8 @@ template <typename T>
 int launch_probabilities(const void *logits, const float *pv, const int64_t *qpos, const float *kpos, float *probs,
                          float *op, int64_t rows, int groups, int64_t length, float scale, cudaStream_t stream) {
   const T *in = static_cast<const T *>(logits);
-  const int mode = rows::choose_stage<T>(length);
+  const bool aligned_rows = aligned(logits, 16) && (length * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+  const int mode = rows::choose_stage<T>(length, aligned_rows);
   const int64_t bytes = rows::staged_bytes<T>(mode, length);
   const unsigned grid = static_cast<unsigned>(rows);
   int status = LRK_OK;
@@ -216,6 +217,12 @@ int launch_probabilities(const void *logits, const float *pv, const int64_t *qpo
     if ((status = allow_shared(probabilities_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
     probabilities_kernel<T, rows::kBits><<<grid, kLanes, bytes, stream>>>(in, pv, qpos, kpos, probs, op, groups,
                                                                           length, scale);
+  } else if (mode == rows::kPacked) {
+    if constexpr (sizeof(T) == 2) {
+      if ((status = allow_shared(probabilities_kernel<T, rows::kPacked>, bytes)) != LRK_OK) return status;
+      probabilities_kernel<T, rows::kPacked><<<grid, kLanes, bytes, stream>>>(in, pv, qpos, kpos, probs, op, groups,
+                                                                              length, scale);
+    }
   } else {
     probabilities_kernel<T, rows::kStream><<<grid, kLanes, 0, stream>>>(in, pv, qpos, kpos, probs, op, groups, length,
                                                                         scale);
@@ -243,7 +250,14 @@ __global__ void divider_check_kernel(uint64_t count, uint64_t seed, unsigned lon
     if ((i & 1023) == 0) a = __uint_as_float((u & 0x007fffffu) | ((v & 1u) ? 0x3f000000u : 0x3e800000u));
     if ((i & 4095) == 1) b = __uint_as_float((__float_as_uint(b) & 0xff800000u) | 0x007ff000u | (v & 0xfffu));
     const rows::Divider divider = rows::make_divider(b);
-    if (__float_as_uint(rows::divide(divider, a)) != __float_as_uint(__fdiv_rn(a, b))) ++local;
+    const float expected = __fdiv_rn(a, b);
+    if (__float_as_uint(rows::divide(divider, a)) != __float_as_uint(expected)) ++local;
+    // The pair form, with a second numerator from the other half of the draw.
+    const float a2 = __uint_as_float(static_cast<uint32_t>(x >> 7) % 0x3f800001u);
+    const float2 pair = rows::divide2(divider, make_float2(a, a2));
+    if (__float_as_uint(pair.x) != __float_as_uint(expected) ||
+        __float_as_uint(pair.y) != __float_as_uint(__fdiv_rn(a2, b)))
+      ++local;
   }
   if (local) atomicAdd(mismatches, local);
 }

@@ -77,6 +77,11 @@ CASES = [
     ("f32", 4, 4, 60001, 59000, 60001),
     ("bf16", 8, 4, 18432, 0, 18432),
     ("bf16", 4, 4, 18433, 18000, 18433),
+    # 16-byte aligned rows: lane-major packed stage, with and without a tail
+    ("bf16", 9, 4, 34816, 32768, 34800),
+    ("bf16", 7, 4, 20008, 100, 20000),
+    ("f16", 5, 2, 40000, 0, 40000),
+    ("bf16", 3, 4, 100000, 99000, 100000),
 ]
 
 
@@ -104,7 +109,7 @@ def test_fused_matches_dropin_and_oracle(C, cuda, dtype_name, window, groups, le
 KEY_LAYOUTS = ["sorted_ties", "shuffled", "sorted_nan", "sorted_inf", "descending"]
 
 
-@pytest.mark.parametrize("length", [3001, 20011])
+@pytest.mark.parametrize("length", [3001, 20011, 24576])
 @pytest.mark.parametrize("layout", KEY_LAYOUTS)
 def test_fused_key_position_layouts(C, cuda, layout, length):
     """Masks from every kind of key-position vector: non-decreasing ones take
@@ -230,18 +235,21 @@ def test_audit_tables_agree(cuda):
     assert_scores_close(b.scores.cpu().numpy(), a.scores.cpu().numpy())
 
 
-def test_fused_padded_logits_rows(C, cuda):
+@pytest.mark.parametrize("length", [3001, 30001])
+def test_fused_padded_logits_rows(C, cuda, length):
     """Logits rows with a stride larger than the row (a GEMM over a padded key
-    block) score exactly like contiguous rows."""
+    block) score exactly like contiguous rows.  At 30001 keys the padded rows
+    are 16-byte aligned and take the lane-major packed stage (with a ragged
+    tail), the contiguous ones the plain one."""
     import torch
 
-    g = torch.Generator().manual_seed(12)
-    logits, pv, kpos, qpos = make_head(g, cuda, 40, 4, 3001, torch.bfloat16)
-    padded = torch.zeros(40, 4, 3008, dtype=torch.bfloat16, device=cuda)
-    padded[:, :, :3001] = logits
+    g = torch.Generator().manual_seed(12 + length)
+    logits, pv, kpos, qpos = make_head(g, cuda, 40, 4, length, torch.bfloat16)
+    padded = torch.zeros(40, 4, (length + 7) // 8 * 8, dtype=torch.bfloat16, device=cuda)
+    padded[:, :, :length] = logits
     margin = torch.tensor([0.9], device=cuda)
-    a = C.temporal_scores([logits], [pv], [kpos], [10], [2990], qpos, margin, 0.125, 1e-6)
-    b = C.temporal_scores([padded[:, :, :3001]], [pv], [kpos], [10], [2990], qpos, margin, 0.125, 1e-6)
+    a = C.temporal_scores([logits], [pv], [kpos], [10], [length - 11], qpos, margin, 0.125, 1e-6)
+    b = C.temporal_scores([padded[:, :, :length]], [pv], [kpos], [10], [length - 11], qpos, margin, 0.125, 1e-6)
     assert torch.equal(a, b)
 
 

@@ -336,6 +336,8 @@ PROB_CASES = [
     ("bf16", 6, 4, 1), ("bf16", 3, 4, 255), ("bf16", 2, 4, 256), ("bf16", 5, 4, 4099), ("f16", 4, 2, 8192),
     ("f32", 3, 8, 1030), ("bf16", 4, 4, 35026), ("bf16", 2, 8, 60001), ("bf16", 1, 2, 120001), ("f32", 1, 2, 60001),
     ("bf16", 3, 4, 18432), ("bf16", 3, 4, 18433), ("bf16", 1, 2, 112624), ("bf16", 1, 2, 112625),
+    # 16-byte aligned rows longer than the fp32-weight stage: the lane-major packed layout
+    ("bf16", 3, 4, 20480), ("bf16", 2, 4, 34768), ("f16", 2, 4, 40000), ("bf16", 1, 2, 100000),
 ]
 
 
