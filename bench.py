@@ -350,7 +350,8 @@ def main():
         w, g, length = logits.shape
         return w * g * length * (logits.element_size() + 4) + g * length * 4 + length * 4
 
-    def fused_bytes(logits, projected_values, key_positions, first, last, query_positions, margin, scale, eps):
+    def fused_bytes(logits, projected_values, key_positions, first, last, query_positions, margin, scale, eps,
+                    query_chunks=None):
         # the fused minimum: logits read once, projected values and key positions once, scores written
         total = 0
         for lg, f, l in zip(logits, first, last):
@@ -400,7 +401,8 @@ def main():
         end.record()
         barrier()
     elapsed_ms = start.elapsed_time(end)
-    launches = counter.count + len(timer.pairs) * (2 if fused else 1)
+    # lrk_temporal_scores: visibility, statistics and risk kernels per call (<= 48 segments)
+    launches = counter.count + len(timer.pairs) * (3 if fused else 1)
     for module, function in zip(patched, originals):
         module.operators = function
     local = torch.tensor([elapsed_ms], device=device)

@@ -33,7 +33,8 @@ class Segment(ctypes.Structure):
 class ScoreSegment(ctypes.Structure):
     """lrk_score_segment (include/lrk.h)."""
     _fields_ = [("logits", P), ("projected_values", P), ("projected_stride", I64), ("key_positions", P),
-                ("length", I64), ("first", I64), ("last", I64), ("scores", P), ("logits_stride", I64)]
+                ("length", I64), ("first", I64), ("last", I64), ("scores", P), ("logits_stride", I64),
+                ("query_chunk", I64)]
 
 
 SIGNATURES = {
@@ -61,6 +62,7 @@ SIGNATURES = {
     "lrk_gather_rows": (I32, [P, I64, I64, P, I64, P, P]),
     "lrk_project_values": (I32, [P, I32, I64, I64, P, P, I64, I64, P, P]),
     "lrk_check_division": (I32, [ctypes.c_uint64, ctypes.c_uint64, P, P]),
+    "lrk_logits": (I32, [P, I64, P, I64, I64, I64, P, I64, P]),
     "lrk_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "lrk_register_host": (I32, [P, SIZE]),
     "lrk_unregister_host": (I32, [P]),

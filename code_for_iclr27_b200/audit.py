@@ -49,8 +49,7 @@ def temporal_head_scores(queries, query_positions, keys, key_positions, values, 
     key_positions = key_positions.to(dtype=torch.float32).contiguous()
     query_positions = query_positions.to(dtype=torch.int64).contiguous()
     margin = base_margin.to(device=keys.device, dtype=torch.float32).reshape(1).contiguous()
-    bytes_per_query = queries.shape[1] * keys.shape[0] * (keys.element_size() + 4)
-    chunk_size = min(query_chunk_size, max(1, (64 * 1024 ** 2) // bytes_per_query))
+    chunk_size = query_chunk(query_chunk_size, queries.shape[1], keys.shape[0], keys.element_size())
     result = None
     for start in range(0, queries.shape[0], chunk_size):
         end = min(start + chunk_size, queries.shape[0])
@@ -102,6 +101,32 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
     return ScoreTable(torch.cat(parts), segments, ends)
 
 
+def head_logits(per_head_queries, keys, start: int, end: int, chunk: int):
+    """bf16 logits [W, G, L] of one head, equal bit for bit to the logits the
+    reference computes per query chunk with torch.matmul (scoring.py:184), as
+    a view of rows padded to a 16-byte multiple where possible.
+
+    cuBLAS accumulates each product in tensor-core steps of 16 terms for an
+    even key count -- the GEMM over the 8-aligned key block, which cuBLAS runs
+    about 5x faster, gives the same bits -- and of 8 terms for an odd one,
+    which lrk_logits reproduces (k_step 8).  An odd key count outside
+    lrk_logits' shapes takes the reference's own chunked GEMM."""
+    import torch
+
+    window, groups, dim = per_head_queries.shape
+    length = end - start
+    flat = per_head_queries.contiguous().view(window * groups, dim)
+    if length % 2 == 0:
+        aligned = _aligned_keys(keys, start, end)
+        return torch.matmul(flat, aligned.transpose(0, 1)).view(window, groups, -1)[:, :, :length]
+    if keys.dtype == torch.bfloat16 and dim in (64, 128):
+        padded = operators().logits(flat, keys[start:end], 8, (length + 7) // 8 * 8)
+        return padded.view(window, groups, -1)[:, :, :length]
+    head_keys = keys[start:end]
+    return torch.cat([torch.matmul(per_head_queries[a:a + chunk], head_keys.transpose(0, 1))
+                      for a in range(0, window, chunk)])
+
+
 def _aligned_keys(keys, start, end, multiple=8):
     """Keys of one head extended to a multiple of 8 rows.  cuBLAS runs the
     [W*G, D] x [D, L] logits GEMM about 5x faster when L is a multiple of 8
@@ -116,14 +141,24 @@ def _aligned_keys(keys, start, end, multiple=8):
     return torch.cat([keys[start:end], keys.new_zeros(padded - (end - start), keys.shape[1])])
 
 
+def query_chunk(query_chunk_size: int, groups: int, keys: int, element_size: int) -> int:
+    """Queries per chunk of temporal_head_scores' running maximum
+    (scoring.py:177-178): at most query_chunk_size, and at most 64 MiB of
+    logits plus probabilities per chunk."""
+    bytes_per_query = groups * keys * (element_size + 4)
+    return min(query_chunk_size, max(1, (64 * 1024 ** 2) // bytes_per_query))
+
+
 def score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
-                      denominator_epsilon=1e-6) -> ScoreTable:
+                      denominator_epsilon=1e-6, query_chunk_size=250) -> ScoreTable:
     """compute_score_table with the fused scorer.  Per layer: one
-    lrk_project_values call (g V^T for every head, scoring.py:175), one bf16
-    Q K^T GEMM per head (scoring.py:184), then one lrk_temporal_scores call
-    over all of the layer's heads -- the probabilities never reach HBM.  Given
-    the same logits and projected values, the scores are bit-identical to the
-    temporal_probabilities + temporal_risk composition."""
+    lrk_project_values call (g V^T for every head, scoring.py:175, in the
+    float32 GEMM's accumulation order), one bf16 Q K^T GEMM per head
+    (scoring.py:184), then one lrk_temporal_scores call over all of the
+    layer's heads -- the probabilities never reach HBM.  Each head keeps the
+    composition's query chunks for its running maximum, so the scores are
+    bit-identical to score_table (the temporal_probabilities + temporal_risk
+    composition)."""
     import torch
 
     C = operators()
@@ -142,26 +177,26 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
         window, dim = layer_queries.shape[0], layer_queries.shape[-1]
         # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
         per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1).contiguous()
-        logits, pvs, kpos, firsts, lasts = [], [], [], [], []
+        logits, pvs, kpos, firsts, lasts, chunks = [], [], [], [], [], []
         for head in range(heads):
             start, end = int(bounds[head]), int(bounds[head + 1])
             candidate_start = int(layer.prompt_lens[head])
             candidate_end = max(candidate_start, end - start - protect_recent)
             if candidate_end <= candidate_start:
                 continue
-            keys = _aligned_keys(layer.keys, start, end)
-            head_logits = torch.matmul(per_head[head].view(window * groups, dim), keys.transpose(0, 1))
-            logits.append(head_logits.view(window, groups, keys.shape[0])[:, :, :end - start])
+            chunk = query_chunk(query_chunk_size, groups, end - start, layer.keys.element_size())
+            logits.append(head_logits(per_head[head], layer.keys, start, end, chunk))
             pvs.append(projected[:, start:end])
             kpos.append(positions[start:end])
             firsts.append(candidate_start)
             lasts.append(candidate_end)
+            chunks.append(chunk)
             segments.append(ScoreSegment(layer_index, head, candidate_start, candidate_end - candidate_start))
             running += candidate_end - candidate_start
             ends.append(running)
         if logits:
             parts.append(C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, scale,
-                                           denominator_epsilon))
+                                           denominator_epsilon, chunks))
     if not parts:
         raise RuntimeError("No eligible KV remains after prompt/recent protection")
     return ScoreTable(torch.cat(parts), segments, ends)
@@ -194,7 +229,7 @@ def audit_pass(cache, queries, query_positions, gradients, base_margin, immediat
     composes them (bit-identical scores); fused=True uses lrk_temporal_scores."""
     if fused:
         table = score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
-                                  denominator_epsilon)
+                                  denominator_epsilon, query_chunk_size)
     else:
         table = score_table(cache, queries, query_positions, gradients, base_margin, protect_recent,
                             denominator_epsilon, query_chunk_size)

@@ -32,6 +32,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <tuple>
+#include <type_traits>
 
 #include "common.cuh"
 #include "rows.cuh"
@@ -115,6 +117,16 @@ int allow_shared(K kernel, int64_t bytes) {
   return e == cudaSuccess ? LRK_OK : fail(LRK_ERR_CUDA, cudaGetErrorString(e));
 }
 
+// Every row of every segment starts on a 16-byte boundary.
+template <typename T>
+bool rows_aligned(const ScoreTableParam &table, int n) {
+  for (int i = 0; i < n; ++i)
+    if (!aligned(table.segment[i].logits, 16) ||
+        (table.segment[i].logits_stride * static_cast<int64_t>(sizeof(T))) % 16 != 0)
+      return false;
+  return true;
+}
+
 template <typename T>
 int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int window, int groups, float scale,
                  float3 *stats, int32_t *visible, int64_t s0, int64_t max_length, cudaStream_t stream) {
@@ -125,11 +137,7 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
   }
   const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
   const dim3 grid(static_cast<unsigned>(rows_per_segment), n);
-  bool aligned_rows = true;  // every row of every segment on a 16-byte boundary
-  for (int i = 0; i < n; ++i)
-    aligned_rows = aligned_rows && aligned(table.segment[i].logits, 16) &&
-              (table.segment[i].logits_stride * static_cast<int64_t>(sizeof(T))) % 16 == 0;
-  const int mode = rows::choose_stage<T>(max_length, aligned_rows);
+  const int mode = rows::choose_stage<T>(max_length, rows_aligned<T>(table, n));
   const int64_t bytes = rows::staged_bytes<T>(mode, max_length);
   int status = LRK_OK;
   if (mode == rows::kWeights) {
@@ -163,6 +171,31 @@ __device__ __forceinline__ double risk64(double margin, double probability, doub
   return fmax(0.0, kl);
 }
 
+// Number of queries per chunk of a segment's running maximum.
+__device__ __forceinline__ int chunk_queries(const lrk_score_segment &seg, int window) {
+  return seg.query_chunk > 0 && seg.query_chunk < window ? static_cast<int>(seg.query_chunk) : window;
+}
+
+// Margin terms shared by every chunk score: m, sigmoid(m), softplus(m).
+struct MarginTerms {
+  double m, probability, base_softplus;
+};
+__device__ __forceinline__ MarginTerms margin_terms(const float *margin) {
+  const double m = static_cast<double>(margin[0]);
+  return {m, 1.0 / (1.0 + exp(-m)), softplus64(m)};
+}
+
+// One chunk's score from its drop range (csrc/scoring.cu:68-128): NaN when a
+// drop was not finite, else max(R(min), R(max)) rounded to float.
+__device__ __forceinline__ float chunk_score(const MarginTerms &t, bool nonfinite, float minimum, float maximum) {
+  if (nonfinite) return NAN;
+  return static_cast<float>(fmax(risk64(t.m, t.probability, t.base_softplus, minimum),
+                                 risk64(t.m, t.probability, t.base_softplus, maximum)));
+}
+
+// The running maximum over chunks, torch.maximum's semantics (NaN wins).
+__device__ __forceinline__ float running_max(float a, float b) { return isnan(a) || isnan(b) ? NAN : fmaxf(a, b); }
+
 // A CTA covers 32 consecutive candidate columns (one warp row, 64-byte bf16
 // reads per logits row) with kQueryLanes query lanes: lane y walks queries
 // y, y + kQueryLanes, ...  The lanes' min / max / non-finite flags meet in
@@ -189,57 +222,230 @@ __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam tabl
   const int64_t count = seg.last - seg.first;
   const int64_t candidate = static_cast<int64_t>(blockIdx.x) * 32 + threadIdx.x;
   const bool active = candidate < count;
-  float minimum = INFINITY, maximum = -INFINITY;
-  int nonfinite = 0;
-  if (active) {
-    const int64_t column = seg.first + candidate;
-    const int64_t stride = seg.logits_stride;
-    const float key_position = __ldg(seg.key_positions + column);
-    float pv[G > 0 ? G : kMaxGroups];
+  const int64_t column = seg.first + (active ? candidate : 0);
+  const int64_t stride = seg.logits_stride;
+  const float key_position = active ? __ldg(seg.key_positions + column) : 0.0f;
+  float pv[G > 0 ? G : kMaxGroups];
 #pragma unroll
-    for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g)
-      pv[g] = g < ng ? __ldg(seg.projected_values + g * seg.projected_stride + column) : 0.0f;
-    const typename D::Bits *base = static_cast<const typename D::Bits *>(seg.logits) + column;
+  for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g)
+    pv[g] = active && g < ng ? __ldg(seg.projected_values + g * seg.projected_stride + column) : 0.0f;
+  const typename D::Bits *base = static_cast<const typename D::Bits *>(seg.logits) + column;
+  const int chunk = chunk_queries(seg, window);
+  const bool leader = threadIdx.y == 0 && active;
+  MarginTerms terms{};
+  if (leader) terms = margin_terms(margin);
+  float result = 0.0f;
+  for (int c0 = 0; c0 < window; c0 += chunk) {
+    const int c1 = min(window, c0 + chunk);
+    float minimum = INFINITY, maximum = -INFINITY;
+    int nonfinite = 0;
+    if (active) {
 #pragma unroll 2
-    for (int q = threadIdx.y; q < window; q += kQueryLanes) {
-      float drop = 0.0f;
+      for (int q = c0 + threadIdx.y; q < c1; q += kQueryLanes) {
+        float drop = 0.0f;
 #pragma unroll
-      for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g) {
-        if (g < ng) {
-          const float4 st = shared_stats[q * ng + g];
-          const float rounded = D::to_float(
-              D::round(D::to_float(__ldg(base + (static_cast<int64_t>(q) * ng + g) * stride)), scale));
-          const float x = key_position <= st.w ? rounded : -INFINITY;
-          const float probability = __fdiv_rn(expf(__fsub_rn(x, st.x)), st.y);
-          const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
-          drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(pv[g], st.z)));
+        for (int g = 0; g < (G > 0 ? G : kMaxGroups); ++g) {
+          if (g < ng) {
+            const float4 st = shared_stats[q * ng + g];
+            const float rounded = D::to_float(
+                D::round(D::to_float(__ldg(base + (static_cast<int64_t>(q) * ng + g) * stride)), scale));
+            const float x = key_position <= st.w ? rounded : -INFINITY;
+            const float probability = __fdiv_rn(expf(__fsub_rn(x, st.x)), st.y);
+            const float ratio = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
+            drop = __fadd_rn(drop, __fmul_rn(ratio, __fsub_rn(pv[g], st.z)));
+          }
+        }
+        nonfinite |= !isfinite(drop);
+        minimum = fminf(minimum, drop);
+        maximum = fmaxf(maximum, drop);
+      }
+    }
+    lane_min[threadIdx.y][threadIdx.x] = minimum;
+    lane_max[threadIdx.y][threadIdx.x] = maximum;
+    lane_bad[threadIdx.y][threadIdx.x] = nonfinite;
+    __syncthreads();
+    if (leader) {
+      for (int y = 1; y < kQueryLanes; ++y) {
+        minimum = fminf(minimum, lane_min[y][threadIdx.x]);
+        maximum = fmaxf(maximum, lane_max[y][threadIdx.x]);
+        nonfinite |= lane_bad[y][threadIdx.x];
+      }
+      const float score = chunk_score(terms, nonfinite != 0, minimum, maximum);
+      result = c0 == 0 ? score : running_max(result, score);
+    }
+    __syncthreads();
+  }
+  if (leader) seg.scores[candidate] = result;
+}
+
+// Vectorised risk for 16-bit logits in 16-byte aligned rows.  A CTA covers
+// 64 consecutive candidate columns from a 16-byte boundary; thread (tx, ty)
+// owns C consecutive candidates (one C * 2-byte load per logits row, C = 8, 4
+// or 2) and
+// walks queries ty, ty + TY, ..., with the next query's rows loaded while the
+// current one computes.  Candidates in pairs share every per-row operand, so
+// the elementwise steps run as float2 operations, and the first division uses
+// the row's correctly rounded reciprocal (rows::divide2).  Per candidate the
+// operations and their order are those of risk_kernel.
+template <typename T, int G, int C>
+__global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTableParam table,
+                                                                const int64_t *__restrict__ qpos, int window,
+                                                                float scale, const float3 *__restrict__ stats,
+                                                                int64_t segment_base,
+                                                                const float *__restrict__ margin, float epsilon) {
+  using D = rows::Dtype<T>;
+  using P = rows::Packed<T>;
+  using Bits = typename D::Bits;
+  using Vec = typename std::conditional<C == 8, uint4, typename std::conditional<C == 4, uint2, uint32_t>::type>::type;
+  constexpr int kTile = 64;
+  constexpr int TX = kTile / C, TY = kRiskThreads / TX;
+  extern __shared__ float4 shared_stats[];  // [window * G] (max, denominator, projection, query position)
+  float *reciprocal = reinterpret_cast<float *>(shared_stats + window * G);  // [window * G]
+  __shared__ float part_min[TY][kTile + 1], part_max[TY][kTile + 1];
+  __shared__ unsigned char part_bad[TY][kTile];
+  const lrk_score_segment &seg = table.segment[blockIdx.y];
+  const int64_t tile = (seg.first & ~int64_t{7}) + static_cast<int64_t>(blockIdx.x) * kTile;
+  if (tile >= seg.last) return;  // the whole CTA: nothing of this segment here
+  for (int i = threadIdx.x; i < window * G; i += kRiskThreads) {
+    const float3 st = stats[(segment_base + blockIdx.y) * window * G + i];
+    shared_stats[i] = make_float4(st.x, st.y, st.z, static_cast<float>(qpos[i / G]));
+    reciprocal[i] = __frcp_rn(st.y);
+  }
+  __syncthreads();
+  const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
+  const int64_t col0 = tile + tx * C;
+  const bool full = col0 + C <= seg.length;
+  float key_position[C], pv[G][C];
+#pragma unroll
+  for (int j = 0; j < C; ++j) {
+    const bool inside = col0 + j < seg.length;
+    key_position[j] = inside ? __ldg(seg.key_positions + col0 + j) : INFINITY;
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      pv[g][j] = inside ? __ldg(seg.projected_values + g * seg.projected_stride + col0 + j) : 0.0f;
+  }
+  const Bits *base = static_cast<const Bits *>(seg.logits) + col0;
+  auto load = [&](int q, int g) -> Vec {
+    const Bits *row = base + (static_cast<int64_t>(q) * G + g) * seg.logits_stride;
+    if (full) return __ldg(reinterpret_cast<const Vec *>(row));
+    uint32_t w[C / 2];
+#pragma unroll
+    for (int i = 0; i < C / 2; ++i) {
+      const uint32_t a = col0 + 2 * i < seg.length ? row[2 * i] : 0u;
+      const uint32_t b = col0 + 2 * i + 1 < seg.length ? row[2 * i + 1] : 0u;
+      w[i] = a | (b << 16);
+    }
+    if constexpr (C == 8) return make_uint4(w[0], w[1], w[2], w[3]);
+    else if constexpr (C == 4) return make_uint2(w[0], w[1]);
+    else return w[0];
+  };
+  auto word_of = [](const Vec &v, int i) -> uint32_t {
+    if constexpr (C == 8) return rows::word(v, i);
+    else if constexpr (C == 4) return i == 0 ? v.x : v.y;
+    else return v;
+  };
+  const float2 scale2 = make_float2(scale, scale), one2 = make_float2(1.0f, 1.0f);
+  const int chunk = chunk_queries(seg, window);
+  const bool leader = threadIdx.x < kTile;
+  MarginTerms terms{};
+  if (leader) terms = margin_terms(margin);
+  float result = 0.0f;
+  for (int c0 = 0; c0 < window; c0 += chunk) {
+    const int c1 = min(window, c0 + chunk);
+    float lo[C], hi[C];
+    uint32_t bad = 0;
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      lo[j] = INFINITY;
+      hi[j] = -INFINITY;
+    }
+    Vec current[G], next[G];
+    if (c0 + ty < c1) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) current[g] = load(c0 + ty, g);
+    }
+    for (int q = c0 + ty; q < c1; q += TY) {
+      if (q + TY < c1) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) next[g] = load(q + TY, g);
+      }
+      const float query_position = shared_stats[q * G].w;
+      float drop[C];
+#pragma unroll
+      for (int j = 0; j < C; ++j) drop[j] = 0.0f;
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 st = shared_stats[q * G + g];
+        rows::Divider divider;
+        divider.b = st.y;
+        divider.y = reciprocal[q * G + g];
+        divider.fast = st.y >= 1.0f && st.y <= 4294967296.0f;
+        const float2 minus_max = make_float2(-st.x, -st.x), minus_projection = make_float2(-st.z, -st.z);
+#pragma unroll
+        for (int i = 0; i < C / 2; ++i) {
+          float2 x = P::unpack(P::round(rows::mul2_rn(P::unpack(word_of(current[g], i)), scale2)));
+          if (!(key_position[2 * i] <= query_position)) x.x = -INFINITY;
+          if (!(key_position[2 * i + 1] <= query_position)) x.y = -INFINITY;
+          const float2 d = rows::add2_rn(x, minus_max);
+          const float2 probability = rows::divide2(divider, make_float2(expf(d.x), expf(d.y)));
+          const float2 rest = rows::add2_rn(one2, make_float2(-probability.x, -probability.y));
+          const float2 ratio = make_float2(__fdiv_rn(probability.x, fmaxf(rest.x, epsilon)),
+                                           __fdiv_rn(probability.y, fmaxf(rest.y, epsilon)));
+          const float2 term = rows::mul2_rn(ratio, rows::add2_rn(make_float2(pv[g][2 * i], pv[g][2 * i + 1]),
+                                                               minus_projection));
+          // Scalar sums: a packed product feeding a packed sum may be fused.
+          drop[2 * i] = __fadd_rn(drop[2 * i], term.x);
+          drop[2 * i + 1] = __fadd_rn(drop[2 * i + 1], term.y);
         }
       }
-      nonfinite |= !isfinite(drop);
-      minimum = fminf(minimum, drop);
-      maximum = fmaxf(maximum, drop);
+#pragma unroll
+      for (int j = 0; j < C; ++j) {
+        bad |= static_cast<uint32_t>(!isfinite(drop[j])) << j;
+        lo[j] = fminf(lo[j], drop[j]);
+        hi[j] = fmaxf(hi[j], drop[j]);
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) current[g] = next[g];
     }
+#pragma unroll
+    for (int j = 0; j < C; ++j) {
+      part_min[ty][tx * C + j] = lo[j];
+      part_max[ty][tx * C + j] = hi[j];
+      part_bad[ty][tx * C + j] = static_cast<unsigned char>((bad >> j) & 1u);
+    }
+    __syncthreads();
+    if (leader) {
+      float minimum = INFINITY, maximum = -INFINITY;
+      bool nonfinite = false;
+      for (int y = 0; y < TY; ++y) {
+        minimum = fminf(minimum, part_min[y][threadIdx.x]);
+        maximum = fmaxf(maximum, part_max[y][threadIdx.x]);
+        nonfinite |= part_bad[y][threadIdx.x] != 0;
+      }
+      const float score = chunk_score(terms, nonfinite, minimum, maximum);
+      result = c0 == 0 ? score : running_max(result, score);
+    }
+    __syncthreads();
   }
-  lane_min[threadIdx.y][threadIdx.x] = minimum;
-  lane_max[threadIdx.y][threadIdx.x] = maximum;
-  lane_bad[threadIdx.y][threadIdx.x] = nonfinite;
-  __syncthreads();
-  if (threadIdx.y != 0 || !active) return;
-  for (int y = 1; y < kQueryLanes; ++y) {
-    minimum = fminf(minimum, lane_min[y][threadIdx.x]);
-    maximum = fmaxf(maximum, lane_max[y][threadIdx.x]);
-    nonfinite |= lane_bad[y][threadIdx.x];
+  if (!leader) return;
+  const int64_t column = tile + threadIdx.x;
+  if (column < seg.first || column >= seg.last) return;
+  seg.scores[column - seg.first] = result;
+}
+
+template <typename T, int G, int C>
+int launch_risk_vec(const ScoreTableParam &table, int n, const int64_t *qpos, int window, float scale,
+                    const float3 *stats, int64_t s0, const float *margin, float epsilon, int64_t max_span,
+                    cudaStream_t stream) {
+  const size_t shared = static_cast<size_t>(window) * G * (sizeof(float4) + sizeof(float));
+  auto kernel = risk_vec_kernel<T, G, C>;
+  if (shared > 16 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
+    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
-  float result;
-  if (nonfinite) {
-    result = NAN;
-  } else {
-    const double m = static_cast<double>(margin[0]);
-    const double probability = 1.0 / (1.0 + exp(-m));
-    const double base_sp = softplus64(m);
-    result = static_cast<float>(fmax(risk64(m, probability, base_sp, minimum), risk64(m, probability, base_sp, maximum)));
-  }
-  seg.scores[candidate] = result;
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_span, 64))), n);
+  kernel<<<grid, kRiskThreads, shared, stream>>>(table, qpos, window, scale, stats, s0, margin, epsilon);
+  return launch_status("lrk_temporal_scores");
 }
 
 template <typename T>
@@ -255,10 +461,26 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
       table.segment[i] = segments[s0 + i];
       max_candidates = std::max<int64_t>(max_candidates, segments[s0 + i].last - segments[s0 + i].first);
     }
-    int64_t max_length = 0;
-    for (int i = 0; i < n; ++i) max_length = std::max<int64_t>(max_length, table.segment[i].length);
+    int64_t max_length = 0, max_span = 0;
+    for (int i = 0; i < n; ++i) {
+      max_length = std::max<int64_t>(max_length, table.segment[i].length);
+      max_span = std::max<int64_t>(max_span, table.segment[i].last - (table.segment[i].first & ~int64_t{7}));
+    }
     int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, stream);
     if (status != LRK_OK) return status;
+    if constexpr (sizeof(T) == 2) {
+      if (rows_aligned<T>(table, n) && window * groups * 20 <= 200 * 1024 &&
+          (groups == 1 || groups == 2 || groups == 4 || groups == 8)) {
+        const auto args = std::make_tuple(table, n, qpos, window, scale, stats, s0, margin, epsilon, max_span, stream);
+        // Candidates per thread: G * C <= 16 keeps the per-thread state near 80 registers.
+        status = groups == 1   ? std::apply(launch_risk_vec<T, 1, 8>, args)
+                 : groups == 2 ? std::apply(launch_risk_vec<T, 2, 4>, args)
+                 : groups == 4 ? std::apply(launch_risk_vec<T, 4, 4>, args)
+                               : std::apply(launch_risk_vec<T, 8, 2>, args);
+        if (status != LRK_OK) return status;
+        continue;
+      }
+    }
     const size_t shared = static_cast<size_t>(window) * groups * sizeof(float4);
     const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, 32))), n);
     const dim3 block(32, kQueryLanes);
@@ -332,6 +554,7 @@ int check_score_call(const lrk_score_segment *segments, int64_t count, int64_t w
                 "Invalid risk interval");
     LRK_REQUIRE(seg.projected_stride >= seg.length, "projected_stride shorter than the segment");
     LRK_REQUIRE(seg.logits_stride >= seg.length, "logits_stride shorter than the segment");
+    LRK_REQUIRE(seg.query_chunk >= 0, "query_chunk must be >= 0");
   }
   return LRK_OK;
 }

@@ -407,16 +407,19 @@ int launch_gather(const Plan &plan, GatherOut out, int vb, cudaStream_t stream, 
   if (units <= 0 || units > 1024) return fail(LRK_ERR_UNSUPPORTED, "row too wide for the gather engine");
   out.units.init(static_cast<uint32_t>(units));
   // Tile height: 256 rows for narrow rows; 64 normally; 16 when 64-row tiles
-  // would leave SMs idle (small outputs such as an archive pack).
+  // would leave SMs idle, 4 when even 16-row tiles would (small outputs such
+  // as an archive pack: more CTAs keep more row reads in flight).
   const int sms = sm_count();
   const bool narrow = out.row_bytes < 64;
-  const bool small = !narrow && ceil_div(out.rows, 64) < 2 * sms;
-  const int64_t tile_rows = narrow ? 256 : small ? 16 : 64;
+  const bool tiny = !narrow && ceil_div(out.rows, 16) < 2 * sms;
+  const bool small = !narrow && !tiny && ceil_div(out.rows, 64) < 2 * sms;
+  const int64_t tile_rows = narrow ? 256 : tiny ? 4 : small ? 16 : 64;
   const int64_t tiles = ceil_div(out.rows, tile_rows);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, static_cast<int64_t>(sms) * 16));
 #define LRK_GATHER_CASE(VB)                                                              \
   case VB:                                                                               \
     if (narrow) gather_kernel<VB, 256, Plan><<<grid, kThreads, 0, stream>>>(plan, out);     \
+    else if (tiny) gather_kernel<VB, 4, Plan><<<grid, kThreads, 0, stream>>>(plan, out);    \
     else if (small) gather_kernel<VB, 16, Plan><<<grid, kThreads, 0, stream>>>(plan, out);  \
     else gather_kernel<VB, 64, Plan><<<grid, kThreads, 0, stream>>>(plan, out);          \
     break;

@@ -314,6 +314,32 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
   return {maximum, denominator, projection};
 }
 
+// Packed float2 IEEE operations (sm_100 add/mul/fma .rn .f32x2), one
+// rounding per component.  Written as inline PTX so that the compiler cannot
+// merge a product with a following sum into one fused operation (the float2
+// builtins allowed that, which changes the rounding of accumulations).
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2_rn(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // Pairs of 16-bit logits in one 32-bit word (low half = the earlier element).
 template <typename T> struct Packed;
 template <> struct Packed<__nv_bfloat16> {
@@ -350,9 +376,9 @@ template <> struct Packed<__half> {
 // float2 operations (q * (-b) + a is exactly a - q * b before its one rounding).
 __device__ __forceinline__ float2 divide2(const Divider &d, float2 a) {
   const float2 y = make_float2(d.y, d.y), minus_b = make_float2(-d.b, -d.b);
-  float2 q = __fmul2_rn(a, y);
-  q = __ffma2_rn(__ffma2_rn(q, minus_b, a), y, q);
-  q = __ffma2_rn(__ffma2_rn(q, minus_b, a), y, q);
+  float2 q = mul2_rn(a, y);
+  q = fma2_rn(fma2_rn(q, minus_b, a), y, q);
+  q = fma2_rn(fma2_rn(q, minus_b, a), y, q);
   const bool fast = d.fast && a.x >= 8.673617379884035e-19f && a.x <= 4294967296.0f &&
                     a.y >= 8.673617379884035e-19f && a.y <= 4294967296.0f;
   if (!fast) q = make_float2(__fdiv_rn(a.x, d.b), __fdiv_rn(a.y, d.b));
@@ -400,7 +426,7 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   // dtype(x * scale), masked, for the 8 elements from p0 (one vector).
   auto prepare = [&](int64_t p0, uint4 raw) -> uint4 {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) word(raw, i) = P::round(__fmul2_rn(P::unpack(word(raw, i)), scale2));
+    for (int i = 0; i < 4; ++i) word(raw, i) = P::round(mul2_rn(P::unpack(word(raw, i)), scale2));
     if (!sees.all(p0, 8)) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -458,7 +484,7 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
     const uint4 chunk = chunks[kb * kLanes + slot];
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
-      const float2 d = __fadd2_rn(P::unpack(word(chunk, v)), minus_max);
+      const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
       sum = __fadd_rn(sum, expf(d.x));
       sum = __fadd_rn(sum, expf(d.y));
     }
@@ -488,14 +514,14 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
     const uint4 chunk = chunks[kb * kLanes + slot];
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
-      const float2 d = __fadd2_rn(P::unpack(word(chunk, v)), minus_max);
+      const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
       const float2 probability = divide2(divider, make_float2(expf(d.x), expf(d.y)));
       if (probabilities_out != nullptr) {
         float *out = probabilities_out + threadIdx.x + (kb * 8 + 2 * v) * kLanes;
         __stcs(out, probability.x);
         __stcs(out + kLanes, probability.y);
       }
-      const float2 product = __fmul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
+      const float2 product = mul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
       projection = __fadd_rn(projection, product.x);
       projection = __fadd_rn(projection, product.y);
     }

@@ -327,10 +327,11 @@ std::vector<torch::Tensor> topk_smallest(torch::Tensor x, int64_t k) {
 torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<torch::Tensor> projected_values,
                               std::vector<torch::Tensor> key_positions, std::vector<int64_t> first,
                               std::vector<int64_t> last, torch::Tensor query_positions, torch::Tensor margin,
-                              double scale, double epsilon) {
+                              double scale, double epsilon, std::vector<int64_t> query_chunks) {
   const size_t count = logits.size();
   TORCH_CHECK(count > 0 && projected_values.size() == count && key_positions.size() == count &&
-                  first.size() == count && last.size() == count,
+                  first.size() == count && last.size() == count &&
+                  (query_chunks.empty() || query_chunks.size() == count),
               "Segment lists differ in length");
   check_cuda(query_positions, logits[0]);
   check_cuda(margin, logits[0]);
@@ -374,6 +375,7 @@ torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<tor
     s.last = last[i];
     s.scores = scores.data_ptr<float>() + offset;
     s.logits_stride = lg.stride(1);
+    s.query_chunk = query_chunks.empty() ? 0 : query_chunks[i];
     offset += last[i] - first[i];
   }
   const size_t bytes = lrk_temporal_scores_workspace_bytes(static_cast<int64_t>(count), window, groups);
@@ -393,13 +395,30 @@ torch::Tensor project_values(torch::Tensor values, torch::Tensor gradients, torc
   check_cuda(cumulative, values);
   TORCH_CHECK(values.dim() == 2 && gradients.dim() == 2 && gradients.size(1) == values.size(1) &&
                   gradients.scalar_type() == at::kFloat && cumulative.scalar_type() == at::kInt && groups > 0 &&
-                  gradients.size(0) == (cumulative.numel() - 1) * groups,
+                  gradients.size(0) == (cumulative.numel() - 1) * groups && values.is_contiguous() &&
+                  gradients.is_contiguous() && cumulative.is_contiguous(),
               "Invalid projection inputs");
   c10::cuda::CUDAGuard guard(values.device());
   auto out = torch::empty({groups, values.size(0)}, gradients.options());
   check_status(lrk_project_values(values.data_ptr(), dtype_code(values.scalar_type()), values.size(0), values.size(1),
                                   gradients.data_ptr<float>(), cumulative.data_ptr<int32_t>(), cumulative.numel() - 1,
                                   groups, out.data_ptr<float>(), current_stream()));
+  return out;
+}
+
+// Logits [rows, out_stride] bf16 (the first `count` columns are the keys')
+// in torch.matmul's accumulation order for k_step-term steps (lrk_logits).
+torch::Tensor logits(torch::Tensor queries, torch::Tensor keys, int64_t k_step, int64_t out_stride) {
+  check_cuda(queries, queries);
+  check_cuda(keys, queries);
+  TORCH_CHECK(queries.dim() == 2 && keys.dim() == 2 && queries.size(1) == keys.size(1) &&
+                  queries.scalar_type() == at::kBFloat16 && keys.scalar_type() == at::kBFloat16 &&
+                  queries.is_contiguous() && keys.is_contiguous(),
+              "logits takes contiguous bf16 [rows, D] queries and [count, D] keys");
+  c10::cuda::CUDAGuard guard(queries.device());
+  auto out = torch::empty({queries.size(0), out_stride}, queries.options());
+  check_status(lrk_logits(queries.data_ptr(), queries.size(0), keys.data_ptr(), keys.size(0), keys.size(1), k_step,
+                          out.data_ptr(), out_stride, current_stream()));
   return out;
 }
 
@@ -416,6 +435,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("batch_append", &batch_append);
   module.def("refine", &refine);
   module.def("topk_smallest", &topk_smallest);
-  module.def("temporal_scores", &temporal_scores);
+  module.def("logits", &logits);
+  module.def("temporal_scores", &temporal_scores, pybind11::arg("logits"), pybind11::arg("projected_values"),
+             pybind11::arg("key_positions"), pybind11::arg("first"), pybind11::arg("last"),
+             pybind11::arg("query_positions"), pybind11::arg("margin"), pybind11::arg("scale"),
+             pybind11::arg("epsilon"), pybind11::arg("query_chunks") = std::vector<int64_t>{});
   module.def("project_values", &project_values);
 }

@@ -71,32 +71,52 @@ class PackedCache:
 
     def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
         """Drop head-relative rows (cache.py:92-180, GPU branch): one sorted
-        absolute-row list and one _C.compact per touched layer."""
+        absolute-row list and one _C.compact per touched layer.  Duplicate
+        positions of a head count once; any position outside its head raises
+        IndexError before the cache changes.  The host bookkeeping is
+        vectorised over all (layer, head) entries, and the rows of every
+        layer travel to the device in one copy."""
         import torch
 
-        grouped: Dict[int, Dict[int, np.ndarray]] = {}
-        for (layer_index, head), positions in removals.items():
-            positions = np.unique(np.asarray(positions, dtype=np.int64))
-            if positions.size:
-                grouped.setdefault(layer_index, {})[head] = positions
-        by_layer: Dict[int, List[np.ndarray]] = {}
-        removed_total = 0
-        for layer_index, heads in grouped.items():
+        coordinates = np.asarray(list(removals.keys()), dtype=np.int64).reshape(-1, 2)
+        arrays = [np.asarray(value, dtype=np.int64).reshape(-1) for value in removals.values()]
+        sizes = np.asarray([a.size for a in arrays], dtype=np.int64)
+        if not sizes.sum():
+            return 0
+        positions = np.concatenate(arrays)
+        owner = np.repeat(np.arange(len(arrays)), sizes)
+        order = np.lexsort((positions, owner))
+        positions, owner = positions[order], owner[order]
+        fresh = np.ones(positions.size, dtype=bool)
+        fresh[1:] = (positions[1:] != positions[:-1]) | (owner[1:] != owner[:-1])
+        positions, owner = positions[fresh], owner[fresh]
+        bounds = {l: self.layers[l].bounds() for l in np.unique(coordinates[:, 0]).tolist()}
+        head_lens = np.asarray([self.layers[l].head_lens[h] for l, h in coordinates.tolist()], dtype=np.int64)
+        prompt_lens = np.asarray([self.layers[l].prompt_lens[h] for l, h in coordinates.tolist()], dtype=np.int64)
+        bad = (positions < 0) | (positions >= head_lens[owner])
+        if bad.any():
+            layer_index, head = coordinates[owner[np.argmax(bad)]]
+            raise IndexError(f"Invalid removal in layer={int(layer_index)}, head={int(head)}")
+        starts = np.asarray([bounds[l][h] for l, h in coordinates.tolist()], dtype=np.int64)
+        rows = starts[owner] + positions
+        layer_of = coordinates[owner, 0]
+        order = np.lexsort((rows, layer_of))
+        rows, layer_of = rows[order], layer_of[order]
+        removed = np.bincount(owner, minlength=len(arrays))
+        removed_prompt = np.bincount(owner, weights=positions < prompt_lens[owner], minlength=len(arrays))
+        for (layer_index, head), count, prompt in zip(coordinates.tolist(), removed.tolist(), removed_prompt.tolist()):
+            self.layers[layer_index].head_lens[head] -= int(count)
+            self.layers[layer_index].prompt_lens[head] -= int(prompt)
+        touched, first = np.unique(layer_of, return_index=True)
+        last = np.append(first[1:], rows.size)
+        device = self.layers[int(touched[0])].keys.device
+        all_rows = torch.as_tensor(rows).to(device, non_blocking=True)
+        cumulative = np.stack([self.layers[int(l)].bounds() for l in touched]).astype(np.int32)
+        all_cumulative = torch.as_tensor(cumulative).to(device, non_blocking=True)
+        C = operators()
+        for i, layer_index in enumerate(touched.tolist()):
             layer = self.layers[layer_index]
-            bounds = layer.bounds()
-            for head, positions in heads.items():
-                if positions[0] < 0 or positions[-1] >= layer.head_lens[head]:
-                    raise IndexError(f"Invalid removal in layer={layer_index}, head={head}")
-                by_layer.setdefault(layer_index, []).append(bounds[head] + positions)
-            for head, positions in heads.items():
-                layer.head_lens[head] -= int(positions.size)
-                layer.prompt_lens[head] -= int(np.sum(positions < layer.prompt_lens[head]))
-                removed_total += int(positions.size)
-        for layer_index, parts in by_layer.items():
-            layer = self.layers[layer_index]
-            ordered = torch.as_tensor(np.sort(np.concatenate(parts)), dtype=torch.int64).to(layer.keys.device,
-                                                                                             non_blocking=True)
-            layer.keys, layer.values, layer.positions = operators().compact(layer.keys, layer.values,
-                                                                            layer.positions, ordered)
-            self._refresh(layer)
-        return removed_total
+            layer.keys, layer.values, layer.positions = C.compact(layer.keys, layer.values, layer.positions,
+                                                                  all_rows[first[i]:last[i]])
+            layer.cumulative = all_cumulative[i]
+        return int(removed.sum())

@@ -10,6 +10,9 @@ CASE is one of:
   compact        compaction of one layer (279k rows of D=128 bf16) removing 64 rows
   append         one-token append to one layer
   refine         selection over 502k scores in 256 segments
+  project        projected values of one layer (279k rows of D=128 bf16, 4 groups)
+  logits         one head's logits, [1000, 128] x [34880, 128] bf16, 16-term steps
+  logits_odd     the same with 34883 keys, 8-term steps
 Inputs are seeded and generated on the device; each iteration launches the
 operator once.
 """
@@ -23,7 +26,8 @@ LAYER_ROWS = 8 * 34880
 
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine"])
+    parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
+                                           "project", "logits", "logits_odd"])
     parser.add_argument("--iters", type=int, default=3)
     args = parser.parse_args(argv)
 
@@ -67,6 +71,17 @@ def main(argv=None):
             cumulative = torch.arange(0, LAYER_ROWS + 1, 34880, dtype=torch.int32, device=dev)
             new = torch.randn(1, 8, 1, 128, generator=g, device=dev).to(torch.bfloat16)
             run = lambda: C.append(keys, values, positions, new, new, cumulative, 40000, 34880)
+    elif args.case in ("logits", "logits_odd"):
+        count = 34880 if args.case == "logits" else 34883
+        queries = (torch.randn(1000, 128, generator=g, device=dev) * 2).to(torch.bfloat16)
+        keys = torch.randn(count, 128, generator=g, device=dev).to(torch.bfloat16)
+        step = 16 if args.case == "logits" else 8
+        run = lambda: C.logits(queries, keys, step, (count + 7) // 8 * 8)
+    elif args.case == "project":
+        values = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
+        gradients = torch.randn(8 * 4, 128, generator=g, device=dev)
+        cumulative = torch.arange(0, LAYER_ROWS + 1, 34880, dtype=torch.int32, device=dev)
+        run = lambda: C.project_values(values, gradients, cumulative, 4)
     else:
         n = 256 * 1962
         raw = torch.rand(n, generator=g, device=dev)

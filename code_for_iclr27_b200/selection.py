@@ -59,13 +59,17 @@ class ArrayReferences(Sequence):
         return KVReference(float(self.scores[index]), int(layer), int(head), int(self.positions[index]))
 
     def groups(self):
-        """(layer, head) -> ascending positions queued for that head."""
+        """(layer, head) -> ascending positions queued for that head, in
+        ascending segment order."""
         result = {}
         if not len(self):
             return result
-        for segment in np.unique(self.segments):
+        order = np.lexsort((self.positions, self.segments))
+        segments, positions = self.segments[order], self.positions[order]
+        cuts = np.flatnonzero(segments[1:] != segments[:-1]) + 1
+        for segment, part in zip(segments[np.concatenate(([0], cuts))].tolist(), np.split(positions, cuts)):
             layer, head = self.coordinates[segment]
-            result[(int(layer), int(head))] = np.sort(self.positions[self.segments == segment])
+            result[(int(layer), int(head))] = part
         return result
 
 
@@ -94,13 +98,14 @@ def refine_arrays(allocation, refinement, count, references_type=None):
     if not raw.is_cuda:
         raise RuntimeError("refine_arrays runs on CUDA score tables only")
     device = raw.device
-    ends_device = torch.as_tensor(ends, device=device)
-    position_starts = torch.as_tensor([segment.position_start for segment in allocation.segments],
-                                      dtype=torch.int64, device=device)
+    host = np.stack([ends, np.asarray([segment.position_start for segment in allocation.segments], dtype=np.int64)])
+    ends_device, position_starts = torch.as_tensor(host).to(device, non_blocking=True)
     values, segment_ids, positions, stats = operators().refine(
         raw.float().contiguous(), refinement.scores.float().contiguous(), ends_device, position_starts, count)
-    packed = torch.cat([segment_ids, positions, stats]).cpu().numpy()
-    values = values.cpu().numpy()
+    # One device-to-host copy: ids, positions, the two counters, score bits.
+    bits = values.float().contiguous().view(torch.int32).to(torch.int64)
+    packed = torch.cat([segment_ids, positions, stats, bits]).cpu().numpy()
+    values = (packed[2 * count + 2:] & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
     changed, changed_heads = int(packed[2 * count]), int(packed[2 * count + 1])
     return make(values, packed[:count], packed[count:2 * count], coordinates), changed, changed_heads
 

@@ -98,6 +98,7 @@ typedef struct lrk_score_segment {
   int64_t last;
   float *scores;                   /* [last - first] output */
   int64_t logits_stride;           /* elements between consecutive (query, group) rows of logits (>= length) */
+  int64_t query_chunk;             /* queries per chunk of the running maximum; 0: one chunk of all queries */
 } lrk_score_segment;
 
 /* Workspace bytes for lrk_temporal_scores. */
@@ -107,8 +108,10 @@ size_t lrk_temporal_scores_workspace_bytes(int64_t segments, int64_t window, int
  * queries, straight from logits: the composition temporal_probabilities ->
  * temporal_risk -> running maximum over query chunks that
  * src/lazy_recall/scoring.py:179-195 performs per head, without writing the
- * probabilities.  Many heads per call (segments is a HOST array).  Agrees with
- * the drop-in operators within 1e-5 relative (different summation order).
+ * probabilities.  Many heads per call (segments is a HOST array).  With each
+ * segment's query_chunk set to the composition's chunk size (scoring.py:177-178)
+ * the scores are bit-identical to the composition on the same logits and
+ * projected values.
  * No counterpart operator in the reference (new entry point). */
 int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype,
                         const int64_t *query_positions, int64_t window, int64_t groups, float scale,
@@ -144,8 +147,10 @@ int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count,
  * the packed layer, head(r) the KV head whose segment (cumulative, int32
  * [heads + 1], device) holds r -- each head's rows against its own query
  * heads' margin gradients, the product src/lazy_recall/scoring.py:175 forms
- * per head (float32 accumulation; the order of the 128-term dot product is
- * this kernel's own).  values [rows, dimension] of values_dtype; gradients
+ * per head.  Each dot product is accumulated in channel order with one fused
+ * multiply-add per channel from zero, the order of the float32 GEMM that
+ * torch.matmul runs for that product (equal bit for bit on B200, checked by
+ * the tests).  values [rows, dimension] of values_dtype; gradients
  * [heads * groups, dimension] f32; out [groups, rows] f32.  Reads V once.
  * No counterpart operator in the reference (new entry point). */
 int lrk_project_values(const void *values, int values_dtype, int64_t rows, int64_t dimension,
@@ -158,6 +163,19 @@ int lrk_project_values(const void *values, int values_dtype, int64_t rows, int64
  * in any bit from IEEE round-to-nearest division.  Expected 0.
  * No counterpart in the reference. */
 int lrk_check_division(uint64_t count, uint64_t seed, unsigned long long *mismatches_device, lrk_stream_t stream);
+
+/* bf16 logits out[r, n] = sum_d queries[r, d] * keys[n, d] for r < rows,
+ * n < count, accumulated in float32 as k_step-term tensor-core steps (mma
+ * m16n8k8 for k_step 8, m16n8k16 for 16) in increasing d and rounded to bf16.
+ * torch.matmul's bf16 GEMM (src/lazy_recall/scoring.py:184) takes eight-term
+ * steps for an odd key count and sixteen-term steps otherwise; with the
+ * matching k_step the logits equal its output bit for bit, written as rows of
+ * out_stride elements (a multiple of 8, >= count rounded up to 8) for the
+ * scoring kernels.  queries [rows, dim], keys [count, dim] bf16 row-major,
+ * 16-byte aligned, dim 64 or 128.
+ * No counterpart operator in the reference (new entry point). */
+int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, int64_t k_step,
+               void *out, int64_t out_stride, lrk_stream_t stream);
 
 /* ------------------------------------------------- cache data movement */
 

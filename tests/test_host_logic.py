@@ -1,0 +1,35 @@
+"""Host-side queue logic (no GPU): ArrayReferences.groups and slicing follow
+the reference queue's contract (selection.py, ArrayReferences)."""
+import numpy as np
+
+from code_for_iclr27_b200.selection import ArrayReferences, KVReference
+
+
+def naive_groups(refs):
+    out = {}
+    for segment in sorted(set(refs.segments.tolist())):
+        layer, head = refs.coordinates[segment]
+        out[(int(layer), int(head))] = np.sort(refs.positions[refs.segments == segment])
+    return out
+
+
+def test_groups_matches_per_segment_sort():
+    rng = np.random.default_rng(3)
+    coordinates = [(layer, head) for layer in range(4) for head in range(8)]
+    for n in (0, 1, 7, 512, 2048):
+        segments = rng.integers(0, len(coordinates), n)
+        positions = rng.integers(0, 40000, n)
+        refs = ArrayReferences(rng.random(n, dtype=np.float32), segments, positions, coordinates)
+        got, want = refs.groups(), naive_groups(refs)
+        assert list(got) == list(want)
+        for key in want:
+            np.testing.assert_array_equal(got[key], want[key])
+
+
+def test_slicing_and_items():
+    coordinates = [(0, 0), (0, 1), (3, 2)]
+    refs = ArrayReferences(np.array([0.5, 0.25, 0.125], np.float32), [2, 0, 1], [10, 20, 30], coordinates)
+    assert refs[0] == KVReference(0.5, 3, 2, 10)
+    tail = refs[1:]
+    assert len(tail) == 2 and tail[0] == KVReference(0.25, 0, 0, 20)
+    assert list(tail.groups()) == [(0, 0), (0, 1)]
