@@ -193,6 +193,24 @@ __device__ __forceinline__ float chunk_score(const MarginTerms &t, bool nonfinit
                                  risk64(t.m, t.probability, t.base_softplus, maximum)));
 }
 
+// Order-preserving int image of a float (for float min / max through integer
+// atomics): non-negative floats keep their bits, negative ones flip the
+// magnitude bits, so signed comparison of the images orders the floats.  NaN
+// never reaches it (a non-finite drop is flagged instead).
+__device__ __forceinline__ int ordered_key(float f) {
+  const int bits = __float_as_int(f);
+  return bits >= 0 ? bits : bits ^ 0x7fffffff;
+}
+__device__ __forceinline__ float from_ordered_key(int key) {
+  return __int_as_float(key >= 0 ? key : key ^ 0x7fffffff);
+}
+
+// Query chunks one pass of risk_vec_kernel folds in shared memory, and the
+// candidates of one of its CTAs (16: a layer's ~2k candidates per head give
+// ~1k CTAs, enough to fill every SM).
+constexpr int kRiskChunks = 8;
+constexpr int kRiskTile = 16;
+
 // The running maximum over chunks, torch.maximum's semantics (NaN wins).
 __device__ __forceinline__ float running_max(float a, float b) { return isnan(a) || isnan(b) ? NAN : fmaxf(a, b); }
 
@@ -279,7 +297,7 @@ __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam tabl
 }
 
 // Vectorised risk for 16-bit logits in 16-byte aligned rows.  A CTA covers
-// 64 consecutive candidate columns from a 16-byte boundary; thread (tx, ty)
+// kRiskTile consecutive candidate columns from a 16-byte boundary; thread (tx, ty)
 // owns C consecutive candidates (one C * 2-byte load per logits row, C = 8, 4
 // or 2) and
 // walks queries ty, ty + TY, ..., with the next query's rows loaded while the
@@ -297,12 +315,14 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTablePar
   using P = rows::Packed<T>;
   using Bits = typename D::Bits;
   using Vec = typename std::conditional<C == 8, uint4, typename std::conditional<C == 4, uint2, uint32_t>::type>::type;
-  constexpr int kTile = 64;
-  constexpr int TX = kTile / C, TY = kRiskThreads / TX;
+  constexpr int TX = kRiskTile / C, TY = kRiskThreads / TX;
+  constexpr int kTile = kRiskTile;
   extern __shared__ float4 shared_stats[];  // [window * G] (max, denominator, projection, query position)
   float *reciprocal = reinterpret_cast<float *>(shared_stats + window * G);  // [window * G]
-  __shared__ float part_min[TY][kTile + 1], part_max[TY][kTile + 1];
-  __shared__ unsigned char part_bad[TY][kTile];
+  // Per (chunk of this pass, candidate): order-preserving keys of the drop
+  // range and a non-finite flag, folded with integer atomics (order-free).
+  __shared__ int cell_min[kRiskChunks][kTile], cell_max[kRiskChunks][kTile];
+  __shared__ int cell_bad[kRiskChunks][kTile];
   const lrk_score_segment &seg = table.segment[blockIdx.y];
   const int64_t tile = (seg.first & ~int64_t{7}) + static_cast<int64_t>(blockIdx.x) * kTile;
   if (tile >= seg.last) return;  // the whole CTA: nothing of this segment here
@@ -346,12 +366,21 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTablePar
   };
   const float2 scale2 = make_float2(scale, scale), one2 = make_float2(1.0f, 1.0f);
   const int chunk = chunk_queries(seg, window);
+  const int chunks = (window + chunk - 1) / chunk;
   const bool leader = threadIdx.x < kTile;
-  MarginTerms terms{};
-  if (leader) terms = margin_terms(margin);
   float result = 0.0f;
-  for (int c0 = 0; c0 < window; c0 += chunk) {
-    const int c1 = min(window, c0 + chunk);
+  // Passes of up to kRiskChunks chunks: each thread walks its queries of the
+  // pass, folding its candidates' drop range into the chunk's cells whenever
+  // it leaves a chunk; one barrier, then the leaders score the pass's chunks.
+  for (int c_first = 0; c_first < chunks; c_first += kRiskChunks) {
+    const int c_last = min(chunks, c_first + kRiskChunks);
+    for (int i = threadIdx.x; i < (c_last - c_first) * kTile; i += kRiskThreads) {
+      cell_min[i / kTile][i % kTile] = ordered_key(INFINITY);
+      cell_max[i / kTile][i % kTile] = ordered_key(-INFINITY);
+      cell_bad[i / kTile][i % kTile] = 0;
+    }
+    __syncthreads();
+    const int q_begin = c_first * chunk, q_end = min(window, c_last * chunk);
     float lo[C], hi[C];
     uint32_t bad = 0;
 #pragma unroll
@@ -359,15 +388,36 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTablePar
       lo[j] = INFINITY;
       hi[j] = -INFINITY;
     }
-    Vec current[G], next[G];
-    if (c0 + ty < c1) {
+    auto flush = [&](int c) {
 #pragma unroll
-      for (int g = 0; g < G; ++g) current[g] = load(c0 + ty, g);
+      for (int j = 0; j < C; ++j) {
+        atomicMin(&cell_min[c - c_first][tx * C + j], ordered_key(lo[j]));
+        atomicMax(&cell_max[c - c_first][tx * C + j], ordered_key(hi[j]));
+        lo[j] = INFINITY;
+        hi[j] = -INFINITY;
+      }
+      if (bad) {
+#pragma unroll
+        for (int j = 0; j < C; ++j)
+          if ((bad >> j) & 1u) cell_bad[c - c_first][tx * C + j] = 1;
+      }
+      bad = 0;
+    };
+    int current_chunk = -1;
+    Vec current[G], next[G];
+    if (q_begin + ty < q_end) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) current[g] = load(q_begin + ty, g);
     }
-    for (int q = c0 + ty; q < c1; q += TY) {
-      if (q + TY < c1) {
+    for (int q = q_begin + ty; q < q_end; q += TY) {
+      if (q + TY < q_end) {
 #pragma unroll
         for (int g = 0; g < G; ++g) next[g] = load(q + TY, g);
+      }
+      const int c = q / chunk;
+      if (c != current_chunk) {
+        if (current_chunk >= 0) flush(current_chunk);
+        current_chunk = c;
       }
       const float query_position = shared_stats[q * G].w;
       float drop[C];
@@ -407,25 +457,18 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTablePar
 #pragma unroll
       for (int g = 0; g < G; ++g) current[g] = next[g];
     }
-#pragma unroll
-    for (int j = 0; j < C; ++j) {
-      part_min[ty][tx * C + j] = lo[j];
-      part_max[ty][tx * C + j] = hi[j];
-      part_bad[ty][tx * C + j] = static_cast<unsigned char>((bad >> j) & 1u);
-    }
+    if (current_chunk >= 0) flush(current_chunk);
     __syncthreads();
     if (leader) {
-      float minimum = INFINITY, maximum = -INFINITY;
-      bool nonfinite = false;
-      for (int y = 0; y < TY; ++y) {
-        minimum = fminf(minimum, part_min[y][threadIdx.x]);
-        maximum = fmaxf(maximum, part_max[y][threadIdx.x]);
-        nonfinite |= part_bad[y][threadIdx.x] != 0;
+      const MarginTerms terms = margin_terms(margin);
+      for (int c = c_first; c < c_last; ++c) {
+        const float score = chunk_score(terms, cell_bad[c - c_first][threadIdx.x] != 0,
+                                        from_ordered_key(cell_min[c - c_first][threadIdx.x]),
+                                        from_ordered_key(cell_max[c - c_first][threadIdx.x]));
+        result = c == 0 ? score : running_max(result, score);
       }
-      const float score = chunk_score(terms, nonfinite, minimum, maximum);
-      result = c0 == 0 ? score : running_max(result, score);
     }
-    __syncthreads();
+    __syncthreads();  // cells free for the next pass
   }
   if (!leader) return;
   const int64_t column = tile + threadIdx.x;
@@ -443,7 +486,7 @@ int launch_risk_vec(const ScoreTableParam &table, int n, const int64_t *qpos, in
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
     if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
-  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_span, 64))), n);
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_span, kRiskTile))), n);
   kernel<<<grid, kRiskThreads, shared, stream>>>(table, qpos, window, scale, stats, s0, margin, epsilon);
   return launch_status("lrk_temporal_scores");
 }
