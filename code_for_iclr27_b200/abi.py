@@ -63,6 +63,7 @@ SIGNATURES = {
     "lrk_project_values": (I32, [P, I32, I64, I64, P, P, I64, I64, P, P]),
     "lrk_check_division": (I32, [ctypes.c_uint64, ctypes.c_uint64, P, P]),
     "lrk_logits": (I32, [P, I64, P, I64, I64, I64, P, I64, P]),
+    "lrk_logits_timeouts": (I32, [P]),
     "lrk_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "lrk_register_host": (I32, [P, SIZE]),
     "lrk_unregister_host": (I32, [P]),

@@ -1,6 +1,7 @@
 """In-tree build of liblrk.so and the three operator modules.
 
-liblrk.so   <- csrc/host.cu, move.cu, score.cu, select.cu, fused.cu, project.cu, logits.cu (nvcc, sm_100a)
+liblrk.so   <- csrc/host.cu, move.cu, score.cu, select.cu, fused.cu, project.cu, logits.cu,
+               logits_tc.cu (nvcc, sm_100a)
 _C          <- csrc/shim_C.cpp        (torch extension, links liblrk)
 _legacy_C   <- csrc/shim_legacy_C.cpp (torch extension, links liblrk)
 _host       <- csrc/shim_host.cpp     (pybind11 only, links liblrk)
@@ -40,6 +41,7 @@ CUDA_SOURCES = {
     "fused.cu": ["--fmad=false"],
     "project.cu": [],
     "logits.cu": [],
+    "logits_tc.cu": [],
 }
 MODULES = {"_C": "shim_C.cpp", "_legacy_C": "shim_legacy_C.cpp", "_host": "shim_host.cpp"}
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"

@@ -205,6 +205,11 @@ __global__ void __launch_bounds__(kThreads, 3) logits_kernel(const __nv_bfloat16
 }  // namespace
 }  // namespace lrk
 
+namespace lrk {
+int launch_logits_tc(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, bool eight,
+                     void *out, int64_t out_stride, cudaStream_t stream);
+}  // namespace lrk
+
 using namespace lrk;
 
 extern "C" int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim,
@@ -218,6 +223,11 @@ extern "C" int lrk_logits(const void *queries, int64_t rows, const void *keys, i
   if (rows == 0 || count == 0) return LRK_OK;
   LRK_REQUIRE(queries && keys && out, "null pointer");
   LRK_REQUIRE(aligned(queries, 16) && aligned(keys, 16) && aligned(out, 16), "logits operands must be 16-byte aligned");
+#ifndef LRK_LOGITS_MMA_SYNC
+  // Tensor-core (tcgen05) path; the mma.sync kernel below is its reference.
+  return launch_logits_tc(queries, rows, keys, count, dim, k_step == 8, out, out_stride,
+                          reinterpret_cast<cudaStream_t>(stream));
+#endif
   decltype(&logits_kernel<8, 128>) kernel = nullptr;
   size_t shared = 0;
   if (dim == 128) {

@@ -177,6 +177,11 @@ int lrk_check_division(uint64_t count, uint64_t seed, unsigned long long *mismat
 int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, int64_t k_step,
                void *out, int64_t out_stride, lrk_stream_t stream);
 
+/* Number of lrk_logits CTAs (since the library loaded, on the current device)
+ * whose bounded wait for their tensor-core steps ran out; 0 in a healthy run.
+ * Synchronous.  No counterpart in the reference. */
+int lrk_logits_timeouts(unsigned int *count);
+
 /* ------------------------------------------------- cache data movement */
 
 /* Append `added` rows to each head segment of a packed layer.

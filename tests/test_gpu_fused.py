@@ -7,6 +7,7 @@ drop-in operators -- which are bit-identical to the reference kernels -- and
 with the oracle within 1e-5 relative.  The absolute floor is 1e-6 of the
 largest score of the call: scores near zero (a drop close to 0) carry the
 absolute, not the relative, error of the probability sums."""
+import ctypes
 import math
 
 import numpy as np
@@ -376,6 +377,11 @@ def test_logits_equal_torch_matmul(C, cuda, rows, count, dim):
     out = C.logits(queries, keys, 8 if count % 2 else 16, stride)
     assert out.shape == (rows, stride)
     assert torch.equal(out[:, :count], torch.matmul(queries, keys.transpose(0, 1)))
+    from code_for_iclr27_b200 import abi
+
+    timeouts = ctypes.c_uint(0)
+    abi.check(abi.library().lrk_logits_timeouts(ctypes.byref(timeouts)))
+    assert timeouts.value == 0
 
 
 @pytest.mark.parametrize("count", [34176, 34178, 34180, 2002, 514])
