@@ -70,6 +70,15 @@ def parse_args():
     return parser.parse_args()
 
 
+def measured_traffic_ratio():
+    """DRAM bytes per fused scoring call over its algorithmic bytes, from the
+    committed ncu summary of one configs[1] layer call (None when absent)."""
+    path = ROOT / "profiles" / "temporal_scores_traffic.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["traffic_over_algorithmic"])
+    return None
+
+
 def measured_peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -452,6 +461,7 @@ def main():
     e2e_value = world * managed * e2e_steps / (float(e2e_ms.item()) / 1e3)
 
     peak, peak_kind = measured_peaks()
+    traffic_ratio = measured_traffic_ratio()
     kernel_ms = timer.total_ms()
     achieved = timer.bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else 0.0
     result = {
@@ -470,7 +480,10 @@ def main():
         "decode_overhead_us": decode_us,
         "roofline": {"kernel": timed_name, "bound": "hbm", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                     "share_of_step": kernel_ms / elapsed_ms, "traffic": None,
+                     "share_of_step": kernel_ms / elapsed_ms,
+                     "traffic": (None if traffic_ratio is None
+                                 else traffic_ratio * timer.bytes / max(1, len(timer.pairs))),
+                     "traffic_source": "profiles/temporal_scores_traffic.json (ncu dram bytes / algorithmic bytes)",
                      "bytes_per_launch": timer.bytes / max(1, len(timer.pairs)), "launches": len(timer.pairs)},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
