@@ -64,6 +64,8 @@ def parse_args():
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--decode-steps", type=int, default=64)
     parser.add_argument("--seed", type=int, default=0)
+    parser.add_argument("--skip-side", action="store_true",
+                        help="skip the configs[2] batch_append and configs[3] recall measurements (N=1 only)")
     parser.add_argument("--scoring", choices=["fused", "dropin"], default="fused",
                         help="fused: lrk_temporal_scores per layer; dropin: the reference's per-head composition of "
                              "temporal_probabilities + temporal_risk")
@@ -489,6 +491,15 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks.summary(),
     }
+    if world == 1 and not args.skip_side:
+        # The other configurations' hot operators, measured on the same GPU.
+        from code_for_iclr27_b200.workloads import measure_batch_append, measure_recall
+
+        del cache, queries, gradients, host_queries, host_gradients
+        torch.cuda.empty_cache()
+        result["batch_append"] = measure_batch_append(device)
+        torch.cuda.empty_cache()
+        result["recall"] = measure_recall(device)
     if distributed:
         dist.barrier()
         dist.destroy_process_group()

@@ -1,0 +1,287 @@
+"""Measured workloads beside the audit pass: recall transport and
+static-batch append.
+
+Each function builds seeded synthetic inputs of the configuration's shape on
+the GPU (and in host memory for recall), times the operators with CUDA events
+on the current stream, and returns a JSON-ready dict.  bench.py adds them to
+its line.
+"""
+from __future__ import annotations
+
+import mmap
+import time
+
+import numpy as np
+
+from . import abi, host_operators, operators
+
+
+def _events():
+    import torch
+
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def _median(values):
+    values = sorted(values)
+    return values[len(values) // 2]
+
+
+def pinned_h2d_peak(device, megabytes: int = 256, repeats: int = 5) -> float:
+    """GB/s of one large contiguous copy from pinned host memory."""
+    import torch
+
+    host = torch.empty(megabytes << 20, dtype=torch.uint8).pin_memory()
+    dest = torch.empty(megabytes << 20, dtype=torch.uint8, device=device)
+    dest.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(repeats):
+        a, b = _events()
+        a.record()
+        dest.copy_(host, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return (megabytes << 20) / (_median(times) / 1e3) / 1e9
+
+
+class _HostPool:
+    """One request's archive: rows of [2, D] bf16 (K, V) in page-aligned host
+    memory registered for the device (the transport's shared-memory slots,
+    recall/transport.py:16-31, archive layout recall/cpu_worker.py:21-22)."""
+
+    def __init__(self, rows: int, dim: int, seed: int):
+        self.rows, self.row_bytes = rows, 2 * dim * 2
+        self.buffer = mmap.mmap(-1, rows * self.row_bytes)
+        self.array = np.frombuffer(self.buffer, dtype=np.uint16).reshape(rows, 2, dim)
+        rng = np.random.default_rng(seed)
+        # bf16 bit patterns of N(0, 1) samples
+        self.array[:] = (rng.standard_normal(self.array.shape, dtype=np.float32).view(np.uint32) >> 16).astype(
+            np.uint16)
+        self.address = self.array.__array_interface__["data"][0]
+        host_operators().register_host(self.address, rows * self.row_bytes)
+        self.device_address = host_operators().device_pointer(self.address)
+
+    def close(self):
+        host_operators().unregister_host(self.address)
+        del self.array
+        self.buffer.close()
+
+
+def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_rows: int = 256, layers: int = 32,
+                   heads: int = 8, dim: int = 128, cache_rows_per_head: int = 2000, events: int = 20,
+                   seed: int = 3) -> dict:
+    """per recall event, `recall_rows` random rows of each
+    request's host pool reach the GPU and are merged into its cache.
+
+    Two transports are timed: the GPU gathering the rows from the registered
+    pool itself (lrk_gather_rows over the host link), and the reference's path
+    (a CPU gather into a pinned staging slot, then one cudaMemcpyAsync,
+    recall/cpu_worker.py:161-166, transport.py:221-229).  A size sweep gives
+    the link rate where it is not latency-bound, against the pinned-copy peak.
+    The merge (_C.merge, one whole-layer copy per touched layer) is timed for
+    rows spread uniformly over (layer, head)."""
+    import torch
+
+    lib = abi.library()
+    C = operators()
+    stream = torch.cuda.current_stream(device).cuda_stream
+    rng = np.random.default_rng(seed)
+    pools = [_HostPool(pool_rows, dim, seed + r) for r in range(requests)]
+    try:
+        row_bytes = pools[0].row_bytes
+        out = torch.empty(requests, recall_rows, 2, dim, dtype=torch.bfloat16, device=device)
+        host_indices = torch.empty(requests, recall_rows, dtype=torch.int64).pin_memory()
+        dev_indices = torch.empty(requests, recall_rows, dtype=torch.int64, device=device)
+        staging = torch.empty(requests, recall_rows, 2, dim, dtype=torch.int16).pin_memory()
+        staged_out = torch.empty(requests, recall_rows, 2, dim, dtype=torch.int16, device=device)
+
+        # Each event's rows, drawn before the timed region (uniform, without replacement).
+        chosen = [np.stack([rng.choice(pool_rows, recall_rows, replace=False) for _ in range(requests)])
+                  for _ in range(events + 1)]
+
+        def zero_copy_event(i):
+            host_indices.numpy()[:] = chosen[i]
+            dev_indices.copy_(host_indices, non_blocking=True)
+            for r, pool in enumerate(pools):
+                abi.check(lib.lrk_gather_rows(pool.device_address, pool_rows, row_bytes,
+                                              dev_indices[r].data_ptr(), recall_rows, out[r].data_ptr(), stream))
+
+        def staged_event(i):
+            for r, pool in enumerate(pools):
+                staging[r].numpy()[:] = pool.array[chosen[i][r]].view(np.int16)
+            staged_out.copy_(staging, non_blocking=True)
+
+        results = {}
+        for name, event in (("zero_copy", zero_copy_event), ("staged", staged_event)):
+            event(events)
+            torch.cuda.synchronize()
+            device_times, wall_times = [], []
+            for i in range(events):
+                a, b = _events()
+                start = time.perf_counter()
+                a.record()
+                event(i)
+                b.record()
+                torch.cuda.synchronize()
+                wall_times.append((time.perf_counter() - start) * 1e3)
+                device_times.append(a.elapsed_time(b))
+            results[name] = {"event_us": _median(wall_times) * 1e3, "device_us": _median(device_times) * 1e3}
+
+        # Size sweep: zero-copy gather of random rows vs one contiguous pinned copy.
+        peak = pinned_h2d_peak(device)
+        sweep = []
+        for size in (128 << 10, 512 << 10, 2 << 20, 8 << 20, 32 << 20):
+            rows = size // row_bytes
+            picks = torch.from_numpy(rng.choice(pool_rows, rows, replace=False)).to(device)
+            dest = torch.empty(rows, 2, dim, dtype=torch.bfloat16, device=device)
+            contiguous = torch.empty(size, dtype=torch.uint8).pin_memory()
+            contiguous_dest = torch.empty(size, dtype=torch.uint8, device=device)
+
+            def gather():
+                abi.check(lib.lrk_gather_rows(pools[0].device_address, pool_rows, row_bytes, picks.data_ptr(), rows,
+                                              dest.data_ptr(), stream))
+
+            def copy():
+                contiguous_dest.copy_(contiguous, non_blocking=True)
+
+            entry = {"bytes": size}
+            for label, fn in (("zero_copy_gather_GBps", gather), ("pinned_copy_GBps", copy)):
+                fn()
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(10):
+                    a, b = _events()
+                    a.record()
+                    fn()
+                    b.record()
+                    torch.cuda.synchronize()
+                    times.append(a.elapsed_time(b))
+                entry[label] = size / (_median(times) / 1e3) / 1e9
+            sweep.append(entry)
+
+        # Merge: each request's recalled rows into its cache, rows spread over
+        # (layer, head); one whole-layer copy per touched layer.
+        g = torch.Generator(device=device).manual_seed(seed)
+        layer_rows = heads * cache_rows_per_head
+        merge_us = []
+        merged_bytes = 0
+        keys = torch.randn(layer_rows, dim, generator=g, device=device).to(torch.bfloat16)
+        values = torch.randn(layer_rows, dim, generator=g, device=device).to(torch.bfloat16)
+        positions = torch.arange(layer_rows, dtype=torch.float32, device=device).reshape(-1, 1) * 4
+        owners = rng.integers(0, layers * heads, recall_rows)
+        plans = []
+        for layer in range(layers):
+            mine = np.flatnonzero(owners // heads == layer)
+            if not mine.size:
+                continue
+            head_of = owners[mine] % heads
+            mapping = []
+            for h in range(heads):
+                existing = np.arange(h * cache_rows_per_head, (h + 1) * cache_rows_per_head)
+                recalled = np.flatnonzero(head_of == h)
+                # recalled positions fall between existing ones (odd multiples of 2)
+                new_pos = rng.choice(cache_rows_per_head, recalled.size, replace=False) * 4 + 2
+                order = np.argsort(np.concatenate([existing * 4, h * cache_rows_per_head * 4 + new_pos]),
+                                   kind="stable")
+                entries = np.concatenate([existing, -(mine[recalled] + 1)])
+                mapping.append(entries[order])
+            plans.append((torch.from_numpy(np.concatenate(mapping)).to(device), mine.size))
+        recalled_rows = out[0].contiguous()
+        recalled_positions = torch.arange(recall_rows, dtype=torch.float32, device=device) * 4 + 2
+        for _ in range(3):
+            for mapping, _count in plans:
+                C.merge(keys, values, positions, recalled_rows, recalled_positions, mapping)
+        torch.cuda.synchronize()
+        for _ in range(events):
+            a, b = _events()
+            a.record()
+            for mapping, _count in plans:
+                C.merge(keys, values, positions, recalled_rows, recalled_positions, mapping)
+            b.record()
+            torch.cuda.synchronize()
+            merge_us.append(a.elapsed_time(b) * 1e3)
+        for mapping, count in plans:
+            merged_bytes += 2 * (layer_rows + count) * (4 * dim + 4)
+        merge = _median(merge_us)
+
+        link_bytes = requests * recall_rows * (4 * dim + 8)  # K, V rows + the int64 index
+        zero_copy_us = results["zero_copy"]["device_us"]
+        return {
+            "config": f"configs[3]: {requests} requests, host pools of {pool_rows} rows x [2, {dim}] bf16, "
+                      f"{recall_rows} random rows each per event; cache {cache_rows_per_head} rows/head, "
+                      f"{layers} layers x {heads} heads",
+            "pinned_h2d_peak_GBps": peak,
+            "event_zero_copy_us": zero_copy_us,
+            "event_zero_copy_link_GBps": link_bytes / (zero_copy_us / 1e6) / 1e9,
+            "event_staged_us": results["staged"]["event_us"],
+            "event_staged_device_us": results["staged"]["device_us"],
+            "sweep": sweep,
+            "sweep_frac_of_peak_at_32MiB": sweep[-1]["zero_copy_gather_GBps"] / peak,
+            "merge_us_per_request_event": merge,
+            "merge_GBps": merged_bytes / (merge / 1e6) / 1e9,
+        }
+    finally:
+        for pool in pools:
+            pool.close()
+
+
+def measure_batch_append(device, requests: int = 8, layers: int = 32, heads: int = 8, dim: int = 128,
+                         generated: int = 2000, steps: int = 10, seed: int = 2) -> dict:
+    """one decode step of a static batch appends one token per
+    request per layer through _C.batch_append (batch_attention.py:41-64);
+    prompt lengths uniform in [1024, 16384]."""
+    import torch
+
+    C = operators()
+    rng = np.random.default_rng(seed)
+    g = torch.Generator(device=device).manual_seed(seed)
+    prompts = rng.integers(1024, 16385, requests)
+    lengths = [[int(p) + generated] * heads for p in prompts]
+    caches = []
+    for _ in range(layers):
+        ks, vs, ps = [], [], []
+        for r in range(requests):
+            rows = sum(lengths[r])
+            ks.append(torch.randn(rows, dim, generator=g, device=device).to(torch.bfloat16))
+            vs.append(torch.randn(rows, dim, generator=g, device=device).to(torch.bfloat16))
+            ps.append(torch.arange(rows, dtype=torch.float32, device=device).reshape(-1, 1))
+        caches.append([ks, vs, ps])
+    new = torch.randn(requests, heads, 1, dim, generator=g, device=device).to(torch.bfloat16)
+    logical = [int(p) + generated for p in prompts]
+    total_rows = sum(sum(x) for x in lengths)
+
+    def step():
+        nonlocal lengths
+        for layer in range(layers):
+            ks, vs, ps = caches[layer]
+            k, v, p = C.batch_append(ks, vs, ps, new, new, lengths, logical)
+            # the caller keeps per-request views of the packed output (batch_attention.py:54-63)
+            offsets = np.concatenate(([0], np.cumsum([sum(x) + heads for x in lengths])))
+            caches[layer] = [[k[offsets[r]:offsets[r + 1]] for r in range(requests)],
+                             [v[offsets[r]:offsets[r + 1]] for r in range(requests)],
+                             [p[offsets[r]:offsets[r + 1]] for r in range(requests)]]
+        lengths = [[n + 1 for n in row] for row in lengths]
+
+    step()
+    torch.cuda.synchronize()
+    times = []
+    moved = 0
+    for _ in range(steps):
+        rows_before = sum(sum(x) for x in lengths)
+        a, b = _events()
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+        moved = layers * (rows_before + (rows_before + requests * heads)) * (4 * dim + 4)
+    us = _median(times)
+    return {
+        "config": f"configs[2]: {requests} requests, prompts U[1024, 16384] + {generated} generated rows per head, "
+                  f"{layers} layers x {heads} heads x D{dim}",
+        "rows_per_layer": total_rows,
+        "us_per_step": us,
+        "GBps": moved / (us / 1e6) / 1e9,
+    }
