@@ -88,15 +88,29 @@ __global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTab
 // One CTA per (segment, query, group) row: its exact statistics (rows.cuh).
 // stats[(segment * window + query) * groups + group] = (max, denominator, projection).
 // visible may be null (every row compares key positions).
+//
+// CTAs start in grid order (x, then y), so the CTA of flattened row g asks L2
+// for the row `ahead` places later (a whole row, one bulk prefetch, when the
+// rows are 16-byte aligned): its pass A then reads from L2.
 template <typename T, int MODE>
 __global__ void __launch_bounds__(rows::kLanes, 3) stats_kernel(ScoreTableParam table, const int64_t *__restrict__ qpos,
                                                              int groups, float scale, float3 *__restrict__ stats,
                                                              const int32_t *__restrict__ visible,
-                                                             int64_t segment_base, int64_t rows_per_segment) {
+                                                             int64_t segment_base, int64_t rows_per_segment,
+                                                             int64_t ahead) {
   extern __shared__ __align__(16) unsigned char stage[];
   __shared__ float scratch[rows::kLanes];
   const int64_t row = blockIdx.x;
   const int si = blockIdx.y;
+  if (MODE == rows::kPacked && threadIdx.x == 0 && ahead > 0) {
+    const int64_t later = si * rows_per_segment + row + ahead;
+    if (later < rows_per_segment * gridDim.y) {
+      const lrk_score_segment &next = table.segment[later / rows_per_segment];
+      const T *start = static_cast<const T *>(next.logits) + (later % rows_per_segment) * next.logits_stride;
+      const uint32_t bytes = static_cast<uint32_t>(lmin(next.length * static_cast<int64_t>(sizeof(T)), INT32_MAX)) & ~15u;
+      if (bytes > 0) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(start), "r"(bytes) : "memory");
+    }
+  }
   const lrk_score_segment &seg = table.segment[si];
   const int group = static_cast<int>(row % groups);
   const int64_t query = row / groups;
@@ -143,20 +157,22 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
   if (mode == rows::kWeights) {
     if ((status = allow_shared(stats_kernel<T, rows::kWeights>, bytes)) != LRK_OK) return status;
     stats_kernel<T, rows::kWeights><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
-                                                                           visible, s0, rows_per_segment);
+                                                                           visible, s0, rows_per_segment, 0);
   } else if (mode == rows::kBits) {
     if ((status = allow_shared(stats_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
     stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, visible,
-                                                                        s0, rows_per_segment);
+                                                                        s0, rows_per_segment, 0);
   } else if (mode == rows::kPacked) {
     if constexpr (sizeof(T) == 2) {
       if ((status = allow_shared(stats_kernel<T, rows::kPacked>, bytes)) != LRK_OK) return status;
+      // Two waves of 3 CTAs per SM ahead.
+      const int64_t ahead = 6 * static_cast<int64_t>(sm_count());
       stats_kernel<T, rows::kPacked><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
-                                                                            visible, s0, rows_per_segment);
+                                                                            visible, s0, rows_per_segment, ahead);
     }
   } else {
     stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, visible,
-                                                                      s0, rows_per_segment);
+                                                                      s0, rows_per_segment, 0);
   }
   return launch_status("lrk_temporal_scores statistics");
 }

@@ -25,10 +25,10 @@
 // tiles; warp-specialised:
 //   warp 8, one thread   TMA loads of key tiles into a ring of stages
 //                        (full/empty mbarriers) and the UMMAs of each tile
-//                        into one of two TMEM accumulators, committed to the
+//                        into one of four TMEM accumulators (all 512 columns), committed to the
 //                        accumulator's and the stage's mbarriers;
-//   warps 0-7            build the query tile once; then two warpgroups, each
-//                        owning one accumulator and draining alternate tiles:
+//   warps 0-7            build the query tile once; then two warpgroups
+//                        draining alternate tiles:
 //                        tcgen05.ld of the warp's 32 TMEM lanes (= query rows),
 //                        release, round to bf16 into the group's 128B-swizzled
 //                        staging tile, TMA store (which clips columns past
@@ -61,7 +61,8 @@ constexpr int kIssuerWarp = kEpilogueWarps;          // warp 8
 constexpr int kThreadsTc = (kEpilogueWarps + 1) * 32;
 constexpr uint32_t kAtom = kRows * 128;       // one 64-element-wide swizzled atom column of 128 rows: 16 KB
 constexpr uint32_t kOutTile = kRows * kKeys * 2;  // one bf16 output tile (two 64-column halves)
-constexpr uint32_t kTmemColumns = 2 * kKeys;  // two fp32 accumulators
+constexpr int kAccumulators = 4;                       // fp32 accumulators in TMEM
+constexpr uint32_t kTmemColumns = kAccumulators * kKeys;
 constexpr uint32_t kWaitPolls = 1u << 26;
 
 template <int DIM, bool EIGHT>
@@ -70,12 +71,12 @@ struct TcLayout {
   static constexpr int kSteps = EIGHT ? kChunks : kChunks / 2;   // UMMA K=16 steps per tile
   static constexpr int kAAtoms = EIGHT ? DIM / 32 : DIM / 64;    // query tile (interleaved for EIGHT)
   static constexpr int kBAtoms = EIGHT ? (kChunks + 6) / 7 : DIM / 64;
-  static constexpr int kStages = EIGHT ? 2 : 3;
+  static constexpr int kStages = EIGHT ? 2 : 4;
   static constexpr uint32_t kOut = 0;                             // 2 staging tiles
   static constexpr uint32_t kA = kOut + 2 * kOutTile;
   static constexpr uint32_t kB = kA + kAAtoms * kAtom;
   static constexpr uint32_t kStage = kBAtoms * kAtom;
-  static constexpr uint32_t kBarriers = kB + kStages * kStage;   // full[S] empty[S] acc_full[2] acc_empty[2]
+  static constexpr uint32_t kBarriers = kB + kStages * kStage;   // full[S] empty[S] acc_full[4] acc_empty[4]
   static constexpr uint32_t kTmemSlot = kBarriers + 128;
   static constexpr uint32_t kAbort = kTmemSlot + 8;
   static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;       // + alignment slack
@@ -188,8 +189,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   auto full = [&](int s) { return bar + 8 * s; };
   auto empty = [&](int s) { return bar + 8 * (S + s); };
   auto acc_full = [&](int a) { return bar + 8 * (2 * S + a); };
-  auto acc_empty = [&](int a) { return bar + 8 * (2 * S + 2 + a); };
+  auto acc_empty = [&](int a) { return bar + 8 * (2 * S + kAccumulators + a); };
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbort);
+  // The CTAs of the query tiles that share a key range start at different
+  // tiles of it, so they do not all ask L2 for the same key tile at once.
+  const int rotation = tiles > 1 ? static_cast<int>((blockIdx.y * static_cast<int64_t>(tiles)) / gridDim.y) % tiles : 0;
+  auto rotated = [&](int t) { return (t + rotation) % tiles; };
 
   if (warp < kEpilogueWarps) {
     // The query tile, swizzled; for EIGHT each 8-element chunk j is followed
@@ -213,7 +218,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(full(s)) : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(empty(s)) : "memory");
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < kAccumulators; ++a) {
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(acc_full(a)) : "memory");
       asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;\n" ::"r"(acc_empty(a)) : "memory");
     }
@@ -236,7 +241,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       // ------------------------------------------- TMA loads + MMA issue
       auto load_tile = [&](int t, int s) {
         expect_bytes(full(s), L::kStage);
-        const int y = static_cast<int>((t_begin + t) * kKeys);
+        const int y = static_cast<int>((t_begin + rotated(t)) * kKeys);
         const uint32_t dst = base + L::kB + s * L::kStage;
 #pragma unroll
         for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &key_map, (EIGHT ? 7 * b : 8 * b) * 8, y, full(s));
@@ -246,9 +251,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       int issued = 0;  // tiles whose MMAs were issued
       bool ok = true;
       for (int t = 0; t < tiles; ++t) {
-        const int s = t % S, a = t & 1;
+        const int s = t % S, a = t % kAccumulators;
         if (!wait_phase(full(s), (t / S) & 1, abort)) { ok = false; break; }
-        if (t >= 2 && !wait_phase(acc_empty(a), ((t >> 1) - 1) & 1, abort)) { ok = false; break; }
+        if (t >= kAccumulators && !wait_phase(acc_empty(a), ((t / kAccumulators) - 1) & 1, abort)) {
+          ok = false;
+          break;
+        }
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
         const uint32_t A = base + L::kA, B = base + L::kB + s * L::kStage;
         const uint32_t d = tmem + a * kKeys;
@@ -277,13 +285,14 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       for (int t = issued > S ? issued - S : 0; t < issued; ++t) wait_phase(empty(t % S), (t / S) & 1, nullptr);
       if (!ok) {
         for (int t = issued; t < loaded; ++t) wait_phase(full(t % S), (t / S) & 1, nullptr);
-        for (int t = issued > 2 ? issued - 2 : 0; t < issued; ++t) wait_phase(acc_full(t & 1), (t >> 1) & 1, nullptr);
+        for (int t = issued > kAccumulators ? issued - kAccumulators : 0; t < issued; ++t)
+          wait_phase(acc_full(t % kAccumulators), (t / kAccumulators) & 1, nullptr);
         *abort = 1;
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warpgroup g drains the tiles t = g, g + 2, ... from accumulator g.
+    // Warpgroup g drains the tiles t = g, g + 2, ... (accumulator t % 4).
     // Thread = query row r (its TMEM lane).  Each 64-column half of the bf16
     // tile is staged as 128 rows x 128 B with 128B swizzling (16-byte chunk c
     // of row r at chunk c ^ (r % 8): a quarter-warp's 8 rows hit 8 distinct
@@ -294,10 +303,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     const bool issuer = (threadIdx.x & 127) == 0;
     const uint32_t stage_out = base + L::kOut + group * kOutTile;
     for (int t = group; t < tiles; t += kEpilogueGroups) {
-      const int a = group;
+      const int a = t % kAccumulators;
       // The group's 128 threads leave together or not at all (they meet in
       // named barriers below): AND of every thread's wait.
-      const uint32_t got = wait_phase(acc_full(a), (t >> 1) & 1, abort) ? 1u : 0u;
+      const uint32_t got = wait_phase(acc_full(a), (t / kAccumulators) & 1, abort) ? 1u : 0u;
       uint32_t all_got;
       asm volatile(
           "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
@@ -316,7 +325,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
       __syncwarp();
-      if (lane == 0) arrive(acc_empty(a));  // the accumulator is free for tile t + 2
+      if (lane == 0) arrive(acc_empty(a));  // the accumulator is free for tile t + kAccumulators
       // The group's previous store has read the staging tile.
       if (issuer && t >= kEpilogueGroups) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
       asm volatile("bar.sync %0, 128;\n" ::"r"(named) : "memory");
@@ -339,7 +348,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staging -> TMA store reads
       asm volatile("bar.sync %0, 128;\n" ::"r"(named) : "memory");
       if (issuer) {
-        const int x = static_cast<int>((t_begin + t) * kKeys), y = static_cast<int>(m0);
+        const int x = static_cast<int>((t_begin + rotated(t)) * kKeys), y = static_cast<int>(m0);
 #pragma unroll
         for (int half = 0; half < 2; ++half)
           asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(

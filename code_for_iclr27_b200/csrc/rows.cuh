@@ -356,6 +356,11 @@ template <> struct Packed<__nv_bfloat16> {
                                      *reinterpret_cast<const __nv_bfloat162 *>(&b));
     return *reinterpret_cast<const uint32_t *>(&r);
   }
+  static __device__ __forceinline__ uint32_t min_nan(uint32_t a, uint32_t b) {  // NaN wins
+    const __nv_bfloat162 r = __hmin2_nan(*reinterpret_cast<const __nv_bfloat162 *>(&a),
+                                         *reinterpret_cast<const __nv_bfloat162 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
 };
 template <> struct Packed<__half> {
   static constexpr uint32_t kMinusInfinity = 0xfc00fc00u;
@@ -368,6 +373,10 @@ template <> struct Packed<__half> {
   }
   static __device__ __forceinline__ uint32_t max(uint32_t a, uint32_t b) {
     const __half2 r = __hmax2(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
+    return *reinterpret_cast<const uint32_t *>(&r);
+  }
+  static __device__ __forceinline__ uint32_t min_nan(uint32_t a, uint32_t b) {  // NaN wins
+    const __half2 r = __hmin2_nan(*reinterpret_cast<const __half2 *>(&a), *reinterpret_cast<const __half2 *>(&b));
     return *reinterpret_cast<const uint32_t *>(&r);
   }
 };
@@ -384,6 +393,20 @@ __device__ __forceinline__ float2 divide2(const Divider &d, float2 a) {
   if (!fast) q = make_float2(__fdiv_rn(a.x, d.b), __fdiv_rn(a.y, d.b));
   return q;
 }
+
+// divide2 without the operand test, for callers that have established it:
+// d.fast and both numerators in [2^-60, 2^32].
+__device__ __forceinline__ float2 divide2_fast(const Divider &d, float2 a) {
+  const float2 y = make_float2(d.y, d.y), minus_b = make_float2(-d.b, -d.b);
+  float2 q = mul2_rn(a, y);
+  q = fma2_rn(fma2_rn(q, minus_b, a), y, q);
+  return fma2_rn(fma2_rn(q, minus_b, a), y, q);
+}
+
+// Lowest x - max that keeps expf(x - max) inside divide's fast range:
+// expf(-41) = 1.6e-18 > 2^-60 (with room for expf's error), and x <= max
+// bounds the weight by 1 from above.
+constexpr float kFastExponentFloor = -41.0f;
 
 // Word i of a 16-byte vector (i a compile-time constant after unrolling, so
 // the vector stays in registers).
@@ -512,10 +535,18 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
       for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
     }
     const uint4 chunk = chunks[kb * kLanes + slot];
+    // One operand test for the chunk's 8 divisions: its smallest x (NaN if
+    // any is NaN) minus max at or above kFastExponentFloor puts every weight
+    // in [2^-60, 1] (x - max rounds monotonically in x, and x <= max).
+    const uint32_t lowest = P::min_nan(P::min_nan(word(chunk, 0), word(chunk, 1)),
+                                       P::min_nan(word(chunk, 2), word(chunk, 3)));
+    const float2 lowest_d = add2_rn(P::unpack(lowest), minus_max);
+    const bool fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
-      const float2 probability = divide2(divider, make_float2(expf(d.x), expf(d.y)));
+      const float2 w = make_float2(expf(d.x), expf(d.y));
+      const float2 probability = fast ? divide2_fast(divider, w) : make_float2(divide(divider, w.x), divide(divider, w.y));
       if (probabilities_out != nullptr) {
         float *out = probabilities_out + threadIdx.x + (kb * 8 + 2 * v) * kLanes;
         __stcs(out, probability.x);

@@ -197,6 +197,33 @@ def test_fused_many_segments_strided_and_masked(C, cuda):
     assert torch.isnan(fused).all()
 
 
+def test_fused_long_aligned_segments_of_unequal_length(C, cuda):
+    """Segments of 16-byte aligned rows past the fp32-weight stage: the
+    persistent statistics kernel walks rows of every segment in one launch,
+    with k-blocks inside and past its tensor-memory weight cache (16 blocks
+    of 2048 keys), ragged tails, and segments shorter than the cache."""
+    import torch
+
+    g = torch.Generator().manual_seed(31)
+    lengths = [20008, 36864, 34824, 41000, 18440]
+    logits, pvs, kpos, firsts, lasts = [], [], [], [], []
+    window, groups = 11, 4
+    for length in lengths:
+        lg, pv, kp, _ = make_head(g, cuda, window, groups, length, torch.bfloat16)
+        logits.append(lg)
+        pvs.append(pv)
+        kpos.append(kp)
+        firsts.append(length // 3)
+        lasts.append(length - 32)
+    qpos = torch.arange(window, dtype=torch.int64, device=cuda) + max(lengths) - window - 5000
+    margin = torch.tensor([0.8], device=cuda)
+    fused = C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, 0.125, 1e-6, [4] * len(lengths))
+    expected = torch.cat([dropin_scores(C, lg, pv, kp, qpos, margin, f, l, 0.125, chunk=4)
+                          for lg, pv, kp, f, l in zip(logits, pvs, kpos, firsts, lasts)])
+    assert torch.equal(torch.isnan(fused), torch.isnan(expected))
+    assert torch.equal(torch.nan_to_num(fused), torch.nan_to_num(expected))
+
+
 def test_fused_through_c_abi(cuda):
     import torch
 
