@@ -18,7 +18,7 @@ from typing import List
 import numpy as np
 
 from . import operators
-from .selection import ArrayReferences, refine_arrays
+from .selection import ArrayReferences, fetch_references, refine_arrays, refine_device
 
 
 @dataclass(frozen=True)
@@ -234,11 +234,19 @@ def audit_pass(cache, queries, query_positions, gradients, base_margin, immediat
         table = score_table(cache, queries, query_positions, gradients, base_margin, protect_recent,
                             denominator_epsilon, query_chunk_size)
     pooled = pool_table(table, pool_kernel)
-    references, changed, changed_heads = refine_arrays(table, pooled, immediate + queued)
-    if len(references) < immediate:
+    # The segment table is built while the device is still scoring.
+    segments = cache.segment_table([(segment.layer, segment.head) for segment in table.segments])
+    queue = refine_device(table, pooled, immediate + queued)
+    if queue.count < immediate:
         raise RuntimeError("Not enough unprotected candidates to enforce the budget")
-    removals = {key: value for key, value in references[:immediate].groups().items()}
-    evicted = cache.remove_positions(removals) if removals else 0
+    # The queue leaves the device before the compactions are queued and is
+    # unpacked on the host while they run.
+    pending = fetch_references(queue)
+    evicted = 0
+    if immediate:
+        evicted = cache.remove_selected(queue.coordinates, queue.segment_ids[:immediate],
+                                        queue.positions[:immediate], segments)
+    references, changed, changed_heads = pending.result()
     return AuditResult(table, references, changed, changed_heads, evicted)
 
 

@@ -138,6 +138,27 @@ std::vector<torch::Tensor> compact(torch::Tensor keys, torch::Tensor values, tor
   return {output_keys, output_values, output_positions};
 }
 
+// compact() over several layers in one call: layer i drops the sorted rows
+// removed[offsets[i] : offsets[i + 1]].  The per-layer checks, allocations
+// and launches run here instead of once per layer from Python.
+std::vector<std::vector<torch::Tensor>> compact_layers(std::vector<torch::Tensor> keys,
+                                                       std::vector<torch::Tensor> values,
+                                                       std::vector<torch::Tensor> positions, torch::Tensor removed,
+                                                       std::vector<int64_t> offsets) {
+  const size_t n = keys.size();
+  TORCH_CHECK(values.size() == n && positions.size() == n && offsets.size() == n + 1,
+              "compact_layers: one keys/values/positions tensor per layer and layers + 1 offsets");
+  TORCH_CHECK(removed.scalar_type() == at::kLong && removed.dim() == 1 && removed.is_contiguous(), "Invalid removals");
+  TORCH_CHECK(offsets[0] == 0 && offsets[n] == removed.numel(), "compact_layers: offsets must span the removals");
+  std::vector<std::vector<torch::Tensor>> out(3);
+  for (size_t i = 0; i < n; ++i) {
+    TORCH_CHECK(offsets[i + 1] >= offsets[i], "compact_layers: offsets must not decrease");
+    auto layer = compact(keys[i], values[i], positions[i], removed.narrow(0, offsets[i], offsets[i + 1] - offsets[i]));
+    for (int k = 0; k < 3; ++k) out[k].push_back(layer[k]);
+  }
+  return out;
+}
+
 // csrc/scoring.cu:316-329
 torch::Tensor pool(torch::Tensor scores, torch::Tensor bounds, int64_t maximum_count, int64_t width) {
   check_cuda(scores, scores);
@@ -429,6 +450,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("temporal_risk", &temporal_risk);
   module.def("append", &append);
   module.def("compact", &compact);
+  module.def("compact_layers", &compact_layers);
   module.def("pool", &pool);
   module.def("merge", &merge);
   module.def("pack", &pack);

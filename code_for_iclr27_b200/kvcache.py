@@ -69,6 +69,76 @@ class PackedCache:
         layer.keys, layer.values, layer.positions, layer.cumulative = keys, values, positions, cumulative
         layer.head_lens = [length + added for length in layer.head_lens]
 
+    def segment_table(self, coordinates: Sequence[Tuple[int, int]]):
+        """Per (layer, head) segment, as int64 [4, segments] on the device: the
+        layer, the head's first row in the layer, its prompt rows and its rows."""
+        import torch
+
+        coordinates = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)
+        bounds = {int(l): self.layers[int(l)].bounds() for l in np.unique(coordinates[:, 0])}
+        table = np.empty((4, coordinates.shape[0]), dtype=np.int64)
+        for i, (l, h) in enumerate(coordinates.tolist()):
+            layer = self.layers[l]
+            table[:, i] = (l, bounds[l][h], layer.prompt_lens[h], layer.head_lens[h])
+        return torch.as_tensor(table).to(self.layers[0].keys.device, non_blocking=True)
+
+    def remove_selected(self, coordinates: Sequence[Tuple[int, int]], segment_ids, positions, table=None) -> int:
+        """remove_positions for references that are still on the device:
+        ``segment_ids`` and ``positions`` (int64 CUDA tensors, one entry per
+        reference) index ``coordinates``.  The absolute rows are formed and
+        sorted on the device; only per-segment counts (and two check counters)
+        come back before the compactions are queued, so the device idles for
+        the host bookkeeping alone.  A position outside its head raises
+        IndexError before the cache changes; duplicate references fall back to
+        remove_positions, which counts them once."""
+        import torch
+
+        if segment_ids.numel() == 0:
+            return 0
+        segments = len(coordinates)
+        table = self.segment_table(coordinates) if table is None else table
+        seg, pos = segment_ids.reshape(-1), positions.reshape(-1)
+        layer_of, start, prompt, length = table[0][seg], table[1][seg], table[2][seg], table[3][seg]
+        outside = ((pos < 0) | (pos >= length)).sum()
+        keys = torch.sort(layer_of * (1 << 40) + start + pos).values
+        duplicates = (keys[1:] == keys[:-1]).sum()
+        removed = torch.bincount(seg, minlength=segments)
+        removed_prompt = torch.bincount(seg, weights=(pos < prompt).to(torch.float64), minlength=segments)
+        summary = torch.cat([removed, removed_prompt.to(torch.int64), outside.view(1), duplicates.view(1)])
+        host = torch.empty(summary.shape, dtype=summary.dtype, pin_memory=True)
+        host.copy_(summary, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record()
+        ready.synchronize()
+        counts = host.numpy()
+        if counts[2 * segments]:
+            first = int(torch.nonzero((pos < 0) | (pos >= length))[0, 0])
+            layer_index, head = coordinates[int(seg[first])]
+            raise IndexError(f"Invalid removal in layer={int(layer_index)}, head={int(head)}")
+        if counts[2 * segments + 1]:
+            return self.remove_positions({tuple(coordinates[s]): positions[seg == s].cpu().numpy()
+                                          for s in np.flatnonzero(counts[:segments]).tolist()})
+        per_layer = np.zeros(len(self.layers), dtype=np.int64)
+        for (layer_index, head), count, in_prompt in zip(coordinates, counts[:segments].tolist(),
+                                                        counts[segments:2 * segments].tolist()):
+            if count:
+                self.layers[layer_index].head_lens[head] -= int(count)
+                self.layers[layer_index].prompt_lens[head] -= int(in_prompt)
+                per_layer[layer_index] += count
+        touched = np.flatnonzero(per_layer)
+        offsets = np.concatenate(([0], np.cumsum(per_layer[touched]))).tolist()
+        rows = keys & ((1 << 40) - 1)
+        cumulative = np.stack([self.layers[int(l)].bounds() for l in touched]).astype(np.int32)
+        all_cumulative = torch.as_tensor(cumulative).to(rows.device, non_blocking=True)
+        layers = [self.layers[int(l)] for l in touched]
+        keys_out, values_out, positions_out = operators().compact_layers(
+            [layer.keys for layer in layers], [layer.values for layer in layers],
+            [layer.positions for layer in layers], rows, offsets)
+        for i, layer in enumerate(layers):
+            layer.keys, layer.values, layer.positions = keys_out[i], values_out[i], positions_out[i]
+            layer.cumulative = all_cumulative[i]
+        return int(offsets[-1])
+
     def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
         """Drop head-relative rows (cache.py:92-180, GPU branch): one sorted
         absolute-row list and one _C.compact per touched layer.  Duplicate

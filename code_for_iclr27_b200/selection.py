@@ -78,9 +78,27 @@ def refine_arrays(allocation, refinement, count, references_type=None):
     ``refinement`` are score tables with ``scores`` (1-D float32 CUDA tensor),
     ``segments`` (objects with layer, head, position_start, count) and
     ``cumulative_ends``.  Returns (references, changed, changed_heads)."""
+    return fetch_references(refine_device(allocation, refinement, count), references_type).result()
+
+
+@dataclass
+class DeviceQueue:
+    """refine_arrays' queue before it leaves the device: ``count`` slots of
+    raw-score bits, segment ids and head-local positions (CUDA tensors), the
+    two change counters, and the segment -> (layer, head) coordinates."""
+    values: object
+    segment_ids: object
+    positions: object
+    stats: object
+    count: int
+    coordinates: list
+
+
+def refine_device(allocation, refinement, count) -> DeviceQueue:
+    """refine_arrays up to its device-to-host copy: the same checks, then the
+    _C.refine kernels.  Nothing waits for the device."""
     import torch
 
-    make = references_type or ArrayReferences
     if allocation.segments != refinement.segments or allocation.cumulative_ends != refinement.cumulative_ends:
         raise ValueError("Allocation and refinement layouts differ")
     coordinates = [(segment.layer, segment.head) for segment in allocation.segments]
@@ -88,7 +106,7 @@ def refine_arrays(allocation, refinement, count, references_type=None):
         raise ValueError("Each physical head must have exactly one score segment")
     count = min(max(0, int(count)), allocation.scores.numel())
     if not count:
-        return make([], [], [], coordinates), 0, 0
+        return DeviceQueue(None, None, None, None, 0, coordinates)
     ends = np.asarray(allocation.cumulative_ends, dtype=np.int64)
     starts = np.concatenate(([0], ends[:-1]))
     if ends[-1] != allocation.scores.numel() or any(
@@ -102,12 +120,43 @@ def refine_arrays(allocation, refinement, count, references_type=None):
     ends_device, position_starts = torch.as_tensor(host).to(device, non_blocking=True)
     values, segment_ids, positions, stats = operators().refine(
         raw.float().contiguous(), refinement.scores.float().contiguous(), ends_device, position_starts, count)
-    # One device-to-host copy: ids, positions, the two counters, score bits.
-    bits = values.float().contiguous().view(torch.int32).to(torch.int64)
-    packed = torch.cat([segment_ids, positions, stats, bits]).cpu().numpy()
-    values = (packed[2 * count + 2:] & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
-    changed, changed_heads = int(packed[2 * count]), int(packed[2 * count + 1])
-    return make(values, packed[:count], packed[count:2 * count], coordinates), changed, changed_heads
+    return DeviceQueue(values, segment_ids, positions, stats, count, coordinates)
+
+
+class PendingReferences:
+    """A queue on its way to the host: one asynchronous device-to-host copy
+    into pinned memory (ids, positions, the two counters, score bits) and the
+    event after it.  result() waits for that event only, so work queued on
+    the stream after the copy keeps the device busy meanwhile."""
+
+    def __init__(self, queue: DeviceQueue, references_type=None):
+        import torch
+
+        self.make = references_type or ArrayReferences
+        self.queue = queue
+        if not queue.count:
+            return
+        bits = queue.values.float().contiguous().view(torch.int32).to(torch.int64)
+        packed = torch.cat([queue.segment_ids, queue.positions, queue.stats, bits])
+        self.host = torch.empty(packed.shape, dtype=packed.dtype, pin_memory=True)
+        self.host.copy_(packed, non_blocking=True)
+        self.event = torch.cuda.Event()
+        self.event.record()
+
+    def result(self):
+        queue = self.queue
+        if not queue.count:
+            return self.make([], [], [], queue.coordinates), 0, 0
+        self.event.synchronize()
+        packed, count = self.host.numpy(), queue.count
+        values = (packed[2 * count + 2:] & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+        changed, changed_heads = int(packed[2 * count]), int(packed[2 * count + 1])
+        return (self.make(values, packed[:count].copy(), packed[count:2 * count].copy(), queue.coordinates),
+                changed, changed_heads)
+
+
+def fetch_references(queue: DeviceQueue, references_type=None) -> PendingReferences:
+    return PendingReferences(queue, references_type)
 
 
 def allocation_preserving_references(allocation_table, refinement_table, count, references_type=None):

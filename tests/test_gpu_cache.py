@@ -114,3 +114,100 @@ def test_lazy_eviction_removes_audit_time_identities():
     for l, layer in enumerate(cache.layers):
         remaining = set(layer.positions.cpu().numpy().reshape(-1).tolist())
         assert remaining == expected[l] - gone
+
+
+def assert_same_cache(a, b):
+    for x, y in zip(host_copy(a), host_copy(b)):
+        for u, v in zip(x, y):
+            np.testing.assert_array_equal(np.asarray(u), np.asarray(v))
+    for x, y in zip(a.layers, b.layers):
+        np.testing.assert_array_equal(x.cumulative.cpu().numpy(), y.cumulative.cpu().numpy())
+
+
+def device_references(cache, seed, per_head=17, skip=3):
+    """Distinct (segment, position) references in a shuffled queue order, as
+    int64 CUDA tensors, over the cache's (layer, head) segments (every
+    skip-th segment gets none)."""
+    import torch
+
+    rng = np.random.default_rng(seed)
+    coordinates = [(l, h) for l in range(len(cache.layers)) for h in range(len(cache.layers[0].head_lens))]
+    segments, positions = [], []
+    for s, (l, h) in enumerate(coordinates):
+        if s % skip == 1:
+            continue
+        picks = rng.choice(cache.layers[l].head_lens[h], per_head, replace=False)
+        segments += [s] * picks.size
+        positions += picks.tolist()
+    order = rng.permutation(len(segments))
+    seg = torch.as_tensor(np.asarray(segments)[order]).cuda()
+    pos = torch.as_tensor(np.asarray(positions)[order]).cuda()
+    return coordinates, seg, pos
+
+
+@pytest.mark.parametrize("seed", [4, 5])
+def test_remove_selected_equals_remove_positions(seed):
+    """Device-planned eviction (rows formed, sorted and counted on the device,
+    one multi-layer compaction call) leaves the cache bit-identical to the
+    host-planned remove_positions, prompt rows included."""
+    cache_a, cache_b = make_cache(seed, layers=4, heads=8), make_cache(seed, layers=4, heads=8)
+    coordinates, seg, pos = device_references(cache_a, seed)
+    removals = {}
+    for s, p in zip(seg.cpu().numpy().tolist(), pos.cpu().numpy().tolist()):
+        removals.setdefault(tuple(coordinates[s]), []).append(p)
+    removed_b = cache_b.remove_positions(removals)
+    removed_a = cache_a.remove_selected(coordinates, seg, pos)
+    assert removed_a == removed_b == seg.numel()
+    assert_same_cache(cache_a, cache_b)
+
+
+def test_remove_selected_rejects_out_of_range_and_counts_duplicates_once():
+    import torch
+
+    cache = make_cache(6)
+    before = host_copy(cache)
+    coordinates, seg, pos = device_references(cache, 6, per_head=5)
+    bad = pos.clone()
+    bad[len(bad) // 2] = cache.layers[coordinates[int(seg[len(bad) // 2])][0]].head_lens[
+        coordinates[int(seg[len(bad) // 2])][1]]
+    with pytest.raises(IndexError):
+        cache.remove_selected(coordinates, seg, bad)
+    for a, b in zip(before, host_copy(cache)):
+        for x, y in zip(a, b):
+            np.testing.assert_array_equal(np.asarray(x), np.asarray(y))
+    twin = make_cache(6)
+    doubled_seg, doubled_pos = torch.cat([seg, seg[:4]]), torch.cat([pos, pos[:4]])
+    assert cache.remove_selected(coordinates, doubled_seg, doubled_pos) == seg.numel()
+    twin.remove_selected(coordinates, seg, pos)
+    assert_same_cache(cache, twin)
+
+
+def test_audit_pass_evicts_like_the_host_composition():
+    """audit_pass (device-planned eviction, queue copied back while the
+    compactions run) against refine_arrays + groups + remove_positions on an
+    identical cache: same queue, same counters, same cache afterwards."""
+    import math
+
+    import torch
+
+    from code_for_iclr27_b200.audit import audit_pass, pool_table, score_table_fused
+    from code_for_iclr27_b200.selection import refine_arrays
+
+    caches = [make_cache(7, layers=3, heads=4, dim=64) for _ in range(2)]
+    g = torch.Generator().manual_seed(7)
+    window, groups = 16, 2
+    queries = [(torch.randn(window, 4 * groups, 64, generator=g) * 2).to(torch.bfloat16).cuda() for _ in range(3)]
+    gradients = [(torch.randn(4 * groups, 64, generator=g) / math.sqrt(64)).cuda() for _ in range(3)]
+    top = max(sum(layer.head_lens) for layer in caches[0].layers) * 3 + 10
+    qpos = torch.arange(top - window, top, dtype=torch.int64).cuda()
+    margin = torch.tensor([1.0]).cuda()
+    result = audit_pass(caches[0], queries, qpos, gradients, margin, immediate=40, queued=100, protect_recent=8)
+    table = score_table_fused(caches[1], queries, qpos, gradients, margin, 8)
+    references, changed, changed_heads = refine_arrays(table, pool_table(table, 7), 140)
+    removed = caches[1].remove_positions(references[:40].groups())
+    assert result.evicted == removed == 40
+    assert (result.changed, result.changed_heads) == (changed, changed_heads)
+    np.testing.assert_array_equal(result.references.segments, references.segments)
+    np.testing.assert_array_equal(result.references.positions, references.positions)
+    np.testing.assert_array_equal(result.references.scores.view(np.uint32), references.scores.view(np.uint32))
+    assert_same_cache(caches[0], caches[1])
