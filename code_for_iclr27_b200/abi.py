@@ -37,6 +37,18 @@ class ScoreSegment(ctypes.Structure):
                 ("query_chunk", I64)]
 
 
+class KeyLayer(ctypes.Structure):
+    """lrk_key_layer (include/lrk.h)."""
+    _fields_ = [("keys", P), ("rows", I64)]
+
+
+class KeySegment(ctypes.Structure):
+    """lrk_key_segment (include/lrk.h)."""
+    _fields_ = [("layer", I64), ("queries", P), ("query_stride", I64), ("projected_values", P),
+                ("projected_stride", I64), ("key_positions", P), ("key_row", I64), ("length", I64), ("first", I64),
+                ("last", I64), ("scores", P), ("query_chunk", I64)]
+
+
 SIGNATURES = {
     "lrk_last_error": (ctypes.c_char_p, []),
     "lrk_version": (I32, []),
@@ -64,6 +76,10 @@ SIGNATURES = {
     "lrk_check_division": (I32, [ctypes.c_uint64, ctypes.c_uint64, P, P]),
     "lrk_logits": (I32, [P, I64, P, I64, I64, I64, P, I64, P]),
     "lrk_logits_timeouts": (I32, [P]),
+    "lrk_scores_from_keys_workspace_bytes": (SIZE, [ctypes.POINTER(KeySegment), I64, I64, I64]),
+    "lrk_scores_from_keys": (I32, [ctypes.POINTER(KeySegment), I64, ctypes.POINTER(KeyLayer), I64, P, I64, I64, I64,
+                                   F, P, F, P, SIZE, P]),
+    "lrk_scores_from_keys_timeouts": (I32, [P]),
     "lrk_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "lrk_register_host": (I32, [P, SIZE]),
     "lrk_unregister_host": (I32, [P]),

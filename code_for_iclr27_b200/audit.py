@@ -17,7 +17,7 @@ from typing import List
 
 import numpy as np
 
-from . import operators
+from . import operators, upload
 from .selection import ArrayReferences, fetch_references, refine_arrays, refine_device
 
 
@@ -202,11 +202,70 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
     return ScoreTable(torch.cat(parts), segments, ends)
 
 
+def keys_scoring_supported(cache, queries) -> bool:
+    """score_table_from_keys' shapes: bf16 keys and queries, head dimension
+    64 or 128, at most 8 query heads per KV head, contiguous query blocks."""
+    import torch
+
+    layer = cache.layers[0]
+    heads = len(layer.head_lens)
+    first = queries[0]
+    return (layer.keys.dtype == torch.bfloat16 and layer.keys.shape[-1] in (64, 128) and first.dim() == 3
+            and first.shape[1] % heads == 0 and first.shape[1] // heads <= 8
+            and all(q.dtype == torch.bfloat16 and q.is_contiguous() for q in queries))
+
+
+def score_table_from_keys(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
+                          denominator_epsilon=1e-6, query_chunk_size=250) -> ScoreTable:
+    """compute_score_table with the logits never written: one
+    lrk_project_values call per layer (g V^T, scoring.py:175), then a single
+    lrk_scores_from_keys call for every head of every layer, which runs the
+    bf16 Q K^T GEMM (scoring.py:184, cuBLAS's step order for the head's key
+    count) and the row statistics as one tensor-core kernel and writes only
+    the candidate columns' logits for the risk step.  Bit-identical to
+    score_table_fused and score_table."""
+    import torch
+
+    C = operators()
+    device = cache.layers[0].keys.device
+    margin = base_margin.to(device=device, dtype=torch.float32).reshape(1).contiguous()
+    qpos = query_positions.to(dtype=torch.int64).contiguous()
+    keys, layer_queries, projected, positions = [], [], [], []
+    table, segments, ends, running = [], [], [], 0
+    groups = None
+    for layer_index, layer in enumerate(cache.layers):
+        heads = len(layer.head_lens)
+        groups = queries[layer_index].shape[1] // heads
+        bounds = layer.bounds()
+        keys.append(layer.keys)
+        layer_queries.append(queries[layer_index])
+        positions.append(layer.positions.reshape(-1))
+        projected.append(C.project_values(layer.values, gradients[layer_index].float().contiguous(),
+                                          layer.cumulative, groups))
+        for head in range(heads):
+            start, end = int(bounds[head]), int(bounds[head + 1])
+            candidate_start = int(layer.prompt_lens[head])
+            candidate_end = max(candidate_start, end - start - protect_recent)
+            if candidate_end <= candidate_start:
+                continue
+            chunk = query_chunk(query_chunk_size, groups, end - start, layer.keys.element_size())
+            table.append((layer_index, head, start, end - start, candidate_start, candidate_end, chunk))
+            segments.append(ScoreSegment(layer_index, head, candidate_start, candidate_end - candidate_start))
+            running += candidate_end - candidate_start
+            ends.append(running)
+    if not table:
+        raise RuntimeError("No eligible KV remains after prompt/recent protection")
+    scale = 1.0 / math.sqrt(cache.layers[0].keys.shape[-1])
+    scores = C.scores_from_keys(keys, layer_queries, projected, positions, table, groups, qpos, margin, scale,
+                                denominator_epsilon)
+    return ScoreTable(scores, segments, ends)
+
+
 def pool_table(table: ScoreTable, kernel_size: int = 7) -> ScoreTable:
     """pool_score_table (scoring.py:322-335)."""
     import torch
 
-    bounds = torch.tensor([0] + table.cumulative_ends, dtype=torch.int64, device=table.scores.device)
+    bounds = upload(np.asarray([0] + list(table.cumulative_ends), dtype=np.int64), table.scores.device)
     pooled = operators().pool(table.scores.contiguous(), bounds, max(s.count for s in table.segments), kernel_size)
     return ScoreTable(pooled, list(table.segments), list(table.cumulative_ends))
 
@@ -222,12 +281,17 @@ class AuditResult:
 
 def audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
                protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250, pool_kernel=7,
-               fused=True) -> AuditResult:
+               fused=True, from_keys=False) -> AuditResult:
     """Score, pool, select immediate + queued references, evict the immediate
     prefix.  Returns the queue (references[immediate:] is the lazy queue).
     fused=False scores through the drop-in operators exactly as the reference
-    composes them (bit-identical scores); fused=True uses lrk_temporal_scores."""
-    if fused:
+    composes them; fused=True uses lrk_scores_from_keys (from_keys, where the
+    shapes allow) or lrk_temporal_scores.  All three give the same scores bit
+    for bit."""
+    if fused and from_keys and keys_scoring_supported(cache, queries):
+        table = score_table_from_keys(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                                      denominator_epsilon, query_chunk_size)
+    elif fused:
         table = score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
                                   denominator_epsilon, query_chunk_size)
     else:

@@ -507,59 +507,65 @@ int launch_risk_vec(const ScoreTableParam &table, int n, const int64_t *qpos, in
   return launch_status("lrk_temporal_scores");
 }
 
+// The risk kernels of one table of segments (row statistics already in
+// stats[(s0 + segment) * window * groups + row]).
+template <typename T>
+int launch_risk(const ScoreTableParam &table, int n, const int64_t *qpos, int window, int groups, float scale,
+                const float *margin, float epsilon, const float3 *stats, int64_t s0, cudaStream_t stream) {
+  int64_t max_candidates = 0, max_span = 0;
+  for (int i = 0; i < n; ++i) {
+    max_candidates = std::max<int64_t>(max_candidates, table.segment[i].last - table.segment[i].first);
+    max_span = std::max<int64_t>(max_span, table.segment[i].last - (table.segment[i].first & ~int64_t{7}));
+  }
+  if constexpr (sizeof(T) == 2) {
+    if (rows_aligned<T>(table, n) && window * groups * 20 <= 200 * 1024 &&
+        (groups == 1 || groups == 2 || groups == 4 || groups == 8)) {
+      const auto args = std::make_tuple(table, n, qpos, window, scale, stats, s0, margin, epsilon, max_span, stream);
+      // Candidates per thread: G * C <= 16 keeps the per-thread state near 80 registers.
+      return groups == 1   ? std::apply(launch_risk_vec<T, 1, 8>, args)
+             : groups == 2 ? std::apply(launch_risk_vec<T, 2, 4>, args)
+             : groups == 4 ? std::apply(launch_risk_vec<T, 4, 4>, args)
+                           : std::apply(launch_risk_vec<T, 8, 2>, args);
+    }
+  }
+  const size_t shared = static_cast<size_t>(window) * groups * sizeof(float4);
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, 32))), n);
+  const dim3 block(32, kQueryLanes);
+  if (shared > 48 * 1024) {
+    auto set = [&](auto kernel) {
+      return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
+    };
+    cudaError_t e = groups == 4 ? set(risk_kernel<T, 4>) : groups == 8 ? set(risk_kernel<T, 8>) : set(risk_kernel<T, 0>);
+    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+  }
+  if (groups == 4)
+    risk_kernel<T, 4><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin, epsilon);
+  else if (groups == 8)
+    risk_kernel<T, 8><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin, epsilon);
+  else
+    risk_kernel<T, 0><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin, epsilon);
+  return launch_status("lrk_temporal_scores");
+}
+
+ScoreTableParam make_table(const lrk_score_segment *segments, int64_t s0, int n) {
+  ScoreTableParam table;
+  table.count = n;
+  for (int i = 0; i < n; ++i) table.segment[i] = segments[s0 + i];
+  return table;
+}
+
 template <typename T>
 int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window, int groups,
                   float scale, const float *margin, float epsilon, float3 *stats, int32_t *visible,
                   cudaStream_t stream) {
   for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
     const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
-    ScoreTableParam table;
-    table.count = n;
-    int64_t max_candidates = 0;
-    for (int i = 0; i < n; ++i) {
-      table.segment[i] = segments[s0 + i];
-      max_candidates = std::max<int64_t>(max_candidates, segments[s0 + i].last - segments[s0 + i].first);
-    }
-    int64_t max_length = 0, max_span = 0;
-    for (int i = 0; i < n; ++i) {
-      max_length = std::max<int64_t>(max_length, table.segment[i].length);
-      max_span = std::max<int64_t>(max_span, table.segment[i].last - (table.segment[i].first & ~int64_t{7}));
-    }
+    const ScoreTableParam table = make_table(segments, s0, n);
+    int64_t max_length = 0;
+    for (int i = 0; i < n; ++i) max_length = std::max<int64_t>(max_length, table.segment[i].length);
     int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, stream);
     if (status != LRK_OK) return status;
-    if constexpr (sizeof(T) == 2) {
-      if (rows_aligned<T>(table, n) && window * groups * 20 <= 200 * 1024 &&
-          (groups == 1 || groups == 2 || groups == 4 || groups == 8)) {
-        const auto args = std::make_tuple(table, n, qpos, window, scale, stats, s0, margin, epsilon, max_span, stream);
-        // Candidates per thread: G * C <= 16 keeps the per-thread state near 80 registers.
-        status = groups == 1   ? std::apply(launch_risk_vec<T, 1, 8>, args)
-                 : groups == 2 ? std::apply(launch_risk_vec<T, 2, 4>, args)
-                 : groups == 4 ? std::apply(launch_risk_vec<T, 4, 4>, args)
-                               : std::apply(launch_risk_vec<T, 8, 2>, args);
-        if (status != LRK_OK) return status;
-        continue;
-      }
-    }
-    const size_t shared = static_cast<size_t>(window) * groups * sizeof(float4);
-    const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, 32))), n);
-    const dim3 block(32, kQueryLanes);
-    if (shared > 48 * 1024) {
-      auto set = [&](auto kernel) {
-        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
-      };
-      cudaError_t e = groups == 4 ? set(risk_kernel<T, 4>) : groups == 8 ? set(risk_kernel<T, 8>) : set(risk_kernel<T, 0>);
-      if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-    }
-    if (groups == 4)
-      risk_kernel<T, 4><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
-                                                                 epsilon);
-    else if (groups == 8)
-      risk_kernel<T, 8><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
-                                                                 epsilon);
-    else
-      risk_kernel<T, 0><<<grid, block, shared, stream>>>(table, qpos, window, groups, scale, stats, s0, margin,
-                                                                 epsilon);
-    status = launch_status("lrk_temporal_scores");
+    status = launch_risk<T>(table, n, qpos, window, groups, scale, margin, epsilon, stats, s0, stream);
     if (status != LRK_OK) return status;
   }
   return LRK_OK;
@@ -633,6 +639,29 @@ int dispatch_scores(const lrk_score_segment *segments, int64_t count, int logits
 }
 
 }  // namespace
+
+int score_visibility(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window,
+                     int32_t *visible, cudaStream_t stream) {
+  for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
+    const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
+    visibility_kernel<<<n, kVisibilityThreads, 0, stream>>>(make_table(segments, s0, n), qpos, window, visible, s0);
+    const int status = launch_status("lrk_scores_from_keys visibility");
+    if (status != LRK_OK) return status;
+  }
+  return LRK_OK;
+}
+
+int score_risk_bf16(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window, int groups,
+                    float scale, const float *margin, float epsilon, const float3 *stats, cudaStream_t stream) {
+  for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
+    const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
+    const int status = launch_risk<__nv_bfloat16>(make_table(segments, s0, n), n, qpos, window, groups, scale, margin,
+                                                  epsilon, stats, s0, stream);
+    if (status != LRK_OK) return status;
+  }
+  return LRK_OK;
+}
+
 }  // namespace lrk
 
 using namespace lrk;

@@ -46,6 +46,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace lrk {
 
@@ -53,17 +54,15 @@ __device__ unsigned int g_logits_timeouts = 0;
 
 namespace {
 
-constexpr int kRows = 128;   // UMMA M: query rows per CTA
-constexpr int kKeys = 128;   // UMMA N: keys per tile
+using namespace tc;
+
 constexpr int kEpilogueGroups = 2;                  // warpgroups draining alternate tiles
 constexpr int kEpilogueWarps = 4 * kEpilogueGroups;  // warps 0-7
 constexpr int kIssuerWarp = kEpilogueWarps;          // warp 8
 constexpr int kThreadsTc = (kEpilogueWarps + 1) * 32;
-constexpr uint32_t kAtom = kRows * 128;       // one 64-element-wide swizzled atom column of 128 rows: 16 KB
 constexpr uint32_t kOutTile = kRows * kKeys * 2;  // one bf16 output tile (two 64-column halves)
 constexpr int kAccumulators = 4;                       // fp32 accumulators in TMEM
 constexpr uint32_t kTmemColumns = kAccumulators * kKeys;
-constexpr uint32_t kWaitPolls = 1u << 26;
 
 template <int DIM, bool EIGHT>
 struct TcLayout {
@@ -81,92 +80,6 @@ struct TcLayout {
   static constexpr uint32_t kAbort = kTmemSlot + 8;
   static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;       // + alignment slack
 };
-
-__device__ __forceinline__ uint64_t global_nanoseconds() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bounded wait for the mbarrier phase of the given parity.  False on timeout
-// (after which *abort is raised) or when another role raised *abort.
-__device__ __forceinline__ bool wait_phase(uint32_t barrier, uint32_t parity, volatile int *abort) {
-  const uint64_t start = global_nanoseconds();
-  for (uint32_t i = 0; i < kWaitPolls; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(barrier), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((i & 63) == 63) {
-      if (abort != nullptr && *abort) return false;
-      if (global_nanoseconds() - start > 1000000000ull) break;
-    }
-  }
-  if (abort != nullptr) *abort = 1;
-  return false;
-}
-
-__device__ __forceinline__ void arrive(uint32_t barrier) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(barrier) : "memory");
-}
-
-__device__ __forceinline__ void expect_bytes(uint32_t barrier, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(barrier), "r"(bytes) : "memory");
-}
-
-// TMA: a 64-element x 128-row box at (x, y), 128B-swizzled -> 16 KB.
-__device__ __forceinline__ void tma_box(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t barrier) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(barrier)
-      : "memory");
-}
-
-// UMMA shared-memory descriptor, K-major, 128-byte swizzle: 8-row groups 1024
-// bytes apart (stride), leading offset unused (1), version 1 (bits 46-47),
-// layout SWIZZLE_128B (2, bits 61-63).
-__device__ __forceinline__ uint64_t smem_descriptor(uint32_t address) {
-  return static_cast<uint64_t>((address >> 4) & 0x3FFFu) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) |
-         (1ull << 46) | (2ull << 61);
-}
-
-// kind::f16 instruction descriptor: f32 accumulator, bf16 A and B, both
-// K-major, N = 128, M = 128.
-constexpr uint32_t kInstr = (1u << 4) | (1u << 7) | (1u << 10) | ((kKeys >> 3) << 17) | ((kRows >> 4) << 24);
-
-__device__ __forceinline__ void umma(uint32_t tmem, uint64_t a, uint64_t b, bool accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-      "l"(a), "l"(b), "r"(kInstr), "r"(static_cast<uint32_t>(accumulate))
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t barrier) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(barrier)
-               : "memory");
-}
-
-// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_load32(uint32_t address, uint32_t *v) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(address));
-}
-
-// Byte offset of 16-byte chunk c (0..7) of row r inside a 128B-swizzled atom column.
-__device__ __forceinline__ uint32_t swizzled(int r, int c) {
-  return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
 
 template <int DIM, bool EIGHT>
 __global__ void __launch_bounds__(kThreadsTc, 1)
@@ -369,8 +282,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   }
 }
 
+}  // namespace
+
+namespace tc {
+
 // cuTensorMapEncodeTiled, looked up once through the runtime.
-PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
   static std::once_flag once;
   static PFN_cuTensorMapEncodeTiled_v12000 function = nullptr;
   std::call_once(once, [] {
@@ -404,7 +321,7 @@ int make_map(CUtensorMap *map, const void *data, int64_t rows_total, int64_t col
   return LRK_OK;
 }
 
-}  // namespace
+}  // namespace tc
 
 // Tensor-core logits for dim 64 / 128 (LRK_ERR_UNSUPPORTED otherwise).
 int launch_logits_tc(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, bool eight,
@@ -412,9 +329,9 @@ int launch_logits_tc(const void *queries, int64_t rows, const void *keys, int64_
   if (dim != 64 && dim != 128) return LRK_ERR_UNSUPPORTED;
   if (rows > INT32_MAX || count > INT32_MAX) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many rows");
   CUtensorMap key_map, out_map;
-  int status = make_map(&key_map, keys, count, dim, dim, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  int status = tc::make_map(&key_map, keys, count, dim, dim, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (status != LRK_OK) return status;
-  if ((status = make_map(&out_map, out, rows, count, out_stride, 64, CU_TENSOR_MAP_SWIZZLE_128B)) != LRK_OK)
+  if ((status = tc::make_map(&out_map, out, rows, count, out_stride, 64, CU_TENSOR_MAP_SWIZZLE_128B)) != LRK_OK)
     return status;
   auto launch = [&](auto kernel, uint32_t bytes) -> int {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));

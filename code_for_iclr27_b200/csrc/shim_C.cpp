@@ -4,7 +4,9 @@
 // (csrc/bindings.cpp:20-29), its argument checks and messages (TORCH_CHECK ->
 // RuntimeError), its output allocation (torch::empty on the input's device,
 // through the caching allocator) and its stream (the current CUDA stream).
-// Two operators are added for the selection step: refine and topk_smallest.
+// Added operators: refine and topk_smallest (selection); temporal_scores,
+// scores_from_keys, project_values and logits (scoring); compact_layers
+// (eviction over several layers in one call).
 #include <vector>
 
 #include "shim_common.h"
@@ -443,6 +445,83 @@ torch::Tensor logits(torch::Tensor queries, torch::Tensor keys, int64_t k_step, 
   return out;
 }
 
+// Temporal-risk scores of many heads straight from queries and keys
+// (lrk_scores_from_keys).  Per layer l: keys[l] bf16 [rows, D], queries[l]
+// bf16 [window, heads * groups, D] (query heads of KV head h at h * groups ..),
+// projected[l] f32 [groups, rows] (project_values: each row against its own
+// head's gradients), positions[l] f32 [rows].
+// segments: (layer, head, key_row, length, first, last, query_chunk) per
+// head.  Returns the segments' scores concatenated in segment order.
+torch::Tensor scores_from_keys(std::vector<torch::Tensor> keys, std::vector<torch::Tensor> queries,
+                               std::vector<torch::Tensor> projected, std::vector<torch::Tensor> positions,
+                               std::vector<std::vector<int64_t>> segments, int64_t groups,
+                               torch::Tensor query_positions, torch::Tensor margin, double scale, double epsilon) {
+  const size_t layers = keys.size();
+  TORCH_CHECK(layers > 0 && queries.size() == layers && projected.size() == layers && positions.size() == layers,
+              "scores_from_keys: one keys, queries, projected and positions tensor per layer");
+  TORCH_CHECK(!segments.empty() && groups > 0, "scores_from_keys: no segments");
+  const torch::Tensor &reference = keys[0];
+  check_cuda(query_positions, reference);
+  check_cuda(margin, reference);
+  TORCH_CHECK(query_positions.scalar_type() == at::kLong && margin.scalar_type() == at::kFloat && margin.numel() == 1,
+              "scores_from_keys: int64 query positions and one float32 margin");
+  const int64_t dim = reference.size(1), window = queries[0].size(0);
+  TORCH_CHECK(query_positions.numel() == window, "scores_from_keys: one position per query");
+  std::vector<lrk_key_layer> layer_table(layers);
+  for (size_t l = 0; l < layers; ++l) {
+    for (const auto &t : {keys[l], queries[l], projected[l], positions[l]}) check_cuda(t, reference);
+    TORCH_CHECK(keys[l].dim() == 2 && keys[l].size(1) == dim && keys[l].scalar_type() == at::kBFloat16,
+                "scores_from_keys: bf16 [rows, D] keys");
+    TORCH_CHECK(queries[l].dim() == 3 && queries[l].size(0) == window && queries[l].size(1) % groups == 0 &&
+                    queries[l].size(2) == dim && queries[l].scalar_type() == at::kBFloat16,
+                "scores_from_keys: bf16 [window, heads * groups, D] queries");
+    TORCH_CHECK(projected[l].dim() == 2 && projected[l].size(0) == groups &&
+                    projected[l].size(1) == keys[l].size(0) && projected[l].scalar_type() == at::kFloat,
+                "scores_from_keys: float32 [groups, rows] projected values");
+    TORCH_CHECK(positions[l].numel() == keys[l].size(0) && positions[l].scalar_type() == at::kFloat,
+                "scores_from_keys: float32 positions per key row");
+    layer_table[l] = {keys[l].data_ptr(), keys[l].size(0)};
+  }
+  const int64_t count = static_cast<int64_t>(segments.size());
+  std::vector<lrk_key_segment> table(count);
+  std::vector<int64_t> offsets(count);
+  int64_t total = 0;
+  for (int64_t i = 0; i < count; ++i) {
+    const auto &s = segments[i];
+    TORCH_CHECK(s.size() == 7, "scores_from_keys: segments are (layer, head, key_row, length, first, last, chunk)");
+    const int64_t l = s[0], head = s[1];
+    TORCH_CHECK(l >= 0 && l < static_cast<int64_t>(layers), "scores_from_keys: layer out of range");
+    TORCH_CHECK(head >= 0 && (head + 1) * groups <= queries[l].size(1), "scores_from_keys: head out of range");
+    TORCH_CHECK(s[3] > 0 && s[2] >= 0 && s[2] + s[3] <= keys[l].size(0), "scores_from_keys: keys outside the layer");
+    TORCH_CHECK(s[4] >= 0 && s[5] > s[4] && s[5] <= s[3], "Invalid risk interval");
+    lrk_key_segment &t = table[i];
+    t.layer = l;
+    t.queries = static_cast<const at::BFloat16 *>(queries[l].data_ptr()) + head * groups * dim;
+    t.query_stride = queries[l].size(1) * dim;
+    t.projected_values = projected[l].data_ptr<float>() + s[2];
+    t.projected_stride = projected[l].size(1);
+    t.key_positions = positions[l].data_ptr<float>() + s[2];
+    t.key_row = s[2];
+    t.length = s[3];
+    t.first = s[4];
+    t.last = s[5];
+    t.query_chunk = s[6];
+    offsets[i] = total;
+    total += s[5] - s[4];
+  }
+  c10::cuda::CUDAGuard guard(reference.device());
+  auto scores = torch::empty({total}, reference.options().dtype(at::kFloat));
+  for (int64_t i = 0; i < count; ++i) table[i].scores = scores.data_ptr<float>() + offsets[i];
+  const size_t bytes = lrk_scores_from_keys_workspace_bytes(table.data(), count, window, groups);
+  TORCH_CHECK(bytes > 0, "scores_from_keys: invalid segments");
+  auto workspace = torch::empty({static_cast<int64_t>(bytes)}, reference.options().dtype(at::kByte));
+  check_status(lrk_scores_from_keys(table.data(), count, layer_table.data(), static_cast<int64_t>(layers),
+                                    query_positions.data_ptr<int64_t>(), window, groups, dim,
+                                    static_cast<float>(scale), margin.data_ptr<float>(), static_cast<float>(epsilon),
+                                    workspace.data_ptr(), bytes, current_stream()));
+  return scores;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -451,6 +530,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("append", &append);
   module.def("compact", &compact);
   module.def("compact_layers", &compact_layers);
+  module.def("scores_from_keys", &scores_from_keys);
   module.def("pool", &pool);
   module.def("merge", &merge);
   module.def("pack", &pack);

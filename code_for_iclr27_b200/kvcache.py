@@ -16,7 +16,7 @@ from typing import Dict, List, Sequence, Tuple
 
 import numpy as np
 
-from . import operators
+from . import operators, upload
 
 
 @dataclass
@@ -50,8 +50,7 @@ class PackedCache:
     def _refresh(self, layer: LayerState) -> None:
         import torch
 
-        layer.cumulative = torch.as_tensor(layer.bounds(), dtype=torch.int32).to(layer.keys.device,
-                                                                                  non_blocking=True)
+        layer.cumulative = upload(layer.bounds().astype(np.int32), layer.keys.device)
 
     def add_layer(self, keys, values, positions, head_lens: Sequence[int], prompt_lens: Sequence[int]) -> None:
         state = LayerState(keys, values, positions.reshape(-1, 1), list(map(int, head_lens)),
@@ -80,7 +79,7 @@ class PackedCache:
         for i, (l, h) in enumerate(coordinates.tolist()):
             layer = self.layers[l]
             table[:, i] = (l, bounds[l][h], layer.prompt_lens[h], layer.head_lens[h])
-        return torch.as_tensor(table).to(self.layers[0].keys.device, non_blocking=True)
+        return upload(table, self.layers[0].keys.device)
 
     def remove_selected(self, coordinates: Sequence[Tuple[int, int]], segment_ids, positions, table=None) -> int:
         """remove_positions for references that are still on the device:
@@ -102,13 +101,18 @@ class PackedCache:
         outside = ((pos < 0) | (pos >= length)).sum()
         keys = torch.sort(layer_of * (1 << 40) + start + pos).values
         duplicates = (keys[1:] == keys[:-1]).sum()
-        removed = torch.bincount(seg, minlength=segments)
-        removed_prompt = torch.bincount(seg, weights=(pos < prompt).to(torch.float64), minlength=segments)
-        summary = torch.cat([removed, removed_prompt.to(torch.int64), outside.view(1), duplicates.view(1)])
-        host = torch.empty(summary.shape, dtype=summary.dtype, pin_memory=True)
-        host.copy_(summary, non_blocking=True)
+        # Counts by scatter-add (torch.bincount reads its input's maximum back
+        # to the host first).
+        counts = torch.zeros(2 * segments + 2, dtype=torch.int64, device=seg.device)
+        counts.scatter_add_(0, seg, torch.ones_like(seg))
+        counts.scatter_add_(0, seg + segments, (pos < prompt).to(torch.int64))
+        counts[2 * segments] = outside
+        counts[2 * segments + 1] = duplicates
+        host = torch.empty(counts.shape, dtype=counts.dtype, pin_memory=True)
+        host.copy_(counts, non_blocking=True)
         ready = torch.cuda.Event()
         ready.record()
+        rows = keys & ((1 << 40) - 1)  # queued before the host waits
         ready.synchronize()
         counts = host.numpy()
         if counts[2 * segments]:
@@ -119,17 +123,18 @@ class PackedCache:
             return self.remove_positions({tuple(coordinates[s]): positions[seg == s].cpu().numpy()
                                           for s in np.flatnonzero(counts[:segments]).tolist()})
         per_layer = np.zeros(len(self.layers), dtype=np.int64)
-        for (layer_index, head), count, in_prompt in zip(coordinates, counts[:segments].tolist(),
-                                                        counts[segments:2 * segments].tolist()):
-            if count:
-                self.layers[layer_index].head_lens[head] -= int(count)
-                self.layers[layer_index].prompt_lens[head] -= int(in_prompt)
-                per_layer[layer_index] += count
+        removed_counts, prompt_counts = counts[:segments], counts[segments:2 * segments]
+        for s in np.flatnonzero(removed_counts).tolist():
+            layer_index, head = coordinates[s]
+            self.layers[layer_index].head_lens[head] -= int(removed_counts[s])
+            self.layers[layer_index].prompt_lens[head] -= int(prompt_counts[s])
+            per_layer[layer_index] += removed_counts[s]
         touched = np.flatnonzero(per_layer)
         offsets = np.concatenate(([0], np.cumsum(per_layer[touched]))).tolist()
-        rows = keys & ((1 << 40) - 1)
-        cumulative = np.stack([self.layers[int(l)].bounds() for l in touched]).astype(np.int32)
-        all_cumulative = torch.as_tensor(cumulative).to(rows.device, non_blocking=True)
+        lens = np.asarray([self.layers[int(l)].head_lens for l in touched], dtype=np.int64)
+        cumulative = np.zeros((touched.size, lens.shape[1] + 1), dtype=np.int32)
+        np.cumsum(lens, axis=1, out=cumulative[:, 1:])
+        all_cumulative = upload(cumulative, rows.device)
         layers = [self.layers[int(l)] for l in touched]
         keys_out, values_out, positions_out = operators().compact_layers(
             [layer.keys for layer in layers], [layer.values for layer in layers],
@@ -180,9 +185,9 @@ class PackedCache:
         touched, first = np.unique(layer_of, return_index=True)
         last = np.append(first[1:], rows.size)
         device = self.layers[int(touched[0])].keys.device
-        all_rows = torch.as_tensor(rows).to(device, non_blocking=True)
+        all_rows = upload(rows, device)
         cumulative = np.stack([self.layers[int(l)].bounds() for l in touched]).astype(np.int32)
-        all_cumulative = torch.as_tensor(cumulative).to(device, non_blocking=True)
+        all_cumulative = upload(cumulative, device)
         C = operators()
         for i, layer_index in enumerate(touched.tolist()):
             layer = self.layers[layer_index]

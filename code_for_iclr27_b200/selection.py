@@ -21,7 +21,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import operators
+from . import operators, upload
 
 
 @dataclass(order=True, frozen=True)
@@ -117,7 +117,7 @@ def refine_device(allocation, refinement, count) -> DeviceQueue:
         raise RuntimeError("refine_arrays runs on CUDA score tables only")
     device = raw.device
     host = np.stack([ends, np.asarray([segment.position_start for segment in allocation.segments], dtype=np.int64)])
-    ends_device, position_starts = torch.as_tensor(host).to(device, non_blocking=True)
+    ends_device, position_starts = upload(host, device)
     values, segment_ids, positions, stats = operators().refine(
         raw.float().contiguous(), refinement.scores.float().contiguous(), ends_device, position_starts, count)
     return DeviceQueue(values, segment_ids, positions, stats, count, coordinates)

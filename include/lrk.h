@@ -182,6 +182,54 @@ int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t coun
  * Synchronous.  No counterpart in the reference. */
 int lrk_logits_timeouts(unsigned int *count);
 
+/* ---------------------------------------------- scores straight from keys */
+
+/* One layer's keys: bf16 [rows, dim], contiguous, 16-byte aligned. */
+typedef struct lrk_key_layer {
+  const void *keys;
+  int64_t rows;
+} lrk_key_layer;
+
+/* One KV head of an audit, scored from its queries and keys. */
+typedef struct lrk_key_segment {
+  int64_t layer;                  /* index into the call's layers */
+  const void *queries;            /* bf16: query q, group g at queries + q * query_stride + g * dim */
+  int64_t query_stride;           /* elements (multiple of 8, >= groups * dim); 16-byte aligned rows */
+  const float *projected_values;  /* group g at projected_values + g * projected_stride, [length] */
+  int64_t projected_stride;
+  const float *key_positions;     /* [length] */
+  int64_t key_row;                /* the head's first row in its layer's keys */
+  int64_t length;                 /* keys of the head */
+  int64_t first;                  /* candidate interval [first, last) */
+  int64_t last;
+  float *scores;                  /* [last - first] output */
+  int64_t query_chunk;            /* queries per chunk of the running maximum; 0: one chunk */
+} lrk_key_segment;
+
+/* Workspace bytes lrk_scores_from_keys needs for these segments (0 for an
+ * invalid table). */
+size_t lrk_scores_from_keys_workspace_bytes(const lrk_key_segment *segments, int64_t count, int64_t window,
+                                            int64_t groups);
+
+/* lrk_temporal_scores from the queries and keys instead of the logits: the
+ * bf16 logits GEMM of src/lazy_recall/scoring.py:184 (16-term tensor-core
+ * steps for an even key count, 8-term steps for an odd one, as cuBLAS runs
+ * them) and the row statistics run as one tcgen05 kernel whose logits never
+ * reach memory (only each segment's candidate columns, for the risk step).
+ * The scores are bit-identical to lrk_temporal_scores on the logits
+ * torch.matmul produces for the same queries and keys.  Many heads of many
+ * layers per call (segments and layers are HOST arrays).  dim 64 or 128,
+ * groups <= 8.  Every wait inside the kernel is bounded; a CTA that gave up
+ * is counted by lrk_scores_from_keys_timeouts (its scores are then invalid).
+ * No counterpart operator in the reference (new entry point). */
+int lrk_scores_from_keys(const lrk_key_segment *segments, int64_t count, const lrk_key_layer *layers,
+                         int64_t layer_count, const int64_t *query_positions, int64_t window, int64_t groups,
+                         int64_t dim, float scale, const float *margin, float epsilon, void *workspace,
+                         size_t workspace_bytes, lrk_stream_t stream);
+
+/* CTAs of lrk_scores_from_keys that gave up a wait since the library loaded. */
+int lrk_scores_from_keys_timeouts(unsigned int *count);
+
 /* ------------------------------------------------- cache data movement */
 
 /* Append `added` rows to each head segment of a packed layer.

@@ -49,6 +49,13 @@ def test_invalid_arguments_rejected_before_launch():
     assert lib.lrk_batch_append(segments, 2, 1, 1, 64, abi.BF16, 1, 1, 1, 6, None) == abi.ERR_INVALID
     with pytest.raises(abi.LrkError):
         abi.check(lib.lrk_refine(None, None, 10, None, None, 0, 3, None, 0, None, None, None, None, None))
+    keyed = (abi.KeySegment * 1)()
+    keyed[0].first, keyed[0].last = 5, 5  # empty candidate interval
+    assert lib.lrk_scores_from_keys_workspace_bytes(keyed, 1, 10, 4) == 0
+    assert lib.lrk_scores_from_keys(keyed, 1, None, 0, None, 10, 4, 96, 0.1, None, 1e-6, None, 0,
+                                    None) == abi.ERR_INVALID  # head dimension 96
+    assert lib.lrk_scores_from_keys(keyed, 1, None, 0, None, 10, 4, 128, 0.1, None, 1e-6, None, 0,
+                                    None) == abi.ERR_INVALID  # no layers
 
 
 def test_zero_sized_calls_are_noops():
