@@ -13,25 +13,28 @@
 //   pass 3  p = w / denominator (IEEE), p * projected value summed per lane.
 // The reference's 256 lanes are the key index mod 256: a 128-key tile holds
 // lanes 0-127 (even tiles) or 128-255 (odd tiles) of every row, so the
-// epilogue thread of TMEM lane (row) r and column half h owns the
-// sequential partial sums of lanes 64h .. 64h + 63 and 128 + 64h .. + 63,
+// epilogue thread of TMEM lane (row) r and column quarter c owns the
+// sequential partial sums of lanes 32c .. 32c + 31 and 128 + 32c .. + 31,
 // kept in TMEM columns 256 .. 511 of its lane (loaded for a tile, added to in
-// key order -- the reference's per-lane order -- and stored back).  The pairwise tree (csrc/scoring.cu:15-30) is then level
-// 128 inside each thread, level 64 across the two threads of a row (shared
-// memory), levels 32 .. 1 inside the thread of h = 0.  Every element takes
+// key order -- the reference's per-lane order -- and stored back).  The
+// pairwise tree (csrc/scoring.cu:15-30) is then level 128 inside each thread,
+// levels 64 and 32 across the four threads of a row (shared memory), levels
+// 16 .. 1 inside the thread of c = 0.  Every element takes
 // the reference's operations (this file is compiled with --fmad=false), so
 // the statistics equal lrk_temporal_scores' bit for bit on the logits
 // cuBLAS would produce; the step order of the product is the one cuBLAS uses
 // for the head's key count (logits_tc.cu: 16-term steps for an even count,
 // 8-term steps for an odd one).
 //
-// Warp roles (288 threads, one CTA per SM, persistent over units):
-//   warp 8, one thread   TMA loads of key tiles into a ring of stages and
+// Warp roles (544 threads, one CTA per SM, persistent over units):
+//   warp 16, one thread  TMA loads of key tiles into a ring of stages and
 //                        the UMMAs of every (unit, pass, tile) in order;
-//   warps 0-7            per unit: build the query tile (A) in shared
+//   warps 0-15           per unit: build the query tile (A) in shared
 //                        memory once the previous unit's MMAs are done;
 //                        then drain every tile: warp w reads TMEM lanes
-//                        32 (w % 4) .. + 31, columns 64 (w / 4) .. + 63.
+//                        32 (w % 4) .. + 31, columns 32 (w / 4) .. + 31.
+// In pass 3 the epilogue stages each tile's projected values (all groups,
+// zero past the head) in shared memory, one tile ahead.
 // Every wait is bounded (tc::wait_phase); a timeout raises the CTA's abort
 // flag, all roles stop, the issuer waits (bounded) for its work in flight,
 // TMEM is freed and g_scores_tc_timeouts counts the CTA.
@@ -57,14 +60,16 @@ namespace {
 
 using namespace tc;
 
-constexpr int kEpilogueWarps = 8;
+constexpr int kEpilogueWarps = 16;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
 constexpr int kIssuerWarp = kEpilogueWarps;
 constexpr int kThreads = (kEpilogueWarps + 1) * 32;
 constexpr int kAccumulators = 2;
 constexpr uint32_t kPartialColumn = kAccumulators * kKeys;  // lane partial sums: columns 256 .. 511
 constexpr uint32_t kTmemColumns = 512;
-constexpr int kHalf = kKeys / 2;                            // columns per epilogue thread per tile
+constexpr int kQuarter = kKeys / 4;                         // columns per epilogue thread per tile
+constexpr int kMaxGroups = 8;
+constexpr int kValueStride = kKeys + 4;                     // floats per staged projected-value row
 constexpr int kMaxLayers = 32;
 constexpr int kMaxSegments = 256;
 constexpr int kEpilogueBarrier = 1;                       // named barrier of warps 0-7
@@ -107,9 +112,10 @@ struct FusedLayout {
   static constexpr uint32_t kA = 0;
   static constexpr uint32_t kB = kA + kAAtoms * kAtom;
   static constexpr uint32_t kStage = kBAtoms * kAtom;
-  static constexpr uint32_t kExchange = kB + kStages * kStage;        // [64][128] floats
-  static constexpr uint32_t kMaxima = kExchange + kHalf * kRows * 4;  // [2][128] maxima, [128] tree totals
-  static constexpr uint32_t kBarriers = kMaxima + 3 * kRows * 4;
+  static constexpr uint32_t kExchange = kB + kStages * kStage;          // [64][128] floats
+  static constexpr uint32_t kMaxima = kExchange + 2 * kQuarter * kRows * 4;  // [4][128] maxima, [128] totals
+  static constexpr uint32_t kValues = kMaxima + 5 * kRows * 4;           // 2 x [groups][kValueStride] floats
+  static constexpr uint32_t kBarriers = kValues + 2 * kMaxGroups * kValueStride * 4;
   // full[S] empty[S] acc_full[4] acc_empty[4] a_ready
   static constexpr uint32_t kTmemSlot = kBarriers + 8 * (2 * kStages + 2 * kAccumulators + 1);
   static constexpr uint32_t kAbort = kTmemSlot + 8;
@@ -172,7 +178,7 @@ __device__ __forceinline__ void columns_x(const uint32_t *v, float2 scale2, cons
   }
 }
 
-// All 256 epilogue threads agree: true only if every one passes true.
+// All epilogue threads agree: true only if every one passes true.
 __device__ __forceinline__ bool epilogue_all(bool value) {
   uint32_t all;
   asm volatile(
@@ -188,37 +194,49 @@ __device__ __forceinline__ void epilogue_sync() {
 }
 
 // The pairwise tree of csrc/scoring.cu:15-30 over one row's 256 lane sums,
-// kept in TMEM at `partials` (this thread's lanes 64h + c at column c,
-// 128 + 64h + c at column 64 + c).  Level 128 pairs columns c and 64 + c in
-// the thread, level 64 pairs the two threads of the row (shared memory),
-// levels 32 .. 1 run in the thread of h = 0.  Returns the total to every
-// thread of the row.  `exchange` is [64][128] floats, `totals` [128].
-__device__ __forceinline__ float row_tree(uint32_t partials, int h, int r, float *exchange, float *totals) {
+// kept in TMEM at `partials` (this thread's lanes 32c + i at column i,
+// 128 + 32c + i at column 32 + i, c = its column quarter).  Level 128 pairs
+// columns i and 32 + i in the thread; level 64 adds quarters 2, 3 into 0, 1
+// and level 32 quarter 1 into 0 through shared memory; levels 16 .. 1 run in
+// the thread of quarter 0.  Returns the total to every thread of the row.
+// `exchange` is [64][128] floats, `totals` [128].
+__device__ __forceinline__ float row_tree(uint32_t partials, int c, int r, float *exchange, float *totals) {
   tmem_wait_store();
-  float partial[kHalf];
+  float partial[kQuarter];
 #pragma unroll
-  for (int k = 0; k < kHalf / 16; ++k) {
+  for (int k = 0; k < kQuarter / 16; ++k) {
     uint32_t even[16], odd[16];
     tmem_load16(partials + 16 * k, even);
-    tmem_load16(partials + kHalf + 16 * k, odd);
+    tmem_load16(partials + kQuarter + 16 * k, odd);
     tmem_wait_loads();
     tmem_loaded16(even);
     tmem_loaded16(odd);
 #pragma unroll
     for (int i = 0; i < 16; ++i) partial[16 * k + i] = __fadd_rn(__uint_as_float(even[i]), __uint_as_float(odd[i]));
   }
-  if (h == 1) {
+  if (c >= 2) {
 #pragma unroll
-    for (int c = 0; c < kHalf; ++c) exchange[c * kRows + r] = partial[c];
+    for (int i = 0; i < kQuarter; ++i) exchange[((c - 2) * kQuarter + i) * kRows + r] = partial[i];
   }
   epilogue_sync();
-  if (h == 0) {
+  if (c < 2) {
 #pragma unroll
-    for (int c = 0; c < kHalf; ++c) partial[c] = __fadd_rn(partial[c], exchange[c * kRows + r]);  // s = 64
+    for (int i = 0; i < kQuarter; ++i)
+      partial[i] = __fadd_rn(partial[i], exchange[(c * kQuarter + i) * kRows + r]);  // s = 64
+  }
+  epilogue_sync();
+  if (c == 1) {
 #pragma unroll
-    for (int s = kHalf / 2; s > 0; s >>= 1) {
+    for (int i = 0; i < kQuarter; ++i) exchange[i * kRows + r] = partial[i];
+  }
+  epilogue_sync();
+  if (c == 0) {
 #pragma unroll
-      for (int c = 0; c < s; ++c) partial[c] = __fadd_rn(partial[c], partial[c + s]);
+    for (int i = 0; i < kQuarter; ++i) partial[i] = __fadd_rn(partial[i], exchange[i * kRows + r]);  // s = 32
+#pragma unroll
+    for (int s = kQuarter / 2; s > 0; s >>= 1) {
+#pragma unroll
+      for (int i = 0; i < s; ++i) partial[i] = __fadd_rn(partial[i], partial[i + s]);
     }
     totals[r] = partial[0];
   }
@@ -228,13 +246,13 @@ __device__ __forceinline__ float row_tree(uint32_t partials, int h, int r, float
   return total;
 }
 
-// Zeroes this thread's 128 partial-sum columns.
+// Zeroes this thread's 64 partial-sum columns.
 __device__ __forceinline__ void clear_partials(uint32_t partials) {
   uint32_t zero[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) zero[i] = 0u;
 #pragma unroll
-  for (int k = 0; k < kKeys / 16; ++k) tmem_store16(partials + 16 * k, zero);
+  for (int k = 0; k < 2 * kQuarter / 16; ++k) tmem_store16(partials + 16 * k, zero);
 }
 
 template <int DIM, bool EIGHT>
@@ -341,15 +359,19 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const int quarter = warp & 3, h = warp >> 2, r = quarter * 32 + lane;
-    const uint32_t lanes = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + h * kHalf;
-    const uint32_t partials = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + kPartialColumn + h * kKeys;
+    const int quarter = warp & 3, c4 = warp >> 2, r = quarter * 32 + lane;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t lanes = lane_base + c4 * kQuarter;
+    const uint32_t partials = lane_base + kPartialColumn + c4 * 2 * kQuarter;
     float *exchange = reinterpret_cast<float *>(smem + L::kExchange);
     float *maxima = reinterpret_cast<float *>(smem + L::kMaxima);
+    float *totals = maxima + 4 * kRows;
+    float *staged = reinterpret_cast<float *>(smem + L::kValues);  // [2][groups][kValueStride]
     const float2 scale2 = make_float2(p.scale, p.scale);
-    int t = 0, unit_index = 0;
+    const int tid = threadIdx.x;
+    int t = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x, ++unit_index) {
+    for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
       const FusedSegment &seg = p.segment[unit / p.m_tiles];
       const int m = unit % p.m_tiles, row = m * kRows + r;
       const bool valid = row < p.rows;
@@ -358,10 +380,10 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
       const RowMask mask{valid ? min(seg.visible[query], seg.length) : 0, seg.length, seg.key_positions,
                          static_cast<float>(p.query_positions[query])};
       // The query tile (A), after the previous unit's last MMA (whose
-      // accumulator this group has drained).
+      // accumulator every epilogue warp has drained).
       {
         constexpr int kChunks = L::kChunks;
-        for (int i = threadIdx.x; i < kRows * kChunks; i += kEpilogueThreads) {
+        for (int i = tid; i < kRows * kChunks; i += kEpilogueThreads) {
           const int rr = i / kChunks, j = i % kChunks, q_row = m * kRows + rr;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (q_row < p.rows) {
@@ -379,10 +401,9 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         epilogue_sync();
-        if (threadIdx.x == 0) arrive(a_ready);
+        if (tid == 0) arrive(a_ready);
       }
-      // The accumulator of tile t, loaded 16 columns at a time: sub-part k
-      // covers columns 16k .. 16k + 15 of this thread's half.
+      // The accumulator of tile t: every epilogue thread waits, all agree.
       auto next_tile = [&]() -> bool {
         const bool got = wait_phase(acc_full(t % kAccumulators), (t / kAccumulators) & 1, abort);
         if (!epilogue_all(got)) {
@@ -398,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
         if (lane == 0) arrive(acc_empty(t % kAccumulators));
         ++t;
       };
+      // Columns 16k .. 16k + 15 of this thread's quarter of tile t.
       auto load_part = [&](int k, uint32_t *v) {
         tmem_load16(lanes + (t % kAccumulators) * kKeys + k * 16, v);
         tmem_wait_load16(v);
@@ -411,12 +433,12 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
           ok = false;
           break;
         }
-        const int tile0 = j * kKeys + h * kHalf;
+        const int tile0 = j * kKeys + c4 * kQuarter;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < kQuarter / 16; ++k) {
           uint32_t v[16], logit[8], x[8];
           load_part(k, v);
-          if (k == 3) release_tile();
+          if (k == kQuarter / 16 - 1) release_tile();
           const int p0 = tile0 + 16 * k;
           columns_x(v, scale2, mask, p0, logit, x);
 #pragma unroll
@@ -434,28 +456,34 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
         }
       }
       if (!ok) break;
-      const float2 pair_max = P::unpack(max_pair);
-      maxima[h * kRows + r] = fmaxf(pair_max.x, pair_max.y);
+      {
+        const float2 pair_max = P::unpack(max_pair);
+        maxima[c4 * kRows + r] = fmaxf(pair_max.x, pair_max.y);
+      }
       epilogue_sync();
-      const float maximum = fmaxf(maxima[r], maxima[kRows + r]);
+      const float maximum =
+          fmaxf(fmaxf(maxima[r], maxima[kRows + r]), fmaxf(maxima[2 * kRows + r], maxima[3 * kRows + r]));
       const float2 minus_max = make_float2(-maximum, -maximum);
 
-      // The 64 partial sums of this thread's lanes in the tile's parity:
-      // loaded before the tile, stored back after it.
-      float sums[kHalf];
+      // The 32 partial sums of this thread's lanes in the tile's parity:
+      // loaded before the tile, stored back after it.  Keys past the head's
+      // length add +0 (a masked weight, or a zero projected value): a lane
+      // sum starts at +0 and no sum with +0 changes a value that is not -0,
+      // which these sums never are, so the extra terms leave every bit.
+      float sums[kQuarter];
       auto load_sums = [&](int j) {
         tmem_wait_store();
         uint32_t *bits = reinterpret_cast<uint32_t *>(sums);
 #pragma unroll
-        for (int k = 0; k < kHalf / 16; ++k) tmem_load16(partials + (j & 1) * kHalf + 16 * k, bits + 16 * k);
+        for (int k = 0; k < kQuarter / 16; ++k) tmem_load16(partials + (j & 1) * kQuarter + 16 * k, bits + 16 * k);
         tmem_wait_loads();
 #pragma unroll
-        for (int k = 0; k < kHalf / 16; ++k) tmem_loaded16(bits + 16 * k);
+        for (int k = 0; k < kQuarter / 16; ++k) tmem_loaded16(bits + 16 * k);
       };
       auto store_sums = [&](int j) {
         const uint32_t *bits = reinterpret_cast<const uint32_t *>(sums);
 #pragma unroll
-        for (int k = 0; k < kHalf / 16; ++k) tmem_store16(partials + (j & 1) * kHalf + 16 * k, bits + 16 * k);
+        for (int k = 0; k < kQuarter / 16; ++k) tmem_store16(partials + (j & 1) * kQuarter + 16 * k, bits + 16 * k);
       };
 
       // Pass 2: per-lane sums of expf(x - max) in key order.
@@ -466,12 +494,12 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
           break;
         }
         load_sums(j);
-        const int tile0 = j * kKeys + h * kHalf;
+        const int tile0 = j * kKeys + c4 * kQuarter;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < kQuarter / 16; ++k) {
           uint32_t v[16], logit[8], x[8];
           load_part(k, v);
-          if (k == 3) release_tile();
+          if (k == kQuarter / 16 - 1) release_tile();
           columns_x(v, scale2, mask, tile0 + 16 * k, logit, x);
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
@@ -484,57 +512,95 @@ __global__ void __launch_bounds__(kThreads, 1) scores_tc_kernel(const __grid_con
         store_sums(j);
       }
       if (!ok) break;
-      const float denominator = row_tree(partials, h, r, exchange, maxima + 2 * kRows);
+      const float denominator = row_tree(partials, c4, r, exchange, totals);
 
-      // Pass 3: per-lane sums of (w / denominator) * projected value.
+      // Pass 3: per-lane sums of (w / denominator) * projected value.  The
+      // tile's projected values (every group, zero past the head) are staged
+      // in shared memory one tile ahead by all epilogue threads.
       clear_partials(partials);
       const rows::Divider divider = rows::make_divider(denominator);
-      const float *projected = seg.projected + static_cast<int64_t>(group) * seg.projected_stride;
+      constexpr int kStagedPerThread = kMaxGroups * kKeys / kEpilogueThreads;
+      const int staged_count = p.groups * kKeys;
+      float ahead[kStagedPerThread];
+      auto fetch_values = [&](int j) {
+#pragma unroll
+        for (int i = 0; i < kStagedPerThread; ++i) {
+          const int e = tid + i * kEpilogueThreads, g = e / kKeys, column = j * kKeys + e % kKeys;
+          ahead[i] = e < staged_count && column < seg.length
+                         ? __ldg(seg.projected + static_cast<int64_t>(g) * seg.projected_stride + column)
+                         : 0.0f;
+        }
+      };
+      auto stage_values = [&](int j) {
+        float *buffer = staged + (j & 1) * kMaxGroups * kValueStride;
+#pragma unroll
+        for (int i = 0; i < kStagedPerThread; ++i) {
+          const int e = tid + i * kEpilogueThreads;
+          if (e < staged_count) buffer[(e / kKeys) * kValueStride + e % kKeys] = ahead[i];
+        }
+      };
+      fetch_values(0);
+      stage_values(0);  // visible after the barrier in next_tile
       for (int j = 0; j < tiles; ++j) {
         if (!next_tile()) {
           ok = false;
           break;
         }
+        if (j + 1 < tiles) fetch_values(j + 1);
         load_sums(j);
-        const int tile0 = j * kKeys + h * kHalf;
+        const int tile0 = j * kKeys + c4 * kQuarter;
+        const float *values_row = staged + (j & 1) * kMaxGroups * kValueStride + group * kValueStride + c4 * kQuarter;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int p0 = tile0 + 16 * k;
-          const bool inside = p0 + 16 <= seg.length;
-          float values[16];
-#pragma unroll
-          for (int e = 0; e < 16; ++e) values[e] = inside || p0 + e < seg.length ? __ldg(projected + p0 + e) : 0.0f;
+        for (int k = 0; k < kQuarter / 16; ++k) {
           uint32_t v[16], logit[8], x[8];
           load_part(k, v);
-          if (k == 3) release_tile();
-          columns_x(v, scale2, mask, p0, logit, x);
+          if (k == kQuarter / 16 - 1) release_tile();
+          columns_x(v, scale2, mask, tile0 + 16 * k, logit, x);
+          float values[16];
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            // One operand test per 8 divisions (rows::divide2_fast's range).
-            const uint32_t lowest = P::min_nan(P::min_nan(x[4 * half], x[4 * half + 1]),
-                                               P::min_nan(x[4 * half + 2], x[4 * half + 3]));
-            const float2 lowest_d = rows::add2_rn(P::unpack(lowest), minus_max);
-            const bool fast =
-                divider.fast && lowest_d.x >= rows::kFastExponentFloor && lowest_d.y >= rows::kFastExponentFloor;
+          for (int i = 0; i < 4; ++i) {
+            const float4 q = reinterpret_cast<const float4 *>(values_row + 16 * k)[i];
+            values[4 * i] = q.x;
+            values[4 * i + 1] = q.y;
+            values[4 * i + 2] = q.z;
+            values[4 * i + 3] = q.w;
+          }
+          // One operand test for the 16 divisions (rows::divide2_fast's range).
+          const uint32_t lowest =
+              P::min_nan(P::min_nan(P::min_nan(x[0], x[1]), P::min_nan(x[2], x[3])),
+                         P::min_nan(P::min_nan(x[4], x[5]), P::min_nan(x[6], x[7])));
+          const float2 lowest_d = rows::add2_rn(P::unpack(lowest), minus_max);
+          const bool fast =
+              divider.fast && lowest_d.x >= rows::kFastExponentFloor && lowest_d.y >= rows::kFastExponentFloor;
+          if (fast) {
 #pragma unroll
-            for (int i = 4 * half; i < 4 * half + 4; ++i) {
+            for (int i = 0; i < 8; ++i) {
               const float2 d = rows::add2_rn(P::unpack(x[i]), minus_max);
-              const float2 w = make_float2(expf(d.x), expf(d.y));
-              const float2 probability = fast ? rows::divide2_fast(divider, w)
-                                              : make_float2(rows::divide(divider, w.x), rows::divide(divider, w.y));
+              const float2 probability = rows::divide2_fast(divider, make_float2(expf(d.x), expf(d.y)));
               const float2 product = rows::mul2_rn(probability, make_float2(values[2 * i], values[2 * i + 1]));
               const int c = 16 * k + 2 * i;
-              // Keys past the head's length are not the reference's: no sum.
-              if (inside || p0 + 2 * i < seg.length) sums[c] = __fadd_rn(sums[c], product.x);
-              if (inside || p0 + 2 * i + 1 < seg.length) sums[c + 1] = __fadd_rn(sums[c + 1], product.y);
+              sums[c] = __fadd_rn(sums[c], product.x);
+              sums[c + 1] = __fadd_rn(sums[c + 1], product.y);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float2 d = rows::add2_rn(P::unpack(x[i]), minus_max);
+              const float2 probability =
+                  make_float2(rows::divide(divider, expf(d.x)), rows::divide(divider, expf(d.y)));
+              const float2 product = rows::mul2_rn(probability, make_float2(values[2 * i], values[2 * i + 1]));
+              const int c = 16 * k + 2 * i;
+              sums[c] = __fadd_rn(sums[c], product.x);
+              sums[c + 1] = __fadd_rn(sums[c + 1], product.y);
             }
           }
         }
         store_sums(j);
+        if (j + 1 < tiles) stage_values(j + 1);  // the other buffer: its last readers passed next_tile
       }
       if (!ok) break;
-      const float projection = row_tree(partials, h, r, exchange, maxima + 2 * kRows);
-      if (h == 0 && valid) seg.stats[row] = make_float3(maximum, denominator, projection);
+      const float projection = row_tree(partials, c4, r, exchange, totals);
+      if (c4 == 0 && valid) seg.stats[row] = make_float3(maximum, denominator, projection);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
