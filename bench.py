@@ -66,6 +66,10 @@ def parse_args():
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--skip-side", action="store_true",
                         help="skip the configs[2] batch_append and configs[3] recall measurements (N=1 only)")
+    parser.add_argument("--layer-groups", action="store_true",
+                        help="N>1: split ONE request's layers into per-GPU groups (strong scaling; the eviction "
+                             "threshold is fixed by NCCL all-gathers of radix histograms) instead of one request "
+                             "per GPU")
     parser.add_argument("--scoring", choices=["fused", "dropin"], default="fused",
                         help="fused: lrk_temporal_scores per layer; dropin: the reference's per-head composition of "
                              "temporal_probabilities + temporal_risk")
@@ -350,8 +354,19 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    cache, queries, qpos, gradients, margin = build_request(device, args.seed + 1000 * rank)
+    layer_groups = args.layer_groups and distributed
+    cache, queries, qpos, gradients, margin = build_request(device, args.seed + (0 if layer_groups else 1000 * rank))
     managed = cache.total_rows()
+    if layer_groups:
+        # Every rank built the same request; each keeps its contiguous group of layers.
+        from code_for_iclr27_b200.distributed import layer_group_audit_pass
+        from code_for_iclr27_b200.kvcache import PackedCache
+
+        if LAYERS % world:
+            raise SystemExit(f"--layer-groups needs the {LAYERS} layers to split evenly over {world} GPUs")
+        mine = slice(rank * (LAYERS // world), (rank + 1) * (LAYERS // world))
+        cache = PackedCache(layers=cache.layers[mine], seen_tokens=cache.seen_tokens)
+        queries, gradients = queries[mine], gradients[mine]
     C = operators()
     counter = LaunchCounter(C)
     timer = KernelTimer()
@@ -386,6 +401,9 @@ def main():
     route(lambda: counter)
 
     def one_pass():
+        if layer_groups:
+            return layer_group_audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED,
+                                          protect_recent=PROTECT_RECENT)
         return audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT, fused=fused)
 
     for _ in range(args.warmup):
@@ -420,25 +438,31 @@ def main():
     if distributed:
         dist.all_reduce(local, op=dist.ReduceOp.MAX)
     elapsed_ms = float(local.item())
-    value = world * managed * args.steps / (elapsed_ms / 1e3)
+    requests = 1 if layer_groups else world
+    value = requests * managed * args.steps / (elapsed_ms / 1e3)
 
     # Per-decode-step overhead: append one token to every layer, evict a
     # staging-sized queue prefix every EVICT_INTERVAL steps.
-    queue, removed_at_audit = last.references[IMMEDIATE:], {}
-    g = torch.Generator(device=device).manual_seed(args.seed + 7)
-    new_keys = torch.randn(args.decode_steps, LAYERS, 1, HEADS, 1, DIM, generator=g, device=device).to(torch.bfloat16)
-    barrier()
-    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d0.record()
-    for step in range(args.decode_steps):
-        for layer in range(LAYERS):
-            cache.append(layer, new_keys[step, layer], new_keys[step, layer], cache.seen_tokens)
-        cache.seen_tokens += 1
-        if (step + 1) % EVICT_INTERVAL == 0 and len(queue) >= STAGING:
-            queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
-    d1.record()
-    barrier()
-    decode_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
+    # (Request sharding only: with layer groups the lazy queue is split over
+    # ranks and its prefixes would need the request-wide rounds as well.)
+    decode_us = None
+    if not layer_groups:
+        queue, removed_at_audit = last.references[IMMEDIATE:], {}
+        g = torch.Generator(device=device).manual_seed(args.seed + 7)
+        new_keys = torch.randn(args.decode_steps, LAYERS, 1, HEADS, 1, DIM, generator=g,
+                               device=device).to(torch.bfloat16)
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record()
+        for step in range(args.decode_steps):
+            for layer in range(LAYERS):
+                cache.append(layer, new_keys[step, layer], new_keys[step, layer], cache.seen_tokens)
+            cache.seen_tokens += 1
+            if (step + 1) % EVICT_INTERVAL == 0 and len(queue) >= STAGING:
+                queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
+        d1.record()
+        barrier()
+        decode_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
 
     # End to end through the public API: audit inputs copied from pinned host
     # memory each step, the queue read back (refine_arrays returns host arrays).
@@ -451,8 +475,12 @@ def main():
     def e2e_pass():
         device_queries = [q.to(device, non_blocking=True) for q in host_queries]
         device_gradients = [x.to(device, non_blocking=True) for x in host_gradients]
-        audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT,
-                   fused=fused)
+        if layer_groups:
+            layer_group_audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED,
+                                   protect_recent=PROTECT_RECENT)
+        else:
+            audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT,
+                       fused=fused)
 
     e2e_pass()  # warm-up
     barrier()
@@ -465,7 +493,7 @@ def main():
     e2e_ms = torch.tensor([e_start.elapsed_time(e_end)], device=device)
     if distributed:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = world * managed * e2e_steps / (float(e2e_ms.item()) / 1e3)
+    e2e_value = requests * managed * e2e_steps / (float(e2e_ms.item()) / 1e3)
 
     peak, peak_kind = measured_peaks()
     traffic_ratio = measured_traffic_ratio()
@@ -473,7 +501,8 @@ def main():
     achieved = timer.bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else 0.0
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong" if layer_groups else "weak",
         "vs_baseline": None, "dtype": "f32", "impl": "ours",
         "data": "synthetic (seeded): bf16 K/V ~N(0,1), queries ~N(0,4), margin gradient ~N(0,1/D)",
         "config": {"workload": "configs[1] llama-3-8b single request, steady-state audit pass",
@@ -481,8 +510,10 @@ def main():
                    "layers": LAYERS, "kv_heads": HEADS, "gqa_group": GROUPS, "head_dim": DIM,
                    "prompt_rows_per_head": PROMPT, "generation_rows": RETAINED + IMMEDIATE, "budget": BUDGET,
                    "temporal_window": WINDOW, "selected_per_audit": IMMEDIATE + QUEUED, "evicted_per_audit": IMMEDIATE,
-                   "managed_rows_per_request": managed, "requests_per_gpu": 1,
-                   "parallelism": f"request-sharded x{world}" if world > 1 else "single request",
+                   "managed_rows_per_request": managed,
+                   "requests_per_gpu": 1 / world if layer_groups else 1,
+                   "parallelism": (f"layer-groups x{world} (one request, NCCL histogram selection)" if layer_groups
+                                   else f"request-sharded x{world}" if world > 1 else "single request"),
                    "l2": "no flush: 4.6 GB of K/V per request, larger than L2"},
         "decode_overhead_us": decode_us,
         "roofline": {"kernel": timed_name, "bound": "hbm", "achieved": achieved, "peak": peak,

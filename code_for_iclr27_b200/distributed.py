@@ -119,3 +119,43 @@ def prefix_split(scores: torch.Tensor, chosen: torch.Tensor, prefix: int, group=
     """Mask of this rank's chosen rows that fall in the first `prefix` slots of
     the request-wide queue (an immediate or lazy eviction batch)."""
     return select_smallest(scores, prefix, group, eligible=chosen)
+
+
+def layer_group_audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
+                           group=None, protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250,
+                           pool_kernel=7):
+    """audit_pass (score, Pool7, select, evict the immediate prefix) for one
+    rank's contiguous group of a request's layers: `cache`, `queries` and
+    `gradients` hold this rank's layers only, ranks in layer order.
+
+    Scoring, pooling, refinement and compaction are layer-local.  The
+    request-wide choices go through select_smallest / prefix_split (radix
+    histograms all-gathered over `group`): this rank's share of the
+    bottom-(immediate + queued) raw scores is exactly its local bottom-k for k
+    = its share (ties by index on both sides), so a local refine_arrays with
+    that count gives the single-GPU quotas, refined positions and queue order
+    for these layers; the rank then evicts its share of the request-wide
+    immediate prefix, the first slots of its local queue.  Returns the local
+    AuditResult (its references are this rank's queue slots)."""
+    from .audit import AuditResult, pool_table, score_table_fused
+    from .selection import fetch_references, refine_device
+
+    table = score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                              denominator_epsilon, query_chunk_size)
+    pooled = pool_table(table, pool_kernel)
+    total = torch.tensor([table.scores.numel()], dtype=torch.int64, device=table.scores.device)
+    dist.all_reduce(total, group=group)
+    count = min(immediate + queued, int(total.item()))
+    if count < immediate:
+        raise RuntimeError("Not enough unprotected candidates to enforce the budget")
+    chosen = select_smallest(table.scores, count, group)
+    head = prefix_split(table.scores, chosen, immediate, group)
+    local_count, local_immediate = (int(v) for v in torch.stack([chosen.sum(), head.sum()]).tolist())
+    queue = refine_device(table, pooled, local_count)
+    pending = fetch_references(queue)
+    evicted = 0
+    if local_immediate:
+        evicted = cache.remove_selected(queue.coordinates, queue.segment_ids[:local_immediate],
+                                        queue.positions[:local_immediate])
+    references, changed, changed_heads = pending.result()
+    return AuditResult(table, references, changed, changed_heads, evicted)

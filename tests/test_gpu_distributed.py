@@ -73,3 +73,89 @@ def test_layer_group_selection_over_nccl():
         head = np.concatenate([results[r][i][1] for r in range(2)])
         assert set(chosen.tolist()) == set(order[:count].tolist()), f"case {seed}"
         assert set(head.tolist()) == set(order[:prefix].tolist()), f"prefix of case {seed}"
+
+
+def _layer_cache(device, seed, layers=4, heads=4, dim=64, window=24, groups=2):
+    import torch
+
+    from code_for_iclr27_b200.kvcache import PackedCache
+
+    g = torch.Generator().manual_seed(seed)
+    cache = PackedCache()
+    for _ in range(layers):
+        lens = torch.randint(300, 900, (heads,), generator=g).tolist()
+        rows = sum(lens)
+        keys = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(device)
+        values = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(device)
+        positions = torch.cat([torch.arange(n, dtype=torch.float32) for n in lens]).to(device)
+        cache.add_layer(keys, values, positions, lens, [min(50, n) for n in lens])
+    queries = [(torch.randn(window, heads * groups, dim, generator=g) * 2).to(torch.bfloat16).to(device)
+               for _ in range(layers)]
+    grads = [(torch.randn(heads * groups, dim, generator=g) / 8).to(device) for _ in range(layers)]
+    top = min(min(layer.head_lens) for layer in cache.layers)
+    qpos = torch.arange(top - window, top, dtype=torch.int64, device=device)
+    return cache, queries, grads, qpos, torch.tensor(0.8, device=device)
+
+
+def _digest(cache, offset):
+    import torch
+
+    return {offset + i: (layer.keys.view(torch.int16).cpu().numpy().copy(),
+                         layer.positions.cpu().numpy().copy(), list(layer.head_lens), list(layer.prompt_lens))
+            for i, layer in enumerate(cache.layers)}
+
+
+def _audit_worker(rank, world, port, results):
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from code_for_iclr27_b200.kvcache import PackedCache
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    device = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=device)
+    try:
+        from code_for_iclr27_b200.audit import audit_pass
+        from code_for_iclr27_b200.distributed import layer_group_audit_pass
+
+        cache, queries, grads, qpos, margin = _layer_cache(device, 21)
+        per = len(cache.layers) // world
+        mine = slice(rank * per, (rank + 1) * per)
+        part = PackedCache(layers=cache.layers[mine])
+        result = layer_group_audit_pass(part, queries[mine], qpos, grads[mine], margin, immediate=40, queued=150)
+        out = {"part": _digest(part, rank * per), "evicted": result.evicted}
+        if rank == 0:
+            full, queries, grads, qpos, margin = _layer_cache(device, 21)
+            expected = audit_pass(full, queries, qpos, grads, margin, immediate=40, queued=150)
+            out["full"] = _digest(full, 0)
+            out["full_evicted"] = expected.evicted
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_layer_group_audit_pass_equals_single_gpu():
+    """A 4-layer request split into two 2-layer groups (one per GPU, NCCL
+    histogram selection): the same rows are evicted from every layer as by
+    the single-GPU audit pass, and the caches end bit-identical."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    mp.start_processes(_audit_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
+    full = results[0]["full"]
+    assert results[0]["evicted"] + results[1]["evicted"] == results[0]["full_evicted"] == 40
+    for rank in range(2):
+        for layer, (keys, positions, lens, prompts) in results[rank]["part"].items():
+            f_keys, f_positions, f_lens, f_prompts = full[layer]
+            assert lens == f_lens and prompts == f_prompts, f"layer {layer}"
+            np.testing.assert_array_equal(positions, f_positions)
+            np.testing.assert_array_equal(keys, f_keys)
