@@ -37,6 +37,12 @@ class ScoreSegment(ctypes.Structure):
                 ("query_chunk", I64)]
 
 
+class MergeLayer(ctypes.Structure):
+    """lrk_merge_layer (include/lrk.h)."""
+    _fields_ = [("keys", P), ("values", P), ("positions", P), ("rows", I64), ("recalled", P),
+                ("recalled_positions", P), ("recalled_rows", I64), ("mapping", P), ("out_rows", I64)]
+
+
 class KeyLayer(ctypes.Structure):
     """lrk_key_layer (include/lrk.h)."""
     _fields_ = [("keys", P), ("rows", I64)]
@@ -63,6 +69,7 @@ SIGNATURES = {
     "lrk_append": (I32, [P, P, P, I64, P, P, P, I64, I64, I64, I32, I64, P, P, P, P, P, P]),
     "lrk_compact": (I32, [P, P, P, I64, I64, I32, P, I64, P, P, P, P]),
     "lrk_merge": (I32, [P, P, P, I64, P, P, I64, P, I64, I64, I32, P, P, P, P]),
+    "lrk_merge_layers": (I32, [ctypes.POINTER(MergeLayer), I64, I64, I32, P, P, P, P]),
     "lrk_pack": (I32, [P, P, P, I64, I64, I32, P, P, I64, I64, P, P, P]),
     "lrk_batch_append": (I32, [ctypes.POINTER(Segment), I64, P, P, I64, I32, P, P, P, I64, P]),
     "lrk_append_flattened": (I32, [P, I64, P, I64, I64, I64, I32, P, P, P, I64, P]),

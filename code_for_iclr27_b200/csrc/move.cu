@@ -11,6 +11,7 @@
 // The output of a tile is contiguous, so stores are fully coalesced; reads are
 // coalesced within each source row (128-256 B for bf16 D=64/128).
 #include <algorithm>
+#include <vector>
 
 #include "common.cuh"
 
@@ -295,6 +296,57 @@ struct MergePlan {
   }
 };
 
+// lrk_merge_layers: MergePlan over several layers whose outputs are
+// concatenated (layer i's rows start at out_first[i]); each output row finds
+// its layer by binary search over the (<= kMaxMergeLayers) first rows.
+constexpr int kMaxMergeLayers = 64;
+struct MergeLayer {
+  const char *k, *v;
+  const float *positions;
+  int64_t rows;
+  const char *recalled;
+  const float *recalled_positions;
+  int64_t recalled_rows;
+  const int64_t *mapping;
+  int64_t out_first;
+};
+struct MergeLayersPlan {
+  MergeLayer layer[kMaxMergeLayers];
+  int count;
+  int64_t row_bytes;
+  using Shared = NoShared;
+  __device__ void prologue(Shared &) const {}
+  template <int TR>
+  __device__ void fill(int64_t first, int nrows, RowSource *sources, Shared &) const {
+    for (int i = threadIdx.x; i < nrows; i += kThreads) {
+      const int64_t o = first + i;
+      int lo = 0, hi = count - 1;  // last layer with out_first <= o
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (layer[mid].out_first <= o) lo = mid; else hi = mid - 1;
+      }
+      const MergeLayer &L = layer[lo];
+      const int64_t m = L.mapping[o - L.out_first];
+      RowSource out{nullptr, nullptr, 0.0f};
+      if (m >= 0) {
+        if (m < L.rows) {
+          out.k = L.k + m * row_bytes;
+          out.v = L.v + m * row_bytes;
+          out.position = L.positions[m];
+        }
+      } else {
+        const int64_t j = -m - 1;
+        if (j < L.recalled_rows) {
+          out.k = L.recalled + (2 * j) * row_bytes;
+          out.v = L.recalled + (2 * j + 1) * row_bytes;
+          out.position = L.recalled_positions[j];
+        }
+      }
+      sources[i] = out;
+    }
+  }
+};
+
 // Index gather: _C.pack (with metadata) and _legacy_C.compact_flattened_kv.
 struct IndexPlan {
   const char *k, *v;
@@ -388,8 +440,9 @@ struct BatchAppendPlan {
 
 // ------------------------------------------------------------ dispatch
 
-int pick_vector(int64_t row_bytes, std::initializer_list<const void *> pointers,
-                std::initializer_list<int64_t> strides) {
+// Widest vector (bytes) that divides the row and every pointer's alignment.
+template <class Pointers>
+int widest_vector(int64_t row_bytes, const Pointers &pointers, std::initializer_list<int64_t> strides) {
   for (int vb : {16, 8, 4, 2}) {
     if (row_bytes % vb) continue;
     bool ok = true;
@@ -398,6 +451,14 @@ int pick_vector(int64_t row_bytes, std::initializer_list<const void *> pointers,
     if (ok) return vb;
   }
   return 0;
+}
+int pick_vector(int64_t row_bytes, std::initializer_list<const void *> pointers,
+                std::initializer_list<int64_t> strides) {
+  return widest_vector(row_bytes, pointers, strides);
+}
+int pick_vector(int64_t row_bytes, const std::vector<const void *> &pointers,
+                std::initializer_list<int64_t> strides) {
+  return widest_vector(row_bytes, pointers, strides);
 }
 
 template <class Plan>
@@ -524,6 +585,49 @@ extern "C" int lrk_merge(const void *keys, const void *values, const float *posi
   GatherOut out{static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, rb, rb,
                 out_rows, rb, {}};
   return launch_gather(plan, out, vb, reinterpret_cast<cudaStream_t>(stream), "lrk_merge");
+}
+
+extern "C" int lrk_merge_layers(const lrk_merge_layer *layers, int64_t count, int64_t dimension, int dtype,
+                                void *out_keys, void *out_values, float *out_positions, lrk_stream_t stream) {
+  clear_error();
+  const int eb = element_bytes(dtype);
+  LRK_REQUIRE(eb > 0, "unknown dtype");
+  LRK_REQUIRE(count >= 0 && dimension > 0, "invalid merge sizes");
+  if (count == 0) return LRK_OK;
+  LRK_REQUIRE(layers && out_keys && out_values && out_positions, "null pointer");
+  const int64_t rb = dimension * eb;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int64_t written = 0;
+  for (int64_t first = 0; first < count; first += kMaxMergeLayers) {
+    const int n = static_cast<int>(std::min<int64_t>(kMaxMergeLayers, count - first));
+    MergeLayersPlan plan{};
+    plan.count = 0;
+    plan.row_bytes = rb;
+    std::vector<const void *> pointers{static_cast<char *>(out_keys) + written * rb,
+                                       static_cast<char *>(out_values) + written * rb};
+    int64_t rows_out = 0;
+    for (int i = 0; i < n; ++i) {
+      const lrk_merge_layer &l = layers[first + i];
+      LRK_REQUIRE(l.rows >= 0 && l.recalled_rows >= 0 && l.out_rows >= 0, "invalid merge sizes");
+      LRK_REQUIRE(l.out_rows == 0 || l.mapping != nullptr, "null pointer");
+      if (l.out_rows == 0) continue;
+      plan.layer[plan.count++] = {static_cast<const char *>(l.keys), static_cast<const char *>(l.values), l.positions,
+                                  l.rows, static_cast<const char *>(l.recalled), l.recalled_positions, l.recalled_rows,
+                                  l.mapping, rows_out};
+      pointers.push_back(l.keys);
+      pointers.push_back(l.values);
+      pointers.push_back(l.recalled);
+      rows_out += l.out_rows;
+    }
+    if (rows_out == 0) continue;
+    const int vb = pick_vector(rb, pointers, {});
+    GatherOut out{static_cast<char *>(out_keys) + written * rb, static_cast<char *>(out_values) + written * rb,
+                  out_positions + written, rb, rb, rows_out, rb, {}};
+    const int status = launch_gather(plan, out, vb, s, "lrk_merge_layers");
+    if (status != LRK_OK) return status;
+    written += rows_out;
+  }
+  return LRK_OK;
 }
 
 extern "C" int lrk_pack(const void *keys, const void *values, const float *positions, int64_t rows,

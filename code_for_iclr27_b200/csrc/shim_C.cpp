@@ -5,8 +5,8 @@
 // RuntimeError), its output allocation (torch::empty on the input's device,
 // through the caching allocator) and its stream (the current CUDA stream).
 // Added operators: refine and topk_smallest (selection); temporal_scores,
-// scores_from_keys, project_values and logits (scoring); compact_layers
-// (eviction over several layers in one call).
+// scores_from_keys, project_values and logits (scoring); compact_layers and
+// merge_layers (eviction and recall over several layers in one call).
 #include <vector>
 
 #include "shim_common.h"
@@ -204,6 +204,60 @@ std::vector<torch::Tensor> merge(torch::Tensor keys, torch::Tensor values, torch
                            current_stream()));
   }
   return {output_keys, output_values, output_positions};
+}
+
+// merge() of several layers in one launch (lrk_merge_layers): the same
+// checks per layer; the outputs are views into one allocation per tensor kind.
+std::vector<std::vector<torch::Tensor>> merge_layers(std::vector<torch::Tensor> keys, std::vector<torch::Tensor> values,
+                                                     std::vector<torch::Tensor> positions,
+                                                     std::vector<torch::Tensor> recalled,
+                                                     std::vector<torch::Tensor> recalled_positions,
+                                                     std::vector<torch::Tensor> mappings) {
+  const size_t n = keys.size();
+  TORCH_CHECK(n > 0 && values.size() == n && positions.size() == n && recalled.size() == n &&
+                  recalled_positions.size() == n && mappings.size() == n,
+              "merge_layers: one tensor of each kind per layer");
+  const auto dimension = keys[0].size(1);
+  std::vector<lrk_merge_layer> table(n);
+  int64_t total = 0;
+  for (size_t i = 0; i < n; ++i) {
+    for (const auto &tensor : {keys[i], values[i], positions[i], recalled[i], recalled_positions[i], mappings[i]})
+      check_recall_tensor(tensor, keys[0]);
+    TORCH_CHECK(keys[i].dim() == 2 && keys[i].size(1) == dimension && keys[i].sizes() == values[i].sizes(),
+                "Invalid K/V shape");
+    TORCH_CHECK(recalled[i].dim() == 3 && recalled[i].size(1) == 2 && recalled[i].size(2) == dimension,
+                "Invalid recalled shape");
+    TORCH_CHECK(keys[i].scalar_type() == keys[0].scalar_type() && values[i].scalar_type() == keys[0].scalar_type() &&
+                    recalled[i].scalar_type() == keys[0].scalar_type(),
+                "K/V dtypes differ");
+    TORCH_CHECK(positions[i].scalar_type() == at::kFloat && recalled_positions[i].scalar_type() == at::kFloat &&
+                    positions[i].numel() == keys[i].size(0) && recalled_positions[i].numel() == recalled[i].size(0),
+                "Invalid positions");
+    TORCH_CHECK(mappings[i].dim() == 1 && mappings[i].scalar_type() == at::kLong, "Mapping must be int64");
+    table[i] = {keys[i].data_ptr(), values[i].data_ptr(), positions[i].data_ptr<float>(), keys[i].size(0),
+                recalled[i].data_ptr(), recalled_positions[i].data_ptr<float>(), recalled[i].size(0),
+                mappings[i].data_ptr<int64_t>(), mappings[i].numel()};
+    total += mappings[i].numel();
+  }
+  c10::cuda::CUDAGuard guard(keys[0].device());
+  auto all_keys = torch::empty({total, dimension}, keys[0].options());
+  auto all_values = torch::empty_like(all_keys);
+  auto all_positions = torch::empty({total, 1}, positions[0].options());
+  if (total) {
+    check_status(lrk_merge_layers(table.data(), static_cast<int64_t>(n), dimension, dtype_code(keys[0].scalar_type()),
+                                  all_keys.data_ptr(), all_values.data_ptr(), all_positions.data_ptr<float>(),
+                                  current_stream()));
+  }
+  std::vector<std::vector<torch::Tensor>> out(3);
+  int64_t first = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const int64_t rows = mappings[i].numel();
+    out[0].push_back(all_keys.narrow(0, first, rows));
+    out[1].push_back(all_values.narrow(0, first, rows));
+    out[2].push_back(all_positions.narrow(0, first, rows));
+    first += rows;
+  }
+  return out;
 }
 
 // csrc/recall.cu:86-111
@@ -530,6 +584,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("append", &append);
   module.def("compact", &compact);
   module.def("compact_layers", &compact_layers);
+  module.def("merge_layers", &merge_layers);
   module.def("scores_from_keys", &scores_from_keys);
   module.def("pool", &pool);
   module.def("merge", &merge);

@@ -144,6 +144,69 @@ class PackedCache:
             layer.cumulative = all_cumulative[i]
         return int(offsets[-1])
 
+    def insert_payload(self, payload, metadata) -> int:
+        """Recall reinsertion (cache.py:201-253): payload [n, 2, D] (K, V rows
+        on the cache's device), metadata [n, 3] of (layer, head, position).
+        Every touched head's rows are merged with its recalled rows in
+        ascending position order (recall/planning.py:34-52: existing rows
+        first among equal positions is moot, duplicates are rejected); all
+        touched layers move in one lrk_merge_layers launch.  The touched
+        layers' positions come to the host in one copy and their merge maps
+        go back in one copy.  Returns the number of rows inserted."""
+        import torch
+
+        metadata = np.asarray(metadata, dtype=np.int64).reshape(-1, 3)
+        if payload.shape[:2] != (len(metadata), 2):
+            raise ValueError("Recall payload/identity shape mismatch")
+        if not len(metadata):
+            return 0
+        touched = np.unique(metadata[:, 0]).tolist()
+        device = self.layers[touched[0]].keys.device
+        previous = torch.cat([self.layers[l].positions.reshape(-1) for l in touched]).cpu().numpy().astype(np.int64)
+        maps, selections, plans, offset = [], [], [], 0
+        for layer_index in touched:
+            layer = self.layers[layer_index]
+            rows = np.flatnonzero(metadata[:, 0] == layer_index)
+            recalled = metadata[rows]
+            old = previous[offset:offset + sum(layer.head_lens)]
+            offset += sum(layer.head_lens)
+            mapping, lengths, start = [], [], 0
+            for head, length in enumerate(layer.head_lens):
+                chosen = np.flatnonzero(recalled[:, 1] == head)
+                combined = np.concatenate((old[start:start + length], recalled[chosen, 2]))
+                if np.unique(combined).size != combined.size:
+                    raise ValueError("Cannot merge duplicate physical KV identities")
+                sources = np.concatenate((np.arange(start, start + length), -chosen - 1))
+                mapping.append(sources[np.argsort(combined, kind="stable")])
+                lengths.append(int(combined.size))
+                start += length
+            maps.append(np.concatenate(mapping))
+            selections.append(rows)
+            plans.append((layer_index, lengths, recalled[:, 2]))
+        sizes = [m.size for m in maps]
+        all_maps = upload(np.concatenate(maps), device)
+        all_rows = upload(np.concatenate(selections), device)
+        all_positions = upload(np.concatenate([p[2] for p in plans]).astype(np.float32), device)
+        recalled_rows = payload.index_select(0, all_rows).contiguous()
+        counts = [len(s) for s in selections]
+        firsts = np.concatenate(([0], np.cumsum(counts)))
+        map_firsts = np.concatenate(([0], np.cumsum(sizes)))
+        layers = [self.layers[l] for l in touched]
+        keys, values, positions = operators().merge_layers(
+            [layer.keys for layer in layers], [layer.values for layer in layers],
+            [layer.positions for layer in layers],
+            [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
+            [all_positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
+            [all_maps[map_firsts[i]:map_firsts[i + 1]] for i in range(len(layers))])
+        cumulative = np.zeros((len(layers), len(layers[0].head_lens) + 1), dtype=np.int32)
+        np.cumsum(np.asarray([p[1] for p in plans], dtype=np.int64), axis=1, out=cumulative[:, 1:])
+        all_cumulative = upload(cumulative, device)
+        for i, (layer, (_, lengths, _)) in enumerate(zip(layers, plans)):
+            layer.keys, layer.values, layer.positions = keys[i], values[i], positions[i]
+            layer.head_lens = lengths
+            layer.cumulative = all_cumulative[i]
+        return int(len(metadata))
+
     def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
         """Drop head-relative rows (cache.py:92-180, GPU branch): one sorted
         absolute-row list and one _C.compact per touched layer.  Duplicate

@@ -80,8 +80,9 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
     (a CPU gather into a pinned staging slot, then one cudaMemcpyAsync,
     recall/cpu_worker.py:161-166, transport.py:221-229).  A size sweep gives
     the link rate where it is not latency-bound, against the pinned-copy peak.
-    The merge (_C.merge, one whole-layer copy per touched layer) is timed for
-    rows spread uniformly over (layer, head)."""
+    The merge is timed for rows spread uniformly over (layer, head): as
+    _C.merge per touched layer (one whole-layer copy each), and as one
+    lrk_merge_layers launch for all of them."""
     import torch
 
     lib = abi.library()
@@ -205,6 +206,22 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
         for mapping, count in plans:
             merged_bytes += 2 * (layer_rows + count) * (4 * dim + 4)
         merge = _median(merge_us)
+        # The same event as one lrk_merge_layers launch over every touched layer.
+        n = len(plans)
+        layers_args = ([keys] * n, [values] * n, [positions] * n, [recalled_rows] * n, [recalled_positions] * n,
+                       [mapping for mapping, _ in plans])
+        for _ in range(3):
+            C.merge_layers(*layers_args)
+        torch.cuda.synchronize()
+        merge_layers_us = []
+        for _ in range(events):
+            a, b = _events()
+            a.record()
+            C.merge_layers(*layers_args)
+            b.record()
+            torch.cuda.synchronize()
+            merge_layers_us.append(a.elapsed_time(b) * 1e3)
+        merge_layers = _median(merge_layers_us)
 
         link_bytes = requests * recall_rows * (4 * dim + 8)  # K, V rows + the int64 index
         zero_copy_us = results["zero_copy"]["device_us"]
@@ -221,6 +238,8 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
             "sweep_frac_of_peak_at_32MiB": sweep[-1]["zero_copy_gather_GBps"] / peak,
             "merge_us_per_request_event": merge,
             "merge_GBps": merged_bytes / (merge / 1e6) / 1e9,
+            "merge_layers_us_per_request_event": merge_layers,
+            "merge_layers_GBps": merged_bytes / (merge_layers / 1e6) / 1e9,
         }
     finally:
         for pool in pools:

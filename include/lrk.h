@@ -262,6 +262,26 @@ int lrk_merge(const void *keys, const void *values, const float *positions, int6
               const int64_t *mapping, int64_t out_rows, int64_t dimension, int dtype,
               void *out_keys, void *out_values, float *out_positions, lrk_stream_t stream);
 
+/* One layer of lrk_merge_layers: lrk_merge's inputs, and out_rows output rows. */
+typedef struct lrk_merge_layer {
+  const void *keys;                /* [rows, dimension] */
+  const void *values;
+  const float *positions;          /* [rows] */
+  int64_t rows;
+  const void *recalled;            /* [recalled_rows, 2, dimension] (K then V) */
+  const float *recalled_positions; /* [recalled_rows] */
+  int64_t recalled_rows;
+  const int64_t *mapping;          /* [out_rows], as lrk_merge's */
+  int64_t out_rows;
+} lrk_merge_layer;
+
+/* lrk_merge of several layers in one launch: layer i's output rows follow
+ * those of layers 0 .. i-1 in out_keys / out_values / out_positions (one
+ * allocation for every touched layer of a recall event).  Same rows as one
+ * lrk_merge per layer.  No counterpart in the reference (new entry point). */
+int lrk_merge_layers(const lrk_merge_layer *layers, int64_t count, int64_t dimension, int dtype, void *out_keys,
+                     void *out_values, float *out_positions, lrk_stream_t stream);
+
 /* Gather evicted rows into an archive payload.
  * Replaces _C.pack (csrc/recall.cu:86-111, kernel :30-47; bound at
  * csrc/bindings.cpp:27).  payload [count, 2, dimension], metadata [count, 3]

@@ -211,3 +211,67 @@ def test_audit_pass_evicts_like_the_host_composition():
     np.testing.assert_array_equal(result.references.positions, references.positions)
     np.testing.assert_array_equal(result.references.scores.view(np.uint32), references.scores.view(np.uint32))
     assert_same_cache(caches[0], caches[1])
+
+
+def test_insert_payload_restores_evicted_rows():
+    """Round trip: rows evicted from several layers and heads, reinserted with
+    their K/V and positions (one multi-layer merge), leave the cache exactly
+    as before the eviction -- rows back in position order, head lengths and
+    cumulative lengths restored."""
+    import torch
+
+    cache = make_cache(8, layers=4, heads=4, dim=32)
+    before = host_copy(cache)
+    rng = np.random.default_rng(8)
+    removals, metadata, payload = {}, [], []
+    for layer_index, layer in enumerate(cache.layers):
+        if layer_index == 2:
+            continue  # an untouched layer
+        bounds = layer.bounds()
+        for head, length in enumerate(layer.head_lens):
+            picks = np.sort(rng.choice(np.arange(30, length), 9, replace=False))  # not prompt rows
+            removals[(layer_index, head)] = picks
+            rows = torch.as_tensor(bounds[head] + picks, device=layer.keys.device)
+            payload.append(torch.stack([layer.keys[rows], layer.values[rows]], dim=1))
+            for p, position in zip(picks, layer.positions.reshape(-1)[rows].cpu().numpy()):
+                metadata.append((layer_index, head, int(position)))
+    cache.remove_positions(removals)
+    order = rng.permutation(len(metadata))  # any payload order
+    payload = torch.cat(payload)[torch.as_tensor(order, device=payload[0].device)]
+    metadata = np.asarray(metadata)[order]
+    assert cache.insert_payload(payload, metadata) == len(metadata)
+    for layer, (keys, values, positions, lens, prompts) in zip(cache.layers, before):
+        np.testing.assert_array_equal(bits(layer.keys), keys)
+        np.testing.assert_array_equal(bits(layer.values), values)
+        np.testing.assert_array_equal(layer.positions.cpu().numpy(), positions)
+        assert layer.head_lens == lens and layer.prompt_lens == prompts
+        np.testing.assert_array_equal(layer.cumulative.cpu().numpy(), np.concatenate(([0], np.cumsum(lens))))
+    with pytest.raises(ValueError):  # a row that is already resident
+        cache.insert_payload(payload[:1], metadata[:1])
+
+
+def test_merge_layers_equals_per_layer_merge():
+    import torch
+
+    from code_for_iclr27_b200 import operators
+
+    C = operators()
+    g = torch.Generator().manual_seed(4)
+    dev = "cuda"
+    ins, outs = [], []
+    for layer in range(5):
+        rows, dim, recalled = int(torch.randint(10, 300, (1,), generator=g)), 64, int(torch.randint(0, 40, (1,), generator=g))
+        keys = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(dev)
+        values = torch.randn(rows, dim, generator=g).to(torch.bfloat16).to(dev)
+        positions = torch.randn(rows, 1, generator=g).to(dev)
+        rec = torch.randn(max(recalled, 1), 2, dim, generator=g).to(torch.bfloat16).to(dev)
+        rec_pos = torch.randn(max(recalled, 1), generator=g).to(dev)
+        mapping = torch.cat([torch.arange(rows), -torch.arange(recalled) - 1])[torch.randperm(rows + recalled, generator=g)]
+        if layer == 3:
+            mapping = mapping[:0]  # a layer with no output rows
+        ins.append((keys, values, positions, rec, rec_pos, mapping.to(dev)))
+        outs.append(C.merge(*ins[-1]))
+    merged = C.merge_layers(*[list(t) for t in zip(*ins)])
+    for i, expected in enumerate(outs):
+        for got, want in zip((merged[0][i], merged[1][i], merged[2][i]), expected):
+            assert torch.equal(got, want)
