@@ -27,7 +27,7 @@ LAYER_ROWS = 8 * 34880
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
-                                           "project", "logits", "logits_odd"])
+                                           "project", "logits", "logits_odd", "from_keys", "table_fused"])
     parser.add_argument("--iters", type=int, default=3)
     args = parser.parse_args(argv)
 
@@ -77,6 +77,27 @@ def main(argv=None):
         keys = torch.randn(count, 128, generator=g, device=dev).to(torch.bfloat16)
         step = 16 if args.case == "logits" else 8
         run = lambda: C.logits(queries, keys, step, (count + 7) // 8 * 8)
+    elif args.case in ("from_keys", "table_fused"):
+        # One configs[1] layer scored straight from its keys (lrk_scores_from_keys), or
+        # through its logits (table_fused: cuBLAS / lrk_logits, then lrk_temporal_scores):
+        # 8 KV heads of 34,880 / 34,881 keys (both step orders), 250 queries x 4 groups.
+        from .kvcache import PackedCache
+
+        lens = [34880, 34881] * 4
+        rows = sum(lens)
+        cache = PackedCache()
+        keys = torch.randn(rows, 128, generator=g, device=dev).to(torch.bfloat16)
+        values = torch.randn(rows, 128, generator=g, device=dev).to(torch.bfloat16)
+        positions = torch.cat([torch.arange(n, dtype=torch.float32, device=dev) for n in lens])
+        cache.add_layer(keys, values, positions, lens, [32768] * 8)
+        queries = [(torch.randn(250, 32, 128, generator=g, device=dev) * 2).to(torch.bfloat16)]
+        gradients = [torch.randn(32, 128, generator=g, device=dev) / math.sqrt(128)]
+        qpos = torch.arange(34880 - 250, 34880, dtype=torch.int64, device=dev)
+        margin = torch.tensor([1.0], device=dev)
+        from .audit import score_table_from_keys, score_table_fused
+
+        table = score_table_from_keys if args.case == "from_keys" else score_table_fused
+        run = lambda: table(cache, queries, qpos, gradients, margin)
     elif args.case == "project":
         values = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
         gradients = torch.randn(8 * 4, 128, generator=g, device=dev)
@@ -89,10 +110,16 @@ def main(argv=None):
         pooled = C.pool(raw, bounds, 1962, 7)
         starts = torch.zeros(256, dtype=torch.int64, device=dev)
         run = lambda: C.refine(raw, pooled, bounds[1:].contiguous(), starts, 64512)
+    times = []
     for _ in range(args.iters):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
         run()
-    torch.cuda.synchronize()
-    print(f"{args.case}: {args.iters} iterations ok")
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    times.sort()
+    print(f"{args.case}: {args.iters} iterations ok, median {times[len(times) // 2]:.3f} ms (CUDA events)")
 
 
 if __name__ == "__main__":
