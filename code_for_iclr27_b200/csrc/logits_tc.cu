@@ -4,22 +4,22 @@
 //
 // cuBLAS accumulates each product in float32 over K/16 sixteen-term tensor-core
 // steps in increasing k when the key count is even, and over K/8 eight-term
-// steps when it is odd.  A sixteen-term step whose upper eight terms are zero
-// in A (and finite in B) gives exactly the eight-term step's result (measured
-// on B200 over 512k dot products), so both orders run as UMMA
+// steps when it is odd.  A sixteen-term step whose upper or lower eight terms
+// are zero in A (and finite in B) gives exactly the eight-term step's result
+// (measured on B200 against torch.matmul at every tested shape, configs[1]
+// heads included), so both orders run as UMMA
 // (tcgen05.mma kind::f16, M = 128, N = 128, K = 16):
 //   sixteen-term order   A = the query tile, B = the key tile, as usual;
-//   eight-term order     A = the query tile with a zero chunk after each
-//                        8-element chunk (built in shared memory), so step j
-//                        multiplies query chunk j (and zeros); B's step j
-//                        reads key chunks j and j + 1 from a copy of the key
-//                        tile that starts at chunk 7 * (j / 7) -- three
-//                        overlapping 64-element loads (chunks 0-7, 7-14,
-//                        14-21; past chunk 15 the load returns zeros).
+//   eight-term order     step j reads the key tile's 32-byte pair of
+//                        chunks that holds chunk j (the sixteen-term order's
+//                        pairs, each read twice), and A (built in shared
+//                        memory) holds query chunk j in the half of the step
+//                        that meets key chunk j and zeros in the other, so
+//                        the step multiplies query chunk j by key chunk j
+//                        alone.
 // Operands are K-major with 128-byte swizzling (8 rows x 128 B atoms, what a
 // 64-element x 128-row TMA box writes); step j starts inside its atom at
-// 32-byte (sixteen-term A and B, eight-term A) or 16-byte (eight-term B)
-// offsets.
+// 32-byte offsets.
 //
 // One CTA (1 per SM) owns 128 query rows and a contiguous range of 128-key
 // tiles; warp-specialised:
@@ -69,8 +69,8 @@ struct TcLayout {
   static constexpr int kChunks = DIM / 8;                        // 8-element chunks per row
   static constexpr int kSteps = EIGHT ? kChunks : kChunks / 2;   // UMMA K=16 steps per tile
   static constexpr int kAAtoms = EIGHT ? DIM / 32 : DIM / 64;    // query tile (interleaved for EIGHT)
-  static constexpr int kBAtoms = EIGHT ? (kChunks + 6) / 7 : DIM / 64;
-  static constexpr int kStages = EIGHT ? 2 : 4;
+  static constexpr int kBAtoms = DIM / 64;
+  static constexpr int kStages = EIGHT ? 3 : 4;
   static constexpr uint32_t kOut = 0;                             // 2 staging tiles
   static constexpr uint32_t kA = kOut + 2 * kOutTile;
   static constexpr uint32_t kB = kA + kAAtoms * kAtom;
@@ -110,17 +110,18 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   auto rotated = [&](int t) { return (t + rotation) % tiles; };
 
   if (warp < kEpilogueWarps) {
-    // The query tile, swizzled; for EIGHT each 8-element chunk j is followed
-    // by a zero chunk (A-chunk 2j = query chunk j, A-chunk 2j + 1 = 0).
+    // The query tile, swizzled; for EIGHT step j's 32-byte window holds query
+    // chunk j in the half that meets key chunk j and zeros in the other
+    // (A-chunks 2j, 2j + 1 = (q_j, 0) for even j, (0, q_j) for odd j).
     constexpr int kQChunks = DIM / 8;
     for (int i = threadIdx.x; i < kRows * kQChunks; i += kEpilogueWarps * 32) {
       const int r = i / kQChunks, j = i % kQChunks;
       uint4 v = make_uint4(0, 0, 0, 0);
       if (m0 + r < rows) v = __ldg(reinterpret_cast<const uint4 *>(queries + (m0 + r) * DIM) + j);
-      const int a = EIGHT ? 2 * j : j;  // chunk index in the A tile
+      const int a = EIGHT ? 2 * j + (j & 1) : j;  // chunk index in the A tile
       *reinterpret_cast<uint4 *>(smem + L::kA + (a >> 3) * kAtom + swizzled(r, a & 7)) = v;
       if (EIGHT) {
-        const int z = 2 * j + 1;
+        const int z = 2 * j + 1 - (j & 1);
         *reinterpret_cast<uint4 *>(smem + L::kA + (z >> 3) * kAtom + swizzled(r, z & 7)) = make_uint4(0, 0, 0, 0);
       }
     }
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const int y = static_cast<int>((t_begin + rotated(t)) * kKeys);
         const uint32_t dst = base + L::kB + s * L::kStage;
 #pragma unroll
-        for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &key_map, (EIGHT ? 7 * b : 8 * b) * 8, y, full(s));
+        for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &key_map, 64 * b, y, full(s));
       };
       int loaded = 0;  // key tiles whose loads were issued
       for (; loaded < tiles && loaded < S; ++loaded) load_tile(loaded, loaded);
@@ -175,11 +176,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         const uint32_t d = tmem + a * kKeys;
 #pragma unroll
         for (int j = 0; j < L::kSteps; ++j) {
-          // A: 32 bytes per step through its atoms (EIGHT: 2 chunks = query chunk j, zeros).
+          // A: 32 bytes per step through its atoms (EIGHT: query chunk j and zeros).
           const uint32_t a_addr = A + (j >> 2) * kAtom + (j & 3) * 32;
-          uint32_t b_addr;
-          if constexpr (EIGHT) b_addr = B + (j / 7) * kAtom + (j % 7) * 16;  // key chunks j, j + 1
-          else b_addr = B + (j >> 2) * kAtom + (j & 3) * 32;
+          // B: the 32-byte pair of key chunks holding chunk j (EIGHT) or 2j, 2j + 1.
+          const int pair = EIGHT ? j >> 1 : j;
+          const uint32_t b_addr = B + (pair >> 2) * kAtom + (pair & 3) * 32;
           umma(d, smem_descriptor(a_addr), smem_descriptor(b_addr), j > 0);
         }
         umma_commit(acc_full(a));
