@@ -23,10 +23,12 @@
 //
 // One CTA (1 per SM) owns 128 query rows and a contiguous range of 128-key
 // tiles; warp-specialised:
-//   warp 8, one thread   TMA loads of key tiles into a ring of stages
-//                        (full/empty mbarriers) and the UMMAs of each tile
-//                        into one of four TMEM accumulators (all 512 columns), committed to the
-//                        accumulator's and the stage's mbarriers;
+//   warp 9, one thread   TMA loads of key tiles into a ring of stages
+//                        (full/empty mbarriers);
+//   warp 8, one thread   the UMMAs of each tile into one of four TMEM
+//                        accumulators (all 512 columns), committed to the
+//                        accumulator's and the stage's mbarriers -- it never
+//                        waits for its own MMAs, so several tiles stay queued;
 //   warps 0-7            build the query tile once; then two warpgroups
 //                        draining alternate tiles:
 //                        tcgen05.ld of the warp's 32 TMEM lanes (= query rows),
@@ -58,8 +60,9 @@ using namespace tc;
 
 constexpr int kEpilogueGroups = 2;                  // warpgroups draining alternate tiles
 constexpr int kEpilogueWarps = 4 * kEpilogueGroups;  // warps 0-7
-constexpr int kIssuerWarp = kEpilogueWarps;          // warp 8
-constexpr int kThreadsTc = (kEpilogueWarps + 1) * 32;
+constexpr int kIssuerWarp = kEpilogueWarps;          // warp 8: UMMA issue
+constexpr int kLoaderWarp = kEpilogueWarps + 1;      // warp 9: TMA loads
+constexpr int kThreadsTc = (kEpilogueWarps + 2) * 32;
 constexpr uint32_t kOutTile = kRows * kKeys * 2;  // one bf16 output tile (two 64-column halves)
 constexpr int kAccumulators = 4;                       // fp32 accumulators in TMEM
 constexpr uint32_t kTmemColumns = kAccumulators * kKeys;
@@ -78,7 +81,8 @@ struct TcLayout {
   static constexpr uint32_t kBarriers = kB + kStages * kStage;   // full[S] empty[S] acc_full[4] acc_empty[4]
   static constexpr uint32_t kTmemSlot = kBarriers + 128;
   static constexpr uint32_t kAbort = kTmemSlot + 8;
-  static constexpr uint32_t kBytes = kTmemSlot + 16 + 1024;       // + alignment slack
+  static constexpr uint32_t kCounters = kAbort + 8;                // tiles consumed by MMAs, tiles loaded
+  static constexpr uint32_t kBytes = kCounters + 8 + 1024;         // + alignment slack
 };
 
 template <int DIM, bool EIGHT>
@@ -138,6 +142,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     *abort = 0;
+    reinterpret_cast<volatile int *>(smem + L::kCounters)[0] = 0;
+    reinterpret_cast<volatile int *>(smem + L::kCounters)[1] = 0;
   }
   if (warp == kIssuerWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(base + L::kTmemSlot),
@@ -150,18 +156,29 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::kTmemSlot);
 
-  if (warp == kIssuerWarp) {
+  volatile int *counters = reinterpret_cast<volatile int *>(smem + L::kCounters);
+  if (warp == kLoaderWarp) {
     if (lane == 0) {
-      // ------------------------------------------- TMA loads + MMA issue
-      auto load_tile = [&](int t, int s) {
+      // ------------------------------------------------------- TMA loads
+      // Stage t % S takes tile t once the MMAs of tile t - S are done.
+      int loaded = 0;
+      for (int t = 0; t < tiles; ++t) {
+        const int s = t % S;
+        if (t >= S && !wait_phase(empty(s), ((t / S) - 1) & 1, abort)) break;
         expect_bytes(full(s), L::kStage);
         const int y = static_cast<int>((t_begin + rotated(t)) * kKeys);
         const uint32_t dst = base + L::kB + s * L::kStage;
 #pragma unroll
         for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &key_map, 64 * b, y, full(s));
-      };
-      int loaded = 0;  // key tiles whose loads were issued
-      for (; loaded < tiles && loaded < S; ++loaded) load_tile(loaded, loaded);
+        loaded = t + 1;
+      }
+      counters[1] = loaded;
+    }
+  } else if (warp == kIssuerWarp) {
+    if (lane == 0) {
+      // ------------------------------------------------------- MMA issue
+      // Never waits on its own MMAs inside the loop: the tensor pipe keeps
+      // up to kAccumulators tiles queued.
       int issued = 0;  // tiles whose MMAs were issued
       bool ok = true;
       for (int t = 0; t < tiles; ++t) {
@@ -186,23 +203,16 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
         umma_commit(acc_full(a));
         umma_commit(empty(s));
         issued = t + 1;
-        // Refill the stage of the previous tile once its MMAs are done.
-        if (t >= 1 && loaded < tiles) {
-          const int sp = (t - 1) % S;
-          if (!wait_phase(empty(sp), ((t - 1) / S) & 1, abort)) { ok = false; break; }
-          load_tile(loaded, sp);
-          ++loaded;
-        }
       }
       // Before the CTA may exit, every arrival this thread set in motion must
       // have landed (bounded waits, whatever the abort flag says).
       for (int t = issued > S ? issued - S : 0; t < issued; ++t) wait_phase(empty(t % S), (t / S) & 1, nullptr);
       if (!ok) {
-        for (int t = issued; t < loaded; ++t) wait_phase(full(t % S), (t / S) & 1, nullptr);
         for (int t = issued > kAccumulators ? issued - kAccumulators : 0; t < issued; ++t)
           wait_phase(acc_full(t % kAccumulators), (t / kAccumulators) & 1, nullptr);
         *abort = 1;
       }
+      counters[0] = issued;
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -275,6 +285,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     if (issuer) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");  // stores complete before exit
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  // After an abort, loads the MMAs never consumed must land before the
+  // shared memory is released (bounded waits).
+  if (warp == kLoaderWarp && lane == 0 && *abort) {
+    for (int t = counters[0]; t < counters[1]; ++t) wait_phase(full(t % S), (t / S) & 1, nullptr);
+  }
   __syncthreads();
   if (warp == kIssuerWarp) {
     if (lane == 0 && *abort) atomicAdd(&g_logits_timeouts, 1u);
