@@ -149,6 +149,22 @@ def query_chunk(query_chunk_size: int, groups: int, keys: int, element_size: int
     return min(query_chunk_size, max(1, (64 * 1024 ** 2) // bytes_per_query))
 
 
+_STREAMS = {}
+
+
+def _audit_streams(device):
+    """Per device: a stream for the audit's GEMM work and a high-priority
+    stream for its scoring (whose CTAs the block scheduler then takes first
+    when both have work queued)."""
+    import torch
+
+    key = torch.device(device).index
+    if key not in _STREAMS:
+        highest = torch.cuda.Stream.priority_range()[1] if hasattr(torch.cuda.Stream, "priority_range") else -1
+        _STREAMS[key] = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device, priority=highest))
+    return _STREAMS[key]
+
+
 def score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
                       denominator_epsilon=1e-6, query_chunk_size=250) -> ScoreTable:
     """compute_score_table with the fused scorer.  Per layer: one
@@ -162,9 +178,23 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
     import torch
 
     C = operators()
-    margin = base_margin.to(device=cache.layers[0].keys.device, dtype=torch.float32).reshape(1).contiguous()
+    device = cache.layers[0].keys.device
+    margin = base_margin.to(device=device, dtype=torch.float32).reshape(1).contiguous()
     qpos = query_positions.to(dtype=torch.int64).contiguous()
     parts, segments, ends, running = [], [], [], 0
+    # Layer l + 1's projection and logits GEMMs run on a side stream while
+    # layer l is scored on a high-priority stream (at most one layer ahead);
+    # the caller's stream waits for both at the end.
+    main = torch.cuda.current_stream(device)
+    side, scoring = _audit_streams(device)
+    side.wait_stream(main)
+    scoring.wait_stream(main)
+    scored = []
+    # Each layer's GEMM outputs stay referenced until the side stream has
+    # queued its wait for that layer's scoring, so the caching allocator
+    # reuses their blocks on the side stream only after the last read
+    # (no record_stream, whose deferred frees make the pool grow).
+    held = []
     for layer_index, layer in enumerate(cache.layers):
         heads = len(layer.head_lens)
         layer_queries = queries[layer_index]
@@ -172,20 +202,33 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
         scale = 1.0 / math.sqrt(layer.keys.shape[-1])
         bounds = layer.bounds()
         positions = layer.positions.reshape(-1)
-        projected = C.project_values(layer.values, gradients[layer_index].float().contiguous(), layer.cumulative,
-                                     groups)
         window, dim = layer_queries.shape[0], layer_queries.shape[-1]
-        # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
-        per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1).contiguous()
-        logits, pvs, kpos, firsts, lasts, chunks = [], [], [], [], [], []
-        for head in range(heads):
-            start, end = int(bounds[head]), int(bounds[head + 1])
-            candidate_start = int(layer.prompt_lens[head])
-            candidate_end = max(candidate_start, end - start - protect_recent)
-            if candidate_end <= candidate_start:
-                continue
-            chunk = query_chunk(query_chunk_size, groups, end - start, layer.keys.element_size())
-            logits.append(head_logits(per_head[head], layer.keys, start, end, chunk))
+        if layer_index >= 2:
+            side.wait_event(scored[layer_index - 2])
+            held.pop(0)
+        heads_kept = []
+        with torch.cuda.stream(side):
+            projected = C.project_values(layer.values, gradients[layer_index].float().contiguous(), layer.cumulative,
+                                         groups)
+            # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
+            per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1)
+            per_head = per_head.contiguous()
+            logits = []
+            for head in range(heads):
+                start, end = int(bounds[head]), int(bounds[head + 1])
+                candidate_start = int(layer.prompt_lens[head])
+                candidate_end = max(candidate_start, end - start - protect_recent)
+                if candidate_end <= candidate_start:
+                    continue
+                chunk = query_chunk(query_chunk_size, groups, end - start, layer.keys.element_size())
+                logits.append(head_logits(per_head[head], layer.keys, start, end, chunk))
+                heads_kept.append((head, start, end, candidate_start, candidate_end, chunk))
+            ready = torch.cuda.Event()
+            ready.record(side)
+        scoring.wait_event(ready)
+        held.append((projected, per_head, logits))
+        pvs, kpos, firsts, lasts, chunks = [], [], [], [], []
+        for head, start, end, candidate_start, candidate_end, chunk in heads_kept:
             pvs.append(projected[:, start:end])
             kpos.append(positions[start:end])
             firsts.append(candidate_start)
@@ -195,8 +238,19 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
             running += candidate_end - candidate_start
             ends.append(running)
         if logits:
-            parts.append(C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, scale,
-                                           denominator_epsilon, chunks))
+            with torch.cuda.stream(scoring):
+                part = C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, scale, denominator_epsilon,
+                                         chunks)
+            part.record_stream(main)
+            parts.append(part)
+        done = torch.cuda.Event()
+        done.record(scoring)
+        scored.append(done)
+    main.wait_stream(side)
+    main.wait_stream(scoring)
+    # The next work on the side stream (the next call) waits for the caller's
+    # stream, which now waits for every layer's scoring: releasing is safe.
+    held.clear()
     if not parts:
         raise RuntimeError("No eligible KV remains after prompt/recent protection")
     return ScoreTable(torch.cat(parts), segments, ends)
