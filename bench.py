@@ -204,16 +204,56 @@ class LaunchCounter:
 
 
 class Clocks:
-    """nvidia-smi clock and throttle samples during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region: NVML
+    every 10 ms from a thread (read-only queries), else nvidia-smi every
+    200 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
              "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
     def __init__(self, index: int):
-        self.index, self.process = index, None
+        self.index, self.process, self.thread = index, None, None
+        self.samples, self.nvml = [], []
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+
+        pynvml.nvmlInit()
+        uuid = getattr(torch.cuda.get_device_properties(self.index), "uuid", None)
+        if uuid is not None:
+            text = str(uuid)
+            return pynvml.nvmlDeviceGetHandleByUUID(text if text.startswith("GPU-") else "GPU-" + text)
+        return pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+
+        try:
+            import pynvml
+
+            handle = self._nvml_handle()
+            maximum = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.stop = threading.Event()
+
+            def sample():
+                while True:
+                    try:
+                        self.nvml.append((pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM), maximum,
+                                          pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
+                    except Exception:
+                        return
+                    if self.stop.wait(0.01):
+                        return
+
+            self.thread = threading.Thread(target=sample, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.process = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                                              "--format=csv,noheader,nounits", "-lms", "200"],
@@ -223,7 +263,10 @@ class Clocks:
         return self
 
     def __exit__(self, *exc):
-        self.samples = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            return
         if self.process is None:
             return
         self.process.terminate()
@@ -238,13 +281,18 @@ class Clocks:
                 self.samples.append(parts)
 
     def summary(self):
+        if self.nvml:
+            sm = [float(clock) for clock, _, _ in self.nvml]
+            reasons = sorted({name for _, _, mask in self.nvml for name, bit in self.REASONS if mask & bit})
+            return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.nvml[0][1]), "reasons": reasons,
+                    "samples": len(self.nvml), "source": "nvml, 10 ms"}
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(p[1]) for p in self.samples if p[1].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        names = [name for name, _ in self.REASONS]
         reasons = sorted({names[i] for p in self.samples for i in range(4) if p[4 + i].lower() == "active"})
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": float(self.samples[0][2]),
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(self.samples), "source": "nvidia-smi, 200 ms"}
 
 
 # --------------------------------------------------------------- CPU side
