@@ -5,9 +5,10 @@ _core/cache.py:15-93): per layer, keys and values [rows, D] with the rows of
 head 0, then head 1, ...; float32 position rows [rows, 1]; per-head lengths
 on the host and cumulative lengths (int32) on the device.  This class is the
 GPU branch of LazyRecallCache reduced to the KV bookkeeping: append
-(cache.py:33-52 -> _C.append), remove_positions (cache.py:92-180 ->
-_C.compact), insert_payload (cache.py:201-253 -> _C.merge) and archive
-packing (recall/transport.py:148-167 -> _C.pack).
+(cache.py:33-52 -> _C.append), remove_positions / remove_selected
+(cache.py:92-180 -> _C.compact_layers), insert_payload (cache.py:201-253 ->
+_C.merge_layers) and archive packing (recall/transport.py:148-167 ->
+_C.pack).
 """
 from __future__ import annotations
 
@@ -209,7 +210,8 @@ class PackedCache:
 
     def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
         """Drop head-relative rows (cache.py:92-180, GPU branch): one sorted
-        absolute-row list and one _C.compact per touched layer.  Duplicate
+        absolute-row list, then one _C.compact_layers call (a compaction per
+        touched layer).  Duplicate
         positions of a head count once; any position outside its head raises
         IndexError before the cache changes.  The host bookkeeping is
         vectorised over all (layer, head) entries, and the rows of every
@@ -246,15 +248,16 @@ class PackedCache:
             self.layers[layer_index].head_lens[head] -= int(count)
             self.layers[layer_index].prompt_lens[head] -= int(prompt)
         touched, first = np.unique(layer_of, return_index=True)
-        last = np.append(first[1:], rows.size)
         device = self.layers[int(touched[0])].keys.device
         all_rows = upload(rows, device)
         cumulative = np.stack([self.layers[int(l)].bounds() for l in touched]).astype(np.int32)
         all_cumulative = upload(cumulative, device)
-        C = operators()
-        for i, layer_index in enumerate(touched.tolist()):
-            layer = self.layers[layer_index]
-            layer.keys, layer.values, layer.positions = C.compact(layer.keys, layer.values, layer.positions,
-                                                                  all_rows[first[i]:last[i]])
+        layers = [self.layers[int(l)] for l in touched]
+        offsets = np.append(first, rows.size).tolist()
+        keys, values, positions = operators().compact_layers(
+            [layer.keys for layer in layers], [layer.values for layer in layers],
+            [layer.positions for layer in layers], all_rows, offsets)
+        for i, layer in enumerate(layers):
+            layer.keys, layer.values, layer.positions = keys[i], values[i], positions[i]
             layer.cumulative = all_cumulative[i]
         return int(removed.sum())
