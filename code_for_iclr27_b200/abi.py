@@ -43,6 +43,11 @@ class MergeLayer(ctypes.Structure):
                 ("recalled_positions", P), ("recalled_rows", I64), ("mapping", P), ("out_rows", I64)]
 
 
+class LogitsHead(ctypes.Structure):
+    """lrk_logits_head (include/lrk.h)."""
+    _fields_ = [("queries", P), ("keys", P), ("count", I64), ("k_step", I64), ("out", P), ("out_stride", I64)]
+
+
 class KeyLayer(ctypes.Structure):
     """lrk_key_layer (include/lrk.h)."""
     _fields_ = [("keys", P), ("rows", I64)]
@@ -82,6 +87,7 @@ SIGNATURES = {
     "lrk_project_values": (I32, [P, I32, I64, I64, P, P, I64, I64, P, P]),
     "lrk_check_division": (I32, [ctypes.c_uint64, ctypes.c_uint64, P, P]),
     "lrk_logits": (I32, [P, I64, P, I64, I64, I64, P, I64, P]),
+    "lrk_logits_heads": (I32, [P, I64, I64, I64, P]),
     "lrk_logits_timeouts": (I32, [P]),
     "lrk_scores_from_keys_workspace_bytes": (SIZE, [ctypes.POINTER(KeySegment), I64, I64, I64]),
     "lrk_scores_from_keys": (I32, [ctypes.POINTER(KeySegment), I64, ctypes.POINTER(KeyLayer), I64, P, I64, I64, I64,

@@ -53,10 +53,11 @@ def temporal_head_scores(queries, query_positions, keys, key_positions, values, 
     result = None
     for start in range(0, queries.shape[0], chunk_size):
         end = min(start + chunk_size, queries.shape[0])
-        # A contiguous [chunk, G, D] block folds into one [chunk*G, D] x [D, L]
-        # GEMM; the permuted query-history view of scoring.py:260-262 does not,
-        # and torch.matmul then runs `chunk` batched [G, D] x [D, L] products.
-        logits = torch.matmul(queries[start:end].to(keys.dtype).contiguous(), keys.transpose(0, 1))
+        # As scoring.py:184: on the permuted query-history view
+        # (reference_query_view) torch.matmul runs `chunk` batched
+        # [G, D] x [D, L] products; a contiguous block would fold into one
+        # [chunk*G, D] x [D, L] GEMM, which cuBLAS may order differently.
+        logits = torch.matmul(queries[start:end].to(keys.dtype), keys.transpose(0, 1))
         probabilities, output_projection = C.temporal_probabilities(
             logits.contiguous(), projected_values, query_positions[start:end], key_positions,
             1.0 / math.sqrt(keys.shape[-1]))
@@ -86,7 +87,7 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
             candidate_end = max(candidate_start, end - start - protect_recent)
             if candidate_end <= candidate_start:
                 continue
-            mapped = queries[layer_index][:, head * groups:(head + 1) * groups]
+            mapped = reference_query_view(queries[layer_index][:, head * groups:(head + 1) * groups])
             scores = temporal_head_scores(mapped, query_positions, layer.keys[start:end], positions[start:end],
                                           layer.values[start:end], candidate_start, candidate_end,
                                           gradients[layer_index][head * groups:(head + 1) * groups], base_margin,
@@ -101,44 +102,96 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
     return ScoreTable(torch.cat(parts), segments, ends)
 
 
+def reference_query_view(head_queries):
+    """[W, G, D] queries of one KV head laid out as the reference's
+    mapped_queries (scoring.py:260: query_history[0, q0:q1].permute(1, 0, 2)
+    of a contiguous [1, heads * G, W, D] history, i.e. strides (D, W*D, 1)).
+    torch.matmul cannot fold such a view into one matrix, so it runs the
+    batched GEMM the reference runs: one [G, D] x [D, L] product per query."""
+    return head_queries.permute(1, 0, 2).contiguous().permute(1, 0, 2)
+
+
+def tensor_core_order_matches(length: int, window: int, groups: int, chunk: int) -> bool:
+    """Whether the reference's logits GEMM for a head -- torch.matmul of
+    reference_query_view(queries)[a:a + chunk] and the head's keys, a batched
+    GEMM of `chunk` [groups, D] x [D, length] products per query chunk
+    (scoring.py:184) -- takes the tensor-core step order lrk_logits
+    reproduces: 16 terms for an even key count, 8 for an odd one.  Measured on
+    B200 against torch.matmul over groups 1, 2, 4, 8, windows 9, 37, 250 and
+    key counts 1 .. 600 plus larger ones: with one query row per product
+    (groups 1) cuBLAS runs other kernels at almost every odd count; with two
+    or more, every even count matches, and odd counts match from 1024 keys on
+    when every query chunk holds at least 9 queries (chunks of 7 and 2 queries
+    at 8 groups miss even at 34,881 keys).  The other heads take the
+    reference's own GEMM."""
+    if groups < 2:
+        return False
+    if length % 2 == 0:
+        return True
+    batches = {min(chunk, window - a) for a in range(0, window, chunk)}
+    return length >= 1024 and min(batches) >= 9
+
+
 def head_logits(per_head_queries, keys, start: int, end: int, chunk: int):
     """bf16 logits [W, G, L] of one head, equal bit for bit to the logits the
     reference computes per query chunk with torch.matmul (scoring.py:184), as
-    a view of rows padded to a 16-byte multiple where possible.
-
-    cuBLAS accumulates each product in tensor-core steps of 16 terms for an
-    even key count -- the GEMM over the 8-aligned key block, which cuBLAS runs
-    about 5x faster, gives the same bits -- and of 8 terms for an odd one,
-    which lrk_logits reproduces (k_step 8).  An odd key count outside
-    lrk_logits' shapes takes the reference's own chunked GEMM."""
+    a view of rows padded to a 16-byte multiple where lrk_logits computes
+    them (tensor_core_order_matches); otherwise the reference's own chunked
+    GEMM on reference_query_view."""
     import torch
 
     window, groups, dim = per_head_queries.shape
     length = end - start
-    flat = per_head_queries.contiguous().view(window * groups, dim)
-    if length % 2 == 0:
-        aligned = _aligned_keys(keys, start, end)
-        return torch.matmul(flat, aligned.transpose(0, 1)).view(window, groups, -1)[:, :, :length]
-    if keys.dtype == torch.bfloat16 and dim in (64, 128):
-        padded = operators().logits(flat, keys[start:end], 8, (length + 7) // 8 * 8)
+    if (keys.dtype == torch.bfloat16 and per_head_queries.dtype == torch.bfloat16 and dim in (64, 128)
+            and tensor_core_order_matches(length, window, groups, chunk)):
+        flat = per_head_queries.contiguous().view(window * groups, dim)
+        padded = operators().logits(flat, keys[start:end], 8 if length % 2 else 16, (length + 7) // 8 * 8)
         return padded.view(window, groups, -1)[:, :, :length]
+    mapped = reference_query_view(per_head_queries)
     head_keys = keys[start:end]
-    return torch.cat([torch.matmul(per_head_queries[a:a + chunk], head_keys.transpose(0, 1))
+    return torch.cat([torch.matmul(mapped[a:a + chunk].to(keys.dtype), head_keys.transpose(0, 1))
                       for a in range(0, window, chunk)])
 
 
-def _aligned_keys(keys, start, end, multiple=8):
-    """Keys of one head extended to a multiple of 8 rows.  cuBLAS runs the
-    [W*G, D] x [D, L] logits GEMM about 5x faster when L is a multiple of 8
-    (B200: 20 vs 110 us at L ~ 35k); the extra columns are never read.  The
-    view reaches into the next head's rows, or is a zero-padded copy at the
-    end of the layer."""
+def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stream=None):
+    """bf16 logits [W, G, L] of several heads of one layer, each equal bit for
+    bit to head_logits.  per_head: [heads, W * G, D] queries; spans: (head,
+    start, end, chunk) per entry.  The heads whose order lrk_logits
+    reproduces run in one lrk_logits_heads launch (both step orders, one pass
+    over the GPU); the others take the reference's GEMM (head_logits), on
+    reference_stream when given: cuBLAS may pick another algorithm on another
+    stream (measured: the batched GEMV of one query row per product differs
+    in the last bit between streams), so those GEMMs run where the reference
+    runs them, on the caller's stream."""
     import torch
 
-    padded = -(-(end - start) // multiple) * multiple
-    if start + padded <= keys.shape[0]:
-        return keys[start:start + padded]
-    return torch.cat([keys[start:end], keys.new_zeros(padded - (end - start), keys.shape[1])])
+    dim = per_head.shape[-1]
+    out = [None] * len(spans)
+    fast, slow = [], []
+    for i, (head, start, end, chunk) in enumerate(spans):
+        if (keys.dtype == torch.bfloat16 and dim in (64, 128) and per_head.dtype == torch.bfloat16
+                and tensor_core_order_matches(end - start, window, groups, chunk)):
+            fast.append(i)
+        else:
+            slow.append(i)
+    if slow:
+        current = torch.cuda.current_stream(per_head.device)
+        stream = reference_stream if reference_stream is not None else current
+        stream.wait_stream(current)
+        with torch.cuda.stream(stream):
+            for i in slow:
+                head, start, end, chunk = spans[i]
+                out[i] = head_logits(per_head[head].view(window, groups, dim), keys, start, end, chunk)
+        current.wait_stream(stream)
+    if fast:
+        heads = [spans[i][0] for i in fast]
+        starts = [spans[i][1] for i in fast]
+        ends = [spans[i][2] for i in fast]
+        steps = [8 if (e - b) % 2 else 16 for b, e in zip(starts, ends)]
+        views = operators().logits_heads(per_head, keys, heads, starts, ends, steps)
+        for i, view, b, e in zip(fast, views, starts, ends):
+            out[i] = view.view(window, groups, -1)[:, :, :e - b]
+    return out
 
 
 def query_chunk(query_chunk_size: int, groups: int, keys: int, element_size: int) -> int:
@@ -169,8 +222,9 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
                       denominator_epsilon=1e-6, query_chunk_size=250) -> ScoreTable:
     """compute_score_table with the fused scorer.  Per layer: one
     lrk_project_values call (g V^T for every head, scoring.py:175, in the
-    float32 GEMM's accumulation order), one bf16 Q K^T GEMM per head
-    (scoring.py:184), then one lrk_temporal_scores call over all of the
+    float32 GEMM's accumulation order), the bf16 Q K^T GEMMs of all heads
+    (scoring.py:184) in one lrk_logits_heads launch (layer_logits), then one
+    lrk_temporal_scores call over all of the
     layer's heads -- the probabilities never reach HBM.  Each head keeps the
     composition's query chunks for its running maximum, so the scores are
     bit-identical to score_table (the temporal_probabilities + temporal_risk
@@ -213,7 +267,6 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
             # [heads, window * groups, D]: each head's queries one contiguous GEMM operand.
             per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1)
             per_head = per_head.contiguous()
-            logits = []
             for head in range(heads):
                 start, end = int(bounds[head]), int(bounds[head + 1])
                 candidate_start = int(layer.prompt_lens[head])
@@ -221,8 +274,10 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
                 if candidate_end <= candidate_start:
                     continue
                 chunk = query_chunk(query_chunk_size, groups, end - start, layer.keys.element_size())
-                logits.append(head_logits(per_head[head], layer.keys, start, end, chunk))
                 heads_kept.append((head, start, end, candidate_start, candidate_end, chunk))
+            logits = layer_logits(per_head.view(heads, window * groups, dim), layer.keys,
+                                  [(h, b, e, c) for h, b, e, _, _, c in heads_kept], window, groups,
+                                  reference_stream=main)
             ready = torch.cuda.Event()
             ready.record(side)
         scoring.wait_event(ready)
@@ -276,8 +331,10 @@ def score_table_from_keys(cache, queries, query_positions, gradients, base_margi
     lrk_scores_from_keys call for every head of every layer, which runs the
     bf16 Q K^T GEMM (scoring.py:184, cuBLAS's step order for the head's key
     count) and the row statistics as one tensor-core kernel and writes only
-    the candidate columns' logits for the risk step.  Bit-identical to
-    score_table_fused and score_table."""
+    the candidate columns' logits for the risk step.  Heads whose GEMM cuBLAS
+    runs in another order (tensor_core_order_matches false) are scored as in
+    score_table_fused instead.  Bit-identical to score_table_fused and
+    score_table."""
     import torch
 
     C = operators()
@@ -310,9 +367,26 @@ def score_table_from_keys(cache, queries, query_positions, gradients, base_margi
     if not table:
         raise RuntimeError("No eligible KV remains after prompt/recent protection")
     scale = 1.0 / math.sqrt(cache.layers[0].keys.shape[-1])
-    scores = C.scores_from_keys(keys, layer_queries, projected, positions, table, groups, qpos, margin, scale,
-                                denominator_epsilon)
-    return ScoreTable(scores, segments, ends)
+    window = qpos.shape[0]
+    direct = [i for i, entry in enumerate(table) if tensor_core_order_matches(entry[3], window, groups, entry[6])]
+    if len(direct) == len(table):
+        scores = C.scores_from_keys(keys, layer_queries, projected, positions, table, groups, qpos, margin, scale,
+                                    denominator_epsilon)
+        return ScoreTable(scores, segments, ends)
+    parts = [None] * len(table)
+    if direct:
+        scores = C.scores_from_keys(keys, layer_queries, projected, positions, [table[i] for i in direct], groups,
+                                    qpos, margin, scale, denominator_epsilon)
+        for i, part in zip(direct, torch.split(scores, [table[i][5] - table[i][4] for i in direct])):
+            parts[i] = part
+    for i in sorted(set(range(len(table))) - set(direct)):
+        layer_index, head, start, length, first, last, chunk = table[i]
+        head_queries = layer_queries[layer_index][:, head * groups:(head + 1) * groups]
+        logits = head_logits(head_queries, keys[layer_index], start, start + length, chunk)
+        parts[i] = C.temporal_scores([logits], [projected[layer_index][:, start:start + length]],
+                                     [positions[layer_index][start:start + length]], [first], [last], qpos, margin,
+                                     scale, denominator_epsilon, [chunk])
+    return ScoreTable(torch.cat(parts), segments, ends)
 
 
 def pool_table(table: ScoreTable, kernel_size: int = 7) -> ScoreTable:

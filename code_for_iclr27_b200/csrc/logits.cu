@@ -208,13 +208,13 @@ __global__ void __launch_bounds__(kThreads, 3) logits_kernel(const __nv_bfloat16
 namespace lrk {
 int launch_logits_tc(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, bool eight,
                      void *out, int64_t out_stride, cudaStream_t stream);
-}  // namespace lrk
+int launch_logits_heads(const lrk_logits_head *heads, int64_t head_count, int64_t rows, int64_t dim,
+                        cudaStream_t stream);
 
-using namespace lrk;
-
-extern "C" int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim,
-                          int64_t k_step, void *out, int64_t out_stride, lrk_stream_t stream) {
-  clear_error();
+namespace {
+// The argument rules of one head (lrk_logits, lrk_logits_heads).
+int check_logits_head(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim,
+                      int64_t k_step, const void *out, int64_t out_stride) {
   LRK_REQUIRE(rows >= 0 && count >= 0 && dim > 0, "invalid logits sizes");
   LRK_REQUIRE(k_step == 8 || k_step == 16, "k_step must be 8 or 16");
   LRK_REQUIRE(dim == 64 || dim == 128, "lrk_logits takes head dimension 64 or 128");
@@ -223,6 +223,44 @@ extern "C" int lrk_logits(const void *queries, int64_t rows, const void *keys, i
   if (rows == 0 || count == 0) return LRK_OK;
   LRK_REQUIRE(queries && keys && out, "null pointer");
   LRK_REQUIRE(aligned(queries, 16) && aligned(keys, 16) && aligned(out, 16), "logits operands must be 16-byte aligned");
+  return LRK_OK;
+}
+}  // namespace
+}  // namespace lrk
+
+using namespace lrk;
+
+extern "C" int lrk_logits_heads(const lrk_logits_head *heads, int64_t head_count, int64_t rows, int64_t dim,
+                                lrk_stream_t stream) {
+  clear_error();
+  LRK_REQUIRE(head_count >= 0 && rows >= 0, "invalid logits sizes");
+  LRK_REQUIRE(head_count == 0 || heads != nullptr, "null pointer");
+  bool work = false;
+  for (int64_t i = 0; i < head_count; ++i) {
+    const lrk_logits_head &h = heads[i];
+    const int status = check_logits_head(h.queries, rows, h.keys, h.count, dim, h.k_step, h.out, h.out_stride);
+    if (status != LRK_OK) return status;
+    work = work || h.count > 0;
+  }
+  if (rows == 0 || !work) return LRK_OK;
+#ifndef LRK_LOGITS_MMA_SYNC
+  return launch_logits_heads(heads, head_count, rows, dim, reinterpret_cast<cudaStream_t>(stream));
+#else
+  for (int64_t i = 0; i < head_count; ++i) {
+    const lrk_logits_head &h = heads[i];
+    const int status = lrk_logits(h.queries, rows, h.keys, h.count, dim, h.k_step, h.out, h.out_stride, stream);
+    if (status != LRK_OK) return status;
+  }
+  return LRK_OK;
+#endif
+}
+
+extern "C" int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim,
+                          int64_t k_step, void *out, int64_t out_stride, lrk_stream_t stream) {
+  clear_error();
+  const int status = check_logits_head(queries, rows, keys, count, dim, k_step, out, out_stride);
+  if (status != LRK_OK) return status;
+  if (rows == 0 || count == 0) return LRK_OK;
 #ifndef LRK_LOGITS_MMA_SYNC
   // Tensor-core (tcgen05) path; the mma.sync kernel below is its reference.
   return launch_logits_tc(queries, rows, keys, count, dim, k_step == 8, out, out_stride,

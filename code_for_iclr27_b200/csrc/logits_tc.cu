@@ -1,6 +1,6 @@
-// Q K^T logits of one head on the 5th-generation tensor cores (tcgen05), in
-// the accumulation order of the bf16 GEMM torch.matmul runs for the same
-// product (src/lazy_recall/scoring.py:184).
+// Q K^T logits of the KV heads of one layer on the 5th-generation tensor
+// cores (tcgen05), each head in the accumulation order of the bf16 GEMM
+// torch.matmul runs for it (src/lazy_recall/scoring.py:184).
 //
 // cuBLAS accumulates each product in float32 over K/16 sixteen-term tensor-core
 // steps in increasing k when the key count is even, and over K/8 eight-term
@@ -8,33 +8,44 @@
 // are zero in A (and finite in B) gives exactly the eight-term step's result
 // (measured on B200 against torch.matmul at every tested shape, configs[1]
 // heads included), so both orders run as UMMA
-// (tcgen05.mma kind::f16, M = 128, N = 128, K = 16):
-//   sixteen-term order   A = the query tile, B = the key tile, as usual;
-//   eight-term order     step j reads the key tile's 32-byte pair of
-//                        chunks that holds chunk j (the sixteen-term order's
-//                        pairs, each read twice), and A (built in shared
-//                        memory) holds query chunk j in the half of the step
-//                        that meets key chunk j and zeros in the other, so
-//                        the step multiplies query chunk j by key chunk j
+// (tcgen05.mma kind::f16, M = 128, N = 128, K = 16, A in tensor memory):
+//   sixteen-term order   step j: A = query elements 16j .. 16j + 15, B = the
+//                        key tile's 32-byte pair of chunks 2j, 2j + 1;
+//   eight-term order     step j: B = the pair holding key chunk j (each pair
+//                        read twice), A = query chunk j in the half of the
+//                        step that meets key chunk j and zeros in the other,
+//                        so the step multiplies query chunk j by key chunk j
 //                        alone.
-// Operands are K-major with 128-byte swizzling (8 rows x 128 B atoms, what a
+// B is K-major with 128-byte swizzling (8 rows x 128 B atoms, what a
 // 64-element x 128-row TMA box writes); step j starts inside its atom at
-// 32-byte offsets.
+// 32-byte offsets.  A lives in tensor memory (row r in lane r, element k in
+// column k / 2), which halves the shared-memory reads of each UMMA.
 //
-// One CTA (1 per SM) owns 128 query rows and a contiguous range of 128-key
-// tiles; warp-specialised:
+// One launch covers up to kMaxHeads heads.  The key tiles of all heads are
+// laid end to end; CTA (p, m) owns query tile m and a contiguous range p of
+// that sequence, so the query tiles of a range read the same key tiles while
+// they are in L2, and each CTA pays its start-up once for many heads.  Inside
+// a range, each head's part is a segment; the CTA of query tile m starts its
+// segments m tiles in (and wraps around), so that the query tiles of a range
+// do not all ask L2 for the same tile at once yet read each tile within a few
+// tiles' time of one another (it stays in L2 in between).  Warp-specialised,
+// one CTA per SM:
 //   warp 9, one thread   TMA loads of key tiles into a ring of stages
 //                        (full/empty mbarriers);
-//   warp 8, one thread   the UMMAs of each tile into one of four TMEM
-//                        accumulators (all 512 columns), committed to the
-//                        accumulator's and the stage's mbarriers -- it never
-//                        waits for its own MMAs, so several tiles stay queued;
-//   warps 0-7            build the query tile once; then two warpgroups
-//                        draining alternate tiles:
+//   warp 8, one thread   the UMMAs of each tile into one of three TMEM
+//                        accumulators, committed to the accumulator's and the
+//                        stage's mbarriers -- it never waits for its own MMAs
+//                        except where a segment starts: there it commits to
+//                        `a_free` and waits for `a_ready`;
+//   warps 0-7            two warpgroups draining alternate tiles:
 //                        tcgen05.ld of the warp's 32 TMEM lanes (= query rows),
 //                        release, round to bf16 into the group's 128B-swizzled
-//                        staging tile, TMA store (which clips columns past
-//                        `count` and rows past `rows`).
+//                        staging tile, TMA store (which clips columns past the
+//                        head's key count and rows past `rows`).  The group
+//                        that drains a segment's first tile first writes the
+//                        segment's query tile into tensor memory (after
+//                        `a_free`: the previous head's MMAs are complete) and
+//                        arrives on `a_ready`.
 //
 // Every mbarrier wait is bounded (polls and one second of %globaltimer); a
 // timeout raises a CTA-wide abort flag, the roles stop, the issuer waits
@@ -45,9 +56,11 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
+#include "lrk.h"
 #include "tc.cuh"
 
 namespace lrk {
@@ -64,32 +77,120 @@ constexpr int kIssuerWarp = kEpilogueWarps;          // warp 8: UMMA issue
 constexpr int kLoaderWarp = kEpilogueWarps + 1;      // warp 9: TMA loads
 constexpr int kThreadsTc = (kEpilogueWarps + 2) * 32;
 constexpr uint32_t kOutTile = kRows * kKeys * 2;  // one bf16 output tile (two 64-column halves)
-constexpr int kAccumulators = 4;                       // fp32 accumulators in TMEM
-constexpr uint32_t kTmemColumns = kAccumulators * kKeys;
+constexpr int kAccumulators = 3;                  // fp32 accumulators in TMEM, columns 0 .. 383
+constexpr uint32_t kAColumn = kAccumulators * kKeys;  // the query tile: columns 384 .. 511
+constexpr uint32_t kTmemColumns = 512;
+constexpr int kMaxHeads = 16;
+constexpr int kMaxSegments = kMaxHeads;
 
-template <int DIM, bool EIGHT>
-struct TcLayout {
-  static constexpr int kChunks = DIM / 8;                        // 8-element chunks per row
-  static constexpr int kSteps = EIGHT ? kChunks : kChunks / 2;   // UMMA K=16 steps per tile
-  static constexpr int kAAtoms = EIGHT ? DIM / 32 : DIM / 64;    // query tile (interleaved for EIGHT)
-  static constexpr int kBAtoms = DIM / 64;
-  static constexpr int kStages = EIGHT ? 3 : 4;
-  static constexpr uint32_t kOut = 0;                             // 2 staging tiles
-  static constexpr uint32_t kA = kOut + 2 * kOutTile;
-  static constexpr uint32_t kB = kA + kAAtoms * kAtom;
-  static constexpr uint32_t kStage = kBAtoms * kAtom;
-  static constexpr uint32_t kBarriers = kB + kStages * kStage;   // full[S] empty[S] acc_full[4] acc_empty[4]
-  static constexpr uint32_t kTmemSlot = kBarriers + 128;
-  static constexpr uint32_t kAbort = kTmemSlot + 8;
-  static constexpr uint32_t kCounters = kAbort + 8;                // tiles consumed by MMAs, tiles loaded
-  static constexpr uint32_t kBytes = kCounters + 8 + 1024;         // + alignment slack
+// The heads of one launch (kernel parameter space).
+struct HeadTable {
+  CUtensorMap key_map[kMaxHeads];  // [count, dim] keys, 64 x 128 boxes
+  CUtensorMap out_map[kMaxHeads];  // [rows, count] logits (row stride out_stride), 64 x 128 boxes
+  const __nv_bfloat16 *queries[kMaxHeads];
+  int tile_start[kMaxHeads + 1];  // first key tile of each head in the launch's sequence
+  int eight[kMaxHeads];           // 1: eight-term order
+  int heads;
+  int rows;
+  int tiles_per_cta;
 };
 
-template <int DIM, bool EIGHT>
-__global__ void __launch_bounds__(kThreadsTc, 1)
-    logits_tc_kernel(const __nv_bfloat16 *__restrict__ queries, const __grid_constant__ CUtensorMap key_map,
-                     const __grid_constant__ CUtensorMap out_map, int64_t rows, int64_t count, int tiles_per_cta) {
-  using L = TcLayout<DIM, EIGHT>;
+// A CTA's tiles [t0, t0 + n) are key tiles k0 + (i + rot) % n of `head`.
+struct Segment {
+  int t0, n, head, k0, rot;
+};
+
+template <int DIM>
+struct TcLayout {
+  static constexpr int kBAtoms = DIM / 64;
+  static constexpr int kStages = DIM == 128 ? 4 : 8;
+  static constexpr uint32_t kOut = 0;  // 2 staging tiles
+  static constexpr uint32_t kB = kOut + 2 * kOutTile;
+  static constexpr uint32_t kStage = kBAtoms * kAtom;
+  // full[S] empty[S] acc_full[3] acc_empty[3] a_free a_ready
+  static constexpr uint32_t kBarriers = kB + kStages * kStage;
+  static constexpr uint32_t kSegments = kBarriers + 8 * (2 * kStages + 2 * kAccumulators + 2);
+  static constexpr uint32_t kTmemSlot = kSegments + sizeof(Segment) * kMaxSegments + 4;  // + segment count
+  static constexpr uint32_t kAbort = kTmemSlot + 8;
+  static constexpr uint32_t kCounters = kAbort + 8;  // tiles consumed by MMAs, tiles loaded, a_free commits
+  static constexpr uint32_t kBytes = kCounters + 16 + 1024;  // + alignment slack
+};
+
+// Walks a CTA's segments in increasing tile order (each role keeps its own).
+struct Walker {
+  const Segment *segments;
+  int s = 0;
+  __device__ __forceinline__ const Segment &at(int t) {
+    while (t >= segments[s].t0 + segments[s].n) ++s;
+    return segments[s];
+  }
+};
+
+__device__ __forceinline__ int key_tile(const Segment &g, int t) { return g.k0 + (t - g.t0 + g.rot) % g.n; }
+
+// Row m0 + r of a head's queries (zeros past `rows`), as DIM / 8 chunks.
+template <int DIM>
+__device__ __forceinline__ void load_query_row(const HeadTable &P, int head, int64_t m0, int r, uint4 *q) {
+  const bool live = m0 + r < P.rows;
+  const uint4 *src = reinterpret_cast<const uint4 *>(P.queries[head] + (live ? (m0 + r) * DIM : 0));
+#pragma unroll
+  for (int c = 0; c < DIM / 8; ++c) q[c] = live ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+}
+
+// The row's A operand in this thread's TMEM lane from column `address` on:
+// step j in columns 8j .. 8j + 7 (two bf16 per column).  Sixteen-term order:
+// elements 16j .. 16j + 15.  Eight-term order: query chunk j in columns
+// 0-3 of the step for even j, 4-7 for odd j (the half that meets key chunk j
+// in the pair the step reads), zeros in the other half.
+template <int DIM>
+__device__ __forceinline__ void store_query_row(uint32_t address, bool eight, const uint4 *q) {
+  uint32_t w[16];
+  if (eight) {
+#pragma unroll
+    for (int g = 0; g < DIM / 16; ++g) {  // steps 2g, 2g + 1
+      const uint4 even = q[2 * g], odd = q[2 * g + 1];
+      w[0] = even.x, w[1] = even.y, w[2] = even.z, w[3] = even.w;
+      w[4] = w[5] = w[6] = w[7] = 0u;
+      w[8] = w[9] = w[10] = w[11] = 0u;
+      w[12] = odd.x, w[13] = odd.y, w[14] = odd.z, w[15] = odd.w;
+      tmem_store16(address + 16 * g, w);
+    }
+  } else {
+#pragma unroll
+    for (int g = 0; g < DIM / 32; ++g) {  // chunks 4g .. 4g + 3
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = q[4 * g + i];
+        w[4 * i] = v.x, w[4 * i + 1] = v.y, w[4 * i + 2] = v.z, w[4 * i + 3] = v.w;
+      }
+      tmem_store16(address + 16 * g, w);
+    }
+  }
+}
+
+// UMMA with A in tensor memory (kind::f16, bf16 operands, f32 accumulator).
+__device__ __forceinline__ void umma_tmem_a(uint32_t tmem, uint32_t a, uint64_t b, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem),
+      "r"(a), "l"(b), "r"(kInstr), "r"(static_cast<uint32_t>(accumulate))
+      : "memory");
+}
+
+// AND of `value` over the 128 threads of a warpgroup's named barrier.
+__device__ __forceinline__ bool group_all(bool value, uint32_t named) {
+  uint32_t all;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(all)
+      : "r"(value ? 1u : 0u), "r"(named)
+      : "memory");
+  return all != 0;
+}
+
+template <int DIM>
+__global__ void __launch_bounds__(kThreadsTc, 1) logits_tc_kernel(const __grid_constant__ HeadTable P) {
+  using L = TcLayout<DIM>;
   constexpr int S = L::kStages;
   extern __shared__ unsigned char smem_raw[];
   // Swizzled atoms and TMA destinations: 1024-byte aligned base.
@@ -97,9 +198,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char *smem = smem_raw + (base - raw);
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kRows;
-  const int64_t key_tiles = (count + kKeys - 1) / kKeys;
-  const int64_t t_begin = static_cast<int64_t>(blockIdx.x) * tiles_per_cta;
-  const int tiles = static_cast<int>(lmin(key_tiles, t_begin + tiles_per_cta) - t_begin);
+  const int total = P.tile_start[P.heads];
+  const int u0 = static_cast<int>(blockIdx.x) * P.tiles_per_cta;
+  const int tiles = min(total, u0 + P.tiles_per_cta) - u0;
   if (tiles <= 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t bar = base + L::kBarriers;
@@ -107,43 +208,38 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   auto empty = [&](int s) { return bar + 8 * (S + s); };
   auto acc_full = [&](int a) { return bar + 8 * (2 * S + a); };
   auto acc_empty = [&](int a) { return bar + 8 * (2 * S + kAccumulators + a); };
+  const uint32_t a_free = bar + 8 * (2 * S + 2 * kAccumulators), a_ready = a_free + 8;
   volatile int *abort = reinterpret_cast<volatile int *>(smem + L::kAbort);
-  // The CTAs of the query tiles that share a key range start at different
-  // tiles of it, so they do not all ask L2 for the same key tile at once.
-  const int rotation = tiles > 1 ? static_cast<int>((blockIdx.y * static_cast<int64_t>(tiles)) / gridDim.y) % tiles : 0;
-  auto rotated = [&](int t) { return (t + rotation) % tiles; };
+  volatile int *counters = reinterpret_cast<volatile int *>(smem + L::kCounters);
+  Segment *segments = reinterpret_cast<Segment *>(smem + L::kSegments);
 
-  if (warp < kEpilogueWarps) {
-    // The query tile, swizzled; for EIGHT step j's 32-byte window holds query
-    // chunk j in the half that meets key chunk j and zeros in the other
-    // (A-chunks 2j, 2j + 1 = (q_j, 0) for even j, (0, q_j) for odd j).
-    constexpr int kQChunks = DIM / 8;
-    for (int i = threadIdx.x; i < kRows * kQChunks; i += kEpilogueWarps * 32) {
-      const int r = i / kQChunks, j = i % kQChunks;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (m0 + r < rows) v = __ldg(reinterpret_cast<const uint4 *>(queries + (m0 + r) * DIM) + j);
-      const int a = EIGHT ? 2 * j + (j & 1) : j;  // chunk index in the A tile
-      *reinterpret_cast<uint4 *>(smem + L::kA + (a >> 3) * kAtom + swizzled(r, a & 7)) = v;
-      if (EIGHT) {
-        const int z = 2 * j + 1 - (j & 1);
-        *reinterpret_cast<uint4 *>(smem + L::kA + (z >> 3) * kAtom + swizzled(r, z & 7)) = make_uint4(0, 0, 0, 0);
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor-core reads
-  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(full(s)) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(empty(s)) : "memory");
+      init_barrier(full(s), 1);
+      init_barrier(empty(s), 1);
     }
     for (int a = 0; a < kAccumulators; ++a) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(acc_full(a)) : "memory");
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;\n" ::"r"(acc_empty(a)) : "memory");
+      init_barrier(acc_full(a), 1);
+      init_barrier(acc_empty(a), 4);
     }
+    init_barrier(a_free, 1);
+    init_barrier(a_ready, 4);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     *abort = 0;
-    reinterpret_cast<volatile int *>(smem + L::kCounters)[0] = 0;
-    reinterpret_cast<volatile int *>(smem + L::kCounters)[1] = 0;
+    counters[0] = counters[1] = 0;
+    // This CTA's part of each head, rotated by query tile inside the part.
+    int n = 0;
+    for (int h = 0; h < P.heads; ++h) {
+      const int lo = max(u0, P.tile_start[h]), hi = min(u0 + tiles, P.tile_start[h + 1]);
+      if (lo >= hi) continue;
+      Segment g;
+      g.t0 = lo - u0;
+      g.n = hi - lo;
+      g.head = h;
+      g.k0 = lo - P.tile_start[h];
+      g.rot = static_cast<int>(blockIdx.y % g.n);
+      segments[n++] = g;
+    }
   }
   if (warp == kIssuerWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(base + L::kTmemSlot),
@@ -155,8 +251,8 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + L::kTmemSlot);
+  Walker walk{segments};
 
-  volatile int *counters = reinterpret_cast<volatile int *>(smem + L::kCounters);
   if (warp == kLoaderWarp) {
     if (lane == 0) {
       // ------------------------------------------------------- TMA loads
@@ -165,11 +261,12 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       for (int t = 0; t < tiles; ++t) {
         const int s = t % S;
         if (t >= S && !wait_phase(empty(s), ((t / S) - 1) & 1, abort)) break;
-        expect_bytes(full(s), L::kStage);
-        const int y = static_cast<int>((t_begin + rotated(t)) * kKeys);
+        const Segment &g = walk.at(t);
+        const int y = key_tile(g, t) * kKeys;
         const uint32_t dst = base + L::kB + s * L::kStage;
+        expect_bytes(full(s), L::kStage);
 #pragma unroll
-        for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &key_map, 64 * b, y, full(s));
+        for (int b = 0; b < L::kBAtoms; ++b) tma_box(dst + b * kAtom, &P.key_map[g.head], 64 * b, y, full(s));
         loaded = t + 1;
       }
       counters[1] = loaded;
@@ -177,28 +274,37 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   } else if (warp == kIssuerWarp) {
     if (lane == 0) {
       // ------------------------------------------------------- MMA issue
-      // Never waits on its own MMAs inside the loop: the tensor pipe keeps
-      // up to kAccumulators tiles queued.
-      int issued = 0;  // tiles whose MMAs were issued
+      // Never waits on its own MMAs inside the loop (the tensor pipe keeps
+      // up to kAccumulators tiles queued) except through a_free/a_ready
+      // where a segment starts.
+      int issued = 0, frees = 0;
       bool ok = true;
       for (int t = 0; t < tiles; ++t) {
         const int s = t % S, a = t % kAccumulators;
+        const Segment &g = walk.at(t);
+        const bool starts = t == g.t0;
+        if (starts && t > 0) {
+          umma_commit(a_free);  // the previous head's MMAs, before its query tile is replaced
+          ++frees;
+        }
         if (!wait_phase(full(s), (t / S) & 1, abort)) { ok = false; break; }
         if (t >= kAccumulators && !wait_phase(acc_empty(a), ((t / kAccumulators) - 1) & 1, abort)) {
           ok = false;
           break;
         }
+        if (starts && !wait_phase(a_ready, walk.s & 1, abort)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const uint32_t A = base + L::kA, B = base + L::kB + s * L::kStage;
-        const uint32_t d = tmem + a * kKeys;
+        const uint32_t B = base + L::kB + s * L::kStage, d = tmem + a * kKeys, A = tmem + kAColumn;
+        if (P.eight[g.head]) {
 #pragma unroll
-        for (int j = 0; j < L::kSteps; ++j) {
-          // A: 32 bytes per step through its atoms (EIGHT: query chunk j and zeros).
-          const uint32_t a_addr = A + (j >> 2) * kAtom + (j & 3) * 32;
-          // B: the 32-byte pair of key chunks holding chunk j (EIGHT) or 2j, 2j + 1.
-          const int pair = EIGHT ? j >> 1 : j;
-          const uint32_t b_addr = B + (pair >> 2) * kAtom + (pair & 3) * 32;
-          umma(d, smem_descriptor(a_addr), smem_descriptor(b_addr), j > 0);
+          for (int j = 0; j < DIM / 8; ++j) {
+            const int pair = j >> 1;  // the 32-byte pair of key chunks holding chunk j
+            umma_tmem_a(d, A + 8 * j, smem_descriptor(B + (pair >> 2) * kAtom + (pair & 3) * 32), j > 0);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < DIM / 16; ++j)
+            umma_tmem_a(d, A + 8 * j, smem_descriptor(B + (j >> 2) * kAtom + (j & 3) * 32), j > 0);
         }
         umma_commit(acc_full(a));
         umma_commit(empty(s));
@@ -207,6 +313,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       // Before the CTA may exit, every arrival this thread set in motion must
       // have landed (bounded waits, whatever the abort flag says).
       for (int t = issued > S ? issued - S : 0; t < issued; ++t) wait_phase(empty(t % S), (t / S) & 1, nullptr);
+      if (frees > 0) wait_phase(a_free, (frees - 1) & 1, nullptr);
       if (!ok) {
         for (int t = issued > kAccumulators ? issued - kAccumulators : 0; t < issued; ++t)
           wait_phase(acc_full(t % kAccumulators), (t / kAccumulators) & 1, nullptr);
@@ -216,36 +323,46 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    // Warpgroup g drains the tiles t = g, g + 2, ... (accumulator t % 4).
+    // Warpgroup g drains the tiles t = g, g + 2, ... (accumulator t % 3).
     // Thread = query row r (its TMEM lane).  Each 64-column half of the bf16
     // tile is staged as 128 rows x 128 B with 128B swizzling (16-byte chunk c
     // of row r at chunk c ^ (r % 8): a quarter-warp's 8 rows hit 8 distinct
     // bank groups) and leaves with one TMA store, which clips the columns
-    // past `count` and the rows past `rows`.
+    // past the head's key count and the rows past `rows`.
     const int group = warp >> 2, r = (warp & 3) * 32 + lane;
     const uint32_t named = 1 + group;  // this warpgroup's named barrier
     const bool issuer = (threadIdx.x & 127) == 0;
     const uint32_t stage_out = base + L::kOut + group * kOutTile;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     for (int t = group; t < tiles; t += kEpilogueGroups) {
+      const Segment &g = walk.at(t);
       const int a = t % kAccumulators;
+      if (t == g.t0) {
+        // The segment's query tile, once the previous head's MMAs are done.
+        uint4 q[DIM / 8];
+        load_query_row<DIM>(P, g.head, m0, r, q);
+        const bool freed = walk.s == 0 || wait_phase(a_free, (walk.s - 1) & 1, abort);
+        if (!group_all(freed, named)) {
+          *abort = 1;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        store_query_row<DIM>(lane_base + kAColumn, P.eight[g.head] != 0, q);
+        tmem_wait_store();
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncwarp();
+        if (lane == 0) arrive(a_ready);
+      }
       // The group's 128 threads leave together or not at all (they meet in
-      // named barriers below): AND of every thread's wait.
-      const uint32_t got = wait_phase(acc_full(a), (t / kAccumulators) & 1, abort) ? 1u : 0u;
-      uint32_t all_got;
-      asm volatile(
-          "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}\n"
-          : "=r"(all_got)
-          : "r"(got), "r"(named)
-          : "memory");
-      if (!all_got) {
+      // named barriers below).
+      if (!group_all(wait_phase(acc_full(a), (t / kAccumulators) & 1, abort), named)) {
         *abort = 1;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
       uint32_t v[kKeys];
 #pragma unroll
-      for (int part = 0; part < kKeys / 32; ++part)
-        tmem_load32(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + a * kKeys + part * 32, v + part * 32);
+      for (int part = 0; part < kKeys / 32; ++part) tmem_load32(lane_base + a * kKeys + part * 32, v + part * 32);
       asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
       asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
       __syncwarp();
@@ -272,11 +389,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staging -> TMA store reads
       asm volatile("bar.sync %0, 128;\n" ::"r"(named) : "memory");
       if (issuer) {
-        const int x = static_cast<int>((t_begin + rotated(t)) * kKeys), y = static_cast<int>(m0);
+        const int x = key_tile(g, t) * kKeys, y = static_cast<int>(m0);
+        const uint64_t map = reinterpret_cast<uint64_t>(&P.out_map[g.head]);
 #pragma unroll
         for (int half = 0; half < 2; ++half)
-          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(
-                           reinterpret_cast<uint64_t>(&out_map)),
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"(map),
                        "r"(x + half * 64), "r"(y), "r"(stage_out + half * (kOutTile / 2))
                        : "memory");
         asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
@@ -340,34 +457,67 @@ int make_map(CUtensorMap *map, const void *data, int64_t rows_total, int64_t col
 
 }  // namespace tc
 
-// Tensor-core logits for dim 64 / 128 (LRK_ERR_UNSUPPORTED otherwise).
+// Tensor-core logits of several heads (dim 64 / 128, else
+// LRK_ERR_UNSUPPORTED), up to kMaxHeads heads per launch.  Arguments are
+// checked by the caller (lrk_logits_heads).
+int launch_logits_heads(const lrk_logits_head *heads, int64_t head_count, int64_t rows, int64_t dim,
+                        cudaStream_t stream) {
+  if (dim != 64 && dim != 128) return LRK_ERR_UNSUPPORTED;
+  if (rows > INT32_MAX) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many query rows");
+  const int64_t m_tiles = ceil_div(rows, kRows);
+  if (m_tiles > 65535) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many query rows");
+  auto kernel = dim == 128 ? logits_tc_kernel<128> : logits_tc_kernel<64>;
+  const uint32_t bytes = dim == 128 ? TcLayout<128>::kBytes : TcLayout<64>::kBytes;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+  for (int64_t next = 0; next < head_count;) {
+    HeadTable table;
+    memset(&table, 0, sizeof(table));
+    int n = 0;
+    int64_t total = 0;
+    for (; next < head_count && n < kMaxHeads; ++next) {
+      const lrk_logits_head &h = heads[next];
+      if (h.count == 0 || rows == 0) continue;
+      if (h.count > INT32_MAX) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many keys");
+      int status = tc::make_map(&table.key_map[n], h.keys, h.count, dim, dim, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (status != LRK_OK) return status;
+      status = tc::make_map(&table.out_map[n], h.out, rows, h.count, h.out_stride, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (status != LRK_OK) return status;
+      table.queries[n] = static_cast<const __nv_bfloat16 *>(h.queries);
+      table.eight[n] = h.k_step == 8;
+      table.tile_start[n] = static_cast<int>(total);
+      total += ceil_div(h.count, kKeys);
+      ++n;
+    }
+    if (n == 0) continue;
+    if (total > INT32_MAX / 2) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many key tiles");
+    table.tile_start[n] = static_cast<int>(total);
+    table.heads = n;
+    table.rows = static_cast<int>(rows);
+    // One CTA per SM (shared memory): the query tiles of a key range side by
+    // side, as many ranges as fill the SMs once.
+    const int64_t ranges = std::max<int64_t>(1, std::min<int64_t>(total, sm_count() / m_tiles));
+    const int64_t per = ceil_div(total, ranges);
+    table.tiles_per_cta = static_cast<int>(per);
+    const dim3 grid(static_cast<unsigned>(ceil_div(total, per)), static_cast<unsigned>(m_tiles));
+    kernel<<<grid, kThreadsTc, bytes, stream>>>(table);
+    const int status = launch_status("lrk_logits");
+    if (status != LRK_OK) return status;
+  }
+  return LRK_OK;
+}
+
+// One head (lrk_logits).
 int launch_logits_tc(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, bool eight,
                      void *out, int64_t out_stride, cudaStream_t stream) {
-  if (dim != 64 && dim != 128) return LRK_ERR_UNSUPPORTED;
-  if (rows > INT32_MAX || count > INT32_MAX) return fail(LRK_ERR_UNSUPPORTED, "lrk_logits: too many rows");
-  CUtensorMap key_map, out_map;
-  int status = tc::make_map(&key_map, keys, count, dim, dim, 64, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (status != LRK_OK) return status;
-  if ((status = tc::make_map(&out_map, out, rows, count, out_stride, 64, CU_TENSOR_MAP_SWIZZLE_128B)) != LRK_OK)
-    return status;
-  auto launch = [&](auto kernel, uint32_t bytes) -> int {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-    // One CTA per SM (shared memory), each on a contiguous key range; at most
-    // one wave.
-    const int64_t m_tiles = ceil_div(rows, kRows), key_tiles = ceil_div(count, kKeys);
-    const int64_t splits = std::max<int64_t>(1, std::min<int64_t>(key_tiles, sm_count() / m_tiles));
-    const int64_t per = ceil_div(key_tiles, splits);
-    const dim3 grid(static_cast<unsigned>(ceil_div(key_tiles, per)), static_cast<unsigned>(m_tiles));
-    kernel<<<grid, kThreadsTc, bytes, stream>>>(static_cast<const __nv_bfloat16 *>(queries), key_map, out_map, rows,
-                                                count, static_cast<int>(per));
-    return launch_status("lrk_logits");
-  };
-  if (dim == 128)
-    return eight ? launch(logits_tc_kernel<128, true>, TcLayout<128, true>::kBytes)
-                 : launch(logits_tc_kernel<128, false>, TcLayout<128, false>::kBytes);
-  return eight ? launch(logits_tc_kernel<64, true>, TcLayout<64, true>::kBytes)
-               : launch(logits_tc_kernel<64, false>, TcLayout<64, false>::kBytes);
+  lrk_logits_head head;
+  head.queries = queries;
+  head.keys = keys;
+  head.count = count;
+  head.k_step = eight ? 8 : 16;
+  head.out = out;
+  head.out_stride = out_stride;
+  return launch_logits_heads(&head, 1, rows, dim, stream);
 }
 
 }  // namespace lrk

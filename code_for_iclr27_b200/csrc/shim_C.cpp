@@ -5,7 +5,7 @@
 // RuntimeError), its output allocation (torch::empty on the input's device,
 // through the caching allocator) and its stream (the current CUDA stream).
 // Added operators: refine and topk_smallest (selection); temporal_scores,
-// scores_from_keys, project_values and logits (scoring); compact_layers and
+// scores_from_keys, project_values, logits and logits_heads (scoring); compact_layers and
 // merge_layers (eviction and recall over several layers in one call).
 #include <vector>
 
@@ -499,6 +499,51 @@ torch::Tensor logits(torch::Tensor queries, torch::Tensor keys, int64_t k_step, 
   return out;
 }
 
+// Logits of several heads of one layer in one launch (lrk_logits_heads):
+// entry i multiplies queries[heads[i]] ([H, rows, D] bf16) by the key rows
+// starts[i] .. ends[i] of keys ([N, D] bf16) in k_steps[i]-term steps.  One
+// allocation holds every entry's [rows, stride_i] output (stride_i = its key
+// count rounded up to 8); the views are returned in entry order.
+std::vector<torch::Tensor> logits_heads(torch::Tensor queries, torch::Tensor keys, std::vector<int64_t> heads,
+                                        std::vector<int64_t> starts, std::vector<int64_t> ends,
+                                        std::vector<int64_t> k_steps) {
+  check_cuda(queries, queries);
+  check_cuda(keys, queries);
+  TORCH_CHECK(queries.dim() == 3 && keys.dim() == 2 && queries.size(2) == keys.size(1) &&
+                  queries.scalar_type() == at::kBFloat16 && keys.scalar_type() == at::kBFloat16 &&
+                  queries.is_contiguous() && keys.is_contiguous(),
+              "logits_heads takes contiguous bf16 [H, rows, D] queries and [N, D] keys");
+  const size_t n = heads.size();
+  TORCH_CHECK(starts.size() == n && ends.size() == n && k_steps.size() == n,
+              "heads, starts, ends and k_steps must have one entry per head");
+  const int64_t rows = queries.size(1), dim = queries.size(2);
+  std::vector<int64_t> offsets(n + 1, 0);
+  for (size_t i = 0; i < n; ++i) {
+    TORCH_CHECK(heads[i] >= 0 && heads[i] < queries.size(0), "head index out of range");
+    TORCH_CHECK(0 <= starts[i] && starts[i] <= ends[i] && ends[i] <= keys.size(0), "key range out of bounds");
+    offsets[i + 1] = offsets[i] + rows * ((ends[i] - starts[i] + 7) / 8 * 8);
+  }
+  c10::cuda::CUDAGuard guard(queries.device());
+  auto flat = torch::empty({offsets[n]}, queries.options());
+  std::vector<lrk_logits_head> table(n);
+  std::vector<torch::Tensor> out;
+  out.reserve(n);
+  const auto element = keys.element_size();
+  for (size_t i = 0; i < n; ++i) {
+    const int64_t count = ends[i] - starts[i], stride = (count + 7) / 8 * 8;
+    lrk_logits_head &h = table[i];
+    h.queries = static_cast<const char *>(queries.data_ptr()) + heads[i] * rows * dim * element;
+    h.keys = static_cast<const char *>(keys.data_ptr()) + starts[i] * dim * element;
+    h.count = count;
+    h.k_step = k_steps[i];
+    h.out = static_cast<char *>(flat.data_ptr()) + offsets[i] * element;
+    h.out_stride = stride;
+    out.push_back(flat.narrow(0, offsets[i], rows * stride).view({rows, stride}));
+  }
+  check_status(lrk_logits_heads(table.data(), static_cast<int64_t>(n), rows, dim, current_stream()));
+  return out;
+}
+
 // Temporal-risk scores of many heads straight from queries and keys
 // (lrk_scores_from_keys).  Per layer l: keys[l] bf16 [rows, D], queries[l]
 // bf16 [window, heads * groups, D] (query heads of KV head h at h * groups ..),
@@ -593,6 +638,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("refine", &refine);
   module.def("topk_smallest", &topk_smallest);
   module.def("logits", &logits);
+  module.def("logits_heads", &logits_heads, pybind11::arg("queries"), pybind11::arg("keys"), pybind11::arg("heads"),
+             pybind11::arg("starts"), pybind11::arg("ends"), pybind11::arg("k_steps"));
   module.def("temporal_scores", &temporal_scores, pybind11::arg("logits"), pybind11::arg("projected_values"),
              pybind11::arg("key_positions"), pybind11::arg("first"), pybind11::arg("last"),
              pybind11::arg("query_positions"), pybind11::arg("margin"), pybind11::arg("scale"),

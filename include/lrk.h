@@ -177,7 +177,25 @@ int lrk_check_division(uint64_t count, uint64_t seed, unsigned long long *mismat
 int lrk_logits(const void *queries, int64_t rows, const void *keys, int64_t count, int64_t dim, int64_t k_step,
                void *out, int64_t out_stride, lrk_stream_t stream);
 
-/* Number of lrk_logits CTAs (since the library loaded, on the current device)
+/* One head of lrk_logits_heads: the arguments of one lrk_logits call. */
+typedef struct lrk_logits_head {
+  const void *queries; /* bf16 [rows, dim], row-major, 16-byte aligned */
+  const void *keys;    /* bf16 [count, dim], row-major, 16-byte aligned */
+  int64_t count;
+  int64_t k_step;      /* 8 or 16 */
+  void *out;           /* bf16 [rows, out_stride], 16-byte aligned */
+  int64_t out_stride;  /* a multiple of 8, >= count rounded up to 8 */
+} lrk_logits_head;
+
+/* lrk_logits for every head of a layer in one pass over the GPU (the heads
+ * share rows and dim; each has its own keys, step order and output).  The
+ * per-head GEMMs of src/lazy_recall/scoring.py:184 for one layer; results
+ * equal head_count lrk_logits calls bit for bit.
+ * No counterpart operator in the reference (new entry point). */
+int lrk_logits_heads(const lrk_logits_head *heads, int64_t head_count, int64_t rows, int64_t dim,
+                     lrk_stream_t stream);
+
+/* Number of lrk_logits / lrk_logits_heads CTAs (since the library loaded, on the current device)
  * whose bounded wait for their tensor-core steps ran out; 0 in a healthy run.
  * Synchronous.  No counterpart in the reference. */
 int lrk_logits_timeouts(unsigned int *count);

@@ -58,6 +58,28 @@ def test_invalid_arguments_rejected_before_launch():
                                     None) == abi.ERR_INVALID  # no layers
 
 
+def test_logits_heads_checks_every_head_first():
+    """lrk_logits_heads rejects a table with any bad head before launching
+    anything (include/lrk.h), so these calls need no GPU."""
+    lib = abi.library()
+    table = (abi.LogitsHead * 2)()
+    for h in table:
+        h.queries, h.keys, h.out, h.count, h.k_step, h.out_stride = 256, 512, 1024, 100, 16, 104
+    table[1].k_step = 4
+    assert lib.lrk_logits_heads(table, 2, 8, 128, None) == abi.ERR_INVALID  # step 4
+    table[1].k_step, table[1].out_stride = 8, 100
+    assert lib.lrk_logits_heads(table, 2, 8, 128, None) == abi.ERR_INVALID  # stride not a multiple of 8
+    table[1].out_stride = 104
+    assert lib.lrk_logits_heads(table, 2, 8, 96, None) == abi.ERR_INVALID  # head dimension 96
+    table[0].keys = 520
+    assert lib.lrk_logits_heads(table, 2, 8, 128, None) == abi.ERR_INVALID  # unaligned keys
+    assert lib.lrk_logits_heads(None, 2, 8, 128, None) == abi.ERR_INVALID
+    assert lib.lrk_logits_heads(None, 0, 8, 128, None) == abi.OK
+    assert lib.lrk_logits_heads(table, 2, 0, 128, None) == abi.OK  # no rows: nothing to do, like lrk_logits
+    table[0].keys, table[0].count, table[1].count = 512, 0, 0
+    assert lib.lrk_logits_heads(table, 2, 8, 128, None) == abi.OK  # no keys
+
+
 def test_zero_sized_calls_are_noops():
     lib = abi.library()
     assert lib.lrk_compact(None, None, None, 5, 64, abi.BF16, None, 5, None, None, None, None) == abi.OK

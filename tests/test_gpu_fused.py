@@ -411,17 +411,142 @@ def test_logits_equal_torch_matmul(C, cuda, rows, count, dim):
     assert timeouts.value == 0
 
 
-@pytest.mark.parametrize("count", [34176, 34178, 34180, 2002, 514])
-def test_even_key_counts_aligned_gemm_equals_torch_matmul(cuda, count):
-    """For an even key count the GEMM over the 8-aligned key block (the fused
-    audit's logits) equals torch.matmul on the exact key block, bit for bit."""
+@pytest.mark.parametrize("rows,counts,dim", [
+    (1000, [34880, 34881, 34883, 34878, 34885, 34880, 34879, 34882], 128),  # one configs[1] layer
+    (2000, [300, 301, 257, 130, 7, 2, 129, 640, 1, 382, 255, 256, 3, 511, 128, 999], 128),  # ranges cross heads
+    (1000, [5000 + 3 * i for i in range(20)], 128),  # more heads than one launch takes
+    (37, [513, 0, 514, 1, 6000], 64),
+    (129, [65, 66, 0, 4097], 128),
+])
+def test_logits_heads_equal_torch_matmul(C, cuda, rows, counts, dim):
+    """lrk_logits_heads -- every head of a layer in one launch, each in the
+    step order torch.matmul's GEMM takes for its key count -- equals
+    a plain torch.matmul GEMM per head bit for bit wherever cuBLAS takes that
+    order for it (plain_gemm_order_matches), and lrk_logits per head
+    everywhere."""
     import torch
 
-    from code_for_iclr27_b200.audit import _aligned_keys
 
-    g = torch.Generator(device=cuda).manual_seed(count)
-    queries = (torch.randn(320, 128, generator=g, device=cuda) * 2).to(torch.bfloat16)
-    storage = torch.randn(count + 16, 128, generator=g, device=cuda).to(torch.bfloat16)
-    aligned = _aligned_keys(storage, 5, 5 + count)
-    fast = torch.matmul(queries, aligned.transpose(0, 1))[:, :count]
-    assert torch.equal(fast, torch.matmul(queries, storage[5:5 + count].transpose(0, 1)))
+    g = torch.Generator(device=cuda).manual_seed(rows + sum(counts))
+    heads = len(counts)
+    queries = (torch.randn(heads, rows, dim, generator=g, device=cuda) * 2).to(torch.bfloat16)
+    bounds = [0]
+    for n in counts:
+        bounds.append(bounds[-1] + n)
+    keys = torch.randn(bounds[-1] + 8, dim, generator=g, device=cuda).to(torch.bfloat16)
+    order = list(range(heads))[::-1]  # entries need not follow head order
+    outs = C.logits_heads(queries, keys, order, [bounds[h] for h in order], [bounds[h + 1] for h in order],
+                          [8 if counts[h] % 2 else 16 for h in order])
+    for out, h in zip(outs, order):
+        n = counts[h]
+        assert out.shape == (rows, (n + 7) // 8 * 8)
+        if n == 0:
+            continue
+        head_keys = keys[bounds[h]:bounds[h + 1]]
+        if plain_gemm_order_matches(n, rows):
+            assert torch.equal(out[:, :n], torch.matmul(queries[h], head_keys.transpose(0, 1))), f"head {h}"
+        if h % 5 == 0 or not plain_gemm_order_matches(n, rows):
+            single = C.logits(queries[h].contiguous(), head_keys.contiguous(), 8 if n % 2 else 16, out.shape[1])
+            assert torch.equal(single[:, :n], out[:, :n]), f"head {h} vs lrk_logits"
+    from code_for_iclr27_b200 import abi
+
+    timeouts = ctypes.c_uint(0)
+    abi.check(abi.library().lrk_logits_timeouts(ctypes.byref(timeouts)))
+    assert timeouts.value == 0
+
+
+def plain_gemm_order_matches(count, rows):
+    """Where a plain [rows, D] x [D, count] bf16 torch.matmul GEMM takes the
+    16-term (even count) or 8-term (odd count) tensor-core order (measured on
+    B200 for rows 8 .. 2000: odd counts below 288 keys, and below 4098 at 8
+    rows, run other kernels)."""
+    return count % 2 == 0 or (count >= 1024 and rows >= 40)
+
+
+def reference_chunks(head_queries, keys, chunk):
+    """The reference's logits of one head (scoring.py:177-184): torch.matmul
+    of the permuted query-history view, per query chunk."""
+    import torch
+
+    from code_for_iclr27_b200.audit import reference_query_view
+
+    mapped = reference_query_view(head_queries)
+    return torch.cat([torch.matmul(mapped[a:a + chunk], keys.transpose(0, 1))
+                      for a in range(0, mapped.shape[0], chunk)])
+
+
+@pytest.mark.parametrize("groups,window,chunk_size", [(1, 40, 250), (2, 250, 250), (4, 250, 250), (4, 37, 7),
+                                                      (8, 9, 250), (8, 37, 7), (4, 100, 30)])
+def test_tensor_core_order_rule_against_reference_gemm(C, cuda, groups, window, chunk_size):
+    """Wherever tensor_core_order_matches says so, lrk_logits equals the
+    reference's batched GEMM bit for bit; the sweep covers the small key
+    counts and chunks for which cuBLAS picks other kernels."""
+    import torch
+
+    from code_for_iclr27_b200.audit import query_chunk, tensor_core_order_matches
+
+    g = torch.Generator(device=cuda).manual_seed(groups * 1000 + window)
+    queries = (torch.randn(window, groups, 128, generator=g, device=cuda) * 2).to(torch.bfloat16)
+    keys = torch.randn(35000, 128, generator=g, device=cuda).to(torch.bfloat16)
+    flat = queries.reshape(window * groups, 128)
+    checked = 0
+    for n in list(range(1, 80, 3)) + list(range(250, 330, 5)) + [1023, 1024, 1025, 2048, 2049, 4097, 16385, 34881]:
+        chunk = query_chunk(chunk_size, groups, n, 2)
+        if not tensor_core_order_matches(n, window, groups, chunk):
+            continue
+        out = C.logits(flat, keys[:n], 8 if n % 2 else 16, (n + 7) // 8 * 8)[:, :n].view(window, groups, n)
+        assert torch.equal(out, reference_chunks(queries, keys[:n], chunk)), f"{n} keys"
+        checked += 1
+    assert checked > 0 or groups == 1
+
+
+@pytest.mark.parametrize("window,groups", [(250, 4), (9, 4), (100, 8), (40, 1)])
+def test_layer_logits_equal_reference_chunks(C, cuda, window, groups):
+    """layer_logits (the audit's logits: one lrk_logits_heads launch plus the
+    reference GEMM for the heads whose order it does not reproduce) equals
+    the reference's per-chunk torch.matmul (scoring.py:177-184) for every
+    head of a layer."""
+    import torch
+
+    from code_for_iclr27_b200.audit import layer_logits, query_chunk
+
+    g = torch.Generator(device=cuda).manual_seed(window * groups)
+    lens = [34880, 34881, 3, 290, 1025, 2048, 35000, 511]
+    bounds = [0]
+    for n in lens:
+        bounds.append(bounds[-1] + n)
+    keys = torch.randn(bounds[-1], 128, generator=g, device=cuda).to(torch.bfloat16)
+    per_head = (torch.randn(len(lens), window, groups, 128, generator=g, device=cuda) * 2).to(torch.bfloat16)
+    spans = [(h, bounds[h], bounds[h + 1], query_chunk(250, groups, n, 2)) for h, n in enumerate(lens)]
+    got = layer_logits(per_head.view(len(lens), window * groups, 128), keys, spans, window, groups)
+    for (h, start, end, chunk), logits in zip(spans, got):
+        expect = reference_chunks(per_head[h], keys[start:end], chunk)
+        assert logits.shape == expect.shape
+        assert torch.equal(logits, expect), f"head {h} ({end - start} keys, chunk {chunk})"
+
+
+def test_logits_heads_rejects_bad_arguments(C, cuda):
+    """lrk_logits_heads checks every head like lrk_logits (step, stride,
+    alignment) before anything runs."""
+    import torch
+
+    from code_for_iclr27_b200 import abi
+
+    queries = torch.zeros(2, 16, 128, dtype=torch.bfloat16, device=cuda)
+    keys = torch.zeros(64, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(RuntimeError):
+        C.logits_heads(queries, keys, [0], [0], [64], [4])
+    with pytest.raises(RuntimeError):
+        C.logits_heads(queries, keys, [2], [0], [64], [16])
+    out = torch.empty(16, 64, dtype=torch.bfloat16, device=cuda)
+    table = (abi.LogitsHead * 1)()
+    table[0].queries, table[0].keys, table[0].count = queries.data_ptr(), keys.data_ptr(), 64
+    table[0].k_step, table[0].out, table[0].out_stride = 16, out.data_ptr(), 60
+    lib = abi.library()
+    assert lib.lrk_logits_heads(table, 1, 16, 128, None) == abi.ERR_INVALID  # stride not a multiple of 8
+    table[0].out_stride, table[0].keys = 64, keys.data_ptr() + 2
+    assert lib.lrk_logits_heads(table, 1, 16, 128, None) == abi.ERR_INVALID  # unaligned keys
+    table[0].keys = keys.data_ptr()
+    abi.check(lib.lrk_logits_heads(table, 1, 16, 128, None))
+    torch.cuda.synchronize()
+    assert torch.equal(out, torch.matmul(queries[0], keys.transpose(0, 1)))
