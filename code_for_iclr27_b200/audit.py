@@ -107,8 +107,16 @@ def reference_query_view(head_queries):
     mapped_queries (scoring.py:260: query_history[0, q0:q1].permute(1, 0, 2)
     of a contiguous [1, heads * G, W, D] history, i.e. strides (D, W*D, 1)).
     torch.matmul cannot fold such a view into one matrix, so it runs the
-    batched GEMM the reference runs: one [G, D] x [D, L] product per query."""
-    return head_queries.permute(1, 0, 2).contiguous().permute(1, 0, 2)
+    batched GEMM the reference runs: one [G, D] x [D, L] product per query.
+    The [G, W, D] copy is always made: .contiguous() would skip it when torch
+    already counts the permuted tensor as contiguous (one group: a size-1
+    dimension's stride is not checked), and the view would then fold."""
+    import torch
+
+    window, groups, dim = head_queries.shape
+    history = torch.empty((groups, window, dim), dtype=head_queries.dtype, device=head_queries.device)
+    history.copy_(head_queries.permute(1, 0, 2))
+    return history.permute(1, 0, 2)
 
 
 def tensor_core_order_matches(length: int, window: int, groups: int, chunk: int) -> bool:
@@ -159,10 +167,8 @@ def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stre
     start, end, chunk) per entry.  The heads whose order lrk_logits
     reproduces run in one lrk_logits_heads launch (both step orders, one pass
     over the GPU); the others take the reference's GEMM (head_logits), on
-    reference_stream when given: cuBLAS may pick another algorithm on another
-    stream (measured: the batched GEMV of one query row per product differs
-    in the last bit between streams), so those GEMMs run where the reference
-    runs them, on the caller's stream."""
+    reference_stream when given (the caller's stream, where the reference
+    issues them)."""
     import torch
 
     dim = per_head.shape[-1]

@@ -13,6 +13,8 @@ CASE is one of:
   project        projected values of one layer (279k rows of D=128 bf16, 4 groups)
   logits         one head's logits, [1000, 128] x [34880, 128] bf16, 16-term steps
   logits_odd     the same with 34883 keys, 8-term steps
+  logits_layer   one layer's logits in one launch (lrk_logits_heads): 8 heads of
+                 34,878 .. 34,885 keys (both step orders), 1000 query rows each
 Inputs are seeded and generated on the device; each iteration launches the
 operator once.
 """
@@ -27,7 +29,8 @@ LAYER_ROWS = 8 * 34880
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
-                                           "project", "logits", "logits_odd", "from_keys", "table_fused"])
+                                           "project", "logits", "logits_odd", "logits_layer", "from_keys",
+                                           "table_fused"])
     parser.add_argument("--iters", type=int, default=3)
     args = parser.parse_args(argv)
 
@@ -77,6 +80,15 @@ def main(argv=None):
         keys = torch.randn(count, 128, generator=g, device=dev).to(torch.bfloat16)
         step = 16 if args.case == "logits" else 8
         run = lambda: C.logits(queries, keys, step, (count + 7) // 8 * 8)
+    elif args.case == "logits_layer":
+        lens = [34880, 34881, 34883, 34878, 34885, 34880, 34879, 34882]
+        bounds = [0]
+        for n in lens:
+            bounds.append(bounds[-1] + n)
+        queries = (torch.randn(len(lens), 1000, 128, generator=g, device=dev) * 2).to(torch.bfloat16)
+        keys = torch.randn(bounds[-1], 128, generator=g, device=dev).to(torch.bfloat16)
+        steps = [8 if n % 2 else 16 for n in lens]
+        run = lambda: C.logits_heads(queries, keys, list(range(len(lens))), bounds[:-1], bounds[1:], steps)
     elif args.case in ("from_keys", "table_fused"):
         # One configs[1] layer scored straight from its keys (lrk_scores_from_keys), or
         # through its logits (table_fused: cuBLAS / lrk_logits, then lrk_temporal_scores):
