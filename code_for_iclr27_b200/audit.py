@@ -119,25 +119,39 @@ def reference_query_view(head_queries):
     return history.permute(1, 0, 2)
 
 
+# Queries per cuBLAS call (the batch of the reference's batched GEMM) at which
+# torch.matmul took an order other than lrk_logits' for some odd key count in
+# a sweep on B200 (every batch size 1 .. 250, odd key counts 1025 .. 65537):
+# batch 1 everywhere; at 2 groups also scattered sizes, kept here as whole
+# ranges; at 4 groups one isolated size (5, at 24,577 keys).
+_ODD_ORDER_EXCEPTIONS = {
+    2: frozenset([1, *range(12, 26), *range(178, 250)]),
+    4: frozenset([1, 5]),
+    8: frozenset([1, 2]),
+}
+
+
 def tensor_core_order_matches(length: int, window: int, groups: int, chunk: int) -> bool:
     """Whether the reference's logits GEMM for a head -- torch.matmul of
-    reference_query_view(queries)[a:a + chunk] and the head's keys, a batched
-    GEMM of `chunk` [groups, D] x [D, length] products per query chunk
+    reference_query_view(queries)[a:a + chunk] and the head's keys, one
+    batched GEMM of [groups, D] x [D, length] products per query chunk
     (scoring.py:184) -- takes the tensor-core step order lrk_logits
     reproduces: 16 terms for an even key count, 8 for an odd one.  Measured on
-    B200 against torch.matmul over groups 1, 2, 4, 8, windows 9, 37, 250 and
-    key counts 1 .. 600 plus larger ones: with one query row per product
-    (groups 1) cuBLAS runs other kernels at almost every odd count; with two
-    or more, every even count matches, and odd counts match from 1024 keys on
-    when every query chunk holds at least 9 queries (chunks of 7 and 2 queries
-    at 8 groups miss even at 34,881 keys).  The other heads take the
-    reference's own GEMM."""
+    B200: with one query row per product (groups 1) cuBLAS runs other kernels
+    at almost every odd count; with 2, 4 or 8 rows every even count matches,
+    odd counts below 1024 keys often do not, and from 1024 keys on the odd
+    counts match unless a call's batch is one of _ODD_ORDER_EXCEPTIONS.
+    Group counts outside the sweep take the reference's GEMM for odd counts.
+    The other heads take the reference's own GEMM."""
     if groups < 2:
         return False
     if length % 2 == 0:
         return True
+    exceptions = _ODD_ORDER_EXCEPTIONS.get(groups)
+    if exceptions is None or length < 1024:
+        return False
     batches = {min(chunk, window - a) for a in range(0, window, chunk)}
-    return length >= 1024 and min(batches) >= 9
+    return not (batches & exceptions)
 
 
 def head_logits(per_head_queries, keys, start: int, end: int, chunk: int):

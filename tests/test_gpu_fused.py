@@ -500,6 +500,31 @@ def test_tensor_core_order_rule_against_reference_gemm(C, cuda, groups, window, 
     assert checked > 0 or groups == 1
 
 
+@pytest.mark.parametrize("groups", [2, 4, 8])
+def test_tensor_core_order_rule_per_batch(C, cuda, groups):
+    """One cuBLAS call per query chunk: at every batch size the rule lets
+    through (tensor_core_order_matches with one chunk of `batch` queries),
+    lrk_logits equals the reference's batched GEMM at odd key counts from
+    1025 to 34,881 bit for bit."""
+    import torch
+
+    from code_for_iclr27_b200.audit import tensor_core_order_matches
+
+    g = torch.Generator(device=cuda).manual_seed(groups)
+    keys = torch.randn(34881, 128, generator=g, device=cuda).to(torch.bfloat16)
+    checked = 0
+    for batch in list(range(1, 31)) + [80, 81, 82, 83, 100, 170, 250]:
+        queries = (torch.randn(batch, groups, 128, generator=g, device=cuda) * 2).to(torch.bfloat16)
+        flat = queries.reshape(batch * groups, 128)
+        for n in (1025, 4097, 16385, 24577, 34087, 34881):
+            if not tensor_core_order_matches(n, batch, groups, batch):
+                continue
+            out = C.logits(flat, keys[:n], 8, (n + 7) // 8 * 8)[:, :n].view(batch, groups, n)
+            assert torch.equal(out, reference_chunks(queries, keys[:n], batch)), f"batch {batch}, {n} keys"
+            checked += 1
+    assert checked > 100
+
+
 @pytest.mark.parametrize("window,groups", [(250, 4), (9, 4), (100, 8), (40, 1)])
 def test_layer_logits_equal_reference_chunks(C, cuda, window, groups):
     """layer_logits (the audit's logits: one lrk_logits_heads launch plus the
