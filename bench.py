@@ -203,10 +203,25 @@ class LaunchCounter:
         return self.KERNELS.get(name, 1)
 
 
+_NVML_SAMPLER = r"""
+import sys, time
+import pynvml
+pynvml.nvmlInit()
+key = sys.argv[1]
+h = pynvml.nvmlDeviceGetHandleByUUID(key) if key.startswith("GPU-") else pynvml.nvmlDeviceGetHandleByIndex(int(key))
+print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+while True:
+    print(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), pynvml.nvmlDeviceGetCurrentClocksEventReasons(h),
+          flush=True)
+    time.sleep(0.01)
+"""
+
+
 class Clocks:
     """SM clock and throttle reasons sampled during the timed region: NVML
-    every 10 ms from a thread (read-only queries), else nvidia-smi every
-    200 ms."""
+    every 10 ms from a child process (read-only queries; a thread here would
+    wait for the interpreter lock the audit's host code holds), else
+    nvidia-smi every 200 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -215,45 +230,31 @@ class Clocks:
                ("sw_power_cap", 0x4))
 
     def __init__(self, index: int):
-        self.index, self.process, self.thread = index, None, None
-        self.samples, self.nvml = [], []
+        self.index, self.process, self.sampler = index, None, None
+        self.samples, self.nvml, self.maximum = [], [], None
 
-    def _nvml_handle(self):
-        import pynvml
+    def _device_key(self):
         import torch
 
-        pynvml.nvmlInit()
         uuid = getattr(torch.cuda.get_device_properties(self.index), "uuid", None)
-        if uuid is not None:
-            text = str(uuid)
-            return pynvml.nvmlDeviceGetHandleByUUID(text if text.startswith("GPU-") else "GPU-" + text)
-        return pynvml.nvmlDeviceGetHandleByIndex(self.index)
+        if uuid is None:
+            return str(self.index)
+        text = str(uuid)
+        return text if text.startswith("GPU-") else "GPU-" + text
 
     def __enter__(self):
-        import threading
-
         try:
-            import pynvml
-
-            handle = self._nvml_handle()
-            maximum = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
-            self.stop = threading.Event()
-
-            def sample():
-                while True:
-                    try:
-                        self.nvml.append((pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM), maximum,
-                                          pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)))
-                    except Exception:
-                        return
-                    if self.stop.wait(0.01):
-                        return
-
-            self.thread = threading.Thread(target=sample, daemon=True)
-            self.thread.start()
-            return self
-        except Exception:
-            self.thread = None
+            self.sampler = subprocess.Popen([sys.executable, "-c", _NVML_SAMPLER, self._device_key()],
+                                            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.sampler.stdout.readline().split()
+            if len(first) == 2 and first[0] == "ready":
+                self.maximum = float(first[1])
+                return self
+            self.sampler.kill()
+            self.sampler.wait()
+        except OSError:
+            pass
+        self.sampler = None
         try:
             self.process = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                                              "--format=csv,noheader,nounits", "-lms", "200"],
@@ -263,9 +264,17 @@ class Clocks:
         return self
 
     def __exit__(self, *exc):
-        if self.thread is not None:
-            self.stop.set()
-            self.thread.join(timeout=5)
+        if self.sampler is not None:
+            self.sampler.terminate()
+            try:
+                out, _ = self.sampler.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.sampler.kill()
+                out, _ = self.sampler.communicate()
+            for line in out.splitlines():
+                parts = line.split()
+                if len(parts) == 2 and parts[0].isdigit() and parts[1].isdigit():
+                    self.nvml.append((int(parts[0]), self.maximum, int(parts[1])))
             return
         if self.process is None:
             return
