@@ -499,27 +499,42 @@ def main():
     value = requests * managed * args.steps / (elapsed_ms / 1e3)
 
     # Per-decode-step overhead: append one token to every layer, evict a
-    # staging-sized queue prefix every EVICT_INTERVAL steps.
-    # (Request sharding only: with layer groups the lazy queue is split over
-    # ranks and its prefixes would need the request-wide rounds as well.)
-    decode_us = None
-    if not layer_groups:
-        queue, removed_at_audit = last.references[IMMEDIATE:], {}
-        g = torch.Generator(device=device).manual_seed(args.seed + 7)
-        new_keys = torch.randn(args.decode_steps, LAYERS, 1, HEADS, 1, DIM, generator=g,
-                               device=device).to(torch.bfloat16)
-        barrier()
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0.record()
-        for step in range(args.decode_steps):
-            for layer in range(LAYERS):
-                cache.append(layer, new_keys[step, layer], new_keys[step, layer], cache.seen_tokens)
-            cache.seen_tokens += 1
-            if (step + 1) % EVICT_INTERVAL == 0 and len(queue) >= STAGING:
+    # staging-sized queue prefix every EVICT_INTERVAL steps.  With layer
+    # groups each rank appends to its own layers and takes its share of each
+    # request-wide queue prefix (lazy_prefix_share: one all-gather of the
+    # ranks' next queue scores per batch); the audit already evicted its share
+    # of the immediate prefix, the first slots of its local queue.
+    if layer_groups:
+        from code_for_iclr27_b200.distributed import lazy_prefix_share
+
+        queue = last.references[lazy_prefix_share(last.references.scores, IMMEDIATE):]
+    else:
+        queue = last.references[IMMEDIATE:]
+    removed_at_audit = {}
+    layers_here = len(cache.layers)
+    g = torch.Generator(device=device).manual_seed(args.seed + 7)
+    new_keys = torch.randn(args.decode_steps, layers_here, 1, HEADS, 1, DIM, generator=g,
+                           device=device).to(torch.bfloat16)
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for step in range(args.decode_steps):
+        for layer in range(layers_here):
+            cache.append(layer, new_keys[step, layer], new_keys[step, layer], cache.seen_tokens)
+        cache.seen_tokens += 1
+        if (step + 1) % EVICT_INTERVAL == 0:
+            if layer_groups:
+                share = lazy_prefix_share(queue.scores, STAGING)
+                if share:
+                    queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, share)
+            elif len(queue) >= STAGING:
                 queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
-        d1.record()
-        barrier()
-        decode_us = d0.elapsed_time(d1) * 1e3 / args.decode_steps
+    d1.record()
+    barrier()
+    decode_local = torch.tensor([d0.elapsed_time(d1)], device=device)
+    if distributed:
+        dist.all_reduce(decode_local, op=dist.ReduceOp.MAX)
+    decode_us = float(decode_local.item()) * 1e3 / args.decode_steps
 
     # End to end through the public API: audit inputs copied from pinned host
     # memory each step, the queue read back (refine_arrays returns host arrays).

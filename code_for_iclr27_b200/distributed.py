@@ -121,6 +121,41 @@ def prefix_split(scores: torch.Tensor, chosen: torch.Tensor, prefix: int, group=
     return select_smallest(scores, prefix, group, eligible=chosen)
 
 
+def lazy_prefix_share(queue_scores, count: int, group=None) -> int:
+    """This rank's share of the next `count` slots of a request's lazy queue
+    when the request's layers are split over ranks (controller.py:57-70: each
+    lazy batch evicts the next `count` queued references).  queue_scores:
+    this rank's remaining queue slots' scores in queue order (ascending raw
+    score, ties by score-table index), ranks holding consecutive layer groups
+    in rank order -- so the request-wide queue is the merge of the ranks'
+    queues by (score, rank, slot).  Every rank gathers each rank's first
+    `count` scores and takes the same first `count` of that merge.  Returns 0
+    on every rank while the request-wide queue holds fewer than `count`
+    slots (the batch waits, as on one GPU).  One all-gather of the queue
+    lengths and one of `count` scores per call, on every rank."""
+    import numpy as np
+
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    device = (torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl"
+              else torch.device("cpu"))
+    lengths = _all_gather_counts(torch.tensor([len(queue_scores)], dtype=torch.int64, device=device),
+                                 group).reshape(-1)
+    if int(lengths.sum().item()) < count or count <= 0:
+        return 0
+    n = min(count, len(queue_scores))
+    scores = torch.zeros(count, dtype=torch.float32, device=device)
+    if n:
+        scores[:n] = torch.as_tensor(np.asarray(queue_scores[:n], dtype=np.float32), device=device)
+    keys = radix_keys(_all_gather_counts(scores, group))  # [world, count]
+    slots = torch.arange(count, device=device)
+    valid = slots[None, :] < torch.clamp(lengths, max=count)[:, None]
+    keys = torch.where(valid, keys, torch.full_like(keys, 1 << 32))
+    ranks = torch.arange(world, device=device)[:, None]
+    merged = (keys * (world * count) + ranks * count + slots[None, :]).reshape(-1)
+    first = torch.topk(merged, count, largest=False).indices
+    return int(((first // count) == rank).sum().item())
+
+
 def layer_group_audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
                            group=None, protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250,
                            pool_kernel=7):

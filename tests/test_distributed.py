@@ -101,3 +101,66 @@ def test_radix_keys_order_floats():
     keys = radix_keys(x)
     assert torch.all(keys[1:] > keys[:-1])
     np.testing.assert_array_equal(keys.numpy(), O.radix_key(x.numpy()).astype(np.int64))
+
+
+def lazy_worker(rank, world, port, cases, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from code_for_iclr27_b200.distributed import lazy_prefix_share, queue_order, select_smallest
+
+        out = []
+        for seed, n, levels, count, prefix, batch, cuts in cases:
+            scores = torch.from_numpy(make_scores(seed, n, levels))
+            local = scores[cuts[rank]:cuts[rank + 1]]
+            chosen = select_smallest(local, count)
+            queue = local[queue_order(local, chosen)].numpy()  # this rank's queue slots, in queue order
+            shares = [lazy_prefix_share(queue, prefix)]
+            queue = queue[shares[0]:]
+            for _ in range(-(-count // batch) + 1):  # the same number of calls on every rank
+                share = lazy_prefix_share(queue, batch)
+                shares.append(share)
+                queue = queue[share:]
+            out.append(shares)
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+LAZY_CASES = [
+    # seed, n, tie levels, queued count, immediate prefix, lazy batch
+    (11, 3000, 0, 2000, 300, 256),
+    (12, 3000, 3, 2000, 150, 512),   # heavy ties inside batches and across ranks
+    (13, 5000, 40, 4100, 0, 2048),
+    (14, 999, 0, 999, 999, 7),       # the prefix takes everything
+]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_lazy_prefix_shares_match_single_queue(world):
+    """Each rank's share of every lazy batch (and of the immediate prefix)
+    equals the number of its rows in the corresponding slots of the
+    single-process queue (ascending (key, index)); a batch the request-wide
+    queue cannot fill gives 0 on every rank."""
+    cases = []
+    for seed, n, levels, count, prefix, batch in LAZY_CASES:
+        cuts = [int(x) for x in np.linspace(0, n, world + 1).round()]
+        cuts[1] = cuts[1] - 5 * (seed % 7)  # uneven groups
+        cases.append((seed, n, levels, count, prefix, batch, cuts))
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    port = free_port()
+    mp.start_processes(lazy_worker, args=(world, port, cases, results), nprocs=world, join=True, start_method="spawn")
+    for case_index, (seed, n, levels, count, prefix, batch, cuts) in enumerate(cases):
+        scores = make_scores(seed, n, levels)
+        order = np.lexsort((np.arange(n), O.radix_key(scores)))[:count]  # the single-process queue
+        owner = np.searchsorted(np.asarray(cuts), order, side="right") - 1
+        bounds = [(0, prefix)]
+        start = prefix
+        for _ in range(-(-count // batch) + 1):
+            bounds.append((start, start + batch) if start + batch <= count else (start, start))
+            start = min(count, start + batch) if start + batch <= count else start
+        for rank in range(world):
+            expected = [int((owner[a:b] == rank).sum()) for a, b in bounds]
+            assert results[rank][case_index] == expected, f"case {seed}, rank {rank}"
