@@ -220,8 +220,10 @@ while True:
 class Clocks:
     """SM clock and throttle reasons sampled during the timed region: NVML
     every 10 ms from a child process (read-only queries; a thread here would
-    wait for the interpreter lock the audit's host code holds), else
-    nvidia-smi every 200 ms."""
+    wait for the interpreter lock the audit's host code holds), plus one
+    in-process NVML sample at each end of the region; if the child cannot
+    start, an in-process thread samples instead, and without NVML nvidia-smi
+    every 200 ms."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -230,8 +232,8 @@ class Clocks:
                ("sw_power_cap", 0x4))
 
     def __init__(self, index: int):
-        self.index, self.process, self.sampler = index, None, None
-        self.samples, self.nvml, self.maximum = [], [], None
+        self.index, self.process, self.sampler, self.thread, self.handle = index, None, None, None, None
+        self.samples, self.nvml, self.maximum, self.error, self.errors = [], [], None, None, None
 
     def _device_key(self):
         import torch
@@ -242,19 +244,57 @@ class Clocks:
         text = str(uuid)
         return text if text.startswith("GPU-") else "GPU-" + text
 
+    def _sample_here(self):
+        import pynvml
+
+        self.nvml.append((pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM), self.maximum,
+                          pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)))
+
     def __enter__(self):
+        import tempfile
+        import threading
+
+        key = self._device_key()
         try:
-            self.sampler = subprocess.Popen([sys.executable, "-c", _NVML_SAMPLER, self._device_key()],
-                                            stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            first = self.sampler.stdout.readline().split()
-            if len(first) == 2 and first[0] == "ready":
-                self.maximum = float(first[1])
-                return self
-            self.sampler.kill()
-            self.sampler.wait()
-        except OSError:
-            pass
-        self.sampler = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.handle = (pynvml.nvmlDeviceGetHandleByUUID(key) if key.startswith("GPU-")
+                           else pynvml.nvmlDeviceGetHandleByIndex(int(key)))
+            self.maximum = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception as e:  # no NVML: nvidia-smi below
+            self.handle, self.error = None, f"nvml: {e}"
+        if self.handle is not None:
+            try:
+                self.errors = tempfile.TemporaryFile(mode="w+")
+                self.sampler = subprocess.Popen([sys.executable, "-c", _NVML_SAMPLER, key], stdout=subprocess.PIPE,
+                                                stderr=self.errors, text=True)
+                first = self.sampler.stdout.readline().split()
+                if not (len(first) == 2 and first[0] == "ready"):
+                    self.sampler.kill()
+                    self.sampler.wait()
+                    self.errors.seek(0)
+                    lines = self.errors.read().strip().splitlines()
+                    self.error = "sampler: " + (lines[-1] if lines else f"exit {self.sampler.returncode}")
+                    self.sampler = None
+            except OSError as e:
+                self.sampler, self.error = None, f"sampler: {e}"
+            if self.sampler is None:
+                self.stop = threading.Event()
+
+                def sample():
+                    while True:
+                        try:
+                            self._sample_here()
+                        except Exception:
+                            return
+                        if self.stop.wait(0.01):
+                            return
+
+                self.thread = threading.Thread(target=sample, daemon=True)
+                self.thread.start()
+            self._sample_here()
+            return self
         try:
             self.process = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                                              "--format=csv,noheader,nounits", "-lms", "200"],
@@ -264,17 +304,27 @@ class Clocks:
         return self
 
     def __exit__(self, *exc):
-        if self.sampler is not None:
-            self.sampler.terminate()
+        if self.handle is not None:
             try:
-                out, _ = self.sampler.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.sampler.kill()
-                out, _ = self.sampler.communicate()
-            for line in out.splitlines():
-                parts = line.split()
-                if len(parts) == 2 and parts[0].isdigit() and parts[1].isdigit():
-                    self.nvml.append((int(parts[0]), self.maximum, int(parts[1])))
+                self._sample_here()
+            except Exception:
+                pass
+            if self.thread is not None:
+                self.stop.set()
+                self.thread.join(timeout=5)
+            if self.sampler is not None:
+                self.sampler.terminate()
+                try:
+                    out, _ = self.sampler.communicate(timeout=5)
+                except subprocess.TimeoutExpired:
+                    self.sampler.kill()
+                    out, _ = self.sampler.communicate()
+                for line in out.splitlines():
+                    parts = line.split()
+                    if len(parts) == 2 and parts[0].isdigit() and parts[1].isdigit():
+                        self.nvml.append((int(parts[0]), self.maximum, int(parts[1])))
+            if self.errors is not None:
+                self.errors.close()
             return
         if self.process is None:
             return
@@ -293,8 +343,12 @@ class Clocks:
         if self.nvml:
             sm = [float(clock) for clock, _, _ in self.nvml]
             reasons = sorted({name for _, _, mask in self.nvml for name, bit in self.REASONS if mask & bit})
-            return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.nvml[0][1]), "reasons": reasons,
-                    "samples": len(self.nvml), "source": "nvml, 10 ms"}
+            out = {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.nvml[0][1]), "reasons": reasons,
+                   "samples": len(self.nvml),
+                   "source": "nvml, 10 ms, " + ("child process" if self.thread is None else "in-process thread")}
+            if self.error:
+                out["sampler_error"] = self.error
+            return out
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(p[1]) for p in self.samples if p[1].replace(".", "").isdigit()]

@@ -439,7 +439,7 @@ def test_logits_heads_equal_torch_matmul(C, cuda, rows, counts, dim):
                           [8 if counts[h] % 2 else 16 for h in order])
     for out, h in zip(outs, order):
         n = counts[h]
-        assert out.shape == (rows, (n + 7) // 8 * 8)
+        assert out.shape == (rows, (n + 127) // 128 * 128)
         if n == 0:
             continue
         head_keys = keys[bounds[h]:bounds[h + 1]]
