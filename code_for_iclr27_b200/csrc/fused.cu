@@ -321,8 +321,11 @@ __global__ void __launch_bounds__(kRiskThreads) risk_kernel(ScoreTableParam tabl
 // the elementwise steps run as float2 operations, and the first division uses
 // the row's correctly rounded reciprocal (rows::divide2).  Per candidate the
 // operations and their order are those of risk_kernel.
+// Four CTAs per SM (64 registers, a few bytes of spills): the kernel waits on
+// its logits loads, and the fourth CTA hides more of that than the spills cost
+// (measured: 483 instead of 489 us per configs[1] layer call with three).
 template <typename T, int G, int C>
-__global__ void __launch_bounds__(kRiskThreads, 3) risk_vec_kernel(ScoreTableParam table,
+__global__ void __launch_bounds__(kRiskThreads, 4) risk_vec_kernel(ScoreTableParam table,
                                                                 const int64_t *__restrict__ qpos, int window,
                                                                 float scale, const float3 *__restrict__ stats,
                                                                 int64_t segment_base,
@@ -521,7 +524,7 @@ int launch_risk(const ScoreTableParam &table, int n, const int64_t *qpos, int wi
     if (rows_aligned<T>(table, n) && window * groups * 20 <= 200 * 1024 &&
         (groups == 1 || groups == 2 || groups == 4 || groups == 8)) {
       const auto args = std::make_tuple(table, n, qpos, window, scale, stats, s0, margin, epsilon, max_span, stream);
-      // Candidates per thread: G * C <= 16 keeps the per-thread state near 80 registers.
+      // Candidates per thread: G * C <= 16 keeps the per-thread state near 64 registers.
       return groups == 1   ? std::apply(launch_risk_vec<T, 1, 8>, args)
              : groups == 2 ? std::apply(launch_risk_vec<T, 2, 4>, args)
              : groups == 4 ? std::apply(launch_risk_vec<T, 4, 4>, args)
