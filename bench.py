@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Benchmark of the LazyRecall KV-management hot path on B200.
 
-Metric (BASELINE.json): managed KV tokens/s (score + evict + compact) and the
+Metric: managed KV tokens/s (score + evict + compact) and the
 per-decode-step overhead.  A managed token is one resident (layer, KV head,
 position) row that goes through one score -> pool -> select -> compact pass.
 

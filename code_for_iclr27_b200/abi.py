@@ -15,6 +15,9 @@ from . import LIBRARY_PATH
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_WORKSPACE = 0, 1, 2, 3, 4
 F32, F64, F16, BF16 = 0, 1, 2, 3
 STATIC_SCORE_ROWS = 262144  # LRK_STATIC_SCORE_ROWS in include/lrk.h
+# Layer-group selection state (LRK_SELECT_* in include/lrk.h).
+SELECT_BINS, SELECT_ROUNDS, SELECT_STATE_FIELDS = 4096, 3, 8
+SELECT_K, SELECT_PREFIX, SELECT_NEED, SELECT_BELOW, SELECT_LOCAL_BELOW, SELECT_TOTAL, SELECT_SHARE = range(7)
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -96,6 +99,8 @@ SIGNATURES = {
     "lrk_host_device_pointer": (I32, [P, ctypes.POINTER(P)]),
     "lrk_register_host": (I32, [P, SIZE]),
     "lrk_unregister_host": (I32, [P]),
+    "lrk_select_histogram": (I32, [ctypes.POINTER(P), ctypes.POINTER(I64), I64, I64, I32, P, P, P]),
+    "lrk_select_pick": (I32, [P, I64, I64, I64, I64, I32, P, P]),
 }
 
 _library = None

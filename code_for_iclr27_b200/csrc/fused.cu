@@ -27,6 +27,7 @@
 // convex R, so the maximum over chunks is the risk over all queries.
 // Many (layer, head) segments go in one launch: their descriptors travel as a
 // kernel parameter (up to kMaxScoreSegments per launch).
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -578,32 +579,82 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
 // LRK_STATIC_SCORE_ROWS rows.  Every device that loads liblrk holds one copy
 // until the process exits.  Host code must not pass this name to a kernel (on
 // the host it is a stand-in, not a device address); static_scratch() looks up
-// the device address once per device.
+// the device address with cudaGetSymbolAddress.
 __device__ __align__(256) float3 g_static_row_stats[LRK_STATIC_SCORE_ROWS];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_static_mutex;
-float3 *g_static_address[kMaxDevices] = {};
+// The array's device address belongs to one CUDA context (the module is loaded
+// per context), so the looked-up addresses are kept per context, keyed by the
+// context's unique ID (cuCtxGetId: never reused within a process, unlike the
+// context handle).  A context created later -- after cudaDeviceReset, or by a
+// host that makes its own driver contexts -- gets its own lookup.
+using CtxGetCurrent = CUresult (*)(CUcontext *);
+using CtxGetId = CUresult (*)(CUcontext, unsigned long long *);
 
-// Device address of g_static_row_stats on the current device (looked up with
-// cudaGetSymbolAddress on the first call for that device).
-int static_scratch(float3 **address) {
-  int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-  if (device < 0 || device >= kMaxDevices) return fail(LRK_ERR_UNSUPPORTED, "device index out of range");
-  std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (g_static_address[device] == nullptr) {
-    void *found = nullptr;
-    e = cudaGetSymbolAddress(&found, g_static_row_stats);
-    if (e != cudaSuccess) {
-      cudaGetLastError();
-      set_error("cudaGetSymbolAddress(g_static_row_stats): %s", cudaGetErrorString(e));
-      return LRK_ERR_CUDA;
-    }
-    g_static_address[device] = static_cast<float3 *>(found);
+struct StaticEntry {
+  unsigned long long context;
+  float3 *address;
+};
+constexpr int kStaticEntries = 64;
+std::mutex g_static_mutex;
+StaticEntry g_static_entries[kStaticEntries] = {};
+int g_static_used = 0, g_static_next = 0;
+
+template <typename F>
+F driver_function(const char *name) {
+  void *function = nullptr;
+  cudaDriverEntryPointQueryResult found;
+  if (cudaGetDriverEntryPoint(name, &function, cudaEnableDefault, &found) != cudaSuccess ||
+      found != cudaDriverEntryPointSuccess) {
+    cudaGetLastError();
+    return nullptr;
   }
-  *address = g_static_address[device];
+  return reinterpret_cast<F>(function);
+}
+
+int lookup_static_address(float3 **address) {
+  void *found = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&found, g_static_row_stats);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("cudaGetSymbolAddress(g_static_row_stats): %s", cudaGetErrorString(e));
+    return LRK_ERR_CUDA;
+  }
+  *address = static_cast<float3 *>(found);
+  return LRK_OK;
+}
+
+// Device address of g_static_row_stats in the calling thread's current
+// context; the first call in a context looks it up (cudaGetSymbolAddress,
+// which also makes the device's primary context current when none is).
+int static_scratch(float3 **address) {
+  static const CtxGetCurrent get_current = driver_function<CtxGetCurrent>("cuCtxGetCurrent");
+  static const CtxGetId get_id = driver_function<CtxGetId>("cuCtxGetId");
+  if (get_current == nullptr || get_id == nullptr) return fail(LRK_ERR_CUDA, "cuCtxGetCurrent/cuCtxGetId unavailable");
+  CUcontext context = nullptr;
+  if (get_current(&context) != CUDA_SUCCESS) return fail(LRK_ERR_CUDA, "cuCtxGetCurrent failed");
+  float3 *fresh = nullptr;
+  if (context == nullptr) {
+    // No context yet on this thread: the lookup binds the primary context.
+    const int status = lookup_static_address(&fresh);
+    if (status != LRK_OK) return status;
+    if (get_current(&context) != CUDA_SUCCESS || context == nullptr) return fail(LRK_ERR_CUDA, "no CUDA context");
+  }
+  unsigned long long id = 0;
+  if (get_id(context, &id) != CUDA_SUCCESS) return fail(LRK_ERR_CUDA, "cuCtxGetId failed");
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  for (int i = 0; i < g_static_used; ++i) {
+    if (g_static_entries[i].context == id) {
+      *address = g_static_entries[i].address;
+      return LRK_OK;
+    }
+  }
+  if (fresh == nullptr) {
+    const int status = lookup_static_address(&fresh);
+    if (status != LRK_OK) return status;
+  }
+  const int slot = g_static_used < kStaticEntries ? g_static_used++ : (g_static_next++ % kStaticEntries);
+  g_static_entries[slot] = StaticEntry{id, fresh};
+  *address = fresh;
   return LRK_OK;
 }
 

@@ -128,7 +128,106 @@ __global__ void __launch_bounds__(1024) risk_kernel(
   }
 }
 
+// Pool over aligned tiles.  A CTA owns one tile of one segment: the 128
+// 4-element quads that start at A + 512 x, A = the segment's first index
+// rounded down to a multiple of 4.  It stages the tile plus a halo on each
+// side in shared memory with 16-byte loads (quads that cross the array's ends
+// are read element by element); each thread then takes its quad's window of
+// elements into registers, replaces those outside the segment by -inf, and
+// folds each output's window with fmaxf in ascending index order from -inf.
+// Folding an extra -inf changes nothing (fmaxf(v, -inf) == v, and the
+// running value is never NaN), so this equals the reference's clipped window
+// (csrc/scoring.cu:190-203).  Outputs are stored as 16-byte vectors, element
+// by element where a quad crosses the segment's ends.  HALF > 0 fixes the
+// half-width at compile time (Pool7: 3); HALF = 0 reads it from `half`.
+constexpr int kPoolThreads = 128;
+constexpr int kPoolTile = 4 * kPoolThreads;  // elements per tile: one quad per thread
+constexpr int kPoolHalo = 32;                // largest half-width the tiled kernel serves
+
+template <int HALF>
+__global__ void __launch_bounds__(kPoolThreads) pool_tile_kernel(const float *__restrict__ scores, int64_t n,
+                                                                 const int64_t *__restrict__ bounds,
+                                                                 int64_t segments, int half_runtime,
+                                                                 float *__restrict__ out) {
+  __shared__ __align__(16) float tile[kPoolTile + 2 * kPoolHalo];
+  const int half = HALF > 0 ? HALF : half_runtime;
+  const int halo = (half + 3) & ~3;
+  for (int64_t segment = blockIdx.y; segment < segments; segment += gridDim.y) {
+    const int64_t begin = lmax(0, bounds[segment]);
+    const int64_t end = lmin(n, bounds[segment + 1]);
+    const int64_t first = begin & ~int64_t{3};
+    for (int64_t base = first + static_cast<int64_t>(blockIdx.x) * kPoolTile; base < end;
+         base += static_cast<int64_t>(gridDim.x) * kPoolTile) {
+      __syncthreads();  // the previous tile's reads are done
+      const int quads = (kPoolTile + 2 * halo) / 4;
+      for (int q = threadIdx.x; q < quads; q += kPoolThreads) {
+        const int64_t g = base - halo + 4 * q;
+        float4 v;
+        if (g >= 0 && g + 3 < n) {
+          v = __ldcs(reinterpret_cast<const float4 *>(scores + g));
+        } else {
+          v.x = (g >= 0 && g < n) ? scores[g] : 0.0f;
+          v.y = (g + 1 >= 0 && g + 1 < n) ? scores[g + 1] : 0.0f;
+          v.z = (g + 2 >= 0 && g + 2 < n) ? scores[g + 2] : 0.0f;
+          v.w = (g + 3 >= 0 && g + 3 < n) ? scores[g + 3] : 0.0f;
+        }
+        *reinterpret_cast<float4 *>(tile + 4 * q) = v;
+      }
+      __syncthreads();
+      const int64_t g = base + 4 * threadIdx.x;
+      if (g >= end) continue;
+      // Segment bounds relative to the quad's first element (small ints).
+      const int lo = static_cast<int>(lmax(begin - g, -(kPoolHalo + 4)));
+      const int hi = static_cast<int>(lmin(end - g, kPoolHalo + 8));
+      const float *at = tile + halo + 4 * threadIdx.x;  // element g
+      float r[4];
+      if (HALF > 0) {
+        // Elements g - H4 .. g + 3 + H4 in registers, H4 = HALF rounded up to 4.
+        constexpr int H4 = (HALF + 3) & ~3;
+        float w[4 + 2 * H4];
+#pragma unroll
+        for (int j = 0; j < 4 + 2 * H4; j += 4) {
+          const float4 v = *reinterpret_cast<const float4 *>(at - H4 + j);
+          w[j] = v.x;
+          w[j + 1] = v.y;
+          w[j + 2] = v.z;
+          w[j + 3] = v.w;
+        }
+#pragma unroll
+        for (int j = 0; j < 4 + 2 * H4; ++j) {
+          const int offset = j - H4;
+          if (offset < lo || offset >= hi) w[j] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float value = -INFINITY;
+#pragma unroll
+          for (int o = -HALF; o <= HALF; ++o) value = fmaxf(value, w[H4 + e + o]);
+          r[e] = value;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float value = -INFINITY;
+          const int from = max(lo, e - half), to = min(hi - 1, e + half);
+          for (int j = from; j <= to; ++j) value = fmaxf(value, at[j]);
+          r[e] = value;
+        }
+      }
+      if (g >= begin && g + 3 < end) {
+        __stcs(reinterpret_cast<float4 *>(out + g), make_float4(r[0], r[1], r[2], r[3]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (g + e >= begin && g + e < end) out[g + e] = r[e];
+      }
+    }
+  }
+}
+
 // Pool: out[i] = max of scores over [i - w/2, i + w/2] clipped to i's segment.
+// Element-per-thread form for unaligned pointers and windows wider than the
+// tiled kernel's halo.
 __global__ void pool_kernel(const float *__restrict__ scores, int64_t n, const int64_t *__restrict__ bounds,
                             int64_t segments, int half, float *__restrict__ out) {
   for (int64_t segment = blockIdx.y; segment < segments; segment += gridDim.y) {
@@ -347,11 +446,23 @@ extern "C" int lrk_pool(const float *scores, int64_t n, const int64_t *bounds, i
   LRK_REQUIRE(segments >= 1 && n >= 0, "Invalid pool layout");
   if (n == 0) return LRK_OK;
   LRK_REQUIRE(scores && bounds && out, "null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (width / 2 <= kPoolHalo && aligned(scores, 16) && aligned(out, 16)) {
+    // Tiles per segment: the longest segment plus its leading misalignment.
+    const int64_t tiles = std::max<int64_t>(1, std::min<int64_t>(ceil_div(maximum_count + 3, kPoolTile), 65535));
+    dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min<int64_t>(segments, 65535)));
+    const int half = static_cast<int>(width / 2);
+    if (half == 3)
+      pool_tile_kernel<3><<<grid, kPoolThreads, 0, s>>>(scores, n, bounds, segments, half, out);
+    else
+      pool_tile_kernel<0><<<grid, kPoolThreads, 0, s>>>(scores, n, bounds, segments, half, out);
+    return launch_status("lrk_pool");
+  }
   const int threads = 256;
   const int64_t tiles = std::max<int64_t>(1, std::min<int64_t>(ceil_div(maximum_count, threads), 65535));
   dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min<int64_t>(segments, 65535)));
   const int half = static_cast<int>(std::min<int64_t>(width / 2, INT32_MAX));
-  pool_kernel<<<grid, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(scores, n, bounds, segments, half, out);
+  pool_kernel<<<grid, threads, 0, s>>>(scores, n, bounds, segments, half, out);
   return launch_status("lrk_pool");
 }
 

@@ -6,7 +6,8 @@
 // through the caching allocator) and its stream (the current CUDA stream).
 // Added operators: refine and topk_smallest (selection); temporal_scores,
 // scores_from_keys, project_values, logits and logits_heads (scoring); compact_layers and
-// merge_layers (eviction and recall over several layers in one call).
+// merge_layers (eviction and recall over several layers in one call);
+// select_histogram and select_pick (layer-group selection across GPUs).
 #include <vector>
 
 #include "shim_common.h"
@@ -624,6 +625,48 @@ torch::Tensor scores_from_keys(std::vector<torch::Tensor> keys, std::vector<torc
   return scores;
 }
 
+// Layer-group selection, one radix round on this rank: the histograms of
+// request r's score table scores[r] (f32 [n_r], CUDA) per question, given the
+// states ([requests, questions, LRK_SELECT_STATE_FIELDS] int64, CUDA).
+// Returns [requests, questions, LRK_SELECT_BINS] int32 (the u32 counts' bits).
+torch::Tensor select_histogram(std::vector<torch::Tensor> scores, torch::Tensor states, int64_t round) {
+  check_cuda(states, states);
+  TORCH_CHECK(states.scalar_type() == at::kLong && states.dim() == 3 && states.size(2) == LRK_SELECT_STATE_FIELDS,
+              "states must be int64 [requests, questions, LRK_SELECT_STATE_FIELDS]");
+  const int64_t requests = states.size(0), questions = states.size(1);
+  TORCH_CHECK(static_cast<int64_t>(scores.size()) == requests, "one score table per request");
+  std::vector<const float *> pointers(requests);
+  std::vector<int64_t> counts(requests);
+  for (int64_t r = 0; r < requests; ++r) {
+    check_cuda(scores[r], states);
+    TORCH_CHECK(scores[r].scalar_type() == at::kFloat && scores[r].dim() == 1, "score tables must be f32 [n]");
+    pointers[r] = scores[r].data_ptr<float>();
+    counts[r] = scores[r].numel();
+  }
+  c10::cuda::CUDAGuard guard(states.device());
+  auto histograms = torch::empty({requests, questions, LRK_SELECT_BINS}, states.options().dtype(at::kInt));
+  check_status(lrk_select_histogram(pointers.data(), counts.data(), requests, questions, static_cast<int>(round),
+                                    states.data_ptr<int64_t>(),
+                                    reinterpret_cast<uint32_t *>(histograms.data_ptr<int32_t>()), current_stream()));
+  return histograms;
+}
+
+// Advance the states by one round from the all-gathered histograms
+// ([world, requests, questions, LRK_SELECT_BINS] int32, CUDA).  In place.
+void select_pick(torch::Tensor gathered, int64_t rank, torch::Tensor states, int64_t round) {
+  check_cuda(gathered, states);
+  check_cuda(states, states);
+  TORCH_CHECK(states.scalar_type() == at::kLong && states.dim() == 3 && states.size(2) == LRK_SELECT_STATE_FIELDS,
+              "states must be int64 [requests, questions, LRK_SELECT_STATE_FIELDS]");
+  TORCH_CHECK(gathered.scalar_type() == at::kInt && gathered.dim() == 4 && gathered.size(1) == states.size(0) &&
+                  gathered.size(2) == states.size(1) && gathered.size(3) == LRK_SELECT_BINS,
+              "gathered must be int32 [world, requests, questions, LRK_SELECT_BINS]");
+  c10::cuda::CUDAGuard guard(states.device());
+  check_status(lrk_select_pick(reinterpret_cast<const uint32_t *>(gathered.data_ptr<int32_t>()), gathered.size(0),
+                               rank, states.size(0), states.size(1), static_cast<int>(round),
+                               states.data_ptr<int64_t>(), current_stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -648,4 +691,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("query_positions"), pybind11::arg("margin"), pybind11::arg("scale"),
              pybind11::arg("epsilon"), pybind11::arg("query_chunks") = std::vector<int64_t>{});
   module.def("project_values", &project_values);
+  module.def("select_histogram", &select_histogram);
+  module.def("select_pick", &select_pick);
 }

@@ -130,9 +130,11 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
  * file-scope device array of LRK_STATIC_SCORE_ROWS row statistics (3 MiB),
  * which every GPU that loads liblrk holds until the process exits.  Calls with
  * segments x window x groups above LRK_STATIC_SCORE_ROWS are rejected with
- * LRK_ERR_INVALID before anything is launched.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress), so make that
- * first call before any stream capture on that device.  All calls share the
+ * LRK_ERR_INVALID before anything is launched.  The first call in each CUDA
+ * context (normally once per device: the runtime's primary context) looks up
+ * the array's device address (cudaGetSymbolAddress); the address is cached
+ * per context ID, so a context made after cudaDeviceReset looks it up again.
+ * Make that first call before any stream capture in that context.  All calls share the
  * one array: calls whose work overlaps on the GPU (other streams, other host
  * threads) race and must be serialised by the caller.  Nothing in the array
  * needs clearing between calls: each call writes every entry it reads first.
@@ -375,6 +377,52 @@ size_t lrk_topk_workspace_bytes(int64_t n);
  * values [k] f32, indices [k] i64 (device). */
 int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
                       size_t workspace_bytes, float *values, int64_t *indices, lrk_stream_t stream);
+
+/* ---------------------------------------------- layer-group selection */
+
+/* The request-wide "k smallest raw scores" when one request's layers are
+ * split over ranks (GPUs): the selection refine_arrays starts from
+ * (src/lazy_recall/selection.py:52-88, torch.topk(largest=False) over the
+ * whole score table), with ties taken in score-table order, which is
+ * layer-major (src/lazy_recall/scoring.py:218-287), so ranks holding
+ * consecutive layer groups in rank order take ties in rank order.  A rank's
+ * share of the k smallest is its local bottom-(share) by (key, index).
+ *
+ * Three radix rounds (12, 12, 8 bits of the order-preserving key, NaN last).
+ * Per round: lrk_select_histogram on every rank, an all-gather of the
+ * histograms by the caller (NCCL), lrk_select_pick on every rank.  The state
+ * stays on the device between rounds; after round 2, state[SHARE] is this
+ * rank's share and state[TOTAL] the request-wide score count.  No counterpart
+ * operator in the reference (its selection runs on one GPU). */
+#define LRK_SELECT_BINS 4096
+#define LRK_SELECT_ROUNDS 3
+#define LRK_SELECT_MAX_QUESTIONS 4
+#define LRK_SELECT_MAX_REQUESTS 64
+/* Fields of one (request, question) state: int64 [LRK_SELECT_STATE_FIELDS].
+ * The caller zeroes a state and sets K before round 0. */
+#define LRK_SELECT_STATE_FIELDS 8
+#define LRK_SELECT_K 0           /* the k asked for (clamped to TOTAL) */
+#define LRK_SELECT_PREFIX 1      /* key bits fixed so far */
+#define LRK_SELECT_NEED 2        /* rank of the k-th key among the keys in play */
+#define LRK_SELECT_BELOW 3       /* request-wide keys below the keys in play */
+#define LRK_SELECT_LOCAL_BELOW 4 /* this rank's keys below the keys in play */
+#define LRK_SELECT_TOTAL 5       /* request-wide key count (set in round 0) */
+#define LRK_SELECT_SHARE 6       /* result: this rank's share of the k smallest
+                                  * (-1: the ranks' histograms were inconsistent) */
+
+/* One round's histograms of this rank's keys: scores[r] / counts[r] is
+ * request r's score table on this rank (device f32, HOST pointer array);
+ * states [requests][questions][FIELDS] i64 (device); histograms
+ * [requests][questions][LRK_SELECT_BINS] u32 (device), cleared here first. */
+int lrk_select_histogram(const float *const *scores, const int64_t *counts, int64_t requests,
+                         int64_t questions, int round, const int64_t *states, uint32_t *histograms,
+                         lrk_stream_t stream);
+
+/* Advance every state by one round from the all-gathered histograms:
+ * gathered [world][requests][questions][LRK_SELECT_BINS] u32 (device), rank
+ * this rank's index in gather order (= its layer group's order). */
+int lrk_select_pick(const uint32_t *gathered, int64_t world, int64_t rank, int64_t requests,
+                    int64_t questions, int round, int64_t *states, lrk_stream_t stream);
 
 /* Gather rows of one table: dst row i = src row indices[i] (row_bytes each);
  * out-of-range indices leave their destination row unwritten.  src may be

@@ -10,7 +10,7 @@ flags (setup.py:15-18) for sm_100a, so that GPU parity tests can compare the
 new kernels with the reference kernels on identical inputs.  The reference's
 setup.py is not run.
 
-Usage: python oracle/build_ref.py [REFERENCE_ROOT]
+Usage: python oracle/build_ref.py [REFERENCE_ROOT]  (default: oracle/reference_root.py)
 Outputs: oracle/_ref/{C,legacy_C,host}/<module>.so (git-ignored, travels with
 the repository snapshot to the GPU box).
 """
@@ -39,7 +39,7 @@ def built_paths():
     return found
 
 
-def build(reference_root: str = "/root/reference", verbose: bool = False) -> dict:
+def build(reference_root: str, verbose: bool = False) -> dict:
     root = Path(reference_root)
     if not (root / "csrc" / "scoring.cu").exists():
         raise FileNotFoundError(f"reference sources not found under {root}")
@@ -66,6 +66,12 @@ def build(reference_root: str = "/root/reference", verbose: bool = False) -> dic
 
 
 if __name__ == "__main__":
-    paths = build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", verbose=True)
+    sys.path.insert(0, str(HERE.parent))
+    from oracle.reference_root import reference_root
+
+    root = sys.argv[1] if len(sys.argv) > 1 else reference_root()
+    if root is None:
+        raise SystemExit("reference sources not found: pass REFERENCE_ROOT or set LAZY_RECALL_REFERENCE")
+    paths = build(str(root), verbose=True)
     for key, path in sorted(paths.items()):
         print(key, path)

@@ -324,10 +324,19 @@ def make_gpu(out: Path):
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("which", choices=["cpu", "gpu"])
-    parser.add_argument("--reference", default="/root/reference/src")
+    parser.add_argument("--reference", default=None,
+                        help="the reference's src/ directory (default: oracle/reference_root.py's tree + /src)")
     parser.add_argument("--out", default=None)
     args = parser.parse_args()
     if args.which == "cpu":
+        if args.reference is None:
+            sys.path.insert(0, str(ROOT))
+            from oracle.reference_root import reference_root
+
+            root = reference_root()
+            if root is None:
+                raise SystemExit("reference sources not found: pass --reference or set LAZY_RECALL_REFERENCE")
+            args.reference = str(root / "src")
         make_cpu(args.reference, Path(args.out or HERE / "reference_cpu.npz"))
     else:
         make_gpu(Path(args.out or HERE / "reference_gpu.npz"))

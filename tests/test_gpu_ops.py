@@ -313,8 +313,10 @@ def test_legacy_decision_risk(L, ref, cuda, values_dtype):
 # --------------------------------------------------------------- pool
 
 
-@pytest.mark.parametrize("width", [1, 3, 7, 9])
+@pytest.mark.parametrize("width", [1, 3, 7, 9, 63, 65])
 def test_pool(C, ref, cuda, width):
+    # Widths up to 65 cover the tiled kernel (half-width <= 32) and the
+    # element-per-thread one beyond it.
     torch = torch_mod()
     g = gen(9)
     lengths = [1, 2, 3, 6, 7, 500, 4096, 1]
@@ -328,6 +330,28 @@ def test_pool(C, ref, cuda, width):
     np.testing.assert_array_equal(out.cpu().numpy(), O.pool(scores.cpu().numpy(), bounds.cpu().numpy(), width))
     if ref is not None:
         assert torch.equal(out, ref["C"].pool(scores, bounds, max(lengths), width))
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+def test_pool_tiles(C, ref, cuda, offset):
+    """Segments longer than one 2048-element tile, starting at every residue
+    mod 4, empty segments, NaN runs, ties; offset 1 passes a 4-byte aligned
+    (not 16-byte aligned) view, which takes the element-per-thread kernel."""
+    torch = torch_mod()
+    g = gen(19)
+    lengths = [0, 5, 2047, 2048, 2049, 0, 0, 6150, 3, 1, 4097, 9, 0, 1962 * 3 + 1]
+    n = sum(lengths)
+    base = (torch.randint(0, 40, (n + offset,), generator=g).float() / 4)
+    base[offset + 3000:offset + 3010] = float("nan")
+    base[offset + 7000] = float("inf")
+    scores = base.to(cuda)[offset:]
+    bounds = torch.tensor(np.concatenate(([0], np.cumsum(lengths))), dtype=torch.int64, device=cuda)
+    for width in (1, 7, 15):
+        out = C.pool(scores, bounds, max(lengths), width)
+        np.testing.assert_array_equal(out.cpu().numpy(),
+                                      O.pool(scores.cpu().numpy(), bounds.cpu().numpy(), width))
+        if ref is not None:
+            assert torch.equal(out, ref["C"].pool(scores, bounds, max(lengths), width))
 
 
 # ------------------------------------------------------------ scoring

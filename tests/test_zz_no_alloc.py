@@ -5,9 +5,14 @@ handed out by another allocator (an inference engine that reserves the
 device's memory at start-up and forbids further cudaMalloc), or a plain C host
 (cgo, JNI) that has no device allocator of its own.  For them the entry point
 takes its scratch from a fixed-size array compiled into liblrk instead of a
-caller-provided workspace.  This test calls it through the C ABI, twice in a
-row on different inputs, and checks each result against the workspace entry
-point (lrk_temporal_scores) with the tolerance of the other scoring tests; it
+caller-provided workspace.  This test calls it through the C ABI,
+three times in a row on different inputs, and checks each result against the
+workspace entry point (lrk_temporal_scores) bit for bit: both run the same
+kernels on the same data, so the scores must be the same floats, NaN in the
+same places.  The static path compares key positions where the workspace path
+uses its visible-prefix table, so one call masks keys (query positions inside
+the key range), and that call has 60 segments, so the scratch rows of a second
+segment table (the kernels take 48 segments per launch) are exercised too.  It
 also checks that a call larger than the static scratch is refused.
 
 It lives in its own file so that pytest collects it last.
@@ -18,20 +23,19 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-RTOL = 1e-5
 
 
-def assert_scores_close(actual, expected):
-    actual = np.asarray(actual, np.float64)
-    expected = np.asarray(expected, np.float64)
+def assert_same_scores(actual, expected):
+    """Bit equality of float32 scores (NaN payloads aside: NaN where the other is NaN)."""
+    actual = np.asarray(actual, np.float32)
+    expected = np.asarray(expected, np.float32)
     assert actual.shape == expected.shape
-    assert (np.isnan(actual) == np.isnan(expected)).all()
-    ok = ~np.isnan(expected)
-    floor = 1e-6 * np.abs(expected[ok]).max() if ok.any() else 0.0
-    assert (np.abs(actual[ok] - expected[ok]) <= RTOL * np.abs(expected[ok]) + floor).all()
+    nan = np.isnan(expected)
+    assert (np.isnan(actual) == nan).all()
+    assert (actual[~nan].view(np.uint32) == expected[~nan].view(np.uint32)).all()
 
 
-def make_call(seed, heads, window, groups, lengths, device):
+def make_call(seed, heads, window, groups, lengths, device, query_start=10 ** 6):
     """Inputs of one scoring call: bf16 logits, projected values, positions."""
     import torch
 
@@ -51,7 +55,7 @@ def make_call(seed, heads, window, groups, lengths, device):
                                        out.data_ptr(), length)
         tensors += [logits, pv, kpos]
         outputs.append(out)
-    qpos = torch.arange(10 ** 6, 10 ** 6 + window, dtype=torch.int64, device=device)
+    qpos = torch.arange(query_start, query_start + window, dtype=torch.int64, device=device)
     margin = torch.tensor([0.8], device=device)
     tensors += [qpos, margin]
     return segments, outputs, qpos, margin, tensors
@@ -86,17 +90,23 @@ def test_static_scratch_matches_workspace_entry_point():
         pytest.skip("no CUDA device")
     device = torch.device("cuda:0")
     lib = abi.library()
-    first = make_call(1, 3, 60, 4, [700, 1300, 257], device)
-    second = make_call(2, 5, 33, 8, [400, 2050, 90, 999, 3001], device)
-    expected_first = run(lib, first, 60, 4, static=False, device=device)
-    expected_second = run(lib, second, 33, 8, static=False, device=device)
-    for out in first[1] + second[1]:
-        out.fill_(-1.0)
-    # Two calls in a row on the shared static scratch.
-    got_first = run(lib, first, 60, 4, static=True, device=device)
-    got_second = run(lib, second, 33, 8, static=True, device=device)
-    for got, want in zip(got_first + got_second, expected_first + expected_second):
-        assert_scores_close(got, want)
+    # (seed, queries, groups, key counts, first query position): the third
+    # call has 60 segments, two segment tables of the scoring kernels, and its
+    # query positions 1000..1015 mask the later keys of its longer heads.
+    calls = [(1, 60, 4, [700, 1300, 257], 10 ** 6), (2, 33, 8, [400, 2050, 90, 999, 3001], 10 ** 6),
+             (3, 16, 4, [64 + 37 * i for i in range(60)], 1000)]
+    inputs = [make_call(seed, len(lengths), window, groups, lengths, device, start)
+              for seed, window, groups, lengths, start in calls]
+    expected = [run(lib, call, window, groups, static=False, device=device)
+                for call, (_, window, groups, _, _) in zip(inputs, calls)]
+    for call in inputs:
+        for out in call[1]:
+            out.fill_(-1.0)
+    # Calls in a row on the shared static scratch.
+    for call, (_, window, groups, _, _), want in zip(inputs, calls, expected):
+        got = run(lib, call, window, groups, static=True, device=device)
+        for g, w in zip(got, want):
+            assert_same_scores(g, w)
 
 
 def test_static_scratch_limit_is_enforced():
