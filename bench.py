@@ -66,10 +66,10 @@ def parse_args():
     parser.add_argument("--seed", type=int, default=0)
     parser.add_argument("--skip-side", action="store_true",
                         help="skip the configs[2] batch_append and configs[3] recall measurements (N=1 only)")
-    parser.add_argument("--layer-groups", action="store_true",
-                        help="N>1: split ONE request's layers into per-GPU groups (strong scaling; the eviction "
-                             "threshold is fixed by NCCL all-gathers of radix histograms) instead of one request "
-                             "per GPU")
+    parser.add_argument("--skip-large", action="store_true", help="skip the configs[4] measurements")
+    parser.add_argument("--large-requests", type=int, default=8, help="configs[4] requests per GPU")
+    parser.add_argument("--large-steps", type=int, default=2, help="configs[4] timed passes")
+    parser.add_argument("--large-warmup", type=int, default=2, help="configs[4] warm-up passes")
     parser.add_argument("--scoring", choices=["fused", "dropin"], default="fused",
                         help="fused: lrk_temporal_scores per layer; dropin: the reference's per-head composition of "
                              "temporal_probabilities + temporal_risk")
@@ -141,6 +141,19 @@ def build_request(device, seed: int):
                                    device=device)
     margin = torch.tensor([1.0], device=device)
     return cache, queries, query_positions, gradients, margin
+
+
+def config_cfg1(world: int, scoring: str) -> dict:
+    """The bench line's config: the configs[1] workload (both arms report it)."""
+    return {"workload": "configs[1] llama-3-8b single request, steady-state audit pass",
+            "scoring": scoring,
+            "layers": LAYERS, "kv_heads": HEADS, "gqa_group": GROUPS, "head_dim": DIM,
+            "prompt_rows_per_head": PROMPT, "generation_rows": RETAINED + IMMEDIATE, "budget": BUDGET,
+            "temporal_window": WINDOW, "selected_per_audit": IMMEDIATE + QUEUED, "evicted_per_audit": IMMEDIATE,
+            "managed_rows_per_request": LAYERS * HEADS * PROMPT + RETAINED + IMMEDIATE,
+            "requests_per_gpu": 1,
+            "parallelism": f"request-sharded x{world}" if world > 1 else "single request",
+            "l2": "no flush: 4.6 GB of K/V per request, larger than L2"}
 
 
 # ------------------------------------------------------------ instruments
@@ -413,23 +426,125 @@ def cpu_baseline(seed: int = 0):
                         "extrapolated_pass": total}}
 
 
+def host_cores() -> dict:
+    """The host's CPU: logical cores, torch's intra-op threads, model name."""
+    import torch
+
+    model = None
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": model}
+
+
+def reference_cpu_sample(seed: int):
+    """The reference's own CPU path -- its unchanged Python package installed
+    with LAZY_RECALL_BUILD_CUDA=0 (oracle/_ref/py, made by
+    oracle/install_ref_py.py) -- on a bounded sample of one configs[1] audit
+    pass, extrapolated to the pass:
+      * one layer's 8 heads scored by temporal_head_scores_reference
+        (scoring.py:75-149: bf16 Q K^T, softmax, risk), x32 layers;
+      * pool_score_table's CPU branch (scoring.py:336-353) and refine_arrays
+        (selection.py:52-88) over the whole 502,272-score table;
+      * one layer's compaction by the CPU branch of remove_positions
+        (cache.py:162-167: keep mask, compact_flattened_kv, index_select), x32
+        (the immediate prefix touches every layer).
+    Returns None when the package is not installed."""
+    from oracle.install_ref_py import installed
+
+    where = installed()
+    if where is None:
+        return None
+    if str(where) not in sys.path:
+        sys.path.insert(0, str(where))
+    import torch
+    from lazy_recall._core.cuda_ops import compact_flattened_kv
+    from lazy_recall._core.scoring import ScoreSegment, ScoreTable
+    from lazy_recall.scoring import pool_score_table, temporal_head_scores_reference
+    from lazy_recall.selection import refine_arrays
+
+    rng = np.random.default_rng(seed)
+    lengths = generation_lengths(rng)
+    g = torch.Generator().manual_seed(seed)
+    qpos = torch.arange(PROMPT + GENERATED - WINDOW, PROMPT + GENERATED)
+    margin = torch.tensor(1.0)
+    t_layer = 0.0
+    for head in range(HEADS):
+        generated = int(lengths[0, head])
+        length = PROMPT + generated
+        keys = torch.randn(length, DIM, generator=g).to(torch.bfloat16)
+        values = torch.randn(length, DIM, generator=g).to(torch.bfloat16)
+        queries = (torch.randn(WINDOW, GROUPS, DIM, generator=g) * 2).to(torch.bfloat16)
+        grad = torch.randn(GROUPS, DIM, generator=g) / math.sqrt(DIM)
+        kpos = torch.from_numpy(head_positions(rng, generated))
+        t0 = time.perf_counter()
+        temporal_head_scores_reference(queries, qpos, keys, kpos, values, PROMPT, length - PROTECT_RECENT, grad,
+                                       margin, 1e-6, WINDOW)
+        t_layer += time.perf_counter() - t0
+    candidates = lengths.reshape(-1) - PROTECT_RECENT
+    ends = np.cumsum(candidates).tolist()
+    segments = [ScoreSegment(l, h, PROMPT, int(c)) for (l, h), c in
+                zip(((l, h) for l in range(LAYERS) for h in range(HEADS)), candidates)]
+    table = ScoreTable(torch.rand(int(candidates.sum()), generator=g), segments, ends, 0.0)
+    t0 = time.perf_counter()
+    pooled = pool_score_table(table, 7)
+    t_pool = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    refine_arrays(table, pooled, IMMEDIATE + QUEUED)
+    t_select = time.perf_counter() - t0
+    rows = int(sum(PROMPT + int(n) for n in lengths[0]))
+    keys = torch.randn(rows, DIM, generator=g).to(torch.bfloat16)
+    values = torch.randn(rows, DIM, generator=g).to(torch.bfloat16)
+    position_rows = torch.arange(rows, dtype=torch.float32).reshape(-1, 1)
+    absolute = torch.from_numpy(np.sort(rng.choice(rows, IMMEDIATE // LAYERS, replace=False)))
+    t0 = time.perf_counter()
+    keep_mask = torch.ones(position_rows.shape[0], dtype=torch.bool)
+    keep_mask[absolute] = False
+    keep_indices = torch.nonzero(keep_mask, as_tuple=False).reshape(-1)
+    compact_flattened_kv(keys, values, keep_indices)
+    position_rows.index_select(0, keep_indices)
+    t_compact = time.perf_counter() - t0
+    total = LAYERS * t_layer + t_pool + t_select + LAYERS * t_compact
+    managed = LAYERS * HEADS * PROMPT + RETAINED + IMMEDIATE
+    return {"value": managed / total, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": (f"reference package (oracle/_ref/py, LAZY_RECALL_BUILD_CUDA=0): 1 of {LAYERS} layers scored by "
+                       f"temporal_head_scores_reference ({HEADS} heads, Lh~{PROMPT + int(lengths[0].mean())}, "
+                       f"W={WINDOW}, G={GROUPS}, D={DIM}) x{LAYERS} + pool_score_table + refine_arrays over "
+                       f"{table.scores.numel()} scores + 1 of {LAYERS} layer compactions x{LAYERS}"),
+            "host": host_cores(),
+            "seconds": {"layer_scores": t_layer, "pool": t_pool, "select": t_select, "compact_layer": t_compact,
+                        "extrapolated_pass": total}}
+
+
 def reference_arm(args, rank: int):
-    """--impl reference: the reference's CPU implementation of the path (the
-    oracle port; the reference's own CPU code is Python that does not travel
-    to the GPU box), timed on the host cores."""
+    """--impl reference: the reference's own CPU implementation of the path
+    (its unchanged Python package, CPU math path), timed on the host cores
+    with all of torch's threads; each step is one bounded sample
+    (reference_cpu_sample), after --warmup untimed samples.  Falls back to the
+    numpy port (cpu_baseline) when the package is not installed.  Under
+    torchrun only rank 0 runs."""
     if rank != 0:
         return
-    for _ in range(args.warmup):
-        pass
-    runs = [cpu_baseline(args.seed + i) for i in range(max(1, args.steps))]
+    import torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    sample = reference_cpu_sample if reference_cpu_sample(args.seed) is not None else cpu_baseline
+    for i in range(args.warmup):
+        sample(args.seed + 100 + i)
+    runs = [sample(args.seed + i) for i in range(max(1, args.steps))]
     value = float(np.median([r["value"] for r in runs]))
-    sample = runs[0]
+    first = runs[0]
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": float(np.median([r["seconds"]["extrapolated_pass"] for r in runs]))
             * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "impl": "reference",
-            "config": {"workload": "configs[1] llama-3-8b audit pass (CPU sample, extrapolated)"},
-            "cpu_baseline": {k: sample[k] for k in ("cores", "kind", "sample")} | {"value": value, "unit": "tokens/s"},
+            "data": "synthetic (seeded): bf16 K/V ~N(0,1), queries ~N(0,4), margin gradient ~N(0,1/D)",
+            "impl": "reference", "config": config_cfg1(args.gpus, "reference CPU path"),
+            "cpu_baseline": {k: first[k] for k in ("cores", "kind", "sample")} | {"value": value, "unit": "tokens/s",
+                                                                                   "host": host_cores()},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -437,71 +552,52 @@ def reference_arm(args, rank: int):
 # ---------------------------------------------------------------- GPU arm
 
 
-def main():
-    args = parse_args()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.impl == "reference":
-        return reference_arm(args, rank)
+def fused_bytes(logits, projected_values, key_positions, first, last, query_positions, margin, scale, eps,
+                query_chunks=None):
+    """The fused scorer's algorithmic bytes: the logits read once, projected
+    values and key positions once, the scores written."""
+    total = 0
+    for lg, f, l in zip(logits, first, last):
+        w, g, length = lg.shape
+        total += w * g * length * lg.element_size() + g * length * 4 + length * 4 + (l - f) * 4
+    return total
 
+
+def probability_bytes(logits, projected_values, query_positions, key_positions, scale):
+    # read logits, write probabilities, read projected values and key positions
+    w, g, length = logits.shape
+    return w * g * length * (logits.element_size() + 4) + g * length * 4 + length * 4
+
+
+def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier, layer_groups: bool,
+                 steps: int, warmup: int, with_e2e: bool):
+    """configs[1] audit passes: one request per rank (request sharding), or
+    one request split into per-rank layer groups (layer_groups).  Returns the
+    raw measurements of this rank."""
     import torch
-    import torch.distributed as dist
 
     from code_for_iclr27_b200 import audit as audit_module
+    from code_for_iclr27_b200 import kvcache as kvcache_module
     from code_for_iclr27_b200 import operators
+    from code_for_iclr27_b200 import selection as selection_module
     from code_for_iclr27_b200.audit import audit_pass, evict_prefix
+    from code_for_iclr27_b200.distributed import lazy_prefix_share, layer_group_audit_pass
+    from code_for_iclr27_b200.kvcache import PackedCache
 
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    distributed = world > 1
-    if distributed:
-        from datetime import timedelta
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
-
-    def barrier():
-        if distributed:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    layer_groups = args.layer_groups and distributed
     cache, queries, qpos, gradients, margin = build_request(device, args.seed + (0 if layer_groups else 1000 * rank))
     managed = cache.total_rows()
     if layer_groups:
         # Every rank built the same request; each keeps its contiguous group of layers.
-        from code_for_iclr27_b200.distributed import layer_group_audit_pass
-        from code_for_iclr27_b200.kvcache import PackedCache
-
         if LAYERS % world:
-            raise SystemExit(f"--layer-groups needs the {LAYERS} layers to split evenly over {world} GPUs")
+            raise SystemExit(f"layer groups need the {LAYERS} layers to split evenly over {world} GPUs")
         mine = slice(rank * (LAYERS // world), (rank + 1) * (LAYERS // world))
         cache = PackedCache(layers=cache.layers[mine], seen_tokens=cache.seen_tokens)
         queries, gradients = queries[mine], gradients[mine]
     C = operators()
     counter = LaunchCounter(C)
     timer = KernelTimer()
-
-    def probability_bytes(logits, projected_values, query_positions, key_positions, scale):
-        # read logits, write probabilities, read projected values and key positions
-        w, g, length = logits.shape
-        return w * g * length * (logits.element_size() + 4) + g * length * 4 + length * 4
-
-    def fused_bytes(logits, projected_values, key_positions, first, last, query_positions, margin, scale, eps,
-                    query_chunks=None):
-        # the fused minimum: logits read once, projected values and key positions once, scores written
-        total = 0
-        for lg, f, l in zip(logits, first, last):
-            w, g, length = lg.shape
-            total += w * g * length * lg.element_size() + g * length * 4 + length * 4 + (l - f) * 4
-        return total
-
     fused = args.scoring == "fused"
     timed_name = "temporal_scores" if fused else "temporal_probabilities"
-
-    from code_for_iclr27_b200 import kvcache as kvcache_module
-    from code_for_iclr27_b200 import selection as selection_module
-
     patched = (audit_module, kvcache_module, selection_module)
     originals = [module.operators for module in patched]
 
@@ -509,48 +605,45 @@ def main():
         for module in patched:
             module.operators = provider
 
-    route(lambda: counter)
+    gathers = []
 
-    def one_pass():
+    def one_pass(q=queries, g=gradients, timings=None):
         if layer_groups:
-            return layer_group_audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED,
-                                          protect_recent=PROTECT_RECENT)
-        return audit_pass(cache, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT, fused=fused)
+            return layer_group_audit_pass(cache, q, qpos, g, margin, IMMEDIATE, QUEUED, protect_recent=PROTECT_RECENT,
+                                          timings=timings)
+        return audit_pass(cache, q, qpos, g, margin, IMMEDIATE, QUEUED, PROTECT_RECENT, fused=fused)
 
-    for _ in range(args.warmup):
-        last = one_pass()
-    barrier()
-    # Timed region: K audit passes.
-    counter.count = 0
-    wrapped = timer.wrap(getattr(C, timed_name), fused_bytes if fused else probability_bytes)
-
-    class Timed:
-        def __getattr__(self, name):
-            if name == timed_name:
-                return wrapped
-            return getattr(counter, name)
-
-    timed_ops = Timed()
-    route(lambda: timed_ops)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(torch.cuda.current_device()) as clocks:
-        barrier()
-        start.record()
-        for _ in range(args.steps):
+    route(lambda: counter)
+    try:
+        for _ in range(warmup):
             last = one_pass()
-        end.record()
         barrier()
-    elapsed_ms = start.elapsed_time(end)
-    # lrk_temporal_scores: visibility, statistics and risk kernels per call (<= 48 segments)
-    launches = counter.count + len(timer.pairs) * (3 if fused else 1)
-    for module, function in zip(patched, originals):
-        module.operators = function
-    local = torch.tensor([elapsed_ms], device=device)
-    if distributed:
-        dist.all_reduce(local, op=dist.ReduceOp.MAX)
-    elapsed_ms = float(local.item())
-    requests = 1 if layer_groups else world
-    value = requests * managed * args.steps / (elapsed_ms / 1e3)
+        counter.count = 0
+        wrapped = timer.wrap(getattr(C, timed_name), fused_bytes if fused else probability_bytes)
+
+        class Timed:
+            def __getattr__(self, name):
+                if name == timed_name:
+                    return wrapped
+                return getattr(counter, name)
+
+        timed_ops = Timed()
+        route(lambda: timed_ops)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(torch.cuda.current_device()) as clocks:
+            barrier()
+            start.record()
+            for _ in range(steps):
+                last = one_pass(timings=gathers)
+            end.record()
+            barrier()
+        elapsed_ms = start.elapsed_time(end)
+        # lrk_temporal_scores: visibility, statistics and risk kernels per call (<= 48 segments);
+        # layer groups add 3 histogram + 3 pick launches per pass.
+        launches = counter.count + len(timer.pairs) * (3 if fused else 1) + (6 * steps if layer_groups else 0)
+    finally:
+        for module, function in zip(patched, originals):
+            module.operators = function
 
     # Per-decode-step overhead: append one token to every layer, evict a
     # staging-sized queue prefix every EVICT_INTERVAL steps.  With layer
@@ -559,8 +652,6 @@ def main():
     # ranks' next queue scores per batch); the audit already evicted its share
     # of the immediate prefix, the first slots of its local queue.
     if layer_groups:
-        from code_for_iclr27_b200.distributed import lazy_prefix_share
-
         queue = last.references[lazy_prefix_share(last.references.scores, IMMEDIATE):]
     else:
         queue = last.references[IMMEDIATE:]
@@ -585,80 +676,153 @@ def main():
                 queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
     d1.record()
     barrier()
-    decode_local = torch.tensor([d0.elapsed_time(d1)], device=device)
+    out = {"managed": managed, "elapsed_ms": elapsed_ms, "decode_ms": d0.elapsed_time(d1), "launches": launches,
+           "kernel_ms": timer.total_ms(), "kernel_bytes": timer.bytes, "kernel_launches": len(timer.pairs),
+           "timed_name": timed_name, "clocks": clocks.summary(),
+           "gather_us": [a.elapsed_time(b) * 1e3 for a, b in gathers]}
+    if with_e2e:
+        # End to end through the public API: audit inputs copied from pinned
+        # host memory each step, the queue read back (refine_arrays returns
+        # host arrays).
+        host_queries = [q.cpu().pin_memory() for q in queries]
+        host_gradients = [x.cpu().pin_memory() for x in gradients]
+        out["h2d"] = sum(q.numel() * q.element_size() for q in host_queries) + sum(x.numel() * 4 for x in host_gradients)
+        out["d2h"] = (IMMEDIATE + QUEUED) * (4 + 8 + 8) + 2 * 8
+
+        def e2e_pass():
+            one_pass([q.to(device, non_blocking=True) for q in host_queries],
+                     [x.to(device, non_blocking=True) for x in host_gradients])
+
+        e2e_pass()  # warm-up
+        barrier()
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record()
+        out["e2e_steps"] = max(1, steps)
+        for _ in range(out["e2e_steps"]):
+            e2e_pass()
+        e_end.record()
+        barrier()
+        out["e2e_ms"] = e_start.elapsed_time(e_end)
+    return out
+
+
+def max_over_ranks(values, distributed: bool, device):
+    """Elementwise maximum over ranks of a list of floats."""
+    import torch
+    import torch.distributed as dist
+
+    local = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
     if distributed:
-        dist.all_reduce(decode_local, op=dist.ReduceOp.MAX)
-    decode_us = float(decode_local.item()) * 1e3 / args.decode_steps
+        dist.all_reduce(local, op=dist.ReduceOp.MAX)
+    return local.tolist()
 
-    # End to end through the public API: audit inputs copied from pinned host
-    # memory each step, the queue read back (refine_arrays returns host arrays).
-    host_queries = [q.cpu().pin_memory() for q in queries]
-    host_gradients = [x.cpu().pin_memory() for x in gradients]
-    h2d = sum(q.numel() * q.element_size() for q in host_queries) + sum(x.numel() * 4 for x in host_gradients)
-    d2h = (IMMEDIATE + QUEUED) * (4 + 8 + 8) + 2 * 8
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def e2e_pass():
-        device_queries = [q.to(device, non_blocking=True) for q in host_queries]
-        device_gradients = [x.to(device, non_blocking=True) for x in host_gradients]
-        if layer_groups:
-            layer_group_audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED,
-                                   protect_recent=PROTECT_RECENT)
-        else:
-            audit_pass(cache, device_queries, qpos, device_gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT,
-                       fused=fused)
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return reference_arm(args, rank)
 
-    e2e_pass()  # warm-up
-    barrier()
-    e_start.record()
-    e2e_steps = max(1, args.steps)
-    for _ in range(e2e_steps):
-        e2e_pass()
-    e_end.record()
-    barrier()
-    e2e_ms = torch.tensor([e_start.elapsed_time(e_end)], device=device)
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    distributed = world > 1
     if distributed:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = requests * managed * e2e_steps / (float(e2e_ms.item()) / 1e3)
+        from datetime import timedelta
 
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=device)
+
+    def barrier():
+        if distributed:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    head = measure_cfg1(args, device, world, rank, distributed, barrier, layer_groups=False, steps=args.steps,
+                        warmup=args.warmup, with_e2e=True)
+    elapsed_ms, decode_ms, e2e_ms = max_over_ranks([head["elapsed_ms"], head["decode_ms"], head["e2e_ms"]],
+                                                   distributed, device)
+    value = world * head["managed"] * args.steps / (elapsed_ms / 1e3)
+    e2e_value = world * head["managed"] * head["e2e_steps"] / (e2e_ms / 1e3)
+    candidates = RETAINED + IMMEDIATE - LAYERS * HEADS * PROTECT_RECENT
     peak, peak_kind = measured_peaks()
     traffic_ratio = measured_traffic_ratio()
-    kernel_ms = timer.total_ms()
-    achieved = timer.bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else 0.0
+    kernel_ms = head["kernel_ms"]
+    achieved = head["kernel_bytes"] / (kernel_ms / 1e3) / 1e9 if kernel_ms > 0 else 0.0
+    per_launch = head["kernel_bytes"] / max(1, head["kernel_launches"])
     result = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if layer_groups else "weak",
-        "vs_baseline": None, "dtype": "f32", "impl": "ours",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "ours",
         "data": "synthetic (seeded): bf16 K/V ~N(0,1), queries ~N(0,4), margin gradient ~N(0,1/D)",
-        "config": {"workload": "configs[1] llama-3-8b single request, steady-state audit pass",
-                   "scoring": args.scoring,
-                   "layers": LAYERS, "kv_heads": HEADS, "gqa_group": GROUPS, "head_dim": DIM,
-                   "prompt_rows_per_head": PROMPT, "generation_rows": RETAINED + IMMEDIATE, "budget": BUDGET,
-                   "temporal_window": WINDOW, "selected_per_audit": IMMEDIATE + QUEUED, "evicted_per_audit": IMMEDIATE,
-                   "managed_rows_per_request": managed,
-                   "requests_per_gpu": 1 / world if layer_groups else 1,
-                   "parallelism": (f"layer-groups x{world} (one request, NCCL histogram selection)" if layer_groups
-                                   else f"request-sharded x{world}" if world > 1 else "single request"),
-                   "l2": "no flush: 4.6 GB of K/V per request, larger than L2"},
-        "decode_overhead_us": decode_us,
-        "roofline": {"kernel": timed_name, "bound": "hbm", "achieved": achieved, "peak": peak,
+        "config": config_cfg1(world, args.scoring),
+        "candidate_rows_per_s": world * candidates * args.steps / (elapsed_ms / 1e3),
+        "decode_overhead_us": decode_ms * 1e3 / args.decode_steps,
+        "roofline": {"kernel": head["timed_name"], "bound": "hbm", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
-                     "share_of_step": kernel_ms / elapsed_ms,
-                     "traffic": (None if traffic_ratio is None
-                                 else traffic_ratio * timer.bytes / max(1, len(timer.pairs))),
+                     "share_of_step": kernel_ms / head["elapsed_ms"],
+                     "traffic": None if traffic_ratio is None else traffic_ratio * per_launch,
                      "traffic_source": "profiles/temporal_scores_traffic.json (ncu dram bytes / algorithmic bytes)",
-                     "bytes_per_launch": timer.bytes / max(1, len(timer.pairs)), "launches": len(timer.pairs)},
-        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches,
-        "clocks": clocks.summary(),
+                     "bytes_per_launch": per_launch, "launches": head["kernel_launches"]},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": head["h2d"],
+                "d2h_bytes_per_step": head["d2h"]},
+        "gpu_launches": head["launches"],
+        "clocks": head["clocks"],
     }
+    del head
+    torch.cuda.empty_cache()
+    if distributed:
+        # One request split into per-rank layer groups (strong scaling); the
+        # request-wide selection is the NCCL histogram all-gathers.
+        lg = measure_cfg1(args, device, world, rank, distributed, barrier, layer_groups=True, steps=args.steps,
+                          warmup=args.warmup, with_e2e=False)
+        gather = lg["gather_us"]
+        ms, dec = max_over_ranks([lg["elapsed_ms"], lg["decode_ms"]], distributed, device)
+        rounds = max_over_ranks(gather, distributed, device) if gather else []
+        result["layer_groups"] = {
+            "config": f"configs[1], one request split into {world} groups of {LAYERS // world} layers",
+            "scaling": "strong", "steps": args.steps, "warmup": args.warmup,
+            "ms_per_pass": ms / args.steps, "tokens_per_s": lg["managed"] * args.steps / (ms / 1e3),
+            "decode_overhead_us": dec * 1e3 / args.decode_steps,
+            "allgather_us_per_round": rounds[:3],
+            "allgather_us_per_pass": sum(rounds) / max(1, args.steps),
+            "allgather_share_of_pass": sum(rounds) / ms if ms else None,
+            "gpu_launches": lg["launches"],
+        }
+        del lg
+        torch.cuda.empty_cache()
+    if not args.skip_large:
+        from code_for_iclr27_b200.workloads import measure_large, measure_large_layer_groups
+
+        big = measure_large(device, requests=args.large_requests, steps=args.large_steps, warmup=args.large_warmup,
+                            rank=rank, barrier=barrier, peak_gbs=peak)
+        ms, kms = max_over_ranks([big["ms_per_pass"], big["temporal_scores_ms_per_pass"]], distributed, device)
+        big["ms_per_pass"] = ms
+        big["tokens_per_s"] = world * args.large_requests * big["managed_rows_per_request"] / (ms / 1e3)
+        big["n_gpus"], big["scaling"] = world, "weak"
+        big["temporal_scores_share_of_pass"] = big.pop("temporal_scores_ms_per_pass") / ms
+        result["configs4"] = big
+        torch.cuda.empty_cache()
+        if distributed:
+            lgb = measure_large_layer_groups(device, world, rank, requests=args.large_requests,
+                                             steps=args.large_steps, warmup=args.large_warmup, barrier=barrier)
+            ms, = max_over_ranks([lgb["ms_per_pass"]], distributed, device)
+            rounds = lgb["allgather_us_per_round"]
+            rounds = max_over_ranks(rounds, distributed, device) if rounds else []
+            lgb["ms_per_pass"] = ms
+            lgb["tokens_per_s"] = args.large_requests * big["managed_rows_per_request"] / (ms / 1e3)
+            lgb["allgather_us_per_round"] = rounds[:3]
+            lgb["allgather_share_of_pass"] = sum(rounds) / args.large_steps / 1e3 / ms if ms else None
+            lgb["n_gpus"], lgb["scaling"] = world, "strong"
+            result["configs4_layer_groups"] = lgb
+            torch.cuda.empty_cache()
     if world == 1 and not args.skip_side:
         # The other configurations' hot operators, measured on the same GPU.
         from code_for_iclr27_b200.workloads import measure_batch_append, measure_recall
 
-        del cache, queries, gradients, host_queries, host_gradients
-        torch.cuda.empty_cache()
         result["batch_append"] = measure_batch_append(device)
         torch.cuda.empty_cache()
         result["recall"] = measure_recall(device)
@@ -667,7 +831,10 @@ def main():
         dist.destroy_process_group()
     if rank == 0:
         if world == 1:
-            result["cpu_baseline"] = cpu_baseline(args.seed)
+            import torch
+
+            torch.set_num_threads(os.cpu_count() or 1)
+            result["cpu_baseline"] = reference_cpu_sample(args.seed) or cpu_baseline(args.seed)
         print(json.dumps(result), flush=True)
 
 

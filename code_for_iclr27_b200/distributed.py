@@ -8,31 +8,40 @@ of raw scores.  The only data that crosses ranks is a few histograms:
   1. Each rank maps its scores to order-preserving 32-bit keys (the map
      PyTorch's radix select uses; NaN last).
   2. Radix rounds of 12, 12 and 8 bits: every rank histograms the digit of
-     the keys still in play, the histograms are all-gathered (NCCL over
-     NVLink on GPUs, gloo on CPU), summed, and the bin holding the k-th key is
-     fixed.  After the rounds every rank knows the exact k-th key and how many
-     keys lie below it request-wide.
+     the keys still in play (lrk_select_histogram), the histograms are
+     all-gathered (one NCCL all-gather per round over NVLink), and every rank
+     sums them and fixes the bin holding the k-th key (lrk_select_pick).  The
+     search state stays on the device from round to round; one copy of the
+     final shares comes back to the host.
   3. Ties at the k-th key are taken in global flat-index order (layer-major,
      the order compute_score_table concatenates heads in, scoring.py:218-287),
-     which is torch.topk's choice: ranks own increasing index ranges, so each
-     rank takes the first ties it holds after the ties of lower ranks (one
-     all-gather of per-rank tie counts).
+     which is torch.topk's choice: ranks own increasing index ranges, and the
+     last round's gathered histograms hold every rank's tie count, so each
+     rank takes the first ties it holds after the ties of lower ranks with no
+     further exchange.
 
-The chosen set equals the single-GPU set exactly.  Queue prefixes (the
-immediate eviction and each lazy prefix of controller.py:57-70) are again
-"k smallest" questions over the chosen set and use the same rounds.
-Per-segment refinement (Pool7 quotas and transplant) is layer-local, so each
-rank finishes it on its own segments.
+A rank's share of the request-wide set is exactly its local bottom-(share) by
+(key, index), so a local refine_arrays with that count gives the single-GPU
+quotas, refined positions and queue order for its layers.  Queue prefixes
+(the immediate eviction) are smaller "k smallest" questions over the same
+keys and run in the same rounds.  Many requests go through one set of rounds.
+
+On CPU tensors (gloo process groups, the multi-process tests) the same rounds
+run as torch operations (_histogram_host, _pick_host): a restatement of the
+two kernels, so the state machine is exercised without a GPU.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
-from typing import Optional, Sequence
+from typing import Sequence
 
 import torch
 import torch.distributed as dist
 
 DIGITS = (12, 12, 8)
+BINS = 4096
+# State fields (LRK_SELECT_* in include/lrk.h).
+K, PREFIX, NEED, BELOW, LOCAL_BELOW, TOTAL, SHARE = range(7)
+FIELDS = 8
 
 
 def radix_keys(scores: torch.Tensor) -> torch.Tensor:
@@ -50,60 +59,132 @@ def _all_gather_counts(local: torch.Tensor, group) -> torch.Tensor:
     return torch.stack(gathered)
 
 
-@dataclass
-class Threshold:
-    key: int          # the k-th smallest key request-wide
-    below: int        # keys strictly below it, request-wide
-    ties_taken: int   # keys equal to it that belong to the chosen k
+def _histogram_host(tables: Sequence[torch.Tensor], states: torch.Tensor, round_index: int) -> torch.Tensor:
+    """lrk_select_histogram restated in torch (CPU tensors): per (request,
+    question) the histogram of this round's digit over the keys whose higher
+    bits equal the question's prefix (all keys in round 0)."""
+    requests, questions = states.shape[:2]
+    shift = 32 - sum(DIGITS[:round_index + 1])
+    width = DIGITS[round_index]
+    out = torch.zeros(requests, questions, BINS, dtype=torch.int32)
+    for r, scores in enumerate(tables):
+        keys = radix_keys(scores)
+        digit = (keys >> shift) & ((1 << width) - 1)
+        for q in range(questions):
+            if round_index == 0:
+                picked = digit
+            elif int(states[r, q, NEED]) > 0:
+                picked = digit[(keys >> (shift + width)) == int(states[r, q, PREFIX])]
+            else:
+                continue
+            out[r, q] = torch.bincount(picked, minlength=BINS).to(torch.int32)
+    return out
 
 
-def global_kth_key(keys: torch.Tensor, k: int, group=None, digits: Sequence[int] = DIGITS) -> Threshold:
-    """Exact k-th smallest (1 <= k <= total) of the union of every rank's keys,
-    found with one histogram all-gather per radix round."""
-    if sum(digits) != 32:
-        raise ValueError("digit widths must cover 32 bits")
-    prefix, done, need, below = 0, 0, int(k), 0
-    in_play = keys
-    for width in digits:
-        shift = 32 - done - width
-        digit = (in_play >> shift) & ((1 << width) - 1)
-        local = torch.bincount(digit, minlength=1 << width).to(torch.int64)
-        total = _all_gather_counts(local, group).sum(0)
-        cumulative = total.cumsum(0)
-        bin_index = int(torch.searchsorted(cumulative, torch.tensor([need], device=cumulative.device)).item())
-        if bin_index >= total.numel():
-            raise ValueError(f"k={k} exceeds the number of keys")
-        skipped = int(cumulative[bin_index].item() - total[bin_index].item())
-        below += skipped
-        need -= skipped
-        prefix = (prefix << width) | bin_index
-        done += width
-        in_play = in_play[digit == bin_index]
-    return Threshold(key=prefix, below=below, ties_taken=need)
+def _pick_host(gathered: torch.Tensor, rank: int, states: torch.Tensor, round_index: int) -> None:
+    """lrk_select_pick restated in torch (CPU tensors), in place on states."""
+    requests, questions = states.shape[:2]
+    width = DIGITS[round_index]
+    for r in range(requests):
+        for q in range(questions):
+            state = states[r, q]
+            counts = gathered[:, r, q, :1 << width].to(torch.int64)  # [world, bins]
+            total = counts.sum(0)
+            if round_index == 0:
+                state[TOTAL] = int(total.sum())
+                state[NEED] = max(0, min(int(state[K]), int(state[TOTAL])))
+            need = int(state[NEED])
+            if need <= 0:
+                if round_index == len(DIGITS) - 1 and need == 0:
+                    state[SHARE] = 0
+                continue
+            cumulative = total.cumsum(0)
+            bin_index = int(torch.searchsorted(cumulative, torch.tensor([need])).item())
+            if bin_index >= total.numel():
+                state[NEED] = -1
+                state[SHARE] = -1
+                continue
+            before = int(cumulative[bin_index] - total[bin_index])
+            state[PREFIX] = (int(state[PREFIX]) << width) | bin_index
+            state[BELOW] += before
+            state[LOCAL_BELOW] += int(counts[rank, :bin_index].sum())
+            state[NEED] = need - before
+            if round_index == len(DIGITS) - 1:
+                ties = counts[:, bin_index]
+                take = max(0, min(need - before - int(ties[:rank].sum()), int(ties[rank])))
+                state[SHARE] = int(state[LOCAL_BELOW]) + take
 
 
-def select_smallest(scores: torch.Tensor, k: int, group=None, eligible: Optional[torch.Tensor] = None) -> torch.Tensor:
+def select_shares(tables: Sequence[torch.Tensor], ks: Sequence[Sequence[int]], group=None, timings=None):
+    """This rank's share of each request's request-wide k smallest scores.
+
+    tables[r]: this rank's score table of request r (1-D float32; ranks hold
+    consecutive layer groups in rank order); ks[r]: the k of each question for
+    request r (the same number of questions for every request).  Returns
+    (shares [requests, questions], totals [requests]) as numpy int64: the
+    count of this rank's rows in each request-wide bottom-k by (key, global
+    index), and each request's request-wide score count (k larger than it is
+    clamped).  Every rank calls this with the same ks.  On CUDA tensors: three
+    rounds of lrk_select_histogram, one NCCL all-gather and lrk_select_pick,
+    with one device-to-host copy at the end; `timings`, a list, receives a
+    (start, end) CUDA event pair around each all-gather."""
+    import numpy as np
+
+    requests = len(tables)
+    questions = len(ks[0]) if requests else 0
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if not requests:
+        return np.zeros((0, questions), np.int64), np.zeros(0, np.int64)
+    host_states = torch.zeros(requests, questions, FIELDS, dtype=torch.int64)
+    host_states[:, :, K] = torch.as_tensor(np.asarray(ks, dtype=np.int64).reshape(requests, questions))
+    device = tables[0].device
+    if device.type == "cuda":
+        from . import operators, upload
+
+        C = operators()
+        states = upload(host_states.numpy(), device)
+        gathered = torch.empty(world, requests, questions, BINS, dtype=torch.int32, device=device)
+        tables = [t.float().contiguous() for t in tables]
+        for round_index in range(len(DIGITS)):
+            histograms = C.select_histogram(tables, states, round_index)
+            if timings is not None:
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+            dist.all_gather_into_tensor(gathered, histograms, group=group)
+            if timings is not None:
+                end.record()
+                timings.append((start, end))
+            C.select_pick(gathered, rank, states, round_index)
+        final = states[:, :, [SHARE, TOTAL]].cpu().numpy()
+    else:
+        states = host_states
+        for round_index in range(len(DIGITS)):
+            histograms = _histogram_host(tables, states, round_index)
+            gathered = _all_gather_counts(histograms, group)
+            _pick_host(gathered, rank, states, round_index)
+        final = states[:, :, [SHARE, TOTAL]].numpy()
+    shares = final[:, :, 0].astype(np.int64)
+    if (shares < 0).any():
+        raise RuntimeError("layer-group selection: the ranks' histograms disagree (inconsistent score tables)")
+    return shares, final[:, 0, 1].astype(np.int64)
+
+
+def local_smallest(scores: torch.Tensor, count: int) -> torch.Tensor:
+    """Mask of the `count` smallest local scores by (key, index)."""
+    mask = torch.zeros(scores.numel(), dtype=torch.bool, device=scores.device)
+    if count > 0:
+        keys = radix_keys(scores)
+        index = torch.arange(scores.numel(), device=scores.device)
+        order = torch.argsort(keys * (scores.numel() + 1) + index, stable=True)
+        mask[order[:count]] = True
+    return mask
+
+
+def select_smallest(scores: torch.Tensor, k: int, group=None) -> torch.Tensor:
     """Boolean mask of this rank's share of the request-wide k smallest
-    scores, ties broken by global flat index (ranks in index order).
-    `eligible` restricts the candidates (e.g. to already-chosen rows)."""
-    keys = radix_keys(scores)
-    if eligible is not None:
-        keys = torch.where(eligible, keys, torch.full_like(keys, 1 << 32))  # beyond every real key
-    if k <= 0:
-        return torch.zeros_like(keys, dtype=torch.bool)
-    real = keys < (1 << 32)
-    threshold = global_kth_key(keys[real], k, group)
-    below = keys < threshold.key
-    ties = keys == threshold.key
-    tie_counts = _all_gather_counts(ties.sum().reshape(1).to(torch.int64), group).reshape(-1)
-    rank = dist.get_rank(group)
-    before = int(tie_counts[:rank].sum().item())
-    take = max(0, min(threshold.ties_taken - before, int(tie_counts[rank].item())))
-    chosen = below.clone()
-    if take:
-        tie_index = torch.nonzero(ties, as_tuple=False).reshape(-1)[:take]
-        chosen[tie_index] = True
-    return chosen
+    scores, ties broken by global flat index (ranks in index order)."""
+    shares, _ = select_shares([scores], [[max(0, int(k))]], group)
+    return local_smallest(scores, int(shares[0, 0]))
 
 
 def queue_order(scores: torch.Tensor, chosen: torch.Tensor) -> torch.Tensor:
@@ -117,8 +198,9 @@ def queue_order(scores: torch.Tensor, chosen: torch.Tensor) -> torch.Tensor:
 
 def prefix_split(scores: torch.Tensor, chosen: torch.Tensor, prefix: int, group=None) -> torch.Tensor:
     """Mask of this rank's chosen rows that fall in the first `prefix` slots of
-    the request-wide queue (an immediate or lazy eviction batch)."""
-    return select_smallest(scores, prefix, group, eligible=chosen)
+    the request-wide queue (an immediate or lazy eviction batch): with prefix
+    no larger than the chosen count, that is the request-wide bottom-prefix."""
+    return select_smallest(scores, prefix, group) & chosen
 
 
 def lazy_prefix_share(queue_scores, count: int, group=None) -> int:
@@ -156,41 +238,50 @@ def lazy_prefix_share(queue_scores, count: int, group=None) -> int:
     return int(((first // count) == rank).sum().item())
 
 
-def layer_group_audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
-                           group=None, protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250,
-                           pool_kernel=7):
-    """audit_pass (score, Pool7, select, evict the immediate prefix) for one
-    rank's contiguous group of a request's layers: `cache`, `queries` and
-    `gradients` hold this rank's layers only, ranks in layer order.
+def layer_group_audit_requests(requests, query_positions, base_margin, immediate: int, queued: int, group=None,
+                               protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250, pool_kernel=7,
+                               timings=None):
+    """audit_pass (score, Pool7, select, evict the immediate prefix) for this
+    rank's contiguous layer group of each request: requests is a list of
+    (cache, queries, gradients) holding this rank's layers only, ranks in
+    layer order, the same requests in the same order on every rank.
 
     Scoring, pooling, refinement and compaction are layer-local.  The
-    request-wide choices go through select_smallest / prefix_split (radix
-    histograms all-gathered over `group`): this rank's share of the
-    bottom-(immediate + queued) raw scores is exactly its local bottom-k for k
-    = its share (ties by index on both sides), so a local refine_arrays with
-    that count gives the single-GPU quotas, refined positions and queue order
-    for these layers; the rank then evicts its share of the request-wide
-    immediate prefix, the first slots of its local queue.  Returns the local
-    AuditResult (its references are this rank's queue slots)."""
+    request-wide choices of every request come from one select_shares call
+    (three histogram all-gathers in all): this rank's share of the
+    bottom-(immediate + queued) raw scores and of the bottom-immediate.  A
+    local refine_arrays with the first count gives the single-GPU quotas,
+    refined positions and queue order for these layers; the rank then evicts
+    its share of the request-wide immediate prefix, the first slots of its
+    local queue.  Returns the local AuditResults (their references are this
+    rank's queue slots)."""
     from .audit import AuditResult, pool_table, score_table_fused
     from .selection import fetch_references, refine_device
 
-    table = score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
-                              denominator_epsilon, query_chunk_size)
-    pooled = pool_table(table, pool_kernel)
-    total = torch.tensor([table.scores.numel()], dtype=torch.int64, device=table.scores.device)
-    dist.all_reduce(total, group=group)
-    count = min(immediate + queued, int(total.item()))
-    if count < immediate:
+    tables = [score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent,
+                                denominator_epsilon, query_chunk_size) for cache, queries, gradients in requests]
+    pooled = [pool_table(table, pool_kernel) for table in tables]
+    shares, totals = select_shares([table.scores for table in tables],
+                                   [[immediate + queued, immediate]] * len(tables), group, timings)
+    if (totals < immediate).any():
         raise RuntimeError("Not enough unprotected candidates to enforce the budget")
-    chosen = select_smallest(table.scores, count, group)
-    head = prefix_split(table.scores, chosen, immediate, group)
-    local_count, local_immediate = (int(v) for v in torch.stack([chosen.sum(), head.sum()]).tolist())
-    queue = refine_device(table, pooled, local_count)
-    pending = fetch_references(queue)
-    evicted = 0
-    if local_immediate:
-        evicted = cache.remove_selected(queue.coordinates, queue.segment_ids[:local_immediate],
-                                        queue.positions[:local_immediate])
-    references, changed, changed_heads = pending.result()
-    return AuditResult(table, references, changed, changed_heads, evicted)
+    results = []
+    for (cache, _, _), table, pool, (local_count, local_immediate) in zip(requests, tables, pooled, shares.tolist()):
+        queue = refine_device(table, pool, local_count)
+        pending = fetch_references(queue)
+        evicted = 0
+        if local_immediate:
+            evicted = cache.remove_selected(queue.coordinates, queue.segment_ids[:local_immediate],
+                                            queue.positions[:local_immediate])
+        references, changed, changed_heads = pending.result()
+        results.append(AuditResult(table, references, changed, changed_heads, evicted))
+    return results
+
+
+def layer_group_audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
+                           group=None, protect_recent=32, denominator_epsilon=1e-6, query_chunk_size=250,
+                           pool_kernel=7, timings=None):
+    """layer_group_audit_requests for one request."""
+    return layer_group_audit_requests([(cache, queries, gradients)], query_positions, base_margin, immediate, queued,
+                                      group, protect_recent, denominator_epsilon, query_chunk_size, pool_kernel,
+                                      timings)[0]

@@ -304,3 +304,233 @@ def measure_batch_append(device, requests: int = 8, layers: int = 32, heads: int
         "us_per_step": us,
         "GBps": moved / (us / 1e6) / 1e9,
     }
+
+
+# ------------------------------------------------------------- configs[4]
+
+# Llama-3-70B shape: 80 layers x 8 KV heads x D128, GQA group 8; a
+# 32768-row cache per head, every row a generation row (no prompt rows, so
+# every row but the last protect_recent is a candidate); budget 4000.
+LARGE_LAYERS, LARGE_HEADS, LARGE_GROUPS, LARGE_DIM, LARGE_ROWS = 80, 8, 8, 128, 32768
+LARGE_BUDGET, LARGE_WINDOW, LARGE_AUDIT_PERIOD, LARGE_EVICT_INTERVAL, LARGE_PROTECT = 4000, 250, 250, 8, 32
+
+
+def large_counts(layers: int = LARGE_LAYERS, heads: int = LARGE_HEADS, rows: int = LARGE_ROWS,
+                 budget: int = LARGE_BUDGET) -> dict:
+    """The controller's counts for one request's first audit
+    (controller.py:15-18, 148-150): slots per step = layers x heads; wall =
+    budget x slots; staging = evict_interval x slots; the audit evicts down to
+    wall - staging at once and queues audit_period x slots more."""
+    slots = layers * heads
+    wall = budget * slots
+    staging = LARGE_EVICT_INTERVAL * slots
+    managed = slots * rows
+    immediate = managed - (wall - staging)
+    queued = LARGE_AUDIT_PERIOD * slots
+    return {"managed": managed, "immediate": immediate, "queued": queued, "kept": wall - staging,
+            "candidates": slots * (rows - LARGE_PROTECT)}
+
+
+def large_request(device, seed: int, layers=None):
+    """One configs[4] request's cache and audit inputs, or only the layers in
+    `layers` (a range) for a layer group: each layer is generated from its own
+    seed (request seed, layer), so a group's layers equal the whole request's.
+    K/V bf16 ~N(0,1); positions 0..rows-1 per head; queries (the audit's query
+    history, W x 64 query heads) bf16 ~N(0,4), so the scaled logits are
+    ~N(0,4) ("2 N(0,1)"); margin gradients ~N(0, 1/D)."""
+    import torch
+
+    from .kvcache import PackedCache
+
+    layers = range(LARGE_LAYERS) if layers is None else layers
+    cache = PackedCache()
+    queries, gradients = [], []
+    positions = torch.arange(LARGE_ROWS, dtype=torch.float32, device=device).repeat(LARGE_HEADS)
+    for layer in layers:
+        g = torch.Generator(device=device).manual_seed(seed * 1000 + layer)
+        rows = LARGE_HEADS * LARGE_ROWS
+        keys = torch.randn(rows, LARGE_DIM, generator=g, device=device).to(torch.bfloat16)
+        values = torch.randn(rows, LARGE_DIM, generator=g, device=device).to(torch.bfloat16)
+        cache.add_layer(keys, values, positions.clone(), [LARGE_ROWS] * LARGE_HEADS, [0] * LARGE_HEADS)
+        queries.append((torch.randn(LARGE_WINDOW, LARGE_HEADS * LARGE_GROUPS, LARGE_DIM, generator=g, device=device)
+                        * 2).to(torch.bfloat16))
+        gradients.append(torch.randn(LARGE_HEADS * LARGE_GROUPS, LARGE_DIM, generator=g, device=device)
+                         / float(np.sqrt(LARGE_DIM)))
+    cache.seen_tokens = LARGE_ROWS
+    return cache, queries, gradients
+
+
+def _snapshot(cache):
+    return [(layer.keys, layer.values, layer.positions, list(layer.head_lens), list(layer.prompt_lens),
+             layer.cumulative) for layer in cache.layers]
+
+
+def _restore(cache, saved):
+    """Put back the layer tensors an audit replaced (its operators allocate
+    fresh outputs and never write their inputs, so the originals are intact)."""
+    for layer, (k, v, p, lens, prompts, cumulative) in zip(cache.layers, saved):
+        layer.keys, layer.values, layer.positions, layer.cumulative = k, v, p, cumulative
+        layer.head_lens, layer.prompt_lens = lens, prompts
+
+
+class ScoreTimer:
+    """CUDA events around every lrk_temporal_scores call an audit makes (on
+    the stream it is launched on), with its algorithmic bytes: the logits read
+    once, the projected values and key positions once, the scores written."""
+
+    def __init__(self):
+        self.pairs, self.bytes = [], 0
+
+    def __enter__(self):
+        import torch
+
+        from . import audit
+
+        self.module, self.original = audit, audit.operators
+        inner = self.original()
+        timer = self
+
+        class Proxy:
+            def __getattr__(self, name):
+                attribute = getattr(inner, name)
+                if name != "temporal_scores":
+                    return attribute
+
+                def timed(logits, projected, kpos, first, last, *rest, **kw):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record()
+                    out = attribute(logits, projected, kpos, first, last, *rest, **kw)
+                    b.record()
+                    timer.pairs.append((a, b))
+                    for lg, f, l in zip(logits, first, last):
+                        w, g, length = lg.shape
+                        timer.bytes += w * g * length * lg.element_size() + g * length * 4 + length * 4 + (l - f) * 4
+                    return out
+
+                return timed
+
+        proxy = Proxy()
+        audit.operators = lambda: proxy
+        return self
+
+    def __exit__(self, *exc):
+        self.module.operators = self.original
+
+    def reset(self):
+        self.pairs, self.bytes = [], 0
+
+    def total_ms(self):
+        return sum(a.elapsed_time(b) for a, b in self.pairs)
+
+
+def _timed_passes(run, steps: int, warmup: int, barrier, timer: ScoreTimer):
+    import torch
+
+    for _ in range(warmup):
+        run()
+    barrier()
+    timer.reset()
+    a, b = _events()
+    barrier()
+    a.record()
+    for _ in range(steps):
+        run()
+    b.record()
+    barrier()
+    return a.elapsed_time(b)
+
+
+def measure_large(device, requests: int = 8, steps: int = 2, warmup: int = 2, seed: int = 40, rank: int = 0,
+                  barrier=None, peak_gbs=None) -> dict:
+    """configs[4], request sharding: `requests` independent 70B-shaped
+    requests on this GPU, each taken through one audit pass (score every
+    candidate, Pool7, select immediate + queued, evict the immediate prefix:
+    the first audit evicts the cache down to the budget).  Each pass starts
+    from the same state (the replaced layer tensors are put back).  Timed:
+    `steps` passes over all requests after `warmup`."""
+    import torch
+
+    from .audit import audit_pass
+
+    barrier = barrier or torch.cuda.synchronize
+    counts = large_counts()
+    reqs = [large_request(device, seed + 100 * rank + r) for r in range(requests)]
+    qpos = torch.arange(LARGE_ROWS - LARGE_WINDOW, LARGE_ROWS, dtype=torch.int64, device=device)
+    margin = torch.tensor([1.0], device=device)
+    evicted = []
+
+    def run():
+        evicted.clear()
+        for cache, queries, gradients in reqs:
+            saved = _snapshot(cache)
+            result = audit_pass(cache, queries, qpos, gradients, margin, counts["immediate"], counts["queued"],
+                                LARGE_PROTECT)
+            evicted.append(result.evicted)
+            _restore(cache, saved)
+
+    with ScoreTimer() as timer:
+        elapsed = _timed_passes(run, steps, warmup, barrier, timer)
+    kernel_ms = timer.total_ms()
+    out = {
+        "config": (f"configs[4]: {requests} requests per GPU (request sharding, no collective), "
+                   f"{LARGE_LAYERS} layers x {LARGE_HEADS} KV heads x D{LARGE_DIM}, GQA {LARGE_GROUPS}, "
+                   f"{LARGE_ROWS} generation rows per head, budget {LARGE_BUDGET}, window {LARGE_WINDOW}"),
+        "requests": requests, "steps": steps, "warmup": warmup,
+        "managed_rows_per_request": counts["managed"], "candidates_per_request": counts["candidates"],
+        "selected_per_request": counts["immediate"] + counts["queued"], "evicted_per_request": counts["immediate"],
+        "evicted_check": int(evicted[0]) if evicted else None,
+        "ms_per_pass": elapsed / steps,
+        "tokens_per_s": requests * counts["managed"] * steps / (elapsed / 1e3),
+        "temporal_scores_ms_per_pass": kernel_ms / steps,
+        "temporal_scores_GBps": timer.bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms else None,
+    }
+    if peak_gbs and kernel_ms:
+        out["temporal_scores_frac"] = out["temporal_scores_GBps"] / peak_gbs
+    del reqs
+    return out
+
+
+def measure_large_layer_groups(device, world: int, rank: int, requests: int = 8, steps: int = 2, warmup: int = 2,
+                               seed: int = 40, group=None, barrier=None) -> dict:
+    """configs[4], layer groups: `requests` 70B-shaped requests, each split
+    into `world` contiguous groups of layers, one per rank (strong scaling:
+    the total work is fixed).  One audit pass of all requests: every rank
+    scores, pools, refines and compacts its own layers, and the request-wide
+    bottom-k of every request comes from one select_shares call (three
+    histogram all-gathers over NCCL for all requests at once)."""
+    import torch
+
+    from .distributed import layer_group_audit_requests
+
+    barrier = barrier or torch.cuda.synchronize
+    if LARGE_LAYERS % world:
+        raise ValueError(f"{LARGE_LAYERS} layers do not split evenly over {world} ranks")
+    per = LARGE_LAYERS // world
+    counts = large_counts()
+    reqs = [large_request(device, seed + r, range(rank * per, (rank + 1) * per)) for r in range(requests)]
+    qpos = torch.arange(LARGE_ROWS - LARGE_WINDOW, LARGE_ROWS, dtype=torch.int64, device=device)
+    margin = torch.tensor([1.0], device=device)
+    gathers = []
+
+    def run():
+        saved = [_snapshot(cache) for cache, _, _ in reqs]
+        gathers.clear()
+        layer_group_audit_requests(reqs, qpos, margin, counts["immediate"], counts["queued"], group,
+                                   protect_recent=LARGE_PROTECT, timings=gathers)
+        for (cache, _, _), s in zip(reqs, saved):
+            _restore(cache, s)
+
+    with ScoreTimer() as timer:
+        elapsed = _timed_passes(run, steps, warmup, barrier, timer)
+    gather_us = [a.elapsed_time(b) * 1e3 for a, b in gathers]
+    out = {
+        "config": (f"configs[4] layer groups: {requests} requests, each split into {world} groups of {per} layers "
+                   f"(strong scaling), NCCL all-gather of {requests} x 2 x 4096-bin histograms per radix round"),
+        "requests": requests, "layers_per_rank": per, "steps": steps, "warmup": warmup,
+        "ms_per_pass": elapsed / steps,
+        "tokens_per_s": requests * counts["managed"] * steps / (elapsed / 1e3),
+        "allgather_us_per_round": gather_us,
+        "allgather_bytes_per_rank": requests * 2 * 4096 * 4,
+    }
+    del reqs
+    return out

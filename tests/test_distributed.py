@@ -164,3 +164,47 @@ def test_lazy_prefix_shares_match_single_queue(world):
         for rank in range(world):
             expected = [int((owner[a:b] == rank).sum()) for a, b in bounds]
             assert results[rank][case_index] == expected, f"case {seed}, rank {rank}"
+
+
+def shares_worker(rank, world, port, cases, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from code_for_iclr27_b200.distributed import select_shares
+
+        out = []
+        for tables, ks, cuts in cases:
+            local = [torch.from_numpy(t[c[rank]:c[rank + 1]].copy()) for t, c in zip(tables, cuts)]
+            shares, totals = select_shares(local, ks)
+            out.append((shares.tolist(), totals.tolist()))
+        results[rank] = out
+    finally:
+        dist.destroy_process_group()
+
+
+def test_select_shares_many_requests():
+    """select_shares over several requests and two questions at once (the
+    audit's selected count and immediate prefix), including a request with no
+    scores on one rank and k beyond the request's size."""
+    world = 3
+    rng = np.random.default_rng(5)
+    cases = []
+    tables = [make_scores(41, 3000, 0), make_scores(42, 5000, 6), make_scores(43, 40, 2)]
+    cuts = [[0, 1000, 2000, 3000], [0, 0, 2500, 5000], [0, 13, 40, 40]]
+    ks = [[1500, 20], [4999, 4999], [100, 39]]
+    cases.append((tables, ks, cuts))
+    cases.append(([rng.random(7, dtype=np.float32)], [[3, 0]], [[0, 2, 5, 7]]))
+    manager = mp.get_context("spawn").Manager()
+    results = manager.dict()
+    mp.start_processes(shares_worker, args=(world, free_port(), cases, results), nprocs=world, join=True,
+                       start_method="spawn")
+    for c, (tables, ks, cuts) in enumerate(cases):
+        for i, table in enumerate(tables):
+            order = np.lexsort((np.arange(table.size), O.radix_key(table)))
+            owner = np.searchsorted(np.asarray(cuts[i]), order, side="right") - 1
+            for rank in range(world):
+                shares, totals = results[rank][c]
+                assert totals[i] == table.size
+                for q, k in enumerate(ks[i]):
+                    assert shares[i][q] == int((owner[:min(k, table.size)] == rank).sum()), (c, i, q, rank)

@@ -1,6 +1,13 @@
-"""Layer-group selection over NCCL on 2 GPUs (one process per GPU): the ranks'
-union equals the single-process bottom-count, ties broken by global index.
-Skipped with fewer than 2 GPUs."""
+"""Layer-group selection on the GPU.
+
+On one GPU: the selection kernels (lrk_select_histogram, lrk_select_pick) with
+the ranks emulated in one process (each rank's histograms computed on its
+shard, stacked as the all-gather would, then each rank's pick) against the
+torch restatement of the same rounds and against the single-table bottom-k.
+Over NCCL on 2 GPUs (one process per GPU): the ranks' union equals the
+single-process bottom-count, ties broken by global index; and a layer-group
+audit pass equals the single-GPU one.  The NCCL tests skip with fewer than 2
+GPUs."""
 import os
 import socket
 
@@ -21,6 +28,59 @@ def _scores(seed, n, levels):
     if levels:
         return (rng.integers(0, levels, n) / 8).astype(np.float32)
     return rng.random(n, dtype=np.float32)
+
+
+EMULATED = [
+    # seed, world, per-request sizes, tie levels, ks per request (count, prefix)
+    (31, 2, [50_000, 3_000, 70_001], 0, [(20_000, 500), (3_000, 3_000), (1, 1)]),
+    (32, 3, [40_000, 9_999, 1], 5, [(12_345, 77), (9_000, 8_999), (1, 0)]),
+    (33, 4, [120_000, 0, 2_000], 40, [(119_000, 60_000), (5, 5), (2_500, 1_000)]),
+]
+
+
+@pytest.mark.parametrize("seed,world,sizes,levels,ks", EMULATED)
+def test_select_kernels_with_emulated_ranks(cuda, seed, world, sizes, levels, ks):
+    """Every round's histograms and states equal the torch restatement's, and
+    each request's shares add up to its single-table bottom-k by (key,
+    index), split at the ranks' cut points."""
+    import torch
+
+    from code_for_iclr27_b200 import operators
+    from code_for_iclr27_b200.distributed import (BINS, DIGITS, FIELDS, K, SHARE, TOTAL, _histogram_host,
+                                                  _pick_host)
+    from oracle import lrk_oracle as O
+
+    C = operators()
+    tables = [_scores(seed + i, n, levels) for i, n in enumerate(sizes)]
+    tables[0][7] = np.nan  # NaN keys rank last
+    cuts = [[int(x) for x in np.linspace(0, n, world + 1).round()] for n in sizes]
+    requests, questions = len(sizes), 2
+    start = torch.zeros(requests, questions, FIELDS, dtype=torch.int64)
+    start[:, :, K] = torch.tensor(ks)
+    device_states = [start.clone().to(cuda) for _ in range(world)]
+    host_states = [start.clone() for _ in range(world)]
+    shards = [[torch.from_numpy(t[c[r]:c[r + 1]].copy()) for t, c in zip(tables, cuts)] for r in range(world)]
+    for round_index in range(len(DIGITS)):
+        device_hist = [C.select_histogram([x.to(cuda) for x in shards[r]], device_states[r], round_index)
+                       for r in range(world)]
+        host_hist = [_histogram_host(shards[r], host_states[r], round_index) for r in range(world)]
+        for d, h in zip(device_hist, host_hist):
+            assert torch.equal(d.cpu(), h), f"round {round_index} histograms"
+        gathered = torch.stack(device_hist)
+        for r in range(world):
+            C.select_pick(gathered, r, device_states[r], round_index)
+            _pick_host(torch.stack(host_hist), r, host_states[r], round_index)
+            assert torch.equal(device_states[r].cpu(), host_states[r]), f"round {round_index} rank {r} states"
+    assert gathered.shape == (world, requests, questions, BINS)
+    for i, table in enumerate(tables):
+        order = np.lexsort((np.arange(table.size), O.radix_key(table)))
+        owner = np.searchsorted(np.asarray(cuts[i]), order, side="right") - 1
+        for q, k in enumerate(ks[i]):
+            k = min(k, table.size)
+            for r in range(world):
+                state = device_states[r].cpu()[i, q]
+                assert int(state[TOTAL]) == table.size
+                assert int(state[SHARE]) == int((owner[:k] == r).sum()), f"request {i} question {q} rank {r}"
 
 
 CASES = [(11, 400_000, 0, 150_000, 2048), (12, 400_000, 64, 200_000, 4096), (13, 100_000, 3, 99_000, 10)]
