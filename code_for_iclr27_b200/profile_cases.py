@@ -15,8 +15,11 @@ CASE is one of:
   logits_odd     the same with 34883 keys, 8-term steps
   logits_layer   one layer's logits in one launch (lrk_logits_heads): 8 heads of
                  34,878 .. 34,885 keys (both step orders), 1000 query rows each
+  large_pass     one configs[4] audit pass of one 70B-shaped request (80 layers x
+                 8 heads x 32768 rows, GQA 8; score, Pool7, select 18.6M,
+                 evict 18.4M), the layer tensors put back after each pass
 Inputs are seeded and generated on the device; each iteration launches the
-operator once.
+operator once (large_pass: one whole audit pass).
 """
 from __future__ import annotations
 
@@ -30,7 +33,7 @@ def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
                                            "project", "logits", "logits_odd", "logits_layer", "from_keys",
-                                           "table_fused"])
+                                           "table_fused", "large_pass"])
     parser.add_argument("--iters", type=int, default=3)
     args = parser.parse_args(argv)
 
@@ -110,6 +113,20 @@ def main(argv=None):
 
         table = score_table_from_keys if args.case == "from_keys" else score_table_fused
         run = lambda: table(cache, queries, qpos, gradients, margin)
+    elif args.case == "large_pass":
+        from .audit import audit_pass
+        from .workloads import LARGE_PROTECT, LARGE_ROWS, LARGE_WINDOW, _restore, _snapshot, large_counts, \
+            large_request
+
+        counts = large_counts()
+        cache, queries, gradients = large_request(dev, 40)
+        qpos = torch.arange(LARGE_ROWS - LARGE_WINDOW, LARGE_ROWS, dtype=torch.int64, device=dev)
+        margin = torch.tensor([1.0], device=dev)
+
+        def run():
+            saved = _snapshot(cache)
+            audit_pass(cache, queries, qpos, gradients, margin, counts["immediate"], counts["queued"], LARGE_PROTECT)
+            _restore(cache, saved)
     elif args.case == "project":
         values = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
         gradients = torch.randn(8 * 4, 128, generator=g, device=dev)
