@@ -52,21 +52,31 @@ __global__ void __launch_bounds__(kSortThreads) histogram_kernel(const uint64_t 
   counts[static_cast<int64_t>(threadIdx.x) * tiles + blockIdx.x] = hist[threadIdx.x];
 }
 
-// Exclusive scan of `total` uint32 values in place with one 1024-thread CTA.
-__global__ void __launch_bounds__(1024) scan_kernel(uint32_t *__restrict__ data, int64_t total) {
-  constexpr int kItems = 8;
+// Exclusive scan of uint32 values in place with 1024-thread CTAs: CTA b scans
+// [b span, min(total, (b + 1) span)) starting from carry_in[b] (0 without
+// carry_in).  One CTA with span = total scans everything; for long tables
+// the span is kScanSpan and carry_in holds the scanned block sums
+// (block_sums_kernel, then this kernel on the sums).
+constexpr int kScanItems = 8;
+constexpr int64_t kScanSpan = 1024 * kScanItems;
+
+__global__ void __launch_bounds__(1024) scan_kernel(uint32_t *__restrict__ data, int64_t total, int64_t span,
+                                                    const uint32_t *__restrict__ carry_in) {
+  constexpr int kItems = kScanItems;
   __shared__ uint32_t warp_sums[32];
   __shared__ uint32_t carry_shared;
-  if (threadIdx.x == 0) carry_shared = 0;
+  if (threadIdx.x == 0) carry_shared = carry_in != nullptr ? carry_in[blockIdx.x] : 0u;
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t base = 0; base < total; base += 1024 * kItems) {
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * span;
+  const int64_t stop = lmin(total, first + span);
+  for (int64_t base = first; base < stop; base += 1024 * kItems) {
     uint32_t v[kItems];
     uint32_t sum = 0;
     const int64_t start = base + static_cast<int64_t>(threadIdx.x) * kItems;
 #pragma unroll
     for (int j = 0; j < kItems; ++j) {
-      v[j] = start + j < total ? data[start + j] : 0u;
+      v[j] = start + j < stop ? data[start + j] : 0u;
       sum += v[j];
     }
     uint32_t inclusive = sum;
@@ -91,13 +101,50 @@ __global__ void __launch_bounds__(1024) scan_kernel(uint32_t *__restrict__ data,
     uint32_t running = carry + (warp > 0 ? warp_sums[warp - 1] : 0u) + inclusive - sum;
 #pragma unroll
     for (int j = 0; j < kItems; ++j) {
-      if (start + j < total) data[start + j] = running;
+      if (start + j < stop) data[start + j] = running;
       running += v[j];
     }
     __syncthreads();
     if (threadIdx.x == 1023) carry_shared = carry + warp_sums[31];
     __syncthreads();
   }
+}
+
+// Sum of each kScanSpan block of `total` values (one CTA per block).
+__global__ void __launch_bounds__(1024) block_sums_kernel(const uint32_t *__restrict__ data, int64_t total,
+                                                          uint32_t *__restrict__ sums) {
+  __shared__ uint32_t warp_sums[32];
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kScanSpan;
+  uint32_t sum = 0;
+  for (int64_t i = first + threadIdx.x; i < lmin(total, first + kScanSpan); i += 1024) sum += data[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if ((threadIdx.x & 31) == 0) warp_sums[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    sum = warp_sums[threadIdx.x];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (threadIdx.x == 0) sums[blockIdx.x] = sum;
+  }
+}
+
+// Extra uint32 entries a count table of `total` entries needs after it for
+// the block sums of the multi-CTA scan.
+inline int64_t scan_extra(int64_t total) { return total > 4 * kScanSpan ? ceil_div(total, kScanSpan) : 0; }
+
+// Exclusive scan of counts[0, total) in place; the block sums (when used)
+// live at counts + total.
+void exclusive_scan(uint32_t *counts, int64_t total, cudaStream_t stream) {
+  const int64_t blocks = scan_extra(total);
+  if (blocks == 0) {
+    scan_kernel<<<1, 1024, 0, stream>>>(counts, total, total, nullptr);
+    return;
+  }
+  uint32_t *sums = counts + total;
+  block_sums_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(counts, total, sums);
+  scan_kernel<<<1, 1024, 0, stream>>>(sums, blocks, blocks, nullptr);
+  scan_kernel<<<static_cast<unsigned>(blocks), 1024, 0, stream>>>(counts, total, kScanSpan, sums);
 }
 
 __global__ void __launch_bounds__(kSortThreads) scatter_kernel(
@@ -162,7 +209,7 @@ int radix_sort(SortBuffers &b, int64_t n, int bits, cudaStream_t stream, int &st
   for (int shift = 0; shift < bits; shift += 8) {
     histogram_kernel<<<static_cast<unsigned>(tiles), kSortThreads, 0, stream>>>(b.keys[current], n, shift, b.counts,
                                                                               tiles);
-    scan_kernel<<<1, 1024, 0, stream>>>(b.counts, 256 * tiles);
+    exclusive_scan(b.counts, 256 * tiles, stream);
     scatter_kernel<<<static_cast<unsigned>(tiles), kSortThreads, 0, stream>>>(
         b.keys[current], b.values[current], b.keys[current ^ 1], b.values[current ^ 1], n, shift, b.counts, tiles);
     current ^= 1;
@@ -401,7 +448,7 @@ RefineLayout carve_refine(void *workspace, int64_t n, int64_t segments) {
   l.raw_sort.keys[1] = c.take<uint64_t>(n);
   l.raw_sort.values[0] = c.take<uint32_t>(n);
   l.raw_sort.values[1] = c.take<uint32_t>(n);
-  l.raw_sort.counts = c.take<uint32_t>(256 * tiles);
+  l.raw_sort.counts = c.take<uint32_t>(256 * tiles + scan_extra(256 * tiles));
   l.seg_sort.keys[0] = c.take<uint64_t>(n);
   l.seg_sort.keys[1] = c.take<uint64_t>(n);
   l.seg_sort.values[0] = c.take<uint32_t>(n);
@@ -502,7 +549,7 @@ extern "C" size_t lrk_topk_workspace_bytes(int64_t n) {
   c.take<uint64_t>(n);
   c.take<uint32_t>(n);
   c.take<uint32_t>(n);
-  c.take<uint32_t>(256 * tiles);
+  c.take<uint32_t>(256 * tiles + scan_extra(256 * tiles));
   return c.used + 256;
 }
 
@@ -523,7 +570,7 @@ extern "C" int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *wor
   b.keys[1] = c.take<uint64_t>(n);
   b.values[0] = c.take<uint32_t>(n);
   b.values[1] = c.take<uint32_t>(n);
-  b.counts = c.take<uint32_t>(256 * tiles);
+  b.counts = c.take<uint32_t>(256 * tiles + scan_extra(256 * tiles));
   build_keys_kernel<<<grid_for(n), 256, 0, s>>>(x, nullptr, n, nullptr, 0, b.keys[0], b.values[0], nullptr,
                                                 nullptr);
   int status = launch_status("topk keys");

@@ -124,10 +124,12 @@ def refine_device(allocation, refinement, count) -> DeviceQueue:
 
 
 class PendingReferences:
-    """A queue on its way to the host: one asynchronous device-to-host copy
-    into pinned memory (ids, positions, the two counters, score bits) and the
-    event after it.  result() waits for that event only, so work queued on
-    the stream after the copy keeps the device busy meanwhile."""
+    """A queue on its way to the host: asynchronous device-to-host copies
+    into pinned memory -- segment ids, positions and the two counters into one
+    int64 buffer, the raw scores into a float32 buffer -- and the event after
+    them.  result() waits for that event only, so work queued on the stream
+    after the copies keeps the device busy meanwhile; the returned arrays are
+    views of the pinned buffers (no conversion or copy on the host)."""
 
     def __init__(self, queue: DeviceQueue, references_type=None):
         import torch
@@ -136,10 +138,13 @@ class PendingReferences:
         self.queue = queue
         if not queue.count:
             return
-        bits = queue.values.float().contiguous().view(torch.int32).to(torch.int64)
-        packed = torch.cat([queue.segment_ids, queue.positions, queue.stats, bits])
-        self.host = torch.empty(packed.shape, dtype=packed.dtype, pin_memory=True)
-        self.host.copy_(packed, non_blocking=True)
+        count = queue.count
+        self.host = torch.empty(2 * count + 2, dtype=torch.int64, pin_memory=True)
+        self.host[:count].copy_(queue.segment_ids, non_blocking=True)
+        self.host[count:2 * count].copy_(queue.positions, non_blocking=True)
+        self.host[2 * count:].copy_(queue.stats, non_blocking=True)
+        self.host_values = torch.empty(count, dtype=torch.float32, pin_memory=True)
+        self.host_values.copy_(queue.values, non_blocking=True)
         self.event = torch.cuda.Event()
         self.event.record()
 
@@ -149,9 +154,8 @@ class PendingReferences:
             return self.make([], [], [], queue.coordinates), 0, 0
         self.event.synchronize()
         packed, count = self.host.numpy(), queue.count
-        values = (packed[2 * count + 2:] & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
         changed, changed_heads = int(packed[2 * count]), int(packed[2 * count + 1])
-        return (self.make(values, packed[:count].copy(), packed[count:2 * count].copy(), queue.coordinates),
+        return (self.make(self.host_values.numpy(), packed[:count], packed[count:2 * count], queue.coordinates),
                 changed, changed_heads)
 
 

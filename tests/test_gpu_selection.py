@@ -86,6 +86,7 @@ REFINE_CASES = [
     ([150000, 64, 64], 40, 40),      # small quotas in a long segment
     ([7] * 3, 2, 21),
     ([1000] * 4, 5, 1),
+    ([300000, 250000, 60000], 50, 450000),  # > 524k scores: the multi-CTA count scan
 ]
 
 
