@@ -63,6 +63,12 @@ class KeySegment(ctypes.Structure):
                 ("last", I64), ("scores", P), ("query_chunk", I64)]
 
 
+class Arena(ctypes.Structure):
+    """lrk_arena (include/lrk.h)."""
+    _fields_ = [("keys", P), ("values", P), ("positions", P), ("lengths", P), ("heads_total", I64),
+                ("capacity", I64), ("dimension", I64), ("dtype", I32)]
+
+
 SIGNATURES = {
     "lrk_last_error": (ctypes.c_char_p, []),
     "lrk_version": (I32, []),
@@ -101,6 +107,8 @@ SIGNATURES = {
     "lrk_unregister_host": (I32, [P]),
     "lrk_select_histogram": (I32, [ctypes.POINTER(P), ctypes.POINTER(I64), I64, I64, I32, P, P, P]),
     "lrk_select_pick": (I32, [P, I64, I64, I64, I64, I32, P, P]),
+    "lrk_arena_append": (I32, [ctypes.POINTER(Arena), I64, I64, P, P, F, P, P]),
+    "lrk_arena_compact": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
 }
 
 _library = None

@@ -1,0 +1,259 @@
+"""Gapped per-head KV arena: decode appends and evictions without whole-layer copies.
+
+The reference's cache (cache.py:16-265) keeps each layer packed -- K, V
+[rows, D] with the heads back to back -- and replaces the layer's tensors on
+every append (cache.py:33-52), compaction (cache.py:157-170) and merge
+(cache.py:240-246), so every decode step moves every layer through HBM
+(1.8 ms per step at configs[1]).  ArenaCache gives each (layer, head) a slot
+of `capacity` rows in three tensors for the whole cache -- keys and values
+[layers * heads, capacity, D], positions [layers * heads, capacity] -- with the
+head lengths on the device (int32) and mirrored on the host:
+
+* append_all: one lrk_arena_append launch writes one row per head of every
+  layer (2 D + 4 bytes per head) and advances the lengths;
+* remove_positions / remove_selected: one lrk_arena_compact launch shifts
+  the rows after each touched head's first removed row down, in place; heads
+  without removals do not move.
+
+A head's live rows are rows [0, length) of its slot, in the packed layout's
+order, so the packed layer is the slots' live rows back to back (packed_layer;
+the tests check both caches bit for bit through the same operations).  The
+scoring path reads the arena as it is: each layer view is keys/values
+[heads * capacity, D] with head h at rows [h * capacity, h * capacity +
+length), which lrk_logits_heads, lrk_project_values and lrk_temporal_scores
+take as spans.  FlashAttention reads it as flash_attn_with_kvcache(q [heads, 1,
+G, D], k_cache=keys[layer] viewed [heads, capacity, 1, D], v_cache, cache_seqlens
+= the layer's lengths), the decode counterpart of the reference's
+flash_attn_varlen_func call on the packed layer (attention.py:15-35).
+
+The class exposes what audit_pass, evict_prefix and a decode loop use of
+PackedCache (layers, segment_table, remove_selected, remove_positions,
+append), so the audit runs on it unchanged.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Sequence, Tuple
+
+import numpy as np
+
+from . import operators, upload
+
+
+class ArenaLayer:
+    """One layer of an ArenaCache, shaped like kvcache.LayerState: keys and
+    values [heads * capacity, D], positions [heads * capacity, 1] (views of the
+    arena), the host head/prompt lengths, and `cumulative` = the slot starts
+    (int32 [heads + 1], device), which assigns every arena row to its head for
+    lrk_project_values."""
+
+    def __init__(self, cache: "ArenaCache", index: int):
+        heads, cap = cache.heads, cache.capacity
+        rows = slice(index * heads, (index + 1) * heads)
+        self.keys = cache.keys[rows].view(heads * cap, -1)
+        self.values = cache.values[rows].view(heads * cap, -1)
+        self.positions = cache.positions[rows].view(heads * cap, 1)
+        self.head_lens = cache.head_lens[index]
+        self.prompt_lens = cache.prompt_lens[index]
+        self.cumulative = cache.slot_starts
+        self.capacity = cap
+
+    def spans(self) -> List[Tuple[int, int]]:
+        """(first row, end row) of each head's live rows in the layer views."""
+        return [(h * self.capacity, h * self.capacity + n) for h, n in enumerate(self.head_lens)]
+
+
+class ArenaCache:
+    def __init__(self, layers: int, heads: int, dim: int, capacity: int, device, dtype=None):
+        import torch
+
+        dtype = dtype or torch.bfloat16
+        self.heads, self.dim, self.capacity, self.device = heads, dim, int(capacity), torch.device(device)
+        self.keys = torch.empty(layers * heads, self.capacity, dim, dtype=dtype, device=self.device)
+        self.values = torch.empty_like(self.keys)
+        self.positions = torch.zeros(layers * heads, self.capacity, dtype=torch.float32, device=self.device)
+        self.lengths = torch.zeros(layers * heads, dtype=torch.int32, device=self.device)
+        self.head_lens: List[List[int]] = [[0] * heads for _ in range(layers)]
+        self.prompt_lens: List[List[int]] = [[0] * heads for _ in range(layers)]
+        self.seen_tokens = 0
+        self._slot_starts()
+
+    def _slot_starts(self):
+        import torch
+
+        self.slot_starts = torch.arange(0, (self.heads + 1) * self.capacity, self.capacity, dtype=torch.int32,
+                                        device=self.device)
+
+    # ------------------------------------------------------------ building
+
+    @classmethod
+    def from_packed(cls, packed, margin: int = 512) -> "ArenaCache":
+        """An arena holding the same rows as a kvcache.PackedCache, each slot
+        `margin` rows longer than the longest head."""
+        import torch
+
+        first = packed.layers[0]
+        heads, dim = len(first.head_lens), first.keys.shape[-1]
+        longest = max(max(layer.head_lens) for layer in packed.layers)
+        arena = cls(len(packed.layers), heads, dim, longest + margin, first.keys.device, first.keys.dtype)
+        for l, layer in enumerate(packed.layers):
+            bounds = layer.bounds()
+            for h in range(heads):
+                a, b = int(bounds[h]), int(bounds[h + 1])
+                arena.keys[l * heads + h, :b - a] = layer.keys[a:b]
+                arena.values[l * heads + h, :b - a] = layer.values[a:b]
+                arena.positions[l * heads + h, :b - a] = layer.positions.reshape(-1)[a:b]
+            arena.head_lens[l] = list(layer.head_lens)
+            arena.prompt_lens[l] = list(layer.prompt_lens)
+        arena.lengths.copy_(torch.tensor([n for lens in arena.head_lens for n in lens], dtype=torch.int32))
+        arena.seen_tokens = packed.seen_tokens
+        return arena
+
+    # --------------------------------------------------------------- views
+
+    @property
+    def layers(self) -> List[ArenaLayer]:
+        return [ArenaLayer(self, l) for l in range(len(self.head_lens))]
+
+    def total_rows(self) -> int:
+        return sum(sum(lens) for lens in self.head_lens)
+
+    def packed_layer(self, index: int):
+        """The layer in the packed layout (K, V [rows, D], positions [rows, 1]):
+        the heads' live rows back to back (a copy)."""
+        import torch
+
+        rows = torch.cat([torch.arange(n, device=self.device) + (index * self.heads + h) * self.capacity
+                          for h, n in enumerate(self.head_lens[index])])
+        flat_k = self.keys.view(-1, self.dim)
+        flat_v = self.values.view(-1, self.dim)
+        return (flat_k.index_select(0, rows), flat_v.index_select(0, rows),
+                self.positions.view(-1).index_select(0, rows).view(-1, 1))
+
+    def segment_table(self, coordinates: Sequence[Tuple[int, int]]):
+        """As PackedCache.segment_table: int64 [4, segments] (layer, the head's
+        first row in the layer view, prompt rows, rows) on the device."""
+        coordinates = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)
+        table = np.empty((4, coordinates.shape[0]), dtype=np.int64)
+        for i, (l, h) in enumerate(coordinates.tolist()):
+            table[:, i] = (l, h * self.capacity, self.prompt_lens[l][h], self.head_lens[l][h])
+        return upload(table, self.device)
+
+    # -------------------------------------------------------------- append
+
+    def _grow(self, extra: int) -> None:
+        """Reallocate every slot `extra` rows longer (rare: callers size the
+        capacity for the run)."""
+        import torch
+
+        old = self.capacity
+        self.capacity = old + int(extra)
+        for name in ("keys", "values", "positions"):
+            tensor = getattr(self, name)
+            grown = torch.zeros((tensor.shape[0], self.capacity) + tuple(tensor.shape[2:]), dtype=tensor.dtype,
+                                device=self.device)
+            grown[:, :old] = tensor
+            setattr(self, name, grown)
+        self._slot_starts()
+
+    def append_all(self, new_keys, new_values, logical_position: int) -> None:
+        """One decode step for every layer in one launch: new_* [layers * heads,
+        D] (or any shape with that many rows), all at `logical_position`
+        (cache.py:33-52 gives every layer of a step the same position)."""
+        if max(max(lens) for lens in self.head_lens) >= self.capacity:
+            self._grow(max(256, self.capacity // 8))
+        operators().arena_append(self.keys, self.values, self.positions, self.lengths, 0,
+                                 new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
+                                 float(logical_position))
+        for lens in self.head_lens:
+            for h in range(len(lens)):
+                lens[h] += 1
+
+    def append(self, layer_index: int, new_keys, new_values, logical_start: int) -> None:
+        """One decode step for one layer (PackedCache.append's interface):
+        new_* [1, heads, 1, D]."""
+        if max(self.head_lens[layer_index]) >= self.capacity:
+            self._grow(max(256, self.capacity // 8))
+        operators().arena_append(self.keys, self.values, self.positions, self.lengths, layer_index * self.heads,
+                                 new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
+                                 float(logical_start))
+        lens = self.head_lens[layer_index]
+        for h in range(len(lens)):
+            lens[h] += 1
+
+    # ------------------------------------------------------------ eviction
+
+    def _compact(self, flat_heads: np.ndarray, counts: np.ndarray, removed) -> None:
+        """lrk_arena_compact over distinct heads (ascending), removed rows
+        grouped by head in that order (a device int64 tensor)."""
+        offsets = np.concatenate(([0], np.cumsum(counts)[:-1])).astype(np.int64)
+        plan = upload(np.stack([flat_heads, offsets, counts], axis=1).astype(np.int64), self.device)
+        operators().arena_compact(self.keys, self.values, self.positions, self.lengths, plan, removed)
+
+    def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
+        """Drop head-relative rows (cache.py:92-180): duplicates count once,
+        any position outside its head raises IndexError before the cache
+        changes.  One in-place compaction launch for every touched head."""
+        entries = []
+        for (layer, head), positions in removals.items():
+            rows = np.unique(np.asarray(positions, dtype=np.int64).reshape(-1))
+            if not rows.size:
+                continue
+            if rows[0] < 0 or rows[-1] >= self.head_lens[layer][head]:
+                raise IndexError(f"Invalid removal in layer={int(layer)}, head={int(head)}")
+            entries.append((int(layer) * self.heads + int(head), int(layer), int(head), rows))
+        if not entries:
+            return 0
+        entries.sort(key=lambda e: e[0])
+        for _, layer, head, rows in entries:
+            self.head_lens[layer][head] -= int(rows.size)
+            self.prompt_lens[layer][head] -= int((rows < self.prompt_lens[layer][head]).sum())
+        removed = upload(np.concatenate([e[3] for e in entries]), self.device)
+        counts = np.asarray([e[3].size for e in entries], dtype=np.int64)
+        self._compact(np.asarray([e[0] for e in entries], dtype=np.int64), counts, removed)
+        return int(counts.sum())
+
+    def remove_selected(self, coordinates: Sequence[Tuple[int, int]], segment_ids, positions, table=None) -> int:
+        """remove_positions for references still on the device (as
+        PackedCache.remove_selected): the rows are keyed (flat head, position)
+        and sorted on the device; per-segment counts and two check counters
+        come back before the compaction is queued."""
+        import torch
+
+        if segment_ids.numel() == 0:
+            return 0
+        segments = len(coordinates)
+        table = self.segment_table(coordinates) if table is None else table
+        seg, pos = segment_ids.reshape(-1), positions.reshape(-1)
+        flat = table[0][seg] * self.heads + table[1][seg] // self.capacity
+        prompt, length = table[2][seg], table[3][seg]
+        outside = ((pos < 0) | (pos >= length)).sum()
+        keys = torch.sort(flat * (1 << 32) + pos).values
+        duplicates = (keys[1:] == keys[:-1]).sum()
+        counts = torch.zeros(2 * segments + 2, dtype=torch.int64, device=seg.device)
+        counts.scatter_add_(0, seg, torch.ones_like(seg))
+        counts.scatter_add_(0, seg + segments, (pos < prompt).to(torch.int64))
+        counts[2 * segments] = outside
+        counts[2 * segments + 1] = duplicates
+        host = torch.empty(counts.shape, dtype=counts.dtype, pin_memory=True)
+        host.copy_(counts, non_blocking=True)
+        ready = torch.cuda.Event()
+        ready.record()
+        removed = keys & ((1 << 32) - 1)
+        ready.synchronize()
+        counts = host.numpy()
+        if counts[2 * segments]:
+            first = int(torch.nonzero((pos < 0) | (pos >= length))[0, 0])
+            layer_index, head = coordinates[int(seg[first])]
+            raise IndexError(f"Invalid removal in layer={int(layer_index)}, head={int(head)}")
+        if counts[2 * segments + 1]:
+            return self.remove_positions({tuple(coordinates[s]): positions[seg == s].cpu().numpy()
+                                          for s in np.flatnonzero(counts[:segments]).tolist()})
+        touched = np.flatnonzero(counts[:segments])
+        coords = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)[touched]
+        flat_heads = coords[:, 0] * self.heads + coords[:, 1]
+        order = np.argsort(flat_heads)
+        for s, (layer, head) in zip(touched.tolist(), coords.tolist()):
+            self.head_lens[layer][head] -= int(counts[s])
+            self.prompt_lens[layer][head] -= int(counts[segments + s])
+        self._compact(flat_heads[order], counts[:segments][touched][order], removed)
+        return int(counts[:segments].sum())

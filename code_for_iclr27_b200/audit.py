@@ -79,10 +79,10 @@ def score_table(cache, queries, query_positions, gradients, base_margin, protect
     for layer_index, layer in enumerate(cache.layers):
         heads = len(layer.head_lens)
         groups = queries[layer_index].shape[1] // heads
-        bounds = layer.bounds()
+        spans = layer.spans()
         positions = layer.positions.reshape(-1)
         for head in range(heads):
-            start, end = int(bounds[head]), int(bounds[head + 1])
+            start, end = spans[head]
             candidate_start = int(layer.prompt_lens[head])
             candidate_end = max(candidate_start, end - start - protect_recent)
             if candidate_end <= candidate_start:
@@ -274,7 +274,7 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
         layer_queries = queries[layer_index]
         groups = layer_queries.shape[1] // heads
         scale = 1.0 / math.sqrt(layer.keys.shape[-1])
-        bounds = layer.bounds()
+        spans = layer.spans()
         positions = layer.positions.reshape(-1)
         window, dim = layer_queries.shape[0], layer_queries.shape[-1]
         if layer_index >= 2:
@@ -288,7 +288,7 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
             per_head = layer_queries.to(layer.keys.dtype).reshape(window, heads, groups, dim).transpose(0, 1)
             per_head = per_head.contiguous()
             for head in range(heads):
-                start, end = int(bounds[head]), int(bounds[head + 1])
+                start, end = spans[head]
                 candidate_start = int(layer.prompt_lens[head])
                 candidate_end = max(candidate_start, end - start - protect_recent)
                 if candidate_end <= candidate_start:
@@ -367,14 +367,14 @@ def score_table_from_keys(cache, queries, query_positions, gradients, base_margi
     for layer_index, layer in enumerate(cache.layers):
         heads = len(layer.head_lens)
         groups = queries[layer_index].shape[1] // heads
-        bounds = layer.bounds()
+        spans = layer.spans()
         keys.append(layer.keys)
         layer_queries.append(queries[layer_index])
         positions.append(layer.positions.reshape(-1))
         projected.append(C.project_values(layer.values, gradients[layer_index].float().contiguous(),
                                           layer.cumulative, groups))
         for head in range(heads):
-            start, end = int(bounds[head]), int(bounds[head + 1])
+            start, end = spans[head]
             candidate_start = int(layer.prompt_lens[head])
             candidate_end = max(candidate_start, end - start - protect_recent)
             if candidate_end <= candidate_start:

@@ -7,7 +7,8 @@
 // Added operators: refine and topk_smallest (selection); temporal_scores,
 // scores_from_keys, project_values, logits and logits_heads (scoring); compact_layers and
 // merge_layers (eviction and recall over several layers in one call);
-// select_histogram and select_pick (layer-group selection across GPUs).
+// select_histogram and select_pick (layer-group selection across GPUs);
+// arena_append and arena_compact (the gapped per-head KV arena).
 #include <vector>
 
 #include "shim_common.h"
@@ -667,6 +668,65 @@ void select_pick(torch::Tensor gathered, int64_t rank, torch::Tensor states, int
                                states.data_ptr<int64_t>(), current_stream()));
 }
 
+// The KV arena of one cache: keys, values [heads_total, capacity, D] (one
+// dtype), positions [heads_total, capacity] f32, lengths [heads_total] i32.
+lrk_arena arena_of(const torch::Tensor &keys, const torch::Tensor &values, const torch::Tensor &positions,
+                   const torch::Tensor &lengths) {
+  for (const auto &tensor : {keys, values, positions, lengths}) check_cuda(tensor, keys);
+  TORCH_CHECK(keys.dim() == 3 && keys.sizes() == values.sizes() && keys.scalar_type() == values.scalar_type(),
+              "arena keys/values must be [heads, capacity, dimension] of one dtype");
+  TORCH_CHECK(positions.scalar_type() == at::kFloat && positions.dim() == 2 && positions.size(0) == keys.size(0) &&
+                  positions.size(1) == keys.size(1),
+              "arena positions must be float32 [heads, capacity]");
+  TORCH_CHECK(lengths.scalar_type() == at::kInt && lengths.dim() == 1 && lengths.size(0) == keys.size(0),
+              "arena lengths must be int32 [heads]");
+  lrk_arena a{};
+  a.keys = keys.data_ptr();
+  a.values = values.data_ptr();
+  a.positions = positions.data_ptr<float>();
+  a.lengths = lengths.data_ptr<int32_t>();
+  a.heads_total = keys.size(0);
+  a.capacity = keys.size(1);
+  a.dimension = keys.size(2);
+  a.dtype = dtype_code(keys.scalar_type());
+  return a;
+}
+
+// Append one row per head to heads [first_head, first_head + new_keys.size(0))
+// in place; returns the device overflow flag (int32 [1], nonzero if a head
+// was full).
+torch::Tensor arena_append(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor lengths,
+                           int64_t first_head, torch::Tensor new_keys, torch::Tensor new_values, double position) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  check_cuda(new_keys, keys);
+  check_cuda(new_values, keys);
+  TORCH_CHECK(new_keys.scalar_type() == keys.scalar_type() && new_values.scalar_type() == keys.scalar_type() &&
+                  new_keys.numel() == new_values.numel() && new_keys.numel() % keys.size(2) == 0,
+              "new rows must be [heads, dimension] of the arena dtype");
+  c10::cuda::CUDAGuard guard(keys.device());
+  auto flag = torch::zeros({1}, lengths.options());
+  check_status(lrk_arena_append(&a, first_head, new_keys.numel() / keys.size(2), new_keys.data_ptr(),
+                                new_values.data_ptr(), static_cast<float>(position),
+                                reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+  return flag;
+}
+
+// In-place eviction: plan int64 [touched, 3] = (head, offset, count) into
+// removed (int64, ascending per head).  Returns the device error flag.
+torch::Tensor arena_compact(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor lengths,
+                            torch::Tensor plan, torch::Tensor removed) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  check_cuda(plan, keys);
+  check_cuda(removed, keys);
+  TORCH_CHECK(plan.scalar_type() == at::kLong && plan.dim() == 2 && plan.size(1) == 3, "plan must be int64 [n, 3]");
+  TORCH_CHECK(removed.scalar_type() == at::kLong && removed.dim() == 1, "removed must be int64 [n]");
+  c10::cuda::CUDAGuard guard(keys.device());
+  auto flag = torch::zeros({1}, lengths.options());
+  check_status(lrk_arena_compact(&a, plan.data_ptr<int64_t>(), plan.size(0), removed.data_ptr<int64_t>(),
+                                 reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+  return flag;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -693,4 +753,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("project_values", &project_values);
   module.def("select_histogram", &select_histogram);
   module.def("select_pick", &select_pick);
+  module.def("arena_append", &arena_append);
+  module.def("arena_compact", &arena_compact);
 }

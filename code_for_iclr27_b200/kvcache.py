@@ -32,6 +32,11 @@ class LayerState:
     def bounds(self) -> np.ndarray:
         return np.concatenate(([0], np.cumsum(self.head_lens))).astype(np.int64)
 
+    def spans(self):
+        """(first row, end row) of each head in the layer tensors."""
+        bounds = self.bounds().tolist()
+        return list(zip(bounds[:-1], bounds[1:]))
+
 
 @dataclass
 class PackedCache:

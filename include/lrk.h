@@ -378,6 +378,47 @@ size_t lrk_topk_workspace_bytes(int64_t n);
 int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
                       size_t workspace_bytes, float *values, int64_t *indices, lrk_stream_t stream);
 
+/* ---------------------------------------------------------- KV arena */
+
+/* A gapped per-head KV arena: every (layer, head) owns a slot of `capacity`
+ * rows; its live rows are rows [0, lengths[h]) of the slot, in the packed
+ * layout's order (the packed cache is the concatenation of the slots' live
+ * rows).  keys, values [heads_total, capacity, dimension] (dtype);
+ * positions [heads_total, capacity] f32; lengths [heads_total] i32; all
+ * device memory.  FlashAttention's cache entry point consumes it directly
+ * (k_cache [heads, capacity, 1, D], cache_seqlens = lengths).
+ * No counterpart in the reference: its cache is packed and every append,
+ * compaction and merge rebuilds whole layers (csrc/scoring.cu:264-314). */
+typedef struct lrk_arena {
+  void *keys;
+  void *values;
+  float *positions;
+  int32_t *lengths;
+  int64_t heads_total; /* layers x heads */
+  int64_t capacity;    /* rows per head slot */
+  int64_t dimension;
+  int dtype;           /* rows of dimension x dtype bytes, a multiple of 16 */
+} lrk_arena;
+
+/* Decode append without copying the cache: one row per head h in [first_head,
+ * first_head + count) at row lengths[h] of its slot (new_keys, new_values
+ * [count, dimension], device), position `position`, then lengths[h] += 1 --
+ * what _C.append does per layer (csrc/scoring.cu:130-162), for any number of
+ * layers in one launch.  A head at capacity is left unchanged and sets
+ * *overflow (device flag, may be null); callers track lengths and grow first. */
+int lrk_arena_append(const lrk_arena *arena, int64_t first_head, int64_t count, const void *new_keys,
+                     const void *new_values, float position, unsigned int *overflow, lrk_stream_t stream);
+
+/* Eviction in place: for each touched head, plan[t] = (head, offset, count)
+ * (i64 [touched][3], device), the head's rows removed[offset .. offset+count)
+ * (i64, device, strictly ascending, below the head's length) are dropped and
+ * the later rows move down -- the packed result of _C.compact
+ * (csrc/scoring.cu:164-188) restricted to the touched heads, with no other
+ * head moved.  Heads must be distinct; a head whose list is out of order or
+ * out of range is left unchanged and sets *error (device flag, may be null). */
+int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched, const int64_t *removed,
+                      unsigned int *error, lrk_stream_t stream);
+
 /* ---------------------------------------------- layer-group selection */
 
 /* The request-wide "k smallest raw scores" when one request's layers are
