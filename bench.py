@@ -651,11 +651,11 @@ def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier
     # request-wide queue prefix (lazy_prefix_share: one all-gather of the
     # ranks' next queue scores per batch); the audit already evicted its share
     # of the immediate prefix, the first slots of its local queue.
-    if layer_groups:
-        queue = last.references[lazy_prefix_share(last.references.scores, IMMEDIATE):]
-    else:
-        queue = last.references[IMMEDIATE:]
-    removed_at_audit = {}
+    # The lazy queue follows the immediate prefix, whose rows are already gone
+    # (controller.py:154-156: removed_at_audit starts as that prefix).
+    first = lazy_prefix_share(last.references.scores, IMMEDIATE) if layer_groups else IMMEDIATE
+    queue = last.references[first:]
+    removed_at_audit = last.references[:first].groups()
     layers_here = len(cache.layers)
     g = torch.Generator(device=device).manual_seed(args.seed + 7)
     new_keys = torch.randn(args.decode_steps, layers_here, 1, HEADS, 1, DIM, generator=g,
@@ -676,11 +676,14 @@ def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier
                 queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
     d1.record()
     barrier()
+    if with_e2e:
+        out_arena = measure_arena(args, cache, queries, qpos, gradients, margin, steps, warmup, barrier, g)
     out = {"managed": managed, "elapsed_ms": elapsed_ms, "decode_ms": d0.elapsed_time(d1), "launches": launches,
            "kernel_ms": timer.total_ms(), "kernel_bytes": timer.bytes, "kernel_launches": len(timer.pairs),
            "timed_name": timed_name, "clocks": clocks.summary(),
            "gather_us": [a.elapsed_time(b) * 1e3 for a, b in gathers]}
     if with_e2e:
+        out["arena"] = out_arena
         # End to end through the public API: audit inputs copied from pinned
         # host memory each step, the queue read back (refine_arrays returns
         # host arrays).
@@ -704,6 +707,51 @@ def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier
         barrier()
         out["e2e_ms"] = e_start.elapsed_time(e_end)
     return out
+
+
+def measure_arena(args, cache, queries, qpos, gradients, margin, steps: int, warmup: int, barrier, generator):
+    """The same request in the gapped per-head arena (arena.ArenaCache): audit
+    passes that evict in place, then decode steps whose appends are one
+    launch for all layers and whose lazy evictions run on the device from the
+    audit's queue (no host round trip) and shift only the touched heads' rows.
+    Returns this rank's times."""
+    import torch
+
+    from code_for_iclr27_b200.arena import ArenaCache
+    from code_for_iclr27_b200.audit import audit_pass
+
+    arena = ArenaCache.from_packed(cache, margin=args.decode_steps + 256)
+    torch.cuda.empty_cache()
+    for _ in range(warmup):
+        last = audit_pass(arena, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT)
+    barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record()
+    for _ in range(steps):
+        last = audit_pass(arena, queries, qpos, gradients, margin, IMMEDIATE, QUEUED, PROTECT_RECENT)
+    a1.record()
+    barrier()
+    layers = len(arena.head_lens)
+    new_keys = torch.randn(args.decode_steps, layers * HEADS, DIM, generator=generator,
+                           device=arena.device).to(torch.bfloat16)
+    # Lazy batches straight from the device queue: each slot's (head, logical
+    # position) was gathered at the audit (AuditResult.lazy).
+    flat, logical = last.lazy
+    start = IMMEDIATE
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for step in range(args.decode_steps):
+        arena.append_all(new_keys[step], new_keys[step], arena.seen_tokens)
+        arena.seen_tokens += 1
+        if (step + 1) % EVICT_INTERVAL == 0 and start + STAGING <= flat.numel():
+            arena.evict_logical(flat[start:start + STAGING], logical[start:start + STAGING])
+            start += STAGING
+    d1.record()
+    barrier()
+    return {"pass_ms": a0.elapsed_time(a1), "decode_ms": d0.elapsed_time(d1), "capacity": arena.capacity,
+            "bytes": (arena.keys.numel() + arena.values.numel()) * arena.keys.element_size()
+            + arena.positions.numel() * 4}
 
 
 def max_over_ranks(values, distributed: bool, device):
@@ -771,6 +819,18 @@ def main():
                 "d2h_bytes_per_step": head["d2h"]},
         "gpu_launches": head["launches"],
         "clocks": head["clocks"],
+    }
+    pass_ms, arena_decode_ms = max_over_ranks([head["arena"]["pass_ms"], head["arena"]["decode_ms"]], distributed,
+                                              device)
+    result["arena"] = {
+        "layout": "gapped per-head arena (K, V [layers*heads, capacity, D]): decode appends are one launch for all "
+                  "layers, evictions shift only the touched heads' rows in place (lrk_arena_append, "
+                  "lrk_arena_compact); FlashAttention reads it through flash_attn_with_kvcache",
+        "capacity_rows_per_head": head["arena"]["capacity"], "bytes": head["arena"]["bytes"],
+        "ms_per_pass": pass_ms / args.steps,
+        "tokens_per_s": world * head["managed"] * args.steps / (pass_ms / 1e3),
+        "decode_overhead_us": arena_decode_ms * 1e3 / args.decode_steps,
+        "decode_steps": args.decode_steps,
     }
     del head
     torch.cuda.empty_cache()

@@ -109,6 +109,7 @@ SIGNATURES = {
     "lrk_select_pick": (I32, [P, I64, I64, I64, I64, I32, P, P]),
     "lrk_arena_append": (I32, [ctypes.POINTER(Arena), I64, I64, P, P, F, P, P]),
     "lrk_arena_compact": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
+    "lrk_arena_compact_positions": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
 }
 
 _library = None

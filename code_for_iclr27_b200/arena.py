@@ -72,10 +72,25 @@ class ArenaCache:
         self.values = torch.empty_like(self.keys)
         self.positions = torch.zeros(layers * heads, self.capacity, dtype=torch.float32, device=self.device)
         self.lengths = torch.zeros(layers * heads, dtype=torch.int32, device=self.device)
-        self.head_lens: List[List[int]] = [[0] * heads for _ in range(layers)]
-        self.prompt_lens: List[List[int]] = [[0] * heads for _ in range(layers)]
+        # Host mirrors [layers, heads]: exact, except after evict_logical
+        # (device-only evictions), which leaves the live lengths on the device
+        # until the next read here (_sync).
+        self._head_lens = np.zeros((layers, heads), dtype=np.int64)
+        self.prompt_lens = np.zeros((layers, heads), dtype=np.int64)
+        self._stale = False
         self.seen_tokens = 0
         self._slot_starts()
+
+    @property
+    def head_lens(self) -> np.ndarray:
+        """Live rows per [layer, head] (numpy; rows are views)."""
+        self._sync()
+        return self._head_lens
+
+    def _sync(self) -> None:
+        if self._stale:
+            self._stale = False
+            self._head_lens[:] = self.lengths.cpu().numpy().reshape(self._head_lens.shape)
 
     def _slot_starts(self):
         import torch
@@ -102,9 +117,9 @@ class ArenaCache:
                 arena.keys[l * heads + h, :b - a] = layer.keys[a:b]
                 arena.values[l * heads + h, :b - a] = layer.values[a:b]
                 arena.positions[l * heads + h, :b - a] = layer.positions.reshape(-1)[a:b]
-            arena.head_lens[l] = list(layer.head_lens)
-            arena.prompt_lens[l] = list(layer.prompt_lens)
-        arena.lengths.copy_(torch.tensor([n for lens in arena.head_lens for n in lens], dtype=torch.int32))
+            arena.head_lens[l] = layer.head_lens
+            arena.prompt_lens[l] = layer.prompt_lens
+        arena.lengths.copy_(torch.from_numpy(arena.head_lens.reshape(-1).astype(np.int32)))
         arena.seen_tokens = packed.seen_tokens
         return arena
 
@@ -115,7 +130,7 @@ class ArenaCache:
         return [ArenaLayer(self, l) for l in range(len(self.head_lens))]
 
     def total_rows(self) -> int:
-        return sum(sum(lens) for lens in self.head_lens)
+        return int(self.head_lens.sum())
 
     def packed_layer(self, index: int):
         """The layer in the packed layout (K, V [rows, D], positions [rows, 1]):
@@ -158,27 +173,27 @@ class ArenaCache:
     def append_all(self, new_keys, new_values, logical_position: int) -> None:
         """One decode step for every layer in one launch: new_* [layers * heads,
         D] (or any shape with that many rows), all at `logical_position`
-        (cache.py:33-52 gives every layer of a step the same position)."""
-        if max(max(lens) for lens in self.head_lens) >= self.capacity:
-            self._grow(max(256, self.capacity // 8))
+        (cache.py:33-52 gives every layer of a step the same position).  The
+        capacity check uses the host mirror, an upper bound of the live
+        lengths, so it needs no device round trip."""
+        if int(self._head_lens.max()) >= self.capacity:
+            self._sync()
+            if int(self._head_lens.max()) >= self.capacity:
+                self._grow(max(256, self.capacity // 8))
         operators().arena_append(self.keys, self.values, self.positions, self.lengths, 0,
                                  new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
                                  float(logical_position))
-        for lens in self.head_lens:
-            for h in range(len(lens)):
-                lens[h] += 1
+        self._head_lens += 1
 
     def append(self, layer_index: int, new_keys, new_values, logical_start: int) -> None:
         """One decode step for one layer (PackedCache.append's interface):
         new_* [1, heads, 1, D]."""
-        if max(self.head_lens[layer_index]) >= self.capacity:
+        if int(self.head_lens[layer_index].max()) >= self.capacity:
             self._grow(max(256, self.capacity // 8))
         operators().arena_append(self.keys, self.values, self.positions, self.lengths, layer_index * self.heads,
                                  new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
                                  float(logical_start))
-        lens = self.head_lens[layer_index]
-        for h in range(len(lens)):
-            lens[h] += 1
+        self._head_lens[layer_index] += 1
 
     # ------------------------------------------------------------ eviction
 
@@ -204,8 +219,9 @@ class ArenaCache:
         if not entries:
             return 0
         entries.sort(key=lambda e: e[0])
+        lens = self.head_lens
         for _, layer, head, rows in entries:
-            self.head_lens[layer][head] -= int(rows.size)
+            lens[layer][head] -= int(rows.size)
             self.prompt_lens[layer][head] -= int((rows < self.prompt_lens[layer][head]).sum())
         removed = upload(np.concatenate([e[3] for e in entries]), self.device)
         counts = np.asarray([e[3].size for e in entries], dtype=np.int64)
@@ -252,8 +268,43 @@ class ArenaCache:
         coords = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)[touched]
         flat_heads = coords[:, 0] * self.heads + coords[:, 1]
         order = np.argsort(flat_heads)
+        lens = self.head_lens
         for s, (layer, head) in zip(touched.tolist(), coords.tolist()):
-            self.head_lens[layer][head] -= int(counts[s])
+            lens[layer][head] -= int(counts[s])
             self.prompt_lens[layer][head] -= int(counts[segments + s])
         self._compact(flat_heads[order], counts[:segments][touched][order], removed)
         return int(counts[:segments].sum())
+
+    # ------------------------------------------ lazy eviction on the device
+
+    def queue_positions(self, table, segment_ids, positions):
+        """Each queued reference's (flat head, logical position), gathered on
+        the device from the rows it names now (call before those rows move):
+        a lazy batch later finds each reference's current row from them alone
+        (evict_logical)."""
+        seg, pos = segment_ids.reshape(-1), positions.reshape(-1)
+        flat = table[0][seg] * self.heads + table[1][seg] // self.capacity
+        logical = self.positions.view(-1).index_select(0, flat * self.capacity + pos)
+        return flat, logical
+
+    def evict_logical(self, flat_heads, logical) -> None:
+        """Lazy eviction of a batch of queued references (controller.py:57-70)
+        with no host round trip: the references (flat head, logical position;
+        queue_positions) are sorted by head and position on the device, a
+        dense per-head plan is built there, and one
+        lrk_arena_compact_positions launch finds the rows by their positions
+        and shifts each touched head in place.  The host length mirror becomes
+        an upper bound until it is next read."""
+        import torch
+
+        if flat_heads.numel() == 0:
+            return
+        keys = torch.sort(flat_heads * (1 << 32) + logical.to(torch.int64)).values
+        heads = keys >> 32
+        removed = (keys & ((1 << 32) - 1)).to(torch.float32)
+        total = self.lengths.numel()
+        counts = torch.zeros(total, dtype=torch.int64, device=self.device).scatter_add_(0, heads,
+                                                                                        torch.ones_like(heads))
+        plan = torch.stack([torch.arange(total, device=self.device), torch.cumsum(counts, 0) - counts, counts], 1)
+        operators().arena_compact_positions(self.keys, self.values, self.positions, self.lengths, plan, removed)
+        self._stale = True

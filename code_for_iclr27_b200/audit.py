@@ -425,6 +425,10 @@ class AuditResult:
     changed: int
     changed_heads: int
     evicted: int
+    # For caches that evict lazy batches on the device (arena.ArenaCache):
+    # every queue slot's (flat head, logical position), taken before the
+    # immediate eviction.
+    lazy: tuple = None
 
 
 def audit_pass(cache, queries, query_positions, gradients, base_margin, immediate: int, queued: int,
@@ -454,12 +458,15 @@ def audit_pass(cache, queries, query_positions, gradients, base_margin, immediat
     # The queue leaves the device before the compactions are queued and is
     # unpacked on the host while they run.
     pending = fetch_references(queue)
+    lazy = None
+    if hasattr(cache, "queue_positions") and queue.count:
+        lazy = cache.queue_positions(segments, queue.segment_ids, queue.positions)
     evicted = 0
     if immediate:
         evicted = cache.remove_selected(queue.coordinates, queue.segment_ids[:immediate],
                                         queue.positions[:immediate], segments)
     references, changed, changed_heads = pending.result()
-    return AuditResult(table, references, changed, changed_heads, evicted)
+    return AuditResult(table, references, changed, changed_heads, evicted, lazy)
 
 
 def evict_prefix(cache, queue: ArrayReferences, removed_at_audit: dict, count: int):

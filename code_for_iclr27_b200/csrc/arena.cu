@@ -82,52 +82,79 @@ __host__ __device__ __forceinline__ int64_t chunk_rows_for(int64_t vectors) {
   return rows < kCompactThreads ? rows : kCompactThreads;
 }
 
-// How many entries of removed[0 .. count) (ascending) lie below `row`.
-__device__ __forceinline__ int64_t removed_before(const int64_t *__restrict__ removed, int64_t count, int64_t row) {
+// How many entries of list[0 .. count) (ascending) lie below `value`.
+template <typename V>
+__device__ __forceinline__ int64_t count_below(const V *__restrict__ list, int64_t count, V value) {
   int64_t lo = 0, hi = count;
   while (lo < hi) {
     const int64_t mid = (lo + hi) >> 1;
-    if (__ldg(removed + mid) < row) lo = mid + 1; else hi = mid;
+    if (__ldg(list + mid) < value) lo = mid + 1; else hi = mid;
   }
   return lo;
 }
 
-// One CTA per touched head (grid-stride).  plan [touched][3] = (head, first
-// index into removed, count); removed holds each head's rows to drop, strictly
-// ascending and below the head's length (checked here: a head whose list
-// breaks that is left unchanged and sets error).
+// Compaction of the touched heads, one CTA per head (grid-stride).  plan
+// [touched][3] = (head, first index into the removal lists, count); heads
+// with count 0 are skipped, so a dense plan over every head is allowed.
+// BY_POSITION false: the list holds row indices (int64), strictly ascending,
+// below the head's length.  BY_POSITION true: it holds logical positions
+// (float) of rows to drop, strictly ascending, each present in the head,
+// whose live positions must be ascending (as appends and position-ordered
+// merges keep them); the rows are found by binary search.  A head whose list
+// breaks its rule is left unchanged and sets *error.
+template <bool BY_POSITION>
 __global__ void __launch_bounds__(kCompactThreads) arena_compact_kernel(ArenaParam a,
                                                                         const int64_t *__restrict__ plan,
                                                                         int64_t touched,
-                                                                        const int64_t *__restrict__ removed,
+                                                                        const void *__restrict__ removed,
                                                                         unsigned int *__restrict__ error) {
   extern __shared__ int64_t destination[];  // [rows per chunk]: new row, or -1 for a removed row
+  __shared__ int64_t first_row;
   const int64_t vectors = a.row_bytes / 16;
   const int64_t chunk_rows = chunk_rows_for(vectors);
   for (int64_t t = blockIdx.x; t < touched; t += gridDim.x) {
     const int64_t head = plan[3 * t], offset = plan[3 * t + 1], count = plan[3 * t + 2];
     if (count <= 0 || head < 0 || head >= a.heads_total) continue;
     const int64_t length = a.lengths[head];
-    const int64_t *rows = removed + offset;
+    const int64_t *rows = static_cast<const int64_t *>(removed) + offset;
+    const float *logical = static_cast<const float *>(removed) + offset;
+    float *positions = a.positions + head * a.capacity;
+    if (threadIdx.x == 0) first_row = length;
+    __syncthreads();
     int bad = 0;
     for (int64_t i = threadIdx.x; i < count; i += kCompactThreads) {
-      const int64_t r = rows[i];
-      if (r < 0 || r >= length || (i > 0 && rows[i - 1] >= r)) bad = 1;
+      if (BY_POSITION) {
+        const float value = logical[i];
+        const int64_t at = count_below(positions, length, value);
+        if (at >= length || positions[at] != value || (i > 0 && !(logical[i - 1] < value))) bad = 1;
+        if (i == 0) first_row = at;
+      } else {
+        const int64_t r = rows[i];
+        if (r < 0 || r >= length || (i > 0 && rows[i - 1] >= r)) bad = 1;
+        if (i == 0) first_row = r;
+      }
     }
     if (__syncthreads_or(bad)) {
       if (threadIdx.x == 0 && error != nullptr) atomicOr(error, 1u);
       continue;
     }
-    const int64_t first = rows[0];
+    const int64_t first = first_row;
     char *keys = a.keys + head * a.capacity * a.row_bytes;
     char *values = a.values + head * a.capacity * a.row_bytes;
-    float *positions = a.positions + head * a.capacity;
     for (int64_t base = first + 1; base < length; base += chunk_rows) {
       const int64_t rows_here = lmin(chunk_rows, length - base);
       for (int64_t i = threadIdx.x; i < rows_here; i += kCompactThreads) {
         const int64_t source = base + i;
-        const int64_t below = removed_before(rows, count, source);
-        const bool gone = below < count && __ldg(rows + below) == source;
+        int64_t below;
+        bool gone;
+        if (BY_POSITION) {
+          const float value = positions[source];
+          below = count_below(logical, count, value);
+          gone = below < count && __ldg(logical + below) == value;
+        } else {
+          below = count_below(rows, count, source);
+          gone = below < count && __ldg(rows + below) == source;
+        }
         destination[i] = gone ? -1 : source - below;
       }
       __syncthreads();
@@ -200,8 +227,9 @@ extern "C" int lrk_arena_append(const lrk_arena *arena, int64_t first_head, int6
   return launch_status("lrk_arena_append");
 }
 
-extern "C" int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched, const int64_t *removed,
-                                 unsigned int *error, lrk_stream_t stream) {
+template <bool BY_POSITION>
+int launch_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched, const void *removed,
+                   unsigned int *error, lrk_stream_t stream) {
   clear_error();
   int64_t element = 0;
   int status = check_arena(arena, &element);
@@ -211,8 +239,18 @@ extern "C" int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, in
   LRK_REQUIRE(plan && removed, "null pointer");
   const int64_t chunk_rows = chunk_rows_for(arena->dimension * element / 16);
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(touched, 65535));
-  arena_compact_kernel<<<blocks, kCompactThreads, chunk_rows * sizeof(int64_t),
-                         reinterpret_cast<cudaStream_t>(stream)>>>(param(*arena, element), plan, touched, removed,
-                                                                   error);
+  arena_compact_kernel<BY_POSITION><<<blocks, kCompactThreads, chunk_rows * sizeof(int64_t),
+                                      reinterpret_cast<cudaStream_t>(stream)>>>(param(*arena, element), plan,
+                                                                                touched, removed, error);
   return launch_status("lrk_arena_compact");
+}
+
+extern "C" int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched, const int64_t *removed,
+                                 unsigned int *error, lrk_stream_t stream) {
+  return launch_compact<false>(arena, plan, touched, removed, error, stream);
+}
+
+extern "C" int lrk_arena_compact_positions(const lrk_arena *arena, const int64_t *plan, int64_t touched,
+                                           const float *removed_positions, unsigned int *error, lrk_stream_t stream) {
+  return launch_compact<true>(arena, plan, touched, removed_positions, error, stream);
 }

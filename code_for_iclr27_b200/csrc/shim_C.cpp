@@ -727,6 +727,23 @@ torch::Tensor arena_compact(torch::Tensor keys, torch::Tensor values, torch::Ten
   return flag;
 }
 
+// In-place eviction by logical position: removed is float32 (ascending per
+// head, every position present in its head).  Returns the device error flag.
+torch::Tensor arena_compact_positions(torch::Tensor keys, torch::Tensor values, torch::Tensor positions,
+                                      torch::Tensor lengths, torch::Tensor plan, torch::Tensor removed) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  check_cuda(plan, keys);
+  check_cuda(removed, keys);
+  TORCH_CHECK(plan.scalar_type() == at::kLong && plan.dim() == 2 && plan.size(1) == 3, "plan must be int64 [n, 3]");
+  TORCH_CHECK(removed.scalar_type() == at::kFloat && removed.dim() == 1, "removed must be float32 [n]");
+  c10::cuda::CUDAGuard guard(keys.device());
+  auto flag = torch::zeros({1}, lengths.options());
+  check_status(lrk_arena_compact_positions(&a, plan.data_ptr<int64_t>(), plan.size(0), removed.data_ptr<float>(),
+                                           reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()),
+                                           current_stream()));
+  return flag;
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -755,4 +772,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("select_pick", &select_pick);
   module.def("arena_append", &arena_append);
   module.def("arena_compact", &arena_compact);
+  module.def("arena_compact_positions", &arena_compact_positions);
 }

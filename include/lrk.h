@@ -415,9 +415,21 @@ int lrk_arena_append(const lrk_arena *arena, int64_t first_head, int64_t count, 
  * the later rows move down -- the packed result of _C.compact
  * (csrc/scoring.cu:164-188) restricted to the touched heads, with no other
  * head moved.  Heads must be distinct; a head whose list is out of order or
- * out of range is left unchanged and sets *error (device flag, may be null). */
+ * out of range is left unchanged and sets *error (device flag, may be null).
+ * Plan entries with count 0 are skipped (a dense plan over all heads is fine). */
 int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched, const int64_t *removed,
                       unsigned int *error, lrk_stream_t stream);
+
+/* lrk_arena_compact with each head's rows named by their logical position:
+ * removed_positions (f32, device) holds, per plan entry, positions present in
+ * the head, strictly ascending; the head's live positions must be ascending
+ * (appends and position-ordered merges keep them so).  This is how a lazy
+ * eviction batch finds its rows with no host round trip: a queued reference's
+ * row at audit time, shifted down by the rows removed from its head since
+ * (src/lazy_recall/controller.py:57-70), is the row that now holds the
+ * position it held at the audit. */
+int lrk_arena_compact_positions(const lrk_arena *arena, const int64_t *plan, int64_t touched,
+                                const float *removed_positions, unsigned int *error, lrk_stream_t stream);
 
 /* ---------------------------------------------- layer-group selection */
 

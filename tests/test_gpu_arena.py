@@ -38,14 +38,13 @@ def assert_same(arena, packed):
     import torch
 
     for l, layer in enumerate(packed.layers):
-        assert arena.head_lens[l] == layer.head_lens, l
-        assert arena.prompt_lens[l] == layer.prompt_lens, l
+        assert list(arena.head_lens[l]) == layer.head_lens, l
+        assert list(arena.prompt_lens[l]) == layer.prompt_lens, l
         k, v, p = arena.packed_layer(l)
         assert torch.equal(k.view(torch.int16), layer.keys.view(torch.int16)), l
         assert torch.equal(v.view(torch.int16), layer.values.view(torch.int16)), l
         assert torch.equal(p, layer.positions), l
-    lengths = arena.lengths.cpu().numpy().tolist()
-    assert lengths == [n for lens in arena.head_lens for n in lens]
+    assert arena.lengths.cpu().numpy().tolist() == arena.head_lens.reshape(-1).tolist()
 
 
 def test_arena_equals_packed_through_appends_and_removals(cuda):
@@ -122,6 +121,45 @@ def test_audit_pass_on_arena_equals_packed(cuda):
     np.testing.assert_array_equal(a.references.positions, b.references.positions)
     assert a.evicted == b.evicted == 60
     assert_same(arena, packed)
+
+
+def test_lazy_eviction_on_the_device_equals_evict_prefix(cuda):
+    """After an audit pass on both caches, lazy batches of the queue: on the
+    packed cache by evict_prefix (controller.py:57-70: audit positions shifted
+    by the rows already removed from their head, starting from the immediate
+    prefix), on the arena by evict_logical (device only, rows found by their
+    logical positions), with decode appends in between.  The caches stay
+    equal bit for bit."""
+    import torch
+
+    from code_for_iclr27_b200.arena import ArenaCache
+    from code_for_iclr27_b200.audit import audit_pass, evict_prefix
+
+    packed = make_packed(cuda, seed=8, layers=2, heads=4, prompt=150)
+    arena = ArenaCache.from_packed(packed)
+    g = torch.Generator().manual_seed(9)
+    window, groups, immediate, batch = 16, 2, 40, 37
+    queries = [(torch.randn(window, 4 * groups, 128, generator=g) * 2).to(torch.bfloat16).to(cuda) for _ in range(2)]
+    grads = [(torch.randn(4 * groups, 128, generator=g) / 11).to(cuda) for _ in range(2)]
+    top = min(min(layer.head_lens) for layer in packed.layers)
+    qpos = torch.arange(top - window, top, dtype=torch.int64, device=cuda)
+    margin = torch.tensor([0.9], device=cuda)
+    a = audit_pass(packed, queries, qpos, grads, margin, immediate=immediate, queued=300, protect_recent=4)
+    b = audit_pass(arena, queries, qpos, grads, margin, immediate=immediate, queued=300, protect_recent=4)
+    assert_same(arena, packed)
+    queue, removed = a.references[immediate:], a.references[:immediate].groups()
+    flat, logical = b.lazy
+    start = immediate
+    for step in range(5):
+        new = torch.randn(2, 1, 4, 1, 128, generator=g).to(torch.bfloat16).to(cuda)
+        for l in range(2):
+            packed.append(l, new[l], new[l], packed.seen_tokens)
+        arena.append_all(new, new, packed.seen_tokens)
+        packed.seen_tokens += 1
+        queue, removed = evict_prefix(packed, queue, removed, batch)
+        arena.evict_logical(flat[start:start + batch], logical[start:start + batch])
+        start += batch
+        assert_same(arena, packed)
 
 
 def test_flash_attention_reads_the_arena(cuda):
