@@ -110,6 +110,7 @@ SIGNATURES = {
     "lrk_arena_append": (I32, [ctypes.POINTER(Arena), I64, I64, P, P, F, P, P]),
     "lrk_arena_compact": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
     "lrk_arena_compact_positions": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
+    "lrk_arena_evict": (I32, [ctypes.POINTER(Arena), P, P, I64, P, P]),
 }
 
 _library = None

@@ -79,6 +79,9 @@ class ArenaCache:
         self.prompt_lens = np.zeros((layers, heads), dtype=np.int64)
         self._stale = False
         self.seen_tokens = 0
+        # Device flags the kernels set on a full slot or a bad removal list
+        # (checked by callers that want to: check_flags).
+        self.flags = torch.zeros(2, dtype=torch.int32, device=self.device)
         self._slot_starts()
 
     @property
@@ -180,9 +183,9 @@ class ArenaCache:
             self._sync()
             if int(self._head_lens.max()) >= self.capacity:
                 self._grow(max(256, self.capacity // 8))
-        operators().arena_append(self.keys, self.values, self.positions, self.lengths, 0,
-                                 new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
-                                 float(logical_position))
+        operators().arena_append_into(self.keys, self.values, self.positions, self.lengths, 0,
+                                      new_keys.reshape(-1, self.dim), new_values.reshape(-1, self.dim),
+                                      float(logical_position), self.flags[0:1])
         self._head_lens += 1
 
     def append(self, layer_index: int, new_keys, new_values, logical_start: int) -> None:
@@ -290,21 +293,19 @@ class ArenaCache:
     def evict_logical(self, flat_heads, logical) -> None:
         """Lazy eviction of a batch of queued references (controller.py:57-70)
         with no host round trip: the references (flat head, logical position;
-        queue_positions) are sorted by head and position on the device, a
-        dense per-head plan is built there, and one
-        lrk_arena_compact_positions launch finds the rows by their positions
-        and shifts each touched head in place.  The host length mirror becomes
-        an upper bound until it is next read."""
-        import torch
-
+        queue_positions) go to one lrk_arena_evict launch, in which each head
+        collects and sorts its own entries, finds their rows by position and
+        shifts its rows in place.  The host length mirror becomes an upper
+        bound until it is next read."""
         if flat_heads.numel() == 0:
             return
-        keys = torch.sort(flat_heads * (1 << 32) + logical.to(torch.int64)).values
-        heads = keys >> 32
-        removed = (keys & ((1 << 32) - 1)).to(torch.float32)
-        total = self.lengths.numel()
-        counts = torch.zeros(total, dtype=torch.int64, device=self.device).scatter_add_(0, heads,
-                                                                                        torch.ones_like(heads))
-        plan = torch.stack([torch.arange(total, device=self.device), torch.cumsum(counts, 0) - counts, counts], 1)
-        operators().arena_compact_positions(self.keys, self.values, self.positions, self.lengths, plan, removed)
+        operators().arena_evict(self.keys, self.values, self.positions, self.lengths, flat_heads.contiguous(),
+                                logical.contiguous(), self.flags[1:2])
         self._stale = True
+
+    def check_flags(self) -> None:
+        """Raise if a kernel flagged a full slot or a bad removal list (reads
+        the device flags: a synchronisation)."""
+        overflow, bad = self.flags.tolist()
+        if overflow or bad:
+            raise RuntimeError(f"arena kernels flagged: overflow={overflow}, bad removal list={bad}")

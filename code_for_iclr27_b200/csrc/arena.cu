@@ -82,110 +82,206 @@ __host__ __device__ __forceinline__ int64_t chunk_rows_for(int64_t vectors) {
   return rows < kCompactThreads ? rows : kCompactThreads;
 }
 
-// How many entries of list[0 .. count) (ascending) lie below `value`.
+// How many entries of list[0 .. count) (ascending) lie below `value`.  The
+// list may be in global or shared memory (plain generic loads).
 template <typename V>
-__device__ __forceinline__ int64_t count_below(const V *__restrict__ list, int64_t count, V value) {
+__device__ __forceinline__ int64_t count_below(const V *list, int64_t count, V value) {
   int64_t lo = 0, hi = count;
   while (lo < hi) {
     const int64_t mid = (lo + hi) >> 1;
-    if (__ldg(list + mid) < value) lo = mid + 1; else hi = mid;
+    if (list[mid] < value) lo = mid + 1; else hi = mid;
   }
   return lo;
 }
 
-// Compaction of the touched heads, one CTA per head (grid-stride).  plan
-// [touched][3] = (head, first index into the removal lists, count); heads
-// with count 0 are skipped, so a dense plan over every head is allowed.
-// BY_POSITION false: the list holds row indices (int64), strictly ascending,
-// below the head's length.  BY_POSITION true: it holds logical positions
-// (float) of rows to drop, strictly ascending, each present in the head,
-// whose live positions must be ascending (as appends and position-ordered
-// merges keep them); the rows are found by binary search.  A head whose list
-// breaks its rule is left unchanged and sets *error.
+// Removal lists a CTA keeps in shared memory (longer lists are read from
+// global memory).
+constexpr int kListMax = 2048;
+
+// The chunk loop of one head's in-place compaction (all threads of the CTA):
+// rows [first + 1, length) move down over the removed rows.  Each chunk's
+// rows -- keys, values and positions -- are loaded with no dependence on
+// which of them stay, each row's destination is found from its index
+// (BY_POSITION false: the number of listed rows below it) or its position
+// (BY_POSITION true: the number of listed positions below it), and after a
+// barrier the kept rows are stored.  One memory latency per chunk.
 template <bool BY_POSITION>
-__global__ void __launch_bounds__(kCompactThreads) arena_compact_kernel(ArenaParam a,
+__device__ void compact_head(const ArenaParam &a, int64_t head, int64_t length, int64_t first,
+                             const int64_t *__restrict__ rows_list, const float *__restrict__ position_list,
+                             int64_t count, int64_t *destination) {
+  const int64_t vectors = a.row_bytes / 16;
+  const int64_t chunk_rows = chunk_rows_for(vectors);
+  char *keys = a.keys + head * a.capacity * a.row_bytes;
+  char *values = a.values + head * a.capacity * a.row_bytes;
+  float *positions = a.positions + head * a.capacity;
+  for (int64_t base = first + 1; base < length; base += chunk_rows) {
+    const int64_t rows_here = lmin(chunk_rows, length - base);
+    uint4 k[kCompactVectors], v[kCompactVectors];
+#pragma unroll
+    for (int j = 0; j < kCompactVectors; ++j) {
+      const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
+      const int64_t r = item / vectors, c = item % vectors;
+      if (r < rows_here) {
+        k[j] = reinterpret_cast<const uint4 *>(keys + (base + r) * a.row_bytes)[c];
+        v[j] = reinterpret_cast<const uint4 *>(values + (base + r) * a.row_bytes)[c];
+      }
+    }
+    float p = 0.0f;
+    if (threadIdx.x < rows_here) {
+      const int64_t source = base + threadIdx.x;
+      p = positions[source];
+      int64_t below;
+      bool gone;
+      if (BY_POSITION) {
+        below = count_below(position_list, count, p);
+        gone = below < count && position_list[below] == p;
+      } else {
+        below = count_below(rows_list, count, source);
+        gone = below < count && rows_list[below] == source;
+      }
+      destination[threadIdx.x] = gone ? -1 : source - below;
+    }
+    __syncthreads();  // every load of the chunk is ordered before any store
+#pragma unroll
+    for (int j = 0; j < kCompactVectors; ++j) {
+      const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
+      const int64_t r = item / vectors, c = item % vectors;
+      if (r < rows_here && destination[r] >= 0) {
+        reinterpret_cast<uint4 *>(keys + destination[r] * a.row_bytes)[c] = k[j];
+        reinterpret_cast<uint4 *>(values + destination[r] * a.row_bytes)[c] = v[j];
+      }
+    }
+    if (threadIdx.x < rows_here && destination[threadIdx.x] >= 0) positions[destination[threadIdx.x]] = p;
+    __syncthreads();  // destination[] is reused by the next chunk
+  }
+}
+
+// Check a head's sorted removal list and find its first row; returns false
+// (after flagging) when the list is out of order or names a row / position
+// the head does not hold.
+template <bool BY_POSITION>
+__device__ bool check_list(const ArenaParam &a, int64_t head, int64_t length, const int64_t *rows_list,
+                           const float *position_list, int64_t count, int64_t *first_row, unsigned int *error) {
+  const float *positions = a.positions + head * a.capacity;
+  if (threadIdx.x == 0) *first_row = length;
+  __syncthreads();
+  int bad = 0;
+  for (int64_t i = threadIdx.x; i < count; i += kCompactThreads) {
+    if (BY_POSITION) {
+      const float value = position_list[i];
+      const int64_t at = count_below(positions, length, value);
+      if (at >= length || positions[at] != value || (i > 0 && !(position_list[i - 1] < value))) bad = 1;
+      if (i == 0) *first_row = at;
+    } else {
+      const int64_t r = rows_list[i];
+      if (r < 0 || r >= length || (i > 0 && rows_list[i - 1] >= r)) bad = 1;
+      if (i == 0) *first_row = r;
+    }
+  }
+  if (__syncthreads_or(bad)) {
+    if (threadIdx.x == 0 && error != nullptr) atomicOr(error, 1u);
+    return false;
+  }
+  return true;
+}
+
+// Compaction of the heads a plan names, one CTA per plan entry (grid-stride).
+// plan [touched][3] = (head, first index into the removal lists, count);
+// entries with count 0 are skipped, so a dense plan over every head works.
+// BY_POSITION false: int64 rows, strictly ascending, below the head's length.
+// BY_POSITION true: float logical positions, strictly ascending, each present
+// in the head, whose live positions must be ascending (as appends and
+// position-ordered merges keep them).  A head whose list breaks its rule is
+// left unchanged and sets *error.  Heads must be distinct.
+template <bool BY_POSITION>
+__global__ void __launch_bounds__(kCompactThreads, 2) arena_compact_kernel(ArenaParam a,
                                                                         const int64_t *__restrict__ plan,
                                                                         int64_t touched,
                                                                         const void *__restrict__ removed,
                                                                         unsigned int *__restrict__ error) {
-  extern __shared__ int64_t destination[];  // [rows per chunk]: new row, or -1 for a removed row
+  __shared__ int64_t destination[kCompactThreads];
+  __shared__ __align__(8) unsigned char list_bytes[kListMax * sizeof(int64_t)];
   __shared__ int64_t first_row;
-  const int64_t vectors = a.row_bytes / 16;
-  const int64_t chunk_rows = chunk_rows_for(vectors);
   for (int64_t t = blockIdx.x; t < touched; t += gridDim.x) {
     const int64_t head = plan[3 * t], offset = plan[3 * t + 1], count = plan[3 * t + 2];
     if (count <= 0 || head < 0 || head >= a.heads_total) continue;
     const int64_t length = a.lengths[head];
-    const int64_t *rows = static_cast<const int64_t *>(removed) + offset;
-    const float *logical = static_cast<const float *>(removed) + offset;
-    float *positions = a.positions + head * a.capacity;
-    if (threadIdx.x == 0) first_row = length;
+    // The list, in shared memory when it fits.
+    const int64_t *rows_list = static_cast<const int64_t *>(removed) + offset;
+    const float *position_list = static_cast<const float *>(removed) + offset;
+    if (count <= kListMax) {
+      for (int64_t i = threadIdx.x; i < count; i += kCompactThreads) {
+        if (BY_POSITION) reinterpret_cast<float *>(list_bytes)[i] = position_list[i];
+        else reinterpret_cast<int64_t *>(list_bytes)[i] = rows_list[i];
+      }
+      rows_list = reinterpret_cast<const int64_t *>(list_bytes);
+      position_list = reinterpret_cast<const float *>(list_bytes);
+    }
+    if (check_list<BY_POSITION>(a, head, length, rows_list, position_list, count, &first_row, error)) {
+      compact_head<BY_POSITION>(a, head, length, first_row, rows_list, position_list, count, destination);
+      if (threadIdx.x == 0) a.lengths[head] = static_cast<int32_t>(length - count);
+    }
     __syncthreads();
-    int bad = 0;
-    for (int64_t i = threadIdx.x; i < count; i += kCompactThreads) {
-      if (BY_POSITION) {
-        const float value = logical[i];
-        const int64_t at = count_below(positions, length, value);
-        if (at >= length || positions[at] != value || (i > 0 && !(logical[i - 1] < value))) bad = 1;
-        if (i == 0) first_row = at;
-      } else {
-        const int64_t r = rows[i];
-        if (r < 0 || r >= length || (i > 0 && rows[i - 1] >= r)) bad = 1;
-        if (i == 0) first_row = r;
+  }
+}
+
+// Eviction of an unsorted batch of (head, logical position) references, one
+// CTA per head (grid-stride over every head): the CTA collects its head's
+// entries from the batch, sorts them in shared memory (bitonic), and
+// compacts the head as arena_compact_kernel<true> does.  A head with more
+// than kListMax entries, a duplicate or a position it does not hold is left
+// unchanged and sets *error.
+__global__ void __launch_bounds__(kCompactThreads, 2) arena_evict_kernel(ArenaParam a,
+                                                                      const int64_t *__restrict__ heads,
+                                                                      const float *__restrict__ positions_in,
+                                                                      int64_t n, unsigned int *__restrict__ error) {
+  __shared__ int64_t destination[kCompactThreads];
+  __shared__ float list[kListMax];
+  __shared__ int count_shared;
+  __shared__ int64_t first_row;
+  for (int64_t head = blockIdx.x; head < a.heads_total; head += gridDim.x) {
+    if (threadIdx.x == 0) count_shared = 0;
+    __syncthreads();
+    for (int64_t i = threadIdx.x; i < n; i += kCompactThreads) {
+      if (heads[i] == head) {
+        const int slot = atomicAdd(&count_shared, 1);
+        if (slot < kListMax) list[slot] = positions_in[i];
       }
     }
-    if (__syncthreads_or(bad)) {
+    __syncthreads();
+    const int count = count_shared;
+    __syncthreads();  // every thread has read the count before the next reset
+    if (count == 0) continue;  // uniform: every thread read the same count
+    if (count > kListMax) {
       if (threadIdx.x == 0 && error != nullptr) atomicOr(error, 1u);
       continue;
     }
-    const int64_t first = first_row;
-    char *keys = a.keys + head * a.capacity * a.row_bytes;
-    char *values = a.values + head * a.capacity * a.row_bytes;
-    for (int64_t base = first + 1; base < length; base += chunk_rows) {
-      const int64_t rows_here = lmin(chunk_rows, length - base);
-      for (int64_t i = threadIdx.x; i < rows_here; i += kCompactThreads) {
-        const int64_t source = base + i;
-        int64_t below;
-        bool gone;
-        if (BY_POSITION) {
-          const float value = positions[source];
-          below = count_below(logical, count, value);
-          gone = below < count && __ldg(logical + below) == value;
-        } else {
-          below = count_below(rows, count, source);
-          gone = below < count && __ldg(rows + below) == source;
+    // Bitonic sort of list[0 .. size), padded with +inf.
+    int size = 1;
+    while (size < count) size <<= 1;
+    for (int i = count + threadIdx.x; i < size; i += kCompactThreads) list[i] = INFINITY;
+    __syncthreads();
+    for (int k = 2; k <= size; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < size; i += kCompactThreads) {
+          const int partner = i ^ j;
+          if (partner > i) {
+            const bool up = (i & k) == 0;
+            const float x = list[i], y = list[partner];
+            if ((x > y) == up) {
+              list[i] = y;
+              list[partner] = x;
+            }
+          }
         }
-        destination[i] = gone ? -1 : source - below;
+        __syncthreads();
       }
-      __syncthreads();
-      // Load the chunk's kept rows ...
-      uint4 k[kCompactVectors], v[kCompactVectors];
-      float p = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kCompactVectors; ++j) {
-        const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
-        const int64_t r = item / vectors, c = item % vectors;
-        if (r < rows_here && destination[r] >= 0) {
-          k[j] = reinterpret_cast<const uint4 *>(keys + (base + r) * a.row_bytes)[c];
-          v[j] = reinterpret_cast<const uint4 *>(values + (base + r) * a.row_bytes)[c];
-        }
-      }
-      if (threadIdx.x < rows_here && destination[threadIdx.x] >= 0) p = positions[base + threadIdx.x];
-      __syncthreads();
-      // ... then store them at their new rows (all loads of the chunk are done).
-#pragma unroll
-      for (int j = 0; j < kCompactVectors; ++j) {
-        const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
-        const int64_t r = item / vectors, c = item % vectors;
-        if (r < rows_here && destination[r] >= 0) {
-          reinterpret_cast<uint4 *>(keys + destination[r] * a.row_bytes)[c] = k[j];
-          reinterpret_cast<uint4 *>(values + destination[r] * a.row_bytes)[c] = v[j];
-        }
-      }
-      if (threadIdx.x < rows_here && destination[threadIdx.x] >= 0) positions[destination[threadIdx.x]] = p;
-      __syncthreads();  // destination[] and the moved rows settle before the next chunk
     }
-    if (threadIdx.x == 0) a.lengths[head] = static_cast<int32_t>(length - count);
+    const int64_t length = a.lengths[head];
+    if (check_list<true>(a, head, length, nullptr, list, count, &first_row, error)) {
+      compact_head<true>(a, head, length, first_row, nullptr, list, count, destination);
+      if (threadIdx.x == 0) a.lengths[head] = static_cast<int32_t>(length - count);
+    }
     __syncthreads();
   }
 }
@@ -237,11 +333,9 @@ int launch_compact(const lrk_arena *arena, const int64_t *plan, int64_t touched,
   LRK_REQUIRE(touched >= 0, "invalid plan size");
   if (touched == 0) return LRK_OK;
   LRK_REQUIRE(plan && removed, "null pointer");
-  const int64_t chunk_rows = chunk_rows_for(arena->dimension * element / 16);
   const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(touched, 65535));
-  arena_compact_kernel<BY_POSITION><<<blocks, kCompactThreads, chunk_rows * sizeof(int64_t),
-                                      reinterpret_cast<cudaStream_t>(stream)>>>(param(*arena, element), plan,
-                                                                                touched, removed, error);
+  arena_compact_kernel<BY_POSITION><<<blocks, kCompactThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      param(*arena, element), plan, touched, removed, error);
   return launch_status("lrk_arena_compact");
 }
 
@@ -253,4 +347,19 @@ extern "C" int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, in
 extern "C" int lrk_arena_compact_positions(const lrk_arena *arena, const int64_t *plan, int64_t touched,
                                            const float *removed_positions, unsigned int *error, lrk_stream_t stream) {
   return launch_compact<true>(arena, plan, touched, removed_positions, error, stream);
+}
+
+extern "C" int lrk_arena_evict(const lrk_arena *arena, const int64_t *heads, const float *removed_positions,
+                               int64_t count, unsigned int *error, lrk_stream_t stream) {
+  clear_error();
+  int64_t element = 0;
+  int status = check_arena(arena, &element);
+  if (status != LRK_OK) return status;
+  LRK_REQUIRE(count >= 0, "invalid batch size");
+  if (count == 0 || arena->heads_total == 0) return LRK_OK;
+  LRK_REQUIRE(heads && removed_positions, "null pointer");
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(arena->heads_total, 65535));
+  arena_evict_kernel<<<blocks, kCompactThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      param(*arena, element), heads, removed_positions, count, error);
+  return launch_status("lrk_arena_evict");
 }

@@ -744,6 +744,40 @@ torch::Tensor arena_compact_positions(torch::Tensor keys, torch::Tensor values, 
   return flag;
 }
 
+// Lazy eviction batch: heads int64 [n], removed float32 [n] (any order).
+// Writes the device error flag into `flag` (int32 [1], the caller's).
+void arena_evict(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor lengths,
+                 torch::Tensor heads, torch::Tensor removed, torch::Tensor flag) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  for (const auto &tensor : {heads, removed, flag}) check_cuda(tensor, keys);
+  TORCH_CHECK(heads.scalar_type() == at::kLong && removed.scalar_type() == at::kFloat && heads.dim() == 1 &&
+                  removed.sizes() == heads.sizes(),
+              "heads int64 [n] and removed float32 [n]");
+  TORCH_CHECK(flag.scalar_type() == at::kInt && flag.numel() >= 1, "flag must be int32");
+  c10::cuda::CUDAGuard guard(keys.device());
+  check_status(lrk_arena_evict(&a, heads.data_ptr<int64_t>(), removed.data_ptr<float>(), heads.numel(),
+                               reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+}
+
+// arena_append writing its overflow flag into the caller's `flag` (no
+// allocation per call).
+void arena_append_into(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor lengths,
+                       int64_t first_head, torch::Tensor new_keys, torch::Tensor new_values, double position,
+                       torch::Tensor flag) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  check_cuda(new_keys, keys);
+  check_cuda(new_values, keys);
+  check_cuda(flag, keys);
+  TORCH_CHECK(new_keys.scalar_type() == keys.scalar_type() && new_values.scalar_type() == keys.scalar_type() &&
+                  new_keys.numel() == new_values.numel() && new_keys.numel() % keys.size(2) == 0,
+              "new rows must be [heads, dimension] of the arena dtype");
+  TORCH_CHECK(flag.scalar_type() == at::kInt && flag.numel() >= 1, "flag must be int32");
+  c10::cuda::CUDAGuard guard(keys.device());
+  check_status(lrk_arena_append(&a, first_head, new_keys.numel() / keys.size(2), new_keys.data_ptr(),
+                                new_values.data_ptr(), static_cast<float>(position),
+                                reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -773,4 +807,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("arena_append", &arena_append);
   module.def("arena_compact", &arena_compact);
   module.def("arena_compact_positions", &arena_compact_positions);
+  module.def("arena_evict", &arena_evict);
+  module.def("arena_append_into", &arena_append_into);
 }

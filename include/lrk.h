@@ -431,6 +431,14 @@ int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touch
 int lrk_arena_compact_positions(const lrk_arena *arena, const int64_t *plan, int64_t touched,
                                 const float *removed_positions, unsigned int *error, lrk_stream_t stream);
 
+/* A lazy eviction batch as it leaves the queue: heads [count] (i64: layer x
+ * heads + head) and removed_positions [count] (f32 logical positions), in any
+ * order, device memory.  Each head collects, sorts and removes its own
+ * entries in one launch (up to 2048 per head; more, a duplicate or a position
+ * the head does not hold leave that head unchanged and set *error). */
+int lrk_arena_evict(const lrk_arena *arena, const int64_t *heads, const float *removed_positions, int64_t count,
+                    unsigned int *error, lrk_stream_t stream);
+
 /* ---------------------------------------------- layer-group selection */
 
 /* The request-wide "k smallest raw scores" when one request's layers are

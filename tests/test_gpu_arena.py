@@ -227,3 +227,54 @@ def test_arena_c_abi_and_error_flags(cuda):
                                                           lengths.data_ptr(), heads, cap, 3, abi.BF16)),
                                    plan.data_ptr(), 1, removed.data_ptr(), None, stream)
     assert status == abi.ERR_INVALID  # rows of 6 bytes: not a multiple of 16
+
+
+def test_arena_evict_unsorted_batch_c_abi(cuda):
+    """lrk_arena_evict takes a lazy batch in queue order (unsorted, heads
+    interleaved): the result equals removing the same rows with
+    lrk_arena_compact; a duplicate or an absent position leaves its head
+    unchanged and sets the error flag."""
+    import ctypes
+
+    import torch
+
+    from code_for_iclr27_b200 import abi
+
+    lib = abi.library()
+    heads, cap, dim = 4, 64, 64
+    g = torch.Generator().manual_seed(12)
+
+    def fresh():
+        keys = torch.randn(heads, cap, dim, generator=g).to(torch.bfloat16).to(cuda)
+        positions = (torch.arange(cap, dtype=torch.float32) * 3).repeat(heads, 1).to(cuda)  # ascending, gapped
+        lengths = torch.tensor([60, 10, 0, 64], dtype=torch.int32, device=cuda)
+        return keys, keys.clone(), positions, lengths
+
+    k1, v1, p1, l1 = fresh()
+    k2, v2, p2, l2 = k1.clone(), v1.clone(), p1.clone(), l1.clone()
+    batch_heads = torch.tensor([3, 0, 3, 1, 0, 3], dtype=torch.int64, device=cuda)
+    batch_rows = torch.tensor([63, 7, 0, 9, 59, 30], dtype=torch.int64, device=cuda)
+    batch_positions = (batch_rows * 3).to(torch.float32)
+    flag = torch.zeros(1, dtype=torch.int32, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    a1 = abi.Arena(k1.data_ptr(), v1.data_ptr(), p1.data_ptr(), l1.data_ptr(), heads, cap, dim, abi.BF16)
+    abi.check(lib.lrk_arena_evict(ctypes.byref(a1), batch_heads.data_ptr(), batch_positions.data_ptr(), 6,
+                                  flag.data_ptr(), stream))
+    a2 = abi.Arena(k2.data_ptr(), v2.data_ptr(), p2.data_ptr(), l2.data_ptr(), heads, cap, dim, abi.BF16)
+    plan = torch.tensor([[0, 0, 2], [1, 2, 1], [3, 3, 3]], dtype=torch.int64, device=cuda)
+    removed = torch.tensor([7, 59, 9, 0, 30, 63], dtype=torch.int64, device=cuda)
+    abi.check(lib.lrk_arena_compact(ctypes.byref(a2), plan.data_ptr(), 3, removed.data_ptr(), None, stream))
+    torch.cuda.synchronize()
+    assert int(flag) == 0 and l1.tolist() == l2.tolist() == [58, 9, 0, 61]
+    for h, n in enumerate(l1.tolist()):
+        assert torch.equal(k1[h, :n].view(torch.int16), k2[h, :n].view(torch.int16))
+        assert torch.equal(p1[h, :n], p2[h, :n])
+    before = k1.clone()
+    for heads_bad, positions_bad in (([0, 0], [3.0, 3.0]), ([1], [4.0])):  # duplicate; absent (not a multiple of 3)
+        flag.zero_()
+        hb = torch.tensor(heads_bad, dtype=torch.int64, device=cuda)
+        pb = torch.tensor(positions_bad, dtype=torch.float32, device=cuda)
+        abi.check(lib.lrk_arena_evict(ctypes.byref(a1), hb.data_ptr(), pb.data_ptr(), len(heads_bad),
+                                      flag.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert int(flag) == 1 and l1.tolist() == [58, 9, 0, 61] and torch.equal(k1, before)
