@@ -658,12 +658,11 @@ def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier
     removed_at_audit = last.references[:first].groups()
     layers_here = len(cache.layers)
     g = torch.Generator(device=device).manual_seed(args.seed + 7)
-    new_keys = torch.randn(args.decode_steps, layers_here, 1, HEADS, 1, DIM, generator=g,
+    new_keys = torch.randn(EVICT_INTERVAL + args.decode_steps, layers_here, 1, HEADS, 1, DIM, generator=g,
                            device=device).to(torch.bfloat16)
-    barrier()
-    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d0.record()
-    for step in range(args.decode_steps):
+
+    def decode_step(step):
+        nonlocal queue, removed_at_audit
         for layer in range(layers_here):
             cache.append(layer, new_keys[step, layer], new_keys[step, layer], cache.seen_tokens)
         cache.seen_tokens += 1
@@ -674,6 +673,14 @@ def measure_cfg1(args, device, world: int, rank: int, distributed: bool, barrier
                     queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, share)
             elif len(queue) >= STAGING:
                 queue, removed_at_audit = evict_prefix(cache, queue, removed_at_audit, STAGING)
+
+    for step in range(EVICT_INTERVAL):  # warm-up: one eviction interval, untimed
+        decode_step(step)
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for step in range(EVICT_INTERVAL, EVICT_INTERVAL + args.decode_steps):
+        decode_step(step)
     d1.record()
     barrier()
     if with_e2e:
@@ -732,23 +739,31 @@ def measure_arena(args, cache, queries, qpos, gradients, margin, steps: int, war
     a1.record()
     barrier()
     layers = len(arena.head_lens)
-    new_keys = torch.randn(args.decode_steps, layers * HEADS, DIM, generator=generator,
+    new_keys = torch.randn(EVICT_INTERVAL + args.decode_steps, layers * HEADS, DIM, generator=generator,
                            device=arena.device).to(torch.bfloat16)
     # Lazy batches straight from the device queue: each slot's (head, logical
     # position) was gathered at the audit (AuditResult.lazy).
     flat, logical = last.lazy
     start = IMMEDIATE
-    barrier()
-    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d0.record()
-    for step in range(args.decode_steps):
+
+    def decode_step(step):
+        nonlocal start
         arena.append_all(new_keys[step], new_keys[step], arena.seen_tokens)
         arena.seen_tokens += 1
         if (step + 1) % EVICT_INTERVAL == 0 and start + STAGING <= flat.numel():
             arena.evict_logical(flat[start:start + STAGING], logical[start:start + STAGING])
             start += STAGING
+
+    for step in range(EVICT_INTERVAL):  # warm-up: one eviction interval, untimed
+        decode_step(step)
+    barrier()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record()
+    for step in range(EVICT_INTERVAL, EVICT_INTERVAL + args.decode_steps):
+        decode_step(step)
     d1.record()
     barrier()
+    arena.check_flags()
     return {"pass_ms": a0.elapsed_time(a1), "decode_ms": d0.elapsed_time(d1), "capacity": arena.capacity,
             "bytes": (arena.keys.numel() + arena.values.numel()) * arena.keys.element_size()
             + arena.positions.numel() * 4}
@@ -884,8 +899,10 @@ def main():
             torch.cuda.empty_cache()
     if world == 1 and not args.skip_side:
         # The other configurations' hot operators, measured on the same GPU.
-        from code_for_iclr27_b200.workloads import measure_batch_append, measure_recall
+        from code_for_iclr27_b200.workloads import measure_batch_append, measure_recall, measure_small
 
+        result["configs0"] = measure_small(device, peak_gbs=peak)
+        torch.cuda.empty_cache()
         result["batch_append"] = measure_batch_append(device)
         torch.cuda.empty_cache()
         result["recall"] = measure_recall(device)

@@ -278,32 +278,104 @@ def measure_batch_append(device, requests: int = 8, layers: int = 32, heads: int
             k, v, p = C.batch_append(ks, vs, ps, new, new, lengths, logical)
             # the caller keeps per-request views of the packed output (batch_attention.py:54-63)
             offsets = np.concatenate(([0], np.cumsum([sum(x) + heads for x in lengths])))
-            caches[layer] = [[k[offsets[r]:offsets[r + 1]] for r in range(requests)],
-                             [v[offsets[r]:offsets[r + 1]] for r in range(requests)],
-                             [p[offsets[r]:offsets[r + 1]] for r in range(requests)]]
+            active = len(lengths)
+            caches[layer] = [[k[offsets[r]:offsets[r + 1]] for r in range(active)],
+                             [v[offsets[r]:offsets[r + 1]] for r in range(active)],
+                             [p[offsets[r]:offsets[r + 1]] for r in range(active)]]
         lengths = [[n + 1 for n in row] for row in lengths]
+
+    def timed_steps():
+        times, moved = [], 0
+        for _ in range(steps):
+            rows_before = sum(sum(x) for x in lengths)
+            a, b = _events()
+            a.record()
+            step()
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b) * 1e3)
+            moved = layers * (rows_before + (rows_before + len(lengths) * heads)) * (4 * dim + 4)
+        return _median(times), moved
 
     step()
     torch.cuda.synchronize()
-    times = []
-    moved = 0
-    for _ in range(steps):
-        rows_before = sum(sum(x) for x in lengths)
-        a, b = _events()
-        a.record()
-        step()
-        b.record()
-        torch.cuda.synchronize()
-        times.append(a.elapsed_time(b) * 1e3)
-        moved = layers * (rows_before + (rows_before + requests * heads)) * (4 * dim + 4)
-    us = _median(times)
+    us, moved = timed_steps()
+    # EOS: the request with the earliest end (EOS steps uniform in [500,
+    # 8000]) retires -- batching.py:150-163 drops its cache -- and the next
+    # steps append for the others only.
+    eos = rng.integers(500, 8001, requests)
+    leaving = int(np.argmin(eos))
+    t0 = time.perf_counter()
+    for layer in range(layers):
+        for part in caches[layer]:
+            del part[leaving]
+    del lengths[leaving]
+    del logical[leaving]
+    new = new[[r for r in range(requests) if r != leaving]].contiguous()
+    retire_us = (time.perf_counter() - t0) * 1e6
+    step()
+    torch.cuda.synchronize()
+    us_after, moved_after = timed_steps()
     return {
         "config": f"configs[2]: {requests} requests, prompts U[1024, 16384] + {generated} generated rows per head, "
                   f"{layers} layers x {heads} heads x D{dim}",
         "rows_per_layer": total_rows,
         "us_per_step": us,
         "GBps": moved / (us / 1e6) / 1e9,
+        "eos": {"retired_request": leaving, "eos_step": int(eos[leaving]), "retire_host_us": retire_us,
+                "us_per_step_after": us_after, "GBps_after": moved_after / (us_after / 1e6) / 1e9,
+                "requests_after": requests - 1},
     }
+
+
+def measure_small(device, steps: int = 5, warmup: int = 3, seed: int = 11, peak_gbs=None) -> dict:
+    """one Llama-3.2-1B-shaped request (16 layers x 8 KV heads x
+    D64, GQA 4), 4096 rows per head, every row a generation row (prompt
+    lengths 0), protect_recent 32; one audit pass scores the 520,192
+    candidates, selects 301,312 (immediate 269,312 + 250 x 128 queued:
+    controller.py:148-150 with budget 2000) and evicts the immediate ones.
+    Each pass starts from the same state."""
+    import torch
+
+    from .audit import audit_pass
+    from .kvcache import PackedCache
+
+    layers, heads, groups, dim, rows, window = 16, 8, 4, 64, 4096, 250
+    slots = layers * heads
+    wall, staging = 2000 * slots, 8 * slots
+    immediate = slots * rows - (wall - staging)
+    queued = 250 * slots
+    g = torch.Generator(device=device).manual_seed(seed)
+    cache = PackedCache()
+    positions = torch.arange(rows, dtype=torch.float32, device=device).repeat(heads)
+    for _ in range(layers):
+        cache.add_layer(torch.randn(heads * rows, dim, generator=g, device=device).to(torch.bfloat16),
+                        torch.randn(heads * rows, dim, generator=g, device=device).to(torch.bfloat16),
+                        positions.clone(), [rows] * heads, [0] * heads)
+    cache.seen_tokens = rows
+    queries = [(torch.randn(window, heads * groups, dim, generator=g, device=device) * 2).to(torch.bfloat16)
+               for _ in range(layers)]
+    gradients = [torch.randn(heads * groups, dim, generator=g, device=device) / float(np.sqrt(dim))
+                 for _ in range(layers)]
+    qpos = torch.arange(rows - window, rows, dtype=torch.int64, device=device)
+    margin = torch.tensor([1.0], device=device)
+
+    def run():
+        saved = _snapshot(cache)
+        audit_pass(cache, queries, qpos, gradients, margin, immediate, queued, 32)
+        _restore(cache, saved)
+
+    with ScoreTimer() as timer:
+        elapsed = _timed_passes(run, steps, warmup, torch.cuda.synchronize, timer)
+    kernel_ms = timer.total_ms()
+    out = {"config": "configs[0]: llama-3.2-1b shape, 16 layers x 8 KV heads x D64, 4096 generation rows per head",
+           "managed_rows": slots * rows, "candidates": slots * (rows - 32), "selected": immediate + queued,
+           "evicted": immediate, "steps": steps, "warmup": warmup, "ms_per_pass": elapsed / steps,
+           "tokens_per_s": slots * rows * steps / (elapsed / 1e3),
+           "temporal_scores_GBps": timer.bytes / (kernel_ms / 1e3) / 1e9 if kernel_ms else None}
+    if peak_gbs and kernel_ms:
+        out["temporal_scores_frac"] = out["temporal_scores_GBps"] / peak_gbs
+    return out
 
 
 # ------------------------------------------------------------- configs[4]
