@@ -27,23 +27,26 @@ def _median(values):
     return values[len(values) // 2]
 
 
-def pinned_h2d_peak(device, megabytes: int = 256, repeats: int = 5) -> float:
-    """GB/s of one large contiguous copy from pinned host memory."""
+def pinned_h2d_peak(device, megabytes: int = 256, repeats: int = 10) -> dict:
+    """The host link's copy rate: `repeats` copies of one contiguous pinned
+    buffer of `megabytes` MiB to the device, each timed with CUDA events.
+    Returns the best rate (the peak) and the spread."""
     import torch
 
     host = torch.empty(megabytes << 20, dtype=torch.uint8).pin_memory()
     dest = torch.empty(megabytes << 20, dtype=torch.uint8, device=device)
     dest.copy_(host, non_blocking=True)
     torch.cuda.synchronize()
-    times = []
+    rates = []
     for _ in range(repeats):
         a, b = _events()
         a.record()
         dest.copy_(host, non_blocking=True)
         b.record()
         torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    return (megabytes << 20) / (_median(times) / 1e3) / 1e9
+        rates.append((megabytes << 20) / (a.elapsed_time(b) / 1e3) / 1e9)
+    return {"GBps": max(rates), "min_GBps": min(rates), "median_GBps": _median(rates), "copies": repeats,
+            "bytes": megabytes << 20}
 
 
 class _HostPool:
@@ -131,7 +134,8 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
             results[name] = {"event_us": _median(wall_times) * 1e3, "device_us": _median(device_times) * 1e3}
 
         # Size sweep: zero-copy gather of random rows vs one contiguous pinned copy.
-        peak = pinned_h2d_peak(device)
+        link = pinned_h2d_peak(device)
+        peak = link["GBps"]
         sweep = []
         for size in (128 << 10, 512 << 10, 2 << 20, 8 << 20, 32 << 20):
             rows = size // row_bytes
@@ -230,12 +234,15 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
                       f"{recall_rows} random rows each per event; cache {cache_rows_per_head} rows/head, "
                       f"{layers} layers x {heads} heads",
             "pinned_h2d_peak_GBps": peak,
+            "pinned_h2d_peak": link,
             "event_zero_copy_us": zero_copy_us,
             "event_zero_copy_link_GBps": link_bytes / (zero_copy_us / 1e6) / 1e9,
             "event_staged_us": results["staged"]["event_us"],
             "event_staged_device_us": results["staged"]["device_us"],
             "sweep": sweep,
-            "sweep_frac_of_peak_at_32MiB": sweep[-1]["zero_copy_gather_GBps"] / peak,
+            # A fraction above 1.05 means the peak copy was measured low: not reported.
+            "sweep_frac_of_peak_at_32MiB": (None if sweep[-1]["zero_copy_gather_GBps"] / peak > 1.05
+                                            else sweep[-1]["zero_copy_gather_GBps"] / peak),
             "merge_us_per_request_event": merge,
             "merge_GBps": merged_bytes / (merge / 1e6) / 1e9,
             "merge_layers_us_per_request_event": merge_layers,

@@ -118,6 +118,17 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
                         const float *margin, float epsilon, void *workspace, size_t workspace_bytes,
                         lrk_stream_t stream);
 
+/* Extra workspace bytes for the ratio stash of an lrk_temporal_scores call
+ * (0 for an invalid call): a workspace of
+ * lrk_temporal_scores_workspace_bytes(...) + this many bytes lets the row
+ * statistics store, for every candidate column of every row, the reference's
+ * ratio p / max(1 - p, epsilon) (csrc/scoring.cu:68-128), which the risk step
+ * then reads instead of recomputing p and the ratio per (query, group,
+ * candidate).  The scores are the same bit for bit either way.  Per segment:
+ * window x groups rows of the candidate count rounded up to 16 floats. */
+size_t lrk_temporal_scores_ratio_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
+                                       int64_t groups);
+
 /* Largest segments x window x groups one lrk_temporal_scores_static call takes
  * (one configs[1] audit: 256 heads x 250 queries x 4 groups = 256000). */
 #define LRK_STATIC_SCORE_ROWS 262144
