@@ -77,7 +77,7 @@ SIGNATURES = {
     "lrk_temporal_risk": (I32, [P, P, P, P, P, I64, I64, I64, I64, I64, F, P]),
     "lrk_pool": (I32, [P, I64, P, I64, I64, I64, P, P]),
     "lrk_temporal_scores_workspace_bytes": (SIZE, [I64, I64, I64]),
-    "lrk_temporal_scores_ratio_bytes": (SIZE, [ctypes.POINTER(ScoreSegment), I64, I64, I64]),
+    "lrk_temporal_scores_stash_bytes": (SIZE, [ctypes.POINTER(ScoreSegment), I64, I64, I64]),
     "lrk_temporal_scores": (I32, [ctypes.POINTER(ScoreSegment), I64, I32, P, I64, I64, F, P, F, P, SIZE, P]),
     "lrk_temporal_scores_static": (I32, [ctypes.POINTER(ScoreSegment), I64, I32, P, I64, I64, F, P, F, P]),
     "lrk_decision_risk": (I32, [P, P, I32, P, P, I64, I64, I64, D, F, P, P]),

@@ -49,15 +49,16 @@ constexpr int kMaxGroups = 8;
 
 struct ScoreTableParam {
   lrk_score_segment segment[kMaxScoreSegments];
-  // Ratio stash (risk from stored ratios): segment i's rows start at
-  // ratios + ratio_offset[i], each row ratio_stride(candidates) floats.
-  int64_t ratio_offset[kMaxScoreSegments];
+  // Probability stash (risk from stored candidate probabilities): segment
+  // i's rows start at stash + stash_offset[i], each row
+  // stash_stride(candidates) floats.
+  int64_t stash_offset[kMaxScoreSegments];
   int count;
 };
 
-// Floats per stored ratio row: the candidate count rounded up to 16 (64-byte
-// rows, so every row starts 16-byte aligned for 4-candidate vector loads).
-__host__ __device__ __forceinline__ int64_t ratio_stride(int64_t candidates) { return (candidates + 15) & ~int64_t{15}; }
+// Floats per stashed row: the candidate count rounded up to 16 (64-byte rows,
+// so every row starts 16-byte aligned for 4-candidate vector loads).
+__host__ __device__ __forceinline__ int64_t stash_stride(int64_t candidates) { return (candidates + 15) & ~int64_t{15}; }
 
 constexpr int kVisibilityThreads = 1024;
 
@@ -95,7 +96,9 @@ __global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTab
 
 // One CTA per (segment, query, group) row: its exact statistics (rows.cuh).
 // stats[(segment * window + query) * groups + group] = (max, denominator, projection).
-// visible may be null (every row compares key positions).
+// visible may be null (every row compares key positions).  With `stash`, the
+// row's candidate-column probabilities are stored there (risk_stash_kernel
+// reads them).
 //
 // CTAs start in grid order (x, then y), so the CTA of flattened row g asks L2
 // for the row `ahead` places later (a whole row, one bulk prefetch, when the
@@ -105,8 +108,7 @@ __global__ void __launch_bounds__(rows::kLanes, 3) stats_kernel(ScoreTableParam 
                                                              int groups, float scale, float3 *__restrict__ stats,
                                                              const int32_t *__restrict__ visible,
                                                              int64_t segment_base, int64_t rows_per_segment,
-                                                             int64_t ahead, float *__restrict__ ratios,
-                                                             float epsilon) {
+                                                             int64_t ahead, float *__restrict__ stash) {
   extern __shared__ __align__(16) unsigned char stage[];
   __shared__ float scratch[rows::kLanes];
   const int64_t row = blockIdx.x;
@@ -126,11 +128,11 @@ __global__ void __launch_bounds__(rows::kLanes, 3) stats_kernel(ScoreTableParam 
   const int64_t window = rows_per_segment / groups;
   const rows::Visibility sees{seg.key_positions, static_cast<float>(qpos[query]),
                               visible != nullptr ? visible[(segment_base + si) * window + query] : -1};
-  rows::RatioOut ratio{nullptr, seg.first, seg.last, epsilon};
-  if (ratios != nullptr) ratio.out = ratios + table.ratio_offset[si] + row * ratio_stride(seg.last - seg.first);
+  rows::CandidateOut candidates{nullptr, seg.first, seg.last};
+  if (stash != nullptr) candidates.out = stash + table.stash_offset[si] + row * stash_stride(seg.last - seg.first);
   const rows::RowResult r = rows::row_statistics<T, MODE>(
       static_cast<const T *>(seg.logits) + row * seg.logits_stride, seg.length, sees,
-      seg.projected_values + group * seg.projected_stride, scale, nullptr, stage, scratch, ratio);
+      seg.projected_values + group * seg.projected_stride, scale, nullptr, stage, scratch, candidates);
   if (threadIdx.x == 0)
     stats[(segment_base + si) * rows_per_segment + row] = make_float3(r.maximum, r.denominator, r.projection);
 }
@@ -154,7 +156,7 @@ bool rows_aligned(const ScoreTableParam &table, int n) {
 
 template <typename T>
 int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int window, int groups, float scale,
-                 float3 *stats, int32_t *visible, int64_t s0, int64_t max_length, float *ratios, float epsilon,
+                 float3 *stats, int32_t *visible, int64_t s0, int64_t max_length, float *stash,
                  cudaStream_t stream) {
   if (visible != nullptr) {
     visibility_kernel<<<n, kVisibilityThreads, 0, stream>>>(table, qpos, window, visible, s0);
@@ -169,12 +171,11 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
   if (mode == rows::kWeights) {
     if ((status = allow_shared(stats_kernel<T, rows::kWeights>, bytes)) != LRK_OK) return status;
     stats_kernel<T, rows::kWeights><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
-                                                                           visible, s0, rows_per_segment, 0, ratios,
-                                                                           epsilon);
+                                                                           visible, s0, rows_per_segment, 0, stash);
   } else if (mode == rows::kBits) {
     if ((status = allow_shared(stats_kernel<T, rows::kBits>, bytes)) != LRK_OK) return status;
     stats_kernel<T, rows::kBits><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats, visible,
-                                                                        s0, rows_per_segment, 0, ratios, epsilon);
+                                                                        s0, rows_per_segment, 0, stash);
   } else if (mode == rows::kPacked) {
     if constexpr (sizeof(T) == 2) {
       if ((status = allow_shared(stats_kernel<T, rows::kPacked>, bytes)) != LRK_OK) return status;
@@ -182,11 +183,11 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
       const int64_t ahead = 6 * static_cast<int64_t>(sm_count());
       stats_kernel<T, rows::kPacked><<<grid, rows::kLanes, bytes, stream>>>(table, qpos, groups, scale, stats,
                                                                             visible, s0, rows_per_segment, ahead,
-                                                                            ratios, epsilon);
+                                                                            stash);
     }
   } else {
     stats_kernel<T, rows::kStream><<<grid, rows::kLanes, 0, stream>>>(table, qpos, groups, scale, stats, visible,
-                                                                      s0, rows_per_segment, 0, ratios, epsilon);
+                                                                      s0, rows_per_segment, 0, stash);
   }
   return launch_status("lrk_temporal_scores statistics");
 }
@@ -509,39 +510,42 @@ __global__ void __launch_bounds__(kRiskThreads, 4) risk_vec_kernel(ScoreTablePar
   seg.scores[column - seg.first] = result;
 }
 
-// Risk from stored ratios (the row statistics' pass C wrote ratio = p /
-// max(1 - p, epsilon) for every candidate column of every row).  Per
-// candidate and query, drop = sum over g, in order, of ratio * (pv[g] -
-// projection[q, g]) -- the reference's drop with the ratio it would compute
-// (csrc/scoring.cu:68-128) -- then the drop range of each query chunk, its
-// fp64 risk and the running maximum, exactly as risk_vec_kernel folds them.
-// A CTA covers kRatioTile candidates; thread (tx, ty) owns C consecutive
-// candidates (one 4C-byte load per ratio row; C = 4, or 2 for 8 groups to
-// stay within 64 registers) and walks queries ty, ty + TY, ..., loading the
-// next query's rows while the current one computes.
-constexpr int kRatioTile = 32;
+// Risk from stashed probabilities (the row statistics' pass C stored the
+// probability of every candidate column of every row).  Per candidate and
+// query, drop = sum over g, in order, of ratio * (pv[g] - projection[q, g])
+// with ratio = p / max(1 - p, epsilon) -- the reference's drop
+// (csrc/scoring.cu:68-128) from the same p its probabilities kernel produced
+// -- then the drop range of each query chunk, its fp64 risk and the running
+// maximum, exactly as risk_vec_kernel folds them.  This skips risk_vec's
+// logits load, scale, rounding, mask, expf and first division per element.
+// A CTA covers kStashTile candidates; thread (tx, ty) owns C consecutive
+// candidates (one 4C-byte load per stashed row; C = 4, or 2 for 8 groups to
+// keep the registers in check) and walks queries ty, ty + TY, ..., loading
+// the next query's rows while the current one computes.
+constexpr int kStashTile = 32;
 
 template <int G, int C>
-__global__ void __launch_bounds__(kRiskThreads, 3) risk_ratio_kernel(ScoreTableParam table,
-                                                                  const float *__restrict__ ratios, int window,
+__global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableParam table,
+                                                                  const float *__restrict__ stash, int window,
                                                                   const float3 *__restrict__ stats,
                                                                   int64_t segment_base,
-                                                                  const float *__restrict__ margin) {
+                                                                  const float *__restrict__ margin,
+                                                                  float epsilon) {
   using Vec = typename std::conditional<C == 4, float4, float2>::type;
-  constexpr int TX = kRatioTile / C, TY = kRiskThreads / TX;
+  constexpr int TX = kStashTile / C, TY = kRiskThreads / TX;
   extern __shared__ float projection[];  // [window * G]
-  __shared__ int cell_min[kRiskChunks][kRatioTile], cell_max[kRiskChunks][kRatioTile];
-  __shared__ int cell_bad[kRiskChunks][kRatioTile];
+  __shared__ int cell_min[kRiskChunks][kStashTile], cell_max[kRiskChunks][kStashTile];
+  __shared__ int cell_bad[kRiskChunks][kStashTile];
   const lrk_score_segment &seg = table.segment[blockIdx.y];
   const int64_t count = seg.last - seg.first;
-  const int64_t tile = static_cast<int64_t>(blockIdx.x) * kRatioTile;
+  const int64_t tile = static_cast<int64_t>(blockIdx.x) * kStashTile;
   if (tile >= count) return;  // the whole CTA: nothing of this segment here
   for (int i = threadIdx.x; i < window * G; i += kRiskThreads)
     projection[i] = stats[(segment_base + blockIdx.y) * window * G + i].z;
   __syncthreads();
   const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
   const int64_t col0 = tile + tx * C;  // candidate index of this thread's first candidate
-  const int64_t stride = ratio_stride(count);
+  const int64_t stride = stash_stride(count);
   float pv[G][C];
 #pragma unroll
   for (int j = 0; j < C; ++j) {
@@ -552,20 +556,20 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_ratio_kernel(ScoreTableP
   }
   // Rows are padded to `stride` floats, so a vector past the last candidate
   // stays inside the row (its lanes are never scored).
-  const float *base = ratios + table.ratio_offset[blockIdx.y] + col0;
+  const float *base = stash + table.stash_offset[blockIdx.y] + col0;
   auto load = [&](int q, int g) -> Vec {
     return __ldcs(reinterpret_cast<const Vec *>(base + (static_cast<int64_t>(q) * G + g) * stride));
   };
   const int chunk = chunk_queries(seg, window);
   const int chunks = (window + chunk - 1) / chunk;
-  const bool leader = threadIdx.x < kRatioTile;
+  const bool leader = threadIdx.x < kStashTile;
   float result = 0.0f;
   for (int c_first = 0; c_first < chunks; c_first += kRiskChunks) {
     const int c_last = min(chunks, c_first + kRiskChunks);
-    for (int i = threadIdx.x; i < (c_last - c_first) * kRatioTile; i += kRiskThreads) {
-      cell_min[i / kRatioTile][i % kRatioTile] = ordered_key(INFINITY);
-      cell_max[i / kRatioTile][i % kRatioTile] = ordered_key(-INFINITY);
-      cell_bad[i / kRatioTile][i % kRatioTile] = 0;
+    for (int i = threadIdx.x; i < (c_last - c_first) * kStashTile; i += kRiskThreads) {
+      cell_min[i / kStashTile][i % kStashTile] = ordered_key(INFINITY);
+      cell_max[i / kStashTile][i % kStashTile] = ordered_key(-INFINITY);
+      cell_bad[i / kStashTile][i % kStashTile] = 0;
     }
     __syncthreads();
     const int q_begin = c_first * chunk, q_end = min(window, c_last * chunk);
@@ -613,9 +617,12 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_ratio_kernel(ScoreTableP
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         const float op = projection[q * G + g];
-        const float *r = reinterpret_cast<const float *>(&current[g]);
+        const float *p = reinterpret_cast<const float *>(&current[g]);
 #pragma unroll
-        for (int j = 0; j < C; ++j) drop[j] = __fadd_rn(drop[j], __fmul_rn(r[j], __fsub_rn(pv[g][j], op)));
+        for (int j = 0; j < C; ++j) {
+          const float ratio = __fdiv_rn(p[j], fmaxf(__fsub_rn(1.0f, p[j]), epsilon));
+          drop[j] = __fadd_rn(drop[j], __fmul_rn(ratio, __fsub_rn(pv[g][j], op)));
+        }
       }
 #pragma unroll
       for (int j = 0; j < C; ++j) {
@@ -645,17 +652,17 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_ratio_kernel(ScoreTableP
 }
 
 template <int G>
-int launch_risk_ratio(const ScoreTableParam &table, int n, const float *ratios, int window, const float3 *stats,
-                      int64_t s0, const float *margin, int64_t max_candidates, cudaStream_t stream) {
+int launch_risk_stash(const ScoreTableParam &table, int n, const float *stash, int window, const float3 *stats,
+                      int64_t s0, const float *margin, float epsilon, int64_t max_candidates, cudaStream_t stream) {
   const size_t shared = static_cast<size_t>(window) * G * sizeof(float);
-  auto kernel = risk_ratio_kernel<G, (G >= 8 ? 2 : 4)>;
+  auto kernel = risk_stash_kernel<G, (G >= 8 ? 2 : 4)>;
   if (shared > 16 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
     if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
-  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, kRatioTile))), n);
-  kernel<<<grid, kRiskThreads, shared, stream>>>(table, ratios, window, stats, s0, margin);
-  return launch_status("lrk_temporal_scores risk from ratios");
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, kStashTile))), n);
+  kernel<<<grid, kRiskThreads, shared, stream>>>(table, stash, window, stats, s0, margin, epsilon);
+  return launch_status("lrk_temporal_scores risk from stashed probabilities");
 }
 
 template <typename T, int G, int C>
@@ -718,28 +725,28 @@ ScoreTableParam make_table(const lrk_score_segment *segments, int64_t s0, int n)
   table.count = n;
   for (int i = 0; i < n; ++i) {
     table.segment[i] = segments[s0 + i];
-    table.ratio_offset[i] = 0;
+    table.stash_offset[i] = 0;
   }
   return table;
 }
 
-// Floats of the ratio stash for segments [s0, s0 + n): per segment, its
-// rows x ratio_stride(candidates); fills table.ratio_offset.
-int64_t ratio_layout(ScoreTableParam &table, int n, int64_t rows_per_segment) {
+// Floats of the probability stash for segments [s0, s0 + n): per segment,
+// its rows x stash_stride(candidates); fills table.stash_offset.
+int64_t stash_layout(ScoreTableParam &table, int n, int64_t rows_per_segment) {
   int64_t total = 0;
   for (int i = 0; i < n; ++i) {
-    table.ratio_offset[i] = total;
-    total += rows_per_segment * ratio_stride(table.segment[i].last - table.segment[i].first);
+    table.stash_offset[i] = total;
+    total += rows_per_segment * stash_stride(table.segment[i].last - table.segment[i].first);
   }
   return total;
 }
 
-// The ratio path serves 16-bit or f32 logits with 1, 2, 4 or 8 groups.
-bool ratio_path_supported(int groups) { return groups == 1 || groups == 2 || groups == 4 || groups == 8; }
+// The stash path serves 1, 2, 4 or 8 groups.
+bool stash_supported(int groups) { return groups == 1 || groups == 2 || groups == 4 || groups == 8; }
 
 template <typename T>
 int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window, int groups,
-                  float scale, const float *margin, float epsilon, float3 *stats, int32_t *visible, float *ratios,
+                  float scale, const float *margin, float epsilon, float3 *stats, int32_t *visible, float *stash,
                   cudaStream_t stream) {
   for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
     const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
@@ -749,20 +756,18 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
       max_length = std::max<int64_t>(max_length, table.segment[i].length);
       max_candidates = std::max<int64_t>(max_candidates, table.segment[i].last - table.segment[i].first);
     }
-    float *table_ratios = ratios != nullptr && ratio_path_supported(groups) ? ratios : nullptr;
-    if (table_ratios != nullptr) ratio_layout(table, n, static_cast<int64_t>(window) * groups);
-    int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, table_ratios,
-                                 epsilon, stream);
+    float *table_stash = stash != nullptr && stash_supported(groups) ? stash : nullptr;
+    if (table_stash != nullptr) stash_layout(table, n, static_cast<int64_t>(window) * groups);
+    int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, table_stash,
+                                 stream);
     if (status != LRK_OK) return status;
-    if (table_ratios != nullptr) {
-      status = groups == 1   ? launch_risk_ratio<1>(table, n, table_ratios, window, stats, s0, margin, max_candidates,
-                                                    stream)
-               : groups == 2 ? launch_risk_ratio<2>(table, n, table_ratios, window, stats, s0, margin,
-                                                    max_candidates, stream)
-               : groups == 4 ? launch_risk_ratio<4>(table, n, table_ratios, window, stats, s0, margin,
-                                                    max_candidates, stream)
-                             : launch_risk_ratio<8>(table, n, table_ratios, window, stats, s0, margin,
-                                                    max_candidates, stream);
+    if (table_stash != nullptr) {
+      const auto args = std::make_tuple(table, n, table_stash, window, static_cast<const float3 *>(stats), s0, margin,
+                                        epsilon, max_candidates, stream);
+      status = groups == 1   ? std::apply(launch_risk_stash<1>, args)
+               : groups == 2 ? std::apply(launch_risk_stash<2>, args)
+               : groups == 4 ? std::apply(launch_risk_stash<4>, args)
+                             : std::apply(launch_risk_stash<8>, args);
     } else {
       status = launch_risk<T>(table, n, qpos, window, groups, scale, margin, epsilon, stats, s0, stream);
     }
@@ -771,16 +776,16 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
   return LRK_OK;
 }
 
-// Bytes of the ratio stash for a call: the largest 48-segment table's rows x
-// padded candidates (tables run one after another on one stream, so they
-// share it).
-size_t ratio_bytes(const lrk_score_segment *segments, int64_t count, int64_t window, int64_t groups) {
+// Bytes of the probability stash for a call: the largest 48-segment table's
+// rows x padded candidates (tables run one after another on one stream, so
+// they share it).
+size_t stash_bytes(const lrk_score_segment *segments, int64_t count, int64_t window, int64_t groups) {
   int64_t most = 0;
   for (int64_t s0 = 0; s0 < count; s0 += kMaxScoreSegments) {
     const int n = static_cast<int>(std::min<int64_t>(kMaxScoreSegments, count - s0));
     int64_t total = 0;
     for (int i = 0; i < n; ++i)
-      total += window * groups * ratio_stride(segments[s0 + i].last - segments[s0 + i].first);
+      total += window * groups * stash_stride(segments[s0 + i].last - segments[s0 + i].first);
     most = std::max(most, total);
   }
   return static_cast<size_t>(most) * sizeof(float);
@@ -891,17 +896,17 @@ int check_score_call(const lrk_score_segment *segments, int64_t count, int64_t w
 
 int dispatch_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype, const int64_t *qpos,
                     int64_t window, int64_t groups, float scale, const float *margin, float epsilon, float3 *stats,
-                    int32_t *visible, float *ratios, lrk_stream_t stream) {
+                    int32_t *visible, float *stash, lrk_stream_t stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int w = static_cast<int>(window), g = static_cast<int>(groups);
   switch (logits_dtype) {
     case LRK_BF16:
-      return launch_scores<__nv_bfloat16>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, ratios,
+      return launch_scores<__nv_bfloat16>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, stash,
                                           s);
     case LRK_F16:
-      return launch_scores<__half>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, ratios, s);
+      return launch_scores<__half>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, stash, s);
     case LRK_F32:
-      return launch_scores<float>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, ratios, s);
+      return launch_scores<float>(segments, count, qpos, w, g, scale, margin, epsilon, stats, visible, stash, s);
     default: return fail(LRK_ERR_UNSUPPORTED, "Only FP32/FP16/BF16 scores are supported");
   }
 }
@@ -935,20 +940,20 @@ int score_risk_bf16(const lrk_score_segment *segments, int64_t count, const int6
 using namespace lrk;
 
 // Workspace: the row statistics (float3 per row), then the visible-prefix
-// lengths (int32 per segment and query); optionally, after them, the ratio
-// stash (lrk_temporal_scores_ratio_bytes).
+// lengths (int32 per segment and query); optionally, after them, the
+// probability stash (lrk_temporal_scores_stash_bytes).
 extern "C" size_t lrk_temporal_scores_workspace_bytes(int64_t segments, int64_t window, int64_t groups) {
   if (segments < 0 || window < 0 || groups < 0) return 0;
   return static_cast<size_t>(segments) * window * groups * sizeof(float3) +
          static_cast<size_t>(segments) * window * sizeof(int32_t) + 256;
 }
 
-extern "C" size_t lrk_temporal_scores_ratio_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
+extern "C" size_t lrk_temporal_scores_stash_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
                                                   int64_t groups) {
   if (segments == nullptr || count <= 0 || window <= 0 || groups <= 0) return 0;
   for (int64_t i = 0; i < count; ++i)
     if (segments[i].last < segments[i].first) return 0;
-  return ratio_bytes(segments, count, window, groups) + 256;
+  return stash_bytes(segments, count, window, groups) + 256;
 }
 
 extern "C" int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int logits_dtype,
@@ -962,16 +967,17 @@ extern "C" int lrk_temporal_scores(const lrk_score_segment *segments, int64_t co
   if (workspace == nullptr || workspace_bytes < need) return fail(LRK_ERR_WORKSPACE, "score workspace too small");
   float3 *stats = reinterpret_cast<float3 *>((reinterpret_cast<uintptr_t>(workspace) + 15) & ~uintptr_t{15});
   int32_t *visible = reinterpret_cast<int32_t *>(stats + count * window * groups);
-  // With room for the ratio stash after the base workspace, the risk reads
-  // the ratios the statistics pass stored instead of recomputing them.
-  float *ratios = nullptr;
-  const size_t extra = lrk_temporal_scores_ratio_bytes(segments, count, window, groups);
+  // With room for the probability stash after the base workspace, the risk
+  // reads the candidates' probabilities the statistics pass stored instead of
+  // recomputing them from the logits.
+  float *stash = nullptr;
+  const size_t extra = lrk_temporal_scores_stash_bytes(segments, count, window, groups);
   if (extra > 0 && workspace_bytes >= need + extra) {
     const uintptr_t at = reinterpret_cast<uintptr_t>(workspace) + need;
-    ratios = reinterpret_cast<float *>((at + 255) & ~uintptr_t{255});
+    stash = reinterpret_cast<float *>((at + 255) & ~uintptr_t{255});
   }
   return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
-                         visible, ratios, stream);
+                         visible, stash, stream);
 }
 
 extern "C" int lrk_temporal_scores_static(const lrk_score_segment *segments, int64_t count, int logits_dtype,
@@ -990,8 +996,8 @@ extern "C" int lrk_temporal_scores_static(const lrk_score_segment *segments, int
   float3 *stats = nullptr;
   status = static_scratch(&stats);
   if (status != LRK_OK) return status;
-  // No visible-prefix table and no ratio stash here: every row compares key
-  // positions and the risk recomputes its ratios.
+  // No visible-prefix table and no probability stash here: every row
+  // compares key positions and the risk recomputes its probabilities.
   return dispatch_scores(segments, count, logits_dtype, query_positions, window, groups, scale, margin, epsilon, stats,
                          nullptr, nullptr, stream);
 }

@@ -195,25 +195,22 @@ struct Visibility {
   __device__ __forceinline__ bool all(int64_t p, int n) const { return visible >= 0 && p + n <= visible; }
 };
 
-// Optional output of pass C: for the candidate columns [first, last), the
-// ratio p / max(1 - p, epsilon) of each probability p -- the per-element
-// factor of the reference's risk (csrc/scoring.cu:68-128), in its operation
-// order -- at out[p - first].  Disabled when out is null.
-struct RatioOut {
+// Optional output of pass C: the probability of every candidate column
+// [first, last) at out[p - first] -- the p the reference's risk starts from
+// (csrc/scoring.cu:68-128), so the risk step need not recompute it from the
+// logits.  Disabled when out is null.
+struct CandidateOut {
   float *out;
   int64_t first, last;
-  float epsilon;
   __device__ __forceinline__ bool wanted(int64_t p) const { return p >= first && p < last; }
-  __device__ __forceinline__ void put(int64_t p, float probability) const {
-    out[p - first] = __fdiv_rn(probability, fmaxf(__fsub_rn(1.0f, probability), epsilon));
-  }
+  __device__ __forceinline__ void put(int64_t p, float probability) const { out[p - first] = probability; }
 };
 
 template <typename T>
 __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t length, const Visibility sees,
                                            const float *__restrict__ projected_values, float scale,
                                            float *__restrict__ probabilities_out, unsigned char *stage,
-                                           float *scratch, const RatioOut ratio);
+                                           float *scratch, const CandidateOut candidates);
 
 // Statistics of one row (all 256 threads call).  probabilities_out, when not
 // null, receives every probability (the drop-in operator's output).  `stage`
@@ -224,10 +221,10 @@ template <typename T, int MODE>
 __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, const Visibility sees,
                                     const float *__restrict__ projected_values, float scale,
                                     float *__restrict__ probabilities_out, unsigned char *stage, float *scratch,
-                                    const RatioOut ratio = RatioOut{nullptr, 0, 0, 1.0f}) {
+                                    const CandidateOut candidates = CandidateOut{nullptr, 0, 0}) {
   if constexpr (MODE == kPacked) {
     return row_statistics_packed<T>(row, length, sees, projected_values, scale, probabilities_out, stage, scratch,
-                                    ratio);
+                                    candidates);
   }
   using D = Dtype<T>;
   using Bits = typename D::Bits;
@@ -315,7 +312,7 @@ __device__ RowResult row_statistics(const T *__restrict__ row, int64_t length, c
     const float w = MODE == kWeights ? x_float[p] : expf(__fsub_rn(x_at(p), maximum));
     const float probability = divide(divider, w);
     if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
-    if (ratio.out != nullptr && ratio.wanted(p)) ratio.put(p, probability);
+    if (candidates.out != nullptr && candidates.wanted(p)) candidates.put(p, probability);
     projection = __fadd_rn(projection, __fmul_rn(probability, value));
   };
   int64_t p = threadIdx.x;
@@ -449,7 +446,7 @@ template <typename T>
 __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t length, const Visibility sees,
                                            const float *__restrict__ projected_values, float scale,
                                            float *__restrict__ probabilities_out, unsigned char *stage,
-                                           float *scratch, const RatioOut ratio) {
+                                           float *scratch, const CandidateOut candidates) {
   using P = Packed<T>;
   using D = Dtype<T>;
   constexpr int kBlock = 8 * kLanes;
@@ -561,7 +558,8 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
     const bool fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
     // Does this k-block (positions 2048 kb .. 2048 kb + 2047, every lane) hold
     // candidate columns?  The same answer for the whole CTA.
-    const bool ratios = ratio.out != nullptr && kb * kBlock + kBlock > ratio.first && kb * kBlock < ratio.last;
+    const bool stash = candidates.out != nullptr && kb * kBlock + kBlock > candidates.first &&
+                       kb * kBlock < candidates.last;
 #pragma unroll
     for (int v = 0; v < 4; ++v) {
       const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
@@ -572,10 +570,10 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
         __stcs(out, probability.x);
         __stcs(out + kLanes, probability.y);
       }
-      if (ratios) {
+      if (stash) {
         const int64_t p0 = threadIdx.x + (kb * 8 + 2 * v) * kLanes;
-        if (ratio.wanted(p0)) ratio.put(p0, probability.x);
-        if (ratio.wanted(p0 + kLanes)) ratio.put(p0 + kLanes, probability.y);
+        if (candidates.wanted(p0)) candidates.put(p0, probability.x);
+        if (candidates.wanted(p0 + kLanes)) candidates.put(p0 + kLanes, probability.y);
       }
       const float2 product = mul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
       projection = __fadd_rn(projection, product.x);
@@ -585,7 +583,7 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   for (int64_t p = body + threadIdx.x; p < length; p += kLanes) {
     const float probability = divide(divider, expf(__fsub_rn(D::to_float(tail[p - body]), maximum)));
     if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
-    if (ratio.out != nullptr && ratio.wanted(p)) ratio.put(p, probability);
+    if (candidates.out != nullptr && candidates.wanted(p)) candidates.put(p, probability);
     projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(projected_values + p)));
   }
   projection = tree_sum(projection, scratch);

@@ -406,7 +406,7 @@ std::vector<torch::Tensor> topk_smallest(torch::Tensor x, int64_t k) {
 torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<torch::Tensor> projected_values,
                               std::vector<torch::Tensor> key_positions, std::vector<int64_t> first,
                               std::vector<int64_t> last, torch::Tensor query_positions, torch::Tensor margin,
-                              double scale, double epsilon, std::vector<int64_t> query_chunks, bool ratio_stash) {
+                              double scale, double epsilon, std::vector<int64_t> query_chunks, bool probability_stash) {
   const size_t count = logits.size();
   TORCH_CHECK(count > 0 && projected_values.size() == count && key_positions.size() == count &&
                   first.size() == count && last.size() == count &&
@@ -457,10 +457,10 @@ torch::Tensor temporal_scores(std::vector<torch::Tensor> logits, std::vector<tor
     s.query_chunk = query_chunks.empty() ? 0 : query_chunks[i];
     offset += last[i] - first[i];
   }
-  // With the ratio stash the statistics pass stores each candidate's ratio
-  // and the risk reads it (bit-identical to recomputing it).
+  // With the probability stash the statistics pass stores each candidate's
+  // probability and the risk reads it (bit-identical to recomputing it).
   const size_t bytes = lrk_temporal_scores_workspace_bytes(static_cast<int64_t>(count), window, groups) +
-                       (ratio_stash ? lrk_temporal_scores_ratio_bytes(segments.data(), static_cast<int64_t>(count),
+                       (probability_stash ? lrk_temporal_scores_stash_bytes(segments.data(), static_cast<int64_t>(count),
                                                                       window, groups)
                                     : 0);
   auto workspace = torch::empty({static_cast<int64_t>(bytes)}, margin.options().dtype(at::kByte));
@@ -806,7 +806,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("key_positions"), pybind11::arg("first"), pybind11::arg("last"),
              pybind11::arg("query_positions"), pybind11::arg("margin"), pybind11::arg("scale"),
              pybind11::arg("epsilon"), pybind11::arg("query_chunks") = std::vector<int64_t>{},
-             pybind11::arg("ratio_stash") = true);
+             pybind11::arg("probability_stash") = true);
   module.def("project_values", &project_values);
   module.def("select_histogram", &select_histogram);
   module.def("select_pick", &select_pick);

@@ -118,15 +118,15 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
                         const float *margin, float epsilon, void *workspace, size_t workspace_bytes,
                         lrk_stream_t stream);
 
-/* Extra workspace bytes for the ratio stash of an lrk_temporal_scores call
- * (0 for an invalid call): a workspace of
- * lrk_temporal_scores_workspace_bytes(...) + this many bytes lets the row
- * statistics store, for every candidate column of every row, the reference's
- * ratio p / max(1 - p, epsilon) (csrc/scoring.cu:68-128), which the risk step
- * then reads instead of recomputing p and the ratio per (query, group,
- * candidate).  The scores are the same bit for bit either way.  Per segment:
- * window x groups rows of the candidate count rounded up to 16 floats. */
-size_t lrk_temporal_scores_ratio_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
+/* Extra workspace bytes for the probability stash of an lrk_temporal_scores
+ * call (0 for an invalid call): with a workspace of
+ * lrk_temporal_scores_workspace_bytes(...) + this many bytes, the row
+ * statistics store the probability p of every candidate column of every row,
+ * and the risk step (csrc/scoring.cu:68-128) reads p instead of recomputing
+ * it from the logits (scale, round, mask, expf, division).  The scores are
+ * the same bit for bit either way.  Per segment: window x groups rows of the
+ * candidate count rounded up to 16 floats. */
+size_t lrk_temporal_scores_stash_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
                                        int64_t groups);
 
 /* Largest segments x window x groups one lrk_temporal_scores_static call takes

@@ -1,9 +1,8 @@
-"""The ratio stash of lrk_temporal_scores against recomputing the ratios.
+"""The probability stash of lrk_temporal_scores against recomputing.
 
 With room for it in the workspace, the row statistics store every candidate's
-ratio p / max(1 - p, epsilon) and the risk step reads it; without, the risk
-step recomputes p and the ratio from the logits (risk_vec_kernel /
-risk_kernel).  Both must give the same scores bit for bit, NaN in the same
+probability p and the risk step reads it (risk_stash_kernel); without, the
+risk step recomputes p from the logits (risk_vec_kernel / risk_kernel).  Both must give the same scores bit for bit, NaN in the same
 places, across the staging modes of the statistics (fp32 weights below 18k
 keys, the lane-major packed stage above, the logits dtype for unaligned rows,
 f16 and f32 logits), every group count, masked keys and queries, query
@@ -46,7 +45,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("dtype_name,window,groups,length,first,last,stride,chunk,masked", CASES)
-def test_ratio_stash_equals_recomputed_risk(C, cuda, dtype_name, window, groups, length, first, last, stride, chunk,
+def test_probability_stash_equals_recomputed_risk(C, cuda, dtype_name, window, groups, length, first, last, stride, chunk,
                                             masked):
     import torch
 
@@ -71,13 +70,13 @@ def test_ratio_stash_equals_recomputed_risk(C, cuda, dtype_name, window, groups,
     margin = torch.tensor([0.8], device=cuda)
     chunks = [chunk] * heads
     stash = C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, 1 / math.sqrt(128), 1e-6, chunks,
-                              ratio_stash=True)
+                              probability_stash=True)
     recomputed = C.temporal_scores(logits, pvs, kpos, firsts, lasts, qpos, margin, 1 / math.sqrt(128), 1e-6, chunks,
-                                   ratio_stash=False)
+                                   probability_stash=False)
     same(stash, recomputed)
 
 
-def test_ratio_stash_many_segments(C, cuda):
+def test_probability_stash_many_segments(C, cuda):
     """60 segments (two tables of 48), short heads of assorted lengths."""
     import torch
 
@@ -93,4 +92,4 @@ def test_ratio_stash_many_segments(C, cuda):
     qpos = torch.arange(900, 916, dtype=torch.int64, device=cuda)
     margin = torch.tensor([1.1], device=cuda)
     args = (logits, pvs, kpos, firsts, lasts, qpos, margin, 0.125, 1e-6, [5] * 60)
-    same(C.temporal_scores(*args, ratio_stash=True), C.temporal_scores(*args, ratio_stash=False))
+    same(C.temporal_scores(*args, probability_stash=True), C.temporal_scores(*args, probability_stash=False))
