@@ -434,6 +434,43 @@ __device__ __forceinline__ uint32_t word(const uint4 &v, int i) {
 // and C touch 8 distinct bank groups per quarter-warp.
 __device__ __forceinline__ int chunk_slot(int lane) { return lane ^ ((lane >> 3) & 7); }
 
+// Pass C of the packed stage for one 8-element chunk of one lane (k-block
+// kb): x - max, expf, the division, the optional outputs, and the projection
+// sum in lane order.  STORE compiles in the store of every probability (the
+// drop-in probabilities operator), STASH the candidate stash.
+template <typename P, bool STORE, bool STASH>
+__device__ __forceinline__ void packed_chunk(const uint4 chunk, int64_t kb, const float2 minus_max,
+                                             const Divider &divider, const float (&current)[8],
+                                             float *__restrict__ probabilities_out, const CandidateOut &candidates,
+                                             float &projection) {
+  // One operand test for the chunk's 8 divisions: its smallest x (NaN if
+  // any is NaN) minus max at or above kFastExponentFloor puts every weight
+  // in [2^-60, 1] (x - max rounds monotonically in x, and x <= max).
+  const uint32_t lowest = P::min_nan(P::min_nan(word(chunk, 0), word(chunk, 1)),
+                                     P::min_nan(word(chunk, 2), word(chunk, 3)));
+  const float2 lowest_d = add2_rn(P::unpack(lowest), minus_max);
+  const bool fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
+    const float2 w = make_float2(expf(d.x), expf(d.y));
+    const float2 probability = fast ? divide2_fast(divider, w) : make_float2(divide(divider, w.x), divide(divider, w.y));
+    if constexpr (STORE) {
+      float *out = probabilities_out + threadIdx.x + (kb * 8 + 2 * v) * kLanes;
+      __stcs(out, probability.x);
+      __stcs(out + kLanes, probability.y);
+    }
+    if constexpr (STASH) {
+      const int64_t p0 = threadIdx.x + (kb * 8 + 2 * v) * kLanes;
+      if (candidates.wanted(p0)) candidates.put(p0, probability.x);
+      if (candidates.wanted(p0 + kLanes)) candidates.put(p0 + kLanes, probability.y);
+    }
+    const float2 product = mul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
+    projection = __fadd_rn(projection, product.x);
+    projection = __fadd_rn(projection, product.y);
+  }
+}
+
 // row_statistics for MODE == kPacked: 16-bit logits, row 16-byte aligned.
 // Stage layout: k-blocks of 8 x 256 elements; lane t's elements t + 256 k,
 // k = 8 kb .. 8 kb + 7, sit in order in chunk kb * 256 + chunk_slot(t).  The
@@ -548,36 +585,20 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
 #pragma unroll
       for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
     }
-    const uint4 chunk = chunks[kb * kLanes + slot];
-    // One operand test for the chunk's 8 divisions: its smallest x (NaN if
-    // any is NaN) minus max at or above kFastExponentFloor puts every weight
-    // in [2^-60, 1] (x - max rounds monotonically in x, and x <= max).
-    const uint32_t lowest = P::min_nan(P::min_nan(word(chunk, 0), word(chunk, 1)),
-                                       P::min_nan(word(chunk, 2), word(chunk, 3)));
-    const float2 lowest_d = add2_rn(P::unpack(lowest), minus_max);
-    const bool fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
-    // Does this k-block (positions 2048 kb .. 2048 kb + 2047, every lane) hold
-    // candidate columns?  The same answer for the whole CTA.
+    // The chunk body comes in two compiled forms: with the candidate stash
+    // (k-blocks -- positions 2048 kb .. 2048 kb + 2047 of every lane -- that
+    // hold candidate columns; the same answer for the whole CTA) and without,
+    // so the blocks without candidates run the plain loop.
     const bool stash = candidates.out != nullptr && kb * kBlock + kBlock > candidates.first &&
                        kb * kBlock < candidates.last;
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
-      const float2 w = make_float2(expf(d.x), expf(d.y));
-      const float2 probability = fast ? divide2_fast(divider, w) : make_float2(divide(divider, w.x), divide(divider, w.y));
-      if (probabilities_out != nullptr) {
-        float *out = probabilities_out + threadIdx.x + (kb * 8 + 2 * v) * kLanes;
-        __stcs(out, probability.x);
-        __stcs(out + kLanes, probability.y);
-      }
-      if (stash) {
-        const int64_t p0 = threadIdx.x + (kb * 8 + 2 * v) * kLanes;
-        if (candidates.wanted(p0)) candidates.put(p0, probability.x);
-        if (candidates.wanted(p0 + kLanes)) candidates.put(p0 + kLanes, probability.y);
-      }
-      const float2 product = mul2_rn(probability, make_float2(current[2 * v], current[2 * v + 1]));
-      projection = __fadd_rn(projection, product.x);
-      projection = __fadd_rn(projection, product.y);
+    const uint4 chunk = chunks[kb * kLanes + slot];
+    if (probabilities_out != nullptr) {
+      packed_chunk<P, true, false>(chunk, kb, minus_max, divider, current, probabilities_out, candidates, projection);
+    } else if (stash) {
+      packed_chunk<P, false, true>(chunk, kb, minus_max, divider, current, probabilities_out, candidates, projection);
+    } else {
+      packed_chunk<P, false, false>(chunk, kb, minus_max, divider, current, probabilities_out, candidates,
+                                    projection);
     }
   }
   for (int64_t p = body + threadIdx.x; p < length; p += kLanes) {

@@ -18,6 +18,11 @@ CASE is one of:
   large_pass     one configs[4] audit pass of one 70B-shaped request (80 layers x
                  8 heads x 32768 rows, GQA 8; score, Pool7, select 18.6M,
                  evict 18.4M), the layer tensors put back after each pass
+  arena_evict    one lazy eviction batch (2048 references over 128 heads of
+                 ~34,900 rows, D=128) in a 16-layer KV arena (lrk_arena_evict),
+                 the slots refilled between iterations
+  select         one layer-group selection round-0 histogram over 8 requests x
+                 2.6M scores (lrk_select_histogram, two questions)
 Inputs are seeded and generated on the device; each iteration launches the
 operator once (large_pass: one whole audit pass).
 """
@@ -33,7 +38,7 @@ def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
                                            "project", "logits", "logits_odd", "logits_layer", "from_keys",
-                                           "table_fused", "large_pass"])
+                                           "table_fused", "large_pass", "arena_evict", "select"])
     parser.add_argument("--iters", type=int, default=3)
     args = parser.parse_args(argv)
 
@@ -127,6 +132,29 @@ def main(argv=None):
             saved = _snapshot(cache)
             audit_pass(cache, queries, qpos, gradients, margin, counts["immediate"], counts["queued"], LARGE_PROTECT)
             _restore(cache, saved)
+    elif args.case == "arena_evict":
+        from .arena import ArenaCache
+
+        layers, heads, rows = 16, 8, 34900
+        arena = ArenaCache(layers, heads, 128, rows + 256, dev)
+        arena.keys.normal_(generator=g)
+        arena.values.normal_(generator=g)
+        arena.positions.copy_(torch.arange(rows + 256, dtype=torch.float32, device=dev).expand_as(arena.positions))
+        full = torch.full((layers * heads,), rows, dtype=torch.int32, device=dev)
+        picks = torch.randperm(layers * heads * 2100, generator=g, device=dev)[:2048]
+        flat = (picks // 2100).to(torch.int64)
+        logical = (picks % 2100 + 32768).to(torch.float32)
+
+        def run():
+            arena.lengths.copy_(full)  # the removed rows come back (their positions never moved out of range)
+            arena.positions.copy_(torch.arange(rows + 256, dtype=torch.float32, device=dev).expand_as(arena.positions))
+            C.arena_evict(arena.keys, arena.values, arena.positions, arena.lengths, flat, logical, arena.flags[1:2])
+    elif args.case == "select":
+        requests, n = 8, 2_618_880
+        tables = [torch.rand(n, generator=g, device=dev) for _ in range(requests)]
+        states = torch.zeros(requests, 2, 8, dtype=torch.int64, device=dev)
+        states[:, 0, 0], states[:, 1, 0] = 2_322_080, 2_302_080
+        run = lambda: C.select_histogram(tables, states, 0)
     elif args.case == "project":
         values = torch.randn(LAYER_ROWS, 128, generator=g, device=dev).to(torch.bfloat16)
         gradients = torch.randn(8 * 4, 128, generator=g, device=dev)
