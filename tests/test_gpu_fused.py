@@ -93,6 +93,10 @@ CASES = [
     ("bf16", 7, 4, 20008, 100, 20000),
     ("f16", 5, 2, 40000, 0, 40000),
     ("bf16", 3, 4, 100000, 99000, 100000),
+    # aligned rows of 18,433 .. 36,864 keys: the two-CTA cluster statistics
+    ("bf16", 5, 4, 36864, 100, 36000),
+    ("bf16", 6, 8, 18440, 0, 18440),
+    ("f16", 4, 2, 25600, 25000, 25600),
 ]
 
 
