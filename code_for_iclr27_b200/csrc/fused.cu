@@ -27,7 +27,6 @@
 // convex R, so the maximum over chunks is the risk over all queries.
 // Many (layer, head) segments go in one launch: their descriptors travel as a
 // kernel parameter (up to kMaxScoreSegments per launch).
-#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -138,197 +137,6 @@ __global__ void __launch_bounds__(rows::kLanes, 3) stats_kernel(ScoreTableParam 
     stats[(segment_base + si) * rows_per_segment + row] = make_float3(r.maximum, r.denominator, r.projection);
 }
 
-// Row statistics with the weights kept for pass C, for 16-bit logits in
-// 16-byte aligned rows of up to kPairMax keys: a cluster of two CTAs of 128
-// threads per row.  CTA r owns the reference's lanes 128 r .. 128 r + 127,
-// i.e. the positions p with p mod 256 in that range, and stages them as
-// fp32 in shared memory as [k][lane] (position 256 k + 128 r + lane), so a
-// row's 140 KB of weights at 35k keys is 70 KB per CTA and three CTAs fit an
-// SM.  Pass A loads 16-byte vectors (8 consecutive lanes of one k), scales,
-// rounds, masks and stages them; the row max meets over distributed shared
-// memory.  Pass B replaces each x by w = expf(x - max) in place and sums its
-// lane in order; pass C divides the stored w (no second expf) and sums the
-// projection.  The reference's 256-wide tree starts with lane t + lane
-// t + 128, which is exactly one value from each CTA: the CTAs exchange their
-// 128 lane sums through distributed shared memory and both finish the tree
-// over 128 values, so both hold the same denominator and projection.  Every
-// element keeps the reference's operations and order (consecutive k of a lane
-// are paired only for the float2 forms of the same IEEE operations).
-constexpr int kPairThreads = 128;
-constexpr int64_t kPairMax = 144 * 256;  // rows of up to 36,864 keys (72 KB of weights per CTA)
-
-// The reference's pairwise tree from s = 64 down over 128 values (all 128
-// threads call; tree holds 128 floats).
-__device__ __forceinline__ float tree_sum_128(float value, float *tree) {
-  tree[threadIdx.x] = value;
-  __syncthreads();
-  if (threadIdx.x < 64) tree[threadIdx.x] = __fadd_rn(tree[threadIdx.x], tree[threadIdx.x + 64]);
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = __fadd_rn(tree[threadIdx.x], tree[threadIdx.x + 32]);
-#pragma unroll
-    for (int s = 16; s > 0; s >>= 1) {
-      const float other = __shfl_down_sync(0xffffffffu, v, s);
-      if (threadIdx.x < s) v = __fadd_rn(v, other);
-    }
-    if (threadIdx.x == 0) tree[0] = v;
-  }
-  __syncthreads();
-  const float result = tree[0];
-  __syncthreads();
-  return result;
-}
-
-template <typename T>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 3) stats_pair_kernel(
-    ScoreTableParam table, const int64_t *__restrict__ qpos, int groups, float scale, float3 *__restrict__ stats,
-    const int32_t *__restrict__ visible, int64_t segment_base, int64_t rows_per_segment, int64_t ahead,
-    float *__restrict__ stash) {
-  namespace cg = cooperative_groups;
-  using P = rows::Packed<T>;
-  extern __shared__ __align__(16) float w[];  // [k][128]
-  __shared__ float tree[kPairThreads];
-  __shared__ float warp_max[kPairThreads / 32];
-  __shared__ float exchange_max;
-  __shared__ float exchange_sum[kPairThreads], exchange_projection[kPairThreads];
-  cg::cluster_group cluster = cg::this_cluster();
-  const int rank = static_cast<int>(cluster.block_rank());
-  const int t = threadIdx.x;
-  const int64_t row = blockIdx.x >> 1;
-  const int si = blockIdx.y;
-  if (rank == 0 && t == 0 && ahead > 0) {
-    const int64_t later = si * rows_per_segment + row + ahead;
-    if (later < rows_per_segment * gridDim.y) {
-      const lrk_score_segment &next = table.segment[later / rows_per_segment];
-      const T *start = static_cast<const T *>(next.logits) + (later % rows_per_segment) * next.logits_stride;
-      const uint32_t bytes = static_cast<uint32_t>(lmin(next.length * static_cast<int64_t>(sizeof(T)), INT32_MAX)) & ~15u;
-      if (bytes > 0) asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(start), "r"(bytes) : "memory");
-    }
-  }
-  const lrk_score_segment &seg = table.segment[si];
-  const int group = static_cast<int>(row % groups);
-  const int64_t query = row / groups;
-  const int64_t window = rows_per_segment / groups;
-  const rows::Visibility sees{seg.key_positions, static_cast<float>(qpos[query]),
-                              visible != nullptr ? visible[(segment_base + si) * window + query] : -1};
-  const int64_t length = seg.length;
-  const int64_t blocks = (length + 255) / 256;  // k = 0 .. blocks - 1
-  const int64_t base = 128 * rank;              // this CTA's first lane
-  const T *in = static_cast<const T *>(seg.logits) + row * seg.logits_stride;
-  const float2 scale2 = make_float2(scale, scale);
-
-  // Pass A: vector v = (k, c) holds positions 256 k + base + 8 c .. + 7.
-  float local_max = -INFINITY;
-  const int64_t vectors = blocks * 16;
-  for (int64_t v = t; v < vectors; v += kPairThreads) {
-    const int64_t k = v >> 4;
-    const int c = static_cast<int>(v & 15);
-    const int64_t p0 = 256 * k + base + 8 * c;
-    uint4 raw;
-    if (p0 + 8 <= length) {
-      raw = __ldcs(reinterpret_cast<const uint4 *>(in + p0));
-    } else {
-      unsigned short e[8];
-      const unsigned short *bits = reinterpret_cast<const unsigned short *>(in);
-#pragma unroll
-      for (int m = 0; m < 8; ++m) e[m] = p0 + m < length ? bits[p0 + m] : 0;
-      raw = make_uint4(e[0] | (uint32_t{e[1]} << 16), e[2] | (uint32_t{e[3]} << 16), e[4] | (uint32_t{e[5]} << 16),
-                       e[6] | (uint32_t{e[7]} << 16));
-    }
-    float x[8];
-    const bool all_seen = sees.all(p0, 8) && p0 + 8 <= length;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float2 pair = P::unpack(P::round(rows::mul2_rn(P::unpack(rows::word(raw, i)), scale2)));
-      x[2 * i] = pair.x;
-      x[2 * i + 1] = pair.y;
-    }
-    if (!all_seen) {
-#pragma unroll
-      for (int m = 0; m < 8; ++m)
-        if (p0 + m >= length || !sees(p0 + m)) x[m] = -INFINITY;
-    }
-#pragma unroll
-    for (int m = 0; m < 8; ++m) local_max = fmaxf(local_max, x[m]);
-    float *dst = w + k * kPairThreads + 8 * c;
-    *reinterpret_cast<float4 *>(dst) = make_float4(x[0], x[1], x[2], x[3]);
-    *reinterpret_cast<float4 *>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
-  }
-  local_max = rows::warp_max(local_max);
-  if ((t & 31) == 0) warp_max[t >> 5] = local_max;
-  __syncthreads();
-  if (t == 0)
-    exchange_max = fmaxf(fmaxf(warp_max[0], warp_max[1]), fmaxf(warp_max[2], warp_max[3]));
-  cluster.sync();
-  const float maximum = fmaxf(exchange_max, *cluster.map_shared_rank(&exchange_max, rank ^ 1));
-
-  // Pass B: lane base + t sums positions 256 k + base + t in k order.  Every
-  // k below blocks - 1 is inside the row; the last may not be.
-  const int64_t last_k = blocks - 1;
-  const bool last_inside = 256 * last_k + base + t < length;
-  const float2 minus_max = make_float2(-maximum, -maximum);
-  float sum = 0.0f;
-  int64_t k = 0;
-  for (; k + 1 < last_k; k += 2) {
-    const float2 d = rows::add2_rn(make_float2(w[k * kPairThreads + t], w[(k + 1) * kPairThreads + t]), minus_max);
-    const float e0 = expf(d.x), e1 = expf(d.y);
-    w[k * kPairThreads + t] = e0;
-    w[(k + 1) * kPairThreads + t] = e1;
-    sum = __fadd_rn(sum, e0);
-    sum = __fadd_rn(sum, e1);
-  }
-  for (; k <= last_k; ++k) {
-    if (k == last_k && !last_inside) break;
-    const float e = expf(__fsub_rn(w[k * kPairThreads + t], maximum));
-    w[k * kPairThreads + t] = e;
-    sum = __fadd_rn(sum, e);
-  }
-  exchange_sum[t] = sum;
-  cluster.sync();
-  const float denominator = tree_sum_128(__fadd_rn(sum, *cluster.map_shared_rank(&exchange_sum[t], rank ^ 1)), tree);
-
-  // Pass C: p = w / denominator from the stored weights, the candidate stash,
-  // and the projection sum in k order.
-  const rows::Divider divider = rows::make_divider(denominator);
-  const float *pv = seg.projected_values + group * seg.projected_stride + base + t;
-  rows::CandidateOut candidates{nullptr, seg.first, seg.last};
-  if (stash != nullptr) candidates.out = stash + table.stash_offset[si] + row * stash_stride(seg.last - seg.first);
-  float projection = 0.0f;
-  k = 0;
-  // The pair loop runs while k + 1 < last_k: its first pair exists when last_k >= 2.
-  float2 values = last_k >= 2 ? make_float2(__ldg(pv), __ldg(pv + 256)) : make_float2(0.0f, 0.0f);
-  for (; k + 1 < last_k; k += 2) {
-    const float2 current = values;
-    if (k + 3 < last_k) values = make_float2(__ldg(pv + 256 * (k + 2)), __ldg(pv + 256 * (k + 3)));
-    const float2 weight = make_float2(w[k * kPairThreads + t], w[(k + 1) * kPairThreads + t]);
-    const bool fast = divider.fast && weight.x >= 8.673617379884035e-19f && weight.y >= 8.673617379884035e-19f;
-    const float2 probability = fast ? rows::divide2_fast(divider, weight)
-                                    : make_float2(rows::divide(divider, weight.x), rows::divide(divider, weight.y));
-    if (candidates.out != nullptr && 256 * k + 511 >= candidates.first && 256 * k < candidates.last) {
-      const int64_t p0 = 256 * k + base + t;
-      if (candidates.wanted(p0)) candidates.put(p0, probability.x);
-      if (candidates.wanted(p0 + 256)) candidates.put(p0 + 256, probability.y);
-    }
-    const float2 product = rows::mul2_rn(probability, current);
-    projection = __fadd_rn(projection, product.x);
-    projection = __fadd_rn(projection, product.y);
-  }
-  for (; k <= last_k; ++k) {
-    if (k == last_k && !last_inside) break;
-    const int64_t p = 256 * k + base + t;
-    const float probability = rows::divide(divider, w[k * kPairThreads + t]);
-    if (candidates.out != nullptr && candidates.wanted(p)) candidates.put(p, probability);
-    projection = __fadd_rn(projection, __fmul_rn(probability, __ldg(pv + 256 * k)));
-  }
-  exchange_projection[t] = projection;
-  cluster.sync();
-  const float total = tree_sum_128(
-      __fadd_rn(projection, *cluster.map_shared_rank(&exchange_projection[t], rank ^ 1)), tree);
-  if (rank == 0 && t == 0)
-    stats[(segment_base + si) * rows_per_segment + row] = make_float3(maximum, denominator, total);
-  cluster.sync();  // the peer has read this CTA's exchange buffers
-}
-
 template <typename K>
 int allow_shared(K kernel, int64_t bytes) {
   if (bytes <= 48 * 1024) return LRK_OK;
@@ -356,23 +164,8 @@ int launch_stats(const ScoreTableParam &table, int n, const int64_t *qpos, int w
     if (status != LRK_OK) return status;
   }
   const int64_t rows_per_segment = static_cast<int64_t>(window) * groups;
-  const bool aligned_rows = rows_aligned<T>(table, n);
-  if constexpr (sizeof(T) == 2) {
-    // Rows too long for fp32 weights in one CTA but short enough for two:
-    // the cluster kernel keeps the weights for pass C.
-    if (aligned_rows && max_length > rows::kWeightStageMax && max_length <= kPairMax &&
-        2 * rows_per_segment <= INT32_MAX) {
-      const int64_t bytes = ((max_length + 255) / 256) * kPairThreads * sizeof(float);
-      int status = allow_shared(stats_pair_kernel<T>, bytes);
-      if (status != LRK_OK) return status;
-      const int64_t ahead = 2 * 3 * static_cast<int64_t>(sm_count()) / 2;  // two waves of rows
-      stats_pair_kernel<T><<<dim3(static_cast<unsigned>(2 * rows_per_segment), n), kPairThreads, bytes, stream>>>(
-          table, qpos, groups, scale, stats, visible, s0, rows_per_segment, ahead, stash);
-      return launch_status("lrk_temporal_scores statistics (pairs)");
-    }
-  }
   const dim3 grid(static_cast<unsigned>(rows_per_segment), n);
-  const int mode = rows::choose_stage<T>(max_length, aligned_rows);
+  const int mode = rows::choose_stage<T>(max_length, rows_aligned<T>(table, n));
   const int64_t bytes = rows::staged_bytes<T>(mode, max_length);
   int status = LRK_OK;
   if (mode == rows::kWeights) {
