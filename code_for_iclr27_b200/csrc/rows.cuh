@@ -21,6 +21,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace lrk {
@@ -568,7 +570,11 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   const float denominator = tree_sum(sum, scratch);
 
   // Pass C: probabilities and the value projection; the next chunk's
-  // projected values are loaded while this chunk computes.
+  // projected values are loaded while this chunk computes.  The k-blocks
+  // run as up to three loops, each with one compiled chunk body: the
+  // candidate columns (the stash) lie in one contiguous range of k-blocks
+  // (positions 2048 kb .. 2048 kb + 2047 of every lane; the same answer for
+  // the whole CTA), and the loops before and after it carry no stash code.
   const Divider divider = make_divider(denominator);
   const float *values = projected_values + threadIdx.x;
   float projection = 0.0f;
@@ -577,29 +583,32 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
 #pragma unroll
     for (int m = 0; m < 8; ++m) next[m] = __ldg(values + m * kLanes);
   }
-  for (int64_t kb = 0; kb < blocks; ++kb) {
-    float current[8];
+  auto run = [&](int64_t kb_begin, int64_t kb_end, auto store, auto stash) {
+    constexpr bool kStore = decltype(store)::value, kStash = decltype(stash)::value;
+    for (int64_t kb = kb_begin; kb < kb_end; ++kb) {
+      float current[8];
 #pragma unroll
-    for (int m = 0; m < 8; ++m) current[m] = next[m];
-    if (kb + 1 < blocks) {
+      for (int m = 0; m < 8; ++m) current[m] = next[m];
+      if (kb + 1 < blocks) {
 #pragma unroll
-      for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
+        for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
+      }
+      packed_chunk<P, kStore, kStash>(chunks[kb * kLanes + slot], kb, minus_max, divider, current,
+                                      probabilities_out, candidates, projection);
     }
-    // The chunk body comes in two compiled forms: with the candidate stash
-    // (k-blocks -- positions 2048 kb .. 2048 kb + 2047 of every lane -- that
-    // hold candidate columns; the same answer for the whole CTA) and without,
-    // so the blocks without candidates run the plain loop.
-    const bool stash = candidates.out != nullptr && kb * kBlock + kBlock > candidates.first &&
-                       kb * kBlock < candidates.last;
-    const uint4 chunk = chunks[kb * kLanes + slot];
-    if (probabilities_out != nullptr) {
-      packed_chunk<P, true, false>(chunk, kb, minus_max, divider, current, probabilities_out, candidates, projection);
-    } else if (stash) {
-      packed_chunk<P, false, true>(chunk, kb, minus_max, divider, current, probabilities_out, candidates, projection);
-    } else {
-      packed_chunk<P, false, false>(chunk, kb, minus_max, divider, current, probabilities_out, candidates,
-                                    projection);
-    }
+  };
+  using yes = std::true_type;
+  using no = std::false_type;
+  if (probabilities_out != nullptr) {
+    run(0, blocks, yes{}, no{});
+  } else if (candidates.out != nullptr) {
+    const int64_t lo = lmin(blocks, lmax(0, candidates.first / kBlock));
+    const int64_t hi = lmin(blocks, lmax(lo, (candidates.last + kBlock - 1) / kBlock));
+    run(0, lo, no{}, no{});
+    run(lo, hi, no{}, yes{});
+    run(hi, blocks, no{}, no{});
+  } else {
+    run(0, blocks, no{}, no{});
   }
   for (int64_t p = body + threadIdx.x; p < length; p += kLanes) {
     const float probability = divide(divider, expf(__fsub_rn(D::to_float(tail[p - body]), maximum)));
