@@ -63,6 +63,12 @@ class KeySegment(ctypes.Structure):
                 ("last", I64), ("scores", P), ("query_chunk", I64)]
 
 
+class PlanLayer(ctypes.Structure):
+    """lrk_plan_layer (include/lrk.h)."""
+    _fields_ = [("positions", P), ("head_starts", P), ("recalled_positions", P), ("recalled_index", P),
+                ("recalled_starts", P), ("rows", I64), ("recalled", I64), ("mapping", P)]
+
+
 class Arena(ctypes.Structure):
     """lrk_arena (include/lrk.h)."""
     _fields_ = [("keys", P), ("values", P), ("positions", P), ("lengths", P), ("heads_total", I64),
@@ -112,6 +118,7 @@ SIGNATURES = {
     "lrk_arena_compact": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
     "lrk_arena_compact_positions": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
     "lrk_arena_evict": (I32, [ctypes.POINTER(Arena), P, P, I64, P, P]),
+    "lrk_merge_plan": (I32, [ctypes.POINTER(PlanLayer), I64, I64, P, P]),
 }
 
 _library = None

@@ -2,7 +2,7 @@
 
 liblrk.so   <- csrc/host.cu, move.cu, score.cu, select.cu, fused.cu, project.cu, logits.cu,
                logits_tc.cu, scores_tc.cu, groups.cu,
-               arena.cu (nvcc, sm_100a)
+               arena.cu, plan.cu (nvcc, sm_100a)
 _C          <- csrc/shim_C.cpp        (torch extension, links liblrk)
 _legacy_C   <- csrc/shim_legacy_C.cpp (torch extension, links liblrk)
 _host       <- csrc/shim_host.cpp     (pybind11 only, links liblrk)
@@ -46,6 +46,7 @@ CUDA_SOURCES = {
     "scores_tc.cu": ["--fmad=false"],
     "groups.cu": [],
     "arena.cu": [],
+    "plan.cu": [],
 }
 MODULES = {"_C": "shim_C.cpp", "_legacy_C": "shim_legacy_C.cpp", "_host": "shim_host.cpp"}
 EXT_SUFFIX = sysconfig.get_config_var("EXT_SUFFIX") or ".so"

@@ -783,6 +783,56 @@ void arena_append_into(torch::Tensor keys, torch::Tensor values, torch::Tensor p
                                 reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
 }
 
+// Recall merge plans of several layers on the device (recall/planning.py:34-52).
+// Per layer: positions (f32, the layer's [rows] or [rows, 1]), head_starts
+// (int32 [heads + 1]), recalled positions (f32, sorted by (head, position)),
+// their indices among the layer's recalled rows (int64), recalled_starts
+// (int32 [heads + 1]).  Returns the mappings (int64 [rows + recalled] each) and
+// the device flag (int32 [1]: bit 1 duplicate, bit 2 unsorted head).
+std::tuple<std::vector<torch::Tensor>, torch::Tensor> merge_plan(std::vector<torch::Tensor> positions,
+                                                                 std::vector<torch::Tensor> head_starts,
+                                                                 std::vector<torch::Tensor> recalled_positions,
+                                                                 std::vector<torch::Tensor> recalled_index,
+                                                                 std::vector<torch::Tensor> recalled_starts) {
+  const size_t count = positions.size();
+  TORCH_CHECK(count > 0 && head_starts.size() == count && recalled_positions.size() == count &&
+                  recalled_index.size() == count && recalled_starts.size() == count,
+              "one entry per layer in every list");
+  const auto &reference = positions[0];
+  const int64_t heads = head_starts[0].numel() - 1;
+  std::vector<lrk_plan_layer> table(count);
+  std::vector<torch::Tensor> mappings;
+  c10::cuda::CUDAGuard guard(reference.device());
+  for (size_t i = 0; i < count; ++i) {
+    for (const auto &t : {positions[i], head_starts[i], recalled_positions[i], recalled_index[i],
+                          recalled_starts[i]})
+      check_cuda(t, reference);
+    TORCH_CHECK(positions[i].scalar_type() == at::kFloat && recalled_positions[i].scalar_type() == at::kFloat,
+                "positions must be float32");
+    TORCH_CHECK(head_starts[i].scalar_type() == at::kInt && recalled_starts[i].scalar_type() == at::kInt &&
+                    head_starts[i].numel() == heads + 1 && recalled_starts[i].numel() == heads + 1,
+                "head_starts and recalled_starts must be int32 [heads + 1]");
+    TORCH_CHECK(recalled_index[i].scalar_type() == at::kLong &&
+                    recalled_index[i].numel() == recalled_positions[i].numel(),
+                "recalled_index must be int64, one per recalled position");
+    const int64_t rows = positions[i].numel(), recalled = recalled_positions[i].numel();
+    mappings.push_back(torch::empty({rows + recalled}, reference.options().dtype(at::kLong)));
+    lrk_plan_layer &l = table[i];
+    l.positions = positions[i].data_ptr<float>();
+    l.head_starts = head_starts[i].data_ptr<int32_t>();
+    l.recalled_positions = recalled_positions[i].data_ptr<float>();
+    l.recalled_index = recalled_index[i].data_ptr<int64_t>();
+    l.recalled_starts = recalled_starts[i].data_ptr<int32_t>();
+    l.rows = rows;
+    l.recalled = recalled;
+    l.mapping = mappings.back().data_ptr<int64_t>();
+  }
+  auto flag = torch::zeros({1}, reference.options().dtype(at::kInt));
+  check_status(lrk_merge_plan(table.data(), static_cast<int64_t>(count), heads,
+                              reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+  return {mappings, flag};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -815,4 +865,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("arena_compact_positions", &arena_compact_positions);
   module.def("arena_evict", &arena_evict);
   module.def("arena_append_into", &arena_append_into);
+  module.def("merge_plan", &merge_plan);
 }

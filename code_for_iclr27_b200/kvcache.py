@@ -154,11 +154,16 @@ class PackedCache:
         """Recall reinsertion (cache.py:201-253): payload [n, 2, D] (K, V rows
         on the cache's device), metadata [n, 3] of (layer, head, position).
         Every touched head's rows are merged with its recalled rows in
-        ascending position order (recall/planning.py:34-52: existing rows
-        first among equal positions is moot, duplicates are rejected); all
-        touched layers move in one lrk_merge_layers launch.  The touched
-        layers' positions come to the host in one copy and their merge maps
-        go back in one copy.  Returns the number of rows inserted."""
+        ascending position order (recall/planning.py:34-52).  The recalled
+        rows are sorted by (layer, head, position) on the host and travel in
+        one copy; the merge maps of all touched layers are planned on the
+        device (lrk_merge_plan) from the resident positions, which never come
+        to the host, and all touched layers move in one lrk_merge_layers
+        launch.  One flag word comes back before the merged tensors are
+        adopted: a duplicate identity raises ValueError with the cache
+        unchanged, and a head whose resident positions do not ascend (only a
+        caller's own add_layer can make one) is re-planned on the host.
+        Returns the number of rows inserted."""
         import torch
 
         metadata = np.asarray(metadata, dtype=np.int64).reshape(-1, 3)
@@ -167,16 +172,75 @@ class PackedCache:
         if not len(metadata):
             return 0
         touched = np.unique(metadata[:, 0]).tolist()
-        device = self.layers[touched[0]].keys.device
-        previous = torch.cat([self.layers[l].positions.reshape(-1) for l in touched]).cpu().numpy().astype(np.int64)
-        maps, selections, plans, offset = [], [], [], 0
-        for layer_index in touched:
-            layer = self.layers[layer_index]
-            rows = np.flatnonzero(metadata[:, 0] == layer_index)
-            recalled = metadata[rows]
-            old = previous[offset:offset + sum(layer.head_lens)]
-            offset += sum(layer.head_lens)
-            mapping, lengths, start = [], [], 0
+        layers = [self.layers[l] for l in touched]
+        heads = len(layers[0].head_lens)
+        if ((metadata[:, 1] < 0) | (metadata[:, 1] >= heads)).any():
+            # The reference plans no row for such an identity and fails its
+            # slot-count check after the merge; here the cache stays unchanged.
+            raise AssertionError("Recall changed logical time or inserted an incorrect slot count")
+        device = layers[0].keys.device
+        order = np.lexsort((metadata[:, 2], metadata[:, 1], metadata[:, 0]))
+        ordered = metadata[order]
+        firsts = np.searchsorted(ordered[:, 0], touched + [touched[-1] + 1]).tolist()
+        counts = np.diff(firsts)
+        starts = np.empty((len(layers), heads + 1), dtype=np.int32)
+        for i in range(len(layers)):
+            starts[i] = np.searchsorted(ordered[firsts[i]:firsts[i + 1], 1], np.arange(heads + 1))
+        bounds = np.stack([layer.bounds() for layer in layers]).astype(np.int32)
+        # One upload: payload rows in merge order, 0..max count (every layer's
+        # recalled index), recalled starts and new bounds (int32), positions (float32).
+        int32_words = np.concatenate((starts.reshape(-1), (bounds + starts).reshape(-1)))
+        int32_words = np.concatenate((int32_words, np.zeros(int32_words.size % 2, np.int32)))
+        float_words = ordered[:, 2].astype(np.float32)
+        float_words = np.concatenate((float_words, np.zeros(float_words.size % 2, np.float32)))
+        packed = np.concatenate((order, np.arange(int(counts.max()), dtype=np.int64),
+                                 int32_words.view(np.int64), float_words.view(np.int64)))
+        words = upload(packed, device)
+        n, top, table = len(order), int(counts.max()), starts.size
+        rows, index = words[:n], words[n:n + top]
+        small = words[n + top:n + top + int32_words.size // 2].view(torch.int32)
+        positions = words[n + top + int32_words.size // 2:].view(torch.float32)
+        all_starts, all_bounds = small[:table].view(len(layers), heads + 1), small[table:2 * table].view(len(layers), heads + 1)
+        recalled_positions = [positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))]
+        mappings, flag = operators().merge_plan(
+            [layer.positions for layer in layers], [layer.cumulative for layer in layers], recalled_positions,
+            [index[:int(c)] for c in counts], [all_starts[i] for i in range(len(layers))])
+        recalled_rows = payload.index_select(0, rows).contiguous()
+        keys, values, merged_positions = operators().merge_layers(
+            [layer.keys for layer in layers], [layer.values for layer in layers],
+            [layer.positions for layer in layers],
+            [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))], recalled_positions, mappings)
+        state = int(flag.item())
+        if state & 4:
+            raise RuntimeError("Cache head bounds do not match its rows")
+        if state & 1:
+            raise ValueError("Cannot merge duplicate physical KV identities")
+        if state & 2:
+            mappings = self._host_merge_plan(layers, ordered, firsts)
+            keys, values, merged_positions = operators().merge_layers(
+                [layer.keys for layer in layers], [layer.values for layer in layers],
+                [layer.positions for layer in layers],
+                [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))], recalled_positions,
+                [upload(m, device) for m in mappings])
+        new_lens = np.diff(bounds + starts, axis=1)
+        for i, layer in enumerate(layers):
+            layer.keys, layer.values, layer.positions = keys[i], values[i], merged_positions[i]
+            layer.head_lens = new_lens[i].tolist()
+            layer.cumulative = all_bounds[i]
+        return int(len(metadata))
+
+    @staticmethod
+    def _host_merge_plan(layers, ordered, firsts):
+        """recall/planning.py:34-52 on the host, for heads whose resident
+        positions do not ascend: per head, the stable argsort of the resident
+        positions followed by the recalled ones (``ordered``: the recalled
+        identities sorted by layer, head, position; ``firsts``: each layer's
+        first entry)."""
+        maps = []
+        for i, layer in enumerate(layers):
+            old = layer.positions.reshape(-1).cpu().numpy().astype(np.int64)
+            recalled = ordered[firsts[i]:firsts[i + 1]]
+            mapping, start = [], 0
             for head, length in enumerate(layer.head_lens):
                 chosen = np.flatnonzero(recalled[:, 1] == head)
                 combined = np.concatenate((old[start:start + length], recalled[chosen, 2]))
@@ -184,34 +248,9 @@ class PackedCache:
                     raise ValueError("Cannot merge duplicate physical KV identities")
                 sources = np.concatenate((np.arange(start, start + length), -chosen - 1))
                 mapping.append(sources[np.argsort(combined, kind="stable")])
-                lengths.append(int(combined.size))
                 start += length
             maps.append(np.concatenate(mapping))
-            selections.append(rows)
-            plans.append((layer_index, lengths, recalled[:, 2]))
-        sizes = [m.size for m in maps]
-        all_maps = upload(np.concatenate(maps), device)
-        all_rows = upload(np.concatenate(selections), device)
-        all_positions = upload(np.concatenate([p[2] for p in plans]).astype(np.float32), device)
-        recalled_rows = payload.index_select(0, all_rows).contiguous()
-        counts = [len(s) for s in selections]
-        firsts = np.concatenate(([0], np.cumsum(counts)))
-        map_firsts = np.concatenate(([0], np.cumsum(sizes)))
-        layers = [self.layers[l] for l in touched]
-        keys, values, positions = operators().merge_layers(
-            [layer.keys for layer in layers], [layer.values for layer in layers],
-            [layer.positions for layer in layers],
-            [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
-            [all_positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
-            [all_maps[map_firsts[i]:map_firsts[i + 1]] for i in range(len(layers))])
-        cumulative = np.zeros((len(layers), len(layers[0].head_lens) + 1), dtype=np.int32)
-        np.cumsum(np.asarray([p[1] for p in plans], dtype=np.int64), axis=1, out=cumulative[:, 1:])
-        all_cumulative = upload(cumulative, device)
-        for i, (layer, (_, lengths, _)) in enumerate(zip(layers, plans)):
-            layer.keys, layer.values, layer.positions = keys[i], values[i], positions[i]
-            layer.head_lens = lengths
-            layer.cumulative = all_cumulative[i]
-        return int(len(metadata))
+        return maps
 
     def remove_positions(self, removals: Dict[Tuple[int, int], Sequence[int]]) -> int:
         """Drop head-relative rows (cache.py:92-180, GPU branch): one sorted

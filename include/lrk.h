@@ -389,6 +389,33 @@ size_t lrk_topk_workspace_bytes(int64_t n);
 int lrk_topk_smallest(const float *x, int64_t n, int64_t k, void *workspace,
                       size_t workspace_bytes, float *values, int64_t *indices, lrk_stream_t stream);
 
+/* One layer of a recall merge plan (lrk_merge_plan). */
+typedef struct lrk_plan_layer {
+  const float *positions;          /* [rows] the layer's positions, heads back to back */
+  const int32_t *head_starts;      /* [heads + 1] the heads' row bounds (the layer's cu_seqlens) */
+  const float *recalled_positions; /* [recalled] sorted by (head, position) */
+  const int64_t *recalled_index;   /* [recalled] each one's index among the layer's recalled rows */
+  const int32_t *recalled_starts;  /* [heads + 1] each head's first entry in the two arrays above */
+  int64_t rows, recalled;
+  int64_t *mapping;                /* [rows + recalled] out: row i of the merged layer comes from
+                                      resident row mapping[i], or recalled row -mapping[i] - 1 */
+} lrk_plan_layer;
+
+/* The recall merge plan of every touched layer on the device: the mapping
+ * recall/planning.py:34-52 builds on the host after copying the positions
+ * back (src/lazy_recall/cache.py:216-217), for lrk_merge / lrk_merge_layers.
+ * Resident rows keep their order and recalled rows go in position order
+ * (the stable argsort of the combined positions, given that each head's
+ * resident positions ascend).  *flag (device, the caller zeroes it) gets bit 1
+ * if a position is recalled twice or recalled while resident (the reference
+ * refuses the merge) and bit 2 if a head's resident positions do not ascend
+ * (the host plan is then needed), bit 4 if head_starts / recalled_starts do
+ * not ascend from 0 to rows / recalled (reads and writes stay inside the
+ * layer's arrays all the same); read it before adopting the merged cache.
+ * All pointers device memory except `layers`. */
+int lrk_merge_plan(const lrk_plan_layer *layers, int64_t count, int64_t heads, unsigned int *flag,
+                   lrk_stream_t stream);
+
 /* ---------------------------------------------------------- KV arena */
 
 /* A gapped per-head KV arena: every (layer, head) owns a slot of `capacity`
