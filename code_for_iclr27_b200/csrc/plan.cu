@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(kPlanThreads) merge_plan_kernel(PlanTable tabl
       const float r = l.recalled_positions[e];
       if (e > first && !(l.recalled_positions[e - 1] < r)) atomicOr(flag, 1u);
       to = start + e + below(l.positions + start, end - start, r);
-      from = -l.recalled_index[e] - 1;
+      from = -(l.recalled_index ? l.recalled_index[e] : e) - 1;
     }
     if (to >= 0 && to < total) l.mapping[to] = from;
     else atomicOr(flag, 4u);
@@ -113,7 +113,7 @@ extern "C" int lrk_merge_plan(const lrk_plan_layer *layers, int64_t count, int64
     LRK_REQUIRE(l.rows >= 0 && l.recalled >= 0, "invalid plan layer sizes");
     LRK_REQUIRE(l.head_starts && l.recalled_starts && l.mapping, "null plan layer pointer");
     LRK_REQUIRE(l.rows == 0 || l.positions, "null positions");
-    LRK_REQUIRE(l.recalled == 0 || (l.recalled_positions && l.recalled_index), "null recalled rows");
+    LRK_REQUIRE(l.recalled == 0 || l.recalled_positions, "null recalled positions");
   }
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   for (int64_t l0 = 0; l0 < count; l0 += kPlanLayers) {

@@ -833,6 +833,87 @@ std::tuple<std::vector<torch::Tensor>, torch::Tensor> merge_plan(std::vector<tor
   return {mappings, flag};
 }
 
+// A recall event over several layers in two launches: the merge plan on the
+// device (lrk_merge_plan) and the merge (lrk_merge_layers).  recalled [n, 2,
+// D] and recalled_positions [n] hold the event's rows sorted by (layer, head,
+// position); layer i's are rows firsts[i] .. firsts[i + 1], and
+// recalled_starts[i] (int32 [layers, heads + 1], device) bounds its heads
+// within them.  Returns the merged keys, values and positions per layer
+// (views into one allocation each) and the plan's flag word (int32 [1]),
+// which the caller reads before adopting them.
+std::tuple<std::vector<torch::Tensor>, std::vector<torch::Tensor>, std::vector<torch::Tensor>, torch::Tensor>
+reinsert_layers(std::vector<torch::Tensor> keys, std::vector<torch::Tensor> values,
+                std::vector<torch::Tensor> positions, std::vector<torch::Tensor> head_starts, torch::Tensor recalled,
+                torch::Tensor recalled_positions, torch::Tensor recalled_starts, std::vector<int64_t> firsts) {
+  const size_t n = keys.size();
+  TORCH_CHECK(n > 0 && values.size() == n && positions.size() == n && head_starts.size() == n &&
+                  firsts.size() == n + 1,
+              "reinsert_layers: one tensor of each kind per layer and layers + 1 bounds");
+  const int64_t heads = head_starts[0].numel() - 1;
+  const auto dimension = keys[0].size(1);
+  for (const auto &t : {recalled, recalled_positions, recalled_starts}) check_recall_tensor(t, keys[0]);
+  TORCH_CHECK(recalled.dim() == 3 && recalled.size(1) == 2 && recalled.size(2) == dimension &&
+                  recalled.scalar_type() == keys[0].scalar_type(),
+              "Invalid recalled shape");
+  TORCH_CHECK(recalled_positions.scalar_type() == at::kFloat && recalled_positions.numel() == recalled.size(0),
+              "Invalid positions");
+  TORCH_CHECK(recalled_starts.scalar_type() == at::kInt && recalled_starts.numel() == static_cast<int64_t>(n) * (heads + 1),
+              "recalled_starts must be int32 [layers, heads + 1]");
+  TORCH_CHECK(firsts[0] == 0 && firsts[n] == recalled.size(0), "firsts must run from 0 to the recalled rows");
+  std::vector<lrk_plan_layer> plan(n);
+  std::vector<lrk_merge_layer> table(n);
+  int64_t total = 0;
+  for (size_t i = 0; i < n; ++i) {
+    for (const auto &tensor : {keys[i], values[i], positions[i], head_starts[i]}) check_recall_tensor(tensor, keys[0]);
+    TORCH_CHECK(keys[i].dim() == 2 && keys[i].size(1) == dimension && keys[i].sizes() == values[i].sizes(),
+                "Invalid K/V shape");
+    TORCH_CHECK(keys[i].scalar_type() == keys[0].scalar_type() && values[i].scalar_type() == keys[0].scalar_type(),
+                "K/V dtypes differ");
+    TORCH_CHECK(positions[i].scalar_type() == at::kFloat && positions[i].numel() == keys[i].size(0),
+                "Invalid positions");
+    TORCH_CHECK(head_starts[i].scalar_type() == at::kInt && head_starts[i].numel() == heads + 1,
+                "head_starts must be int32 [heads + 1]");
+    TORCH_CHECK(firsts[i] <= firsts[i + 1], "firsts must ascend");
+    total += keys[i].size(0) + firsts[i + 1] - firsts[i];
+  }
+  c10::cuda::CUDAGuard guard(keys[0].device());
+  auto mapping = torch::empty({total}, keys[0].options().dtype(at::kLong));
+  auto all_keys = torch::empty({total, dimension}, keys[0].options());
+  auto all_values = torch::empty_like(all_keys);
+  auto all_positions = torch::empty({total, 1}, positions[0].options());
+  auto flag = torch::zeros({1}, keys[0].options().dtype(at::kInt));
+  const int64_t row_bytes = 2 * dimension * recalled.element_size();
+  int64_t first = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const int64_t rows = keys[i].size(0), count = firsts[i + 1] - firsts[i];
+    const float *recalled_at = recalled_positions.data_ptr<float>() + firsts[i];
+    plan[i] = {positions[i].data_ptr<float>(), head_starts[i].data_ptr<int32_t>(), recalled_at, nullptr,
+               recalled_starts.data_ptr<int32_t>() + i * (heads + 1), rows, count,
+               mapping.data_ptr<int64_t>() + first};
+    table[i] = {keys[i].data_ptr(), values[i].data_ptr(), positions[i].data_ptr<float>(), rows,
+                static_cast<const char *>(recalled.data_ptr()) + firsts[i] * row_bytes, recalled_at, count,
+                mapping.data_ptr<int64_t>() + first, rows + count};
+    first += rows + count;
+  }
+  if (total) {
+    check_status(lrk_merge_plan(plan.data(), static_cast<int64_t>(n), heads,
+                                reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+    check_status(lrk_merge_layers(table.data(), static_cast<int64_t>(n), dimension, dtype_code(keys[0].scalar_type()),
+                                  all_keys.data_ptr(), all_values.data_ptr(), all_positions.data_ptr<float>(),
+                                  current_stream()));
+  }
+  std::vector<torch::Tensor> out_keys, out_values, out_positions;
+  first = 0;
+  for (size_t i = 0; i < n; ++i) {
+    const int64_t rows = keys[i].size(0) + firsts[i + 1] - firsts[i];
+    out_keys.push_back(all_keys.narrow(0, first, rows));
+    out_values.push_back(all_values.narrow(0, first, rows));
+    out_positions.push_back(all_positions.narrow(0, first, rows));
+    first += rows;
+  }
+  return {out_keys, out_values, out_positions, flag};
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
@@ -866,4 +947,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("arena_evict", &arena_evict);
   module.def("arena_append_into", &arena_append_into);
   module.def("merge_plan", &merge_plan);
+  module.def("reinsert_layers", &reinsert_layers);
 }

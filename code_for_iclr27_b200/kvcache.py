@@ -150,7 +150,7 @@ class PackedCache:
             layer.cumulative = all_cumulative[i]
         return int(offsets[-1])
 
-    def insert_payload(self, payload, metadata) -> int:
+    def insert_payload(self, payload, metadata, plan: str = "device") -> int:
         """Recall reinsertion (cache.py:201-253): payload [n, 2, D] (K, V rows
         on the cache's device), metadata [n, 3] of (layer, head, position).
         Every touched head's rows are merged with its recalled rows in
@@ -159,16 +159,20 @@ class PackedCache:
         one copy; the merge maps of all touched layers are planned on the
         device (lrk_merge_plan) from the resident positions, which never come
         to the host, and all touched layers move in one lrk_merge_layers
-        launch.  One flag word comes back before the merged tensors are
+        launch (both through _C.reinsert_layers).  One flag word comes back before the merged tensors are
         adopted: a duplicate identity raises ValueError with the cache
         unchanged, and a head whose resident positions do not ascend (only a
         caller's own add_layer can make one) is re-planned on the host.
-        Returns the number of rows inserted."""
+        ``plan="host"`` plans every layer on the host instead (the
+        reference's numpy plan after one copy of the positions).  Returns the
+        number of rows inserted."""
         import torch
 
         metadata = np.asarray(metadata, dtype=np.int64).reshape(-1, 3)
         if payload.shape[:2] != (len(metadata), 2):
             raise ValueError("Recall payload/identity shape mismatch")
+        if plan not in ("device", "host"):
+            raise ValueError(f"unknown merge plan {plan!r}")
         if not len(metadata):
             return 0
         touched = np.unique(metadata[:, 0]).tolist()
@@ -181,64 +185,70 @@ class PackedCache:
         device = layers[0].keys.device
         order = np.lexsort((metadata[:, 2], metadata[:, 1], metadata[:, 0]))
         ordered = metadata[order]
-        firsts = np.searchsorted(ordered[:, 0], touched + [touched[-1] + 1]).tolist()
-        counts = np.diff(firsts)
-        starts = np.empty((len(layers), heads + 1), dtype=np.int32)
-        for i in range(len(layers)):
-            starts[i] = np.searchsorted(ordered[firsts[i]:firsts[i + 1], 1], np.arange(heads + 1))
-        bounds = np.stack([layer.bounds() for layer in layers]).astype(np.int32)
-        # One upload: payload rows in merge order, 0..max count (every layer's
-        # recalled index), recalled starts and new bounds (int32), positions (float32).
-        int32_words = np.concatenate((starts.reshape(-1), (bounds + starts).reshape(-1)))
+        slot = np.searchsorted(touched, ordered[:, 0])  # each row's place among the touched layers
+        firsts = np.searchsorted(slot, np.arange(len(layers) + 1))
+        # Per touched layer, each head's first recalled row relative to the layer's first.
+        starts = np.searchsorted(slot * heads + ordered[:, 1], np.arange(len(layers) * (heads + 1)) -
+                                 np.repeat(np.arange(len(layers)), heads + 1)).reshape(len(layers), heads + 1)
+        starts = (starts - firsts[:-1, None]).astype(np.int32)
+        lens = np.asarray([layer.head_lens for layer in layers], dtype=np.int32)
+        new_lens = lens + np.diff(starts, axis=1)
+        bounds = np.zeros_like(starts)
+        np.cumsum(new_lens, axis=1, out=bounds[:, 1:])
+        # One upload: the payload rows in merge order, then the recalled starts
+        # and new bounds (int32), then the positions (float32).
+        int32_words = np.concatenate((starts.reshape(-1), bounds.reshape(-1)))
         int32_words = np.concatenate((int32_words, np.zeros(int32_words.size % 2, np.int32)))
         float_words = ordered[:, 2].astype(np.float32)
         float_words = np.concatenate((float_words, np.zeros(float_words.size % 2, np.float32)))
-        packed = np.concatenate((order, np.arange(int(counts.max()), dtype=np.int64),
-                                 int32_words.view(np.int64), float_words.view(np.int64)))
-        words = upload(packed, device)
-        n, top, table = len(order), int(counts.max()), starts.size
-        rows, index = words[:n], words[n:n + top]
-        small = words[n + top:n + top + int32_words.size // 2].view(torch.int32)
-        positions = words[n + top + int32_words.size // 2:].view(torch.float32)
-        all_starts, all_bounds = small[:table].view(len(layers), heads + 1), small[table:2 * table].view(len(layers), heads + 1)
-        recalled_positions = [positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))]
-        mappings, flag = operators().merge_plan(
-            [layer.positions for layer in layers], [layer.cumulative for layer in layers], recalled_positions,
-            [index[:int(c)] for c in counts], [all_starts[i] for i in range(len(layers))])
-        recalled_rows = payload.index_select(0, rows).contiguous()
-        keys, values, merged_positions = operators().merge_layers(
-            [layer.keys for layer in layers], [layer.values for layer in layers],
-            [layer.positions for layer in layers],
-            [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))], recalled_positions, mappings)
-        state = int(flag.item())
-        if state & 4:
-            raise RuntimeError("Cache head bounds do not match its rows")
-        if state & 1:
-            raise ValueError("Cannot merge duplicate physical KV identities")
-        if state & 2:
-            mappings = self._host_merge_plan(layers, ordered, firsts)
-            keys, values, merged_positions = operators().merge_layers(
-                [layer.keys for layer in layers], [layer.values for layer in layers],
-                [layer.positions for layer in layers],
-                [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))], recalled_positions,
-                [upload(m, device) for m in mappings])
-        new_lens = np.diff(bounds + starts, axis=1)
+        words = upload(np.concatenate((order, int32_words.view(np.int64), float_words.view(np.int64))), device)
+        n, table = len(order), starts.size
+        small = words[n:n + int32_words.size // 2].view(torch.int32)
+        positions = words[n + int32_words.size // 2:].view(torch.float32)[:n]
+        all_bounds = small[table:2 * table].view(len(layers), heads + 1)
+        recalled_rows = payload.index_select(0, words[:n]).contiguous()
+        args = ([layer.keys for layer in layers], [layer.values for layer in layers],
+                [layer.positions for layer in layers])
+        if plan == "host":
+            maps = self._host_merge_plan(layers, ordered, firsts)
+            merged = operators().merge_layers(
+                *args, [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
+                [positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))], [upload(m, device) for m in maps])
+        else:
+            *merged, flag = operators().reinsert_layers(
+                *args, [layer.cumulative for layer in layers], recalled_rows, positions,
+                small[:table], firsts.tolist())
+            state = int(flag.item())
+            if state & 4:
+                raise RuntimeError("Cache head bounds do not match its rows")
+            if state & 1:
+                raise ValueError("Cannot merge duplicate physical KV identities")
+            if state & 2:
+                maps = self._host_merge_plan(layers, ordered, firsts)
+                merged = operators().merge_layers(
+                    *args, [recalled_rows[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
+                    [positions[firsts[i]:firsts[i + 1]] for i in range(len(layers))],
+                    [upload(m, device) for m in maps])
         for i, layer in enumerate(layers):
-            layer.keys, layer.values, layer.positions = keys[i], values[i], merged_positions[i]
+            layer.keys, layer.values, layer.positions = merged[0][i], merged[1][i], merged[2][i]
             layer.head_lens = new_lens[i].tolist()
             layer.cumulative = all_bounds[i]
         return int(len(metadata))
 
     @staticmethod
     def _host_merge_plan(layers, ordered, firsts):
-        """recall/planning.py:34-52 on the host, for heads whose resident
-        positions do not ascend: per head, the stable argsort of the resident
+        """recall/planning.py:34-52 on the host (for heads whose resident
+        positions do not ascend, or plan="host"): per head, the stable argsort of the resident
         positions followed by the recalled ones (``ordered``: the recalled
         identities sorted by layer, head, position; ``firsts``: each layer's
         first entry)."""
+        import torch
+
         maps = []
+        resident = torch.cat([layer.positions.reshape(-1) for layer in layers]).cpu().numpy().astype(np.int64)
+        offsets = np.concatenate(([0], np.cumsum([sum(layer.head_lens) for layer in layers])))
         for i, layer in enumerate(layers):
-            old = layer.positions.reshape(-1).cpu().numpy().astype(np.int64)
+            old = resident[offsets[i]:offsets[i + 1]]
             recalled = ordered[firsts[i]:firsts[i + 1]]
             mapping, start = [], 0
             for head, length in enumerate(layer.head_lens):

@@ -245,6 +245,8 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
             merge_layers_us.append(a.elapsed_time(b) * 1e3)
         merge_layers = _median(merge_layers_us)
 
+        reinsert = measure_reinsert(device, layers, heads, dim, cache_rows_per_head, recall_rows, events, rng)
+
         link_bytes = requests * recall_rows * (4 * dim + 8)  # K, V rows + the int64 index
         zero_copy_us = results["zero_copy"]["device_us"]
         return {
@@ -266,10 +268,57 @@ def measure_recall(device, requests: int = 4, pool_rows: int = 200_000, recall_r
             "merge_GBps": merged_bytes / (merge / 1e6) / 1e9,
             "merge_layers_us_per_request_event": merge_layers,
             "merge_layers_GBps": merged_bytes / (merge_layers / 1e6) / 1e9,
+            "reinsert": reinsert,
         }
     finally:
         for pool in pools:
             pool.close()
+
+
+def measure_reinsert(device, layers, heads, dim, rows_per_head, recall_rows, events, rng) -> dict:
+    """One request's recall event end to end through PackedCache.insert_payload
+    (cache.py:201-253): `recall_rows` identities spread uniformly over
+    (layer, head), positions between resident ones, rows already on the GPU.
+    Timed on the host clock (the call returns after its one flag read), with
+    the merge plan on the device and with the host plan (the resident
+    positions of the touched layers copied to the host, numpy's stable
+    argsort per head, recall/planning.py:34-52); the cache is restored
+    between events."""
+    import torch
+
+    from .kvcache import PackedCache
+
+    g = torch.Generator(device=device).manual_seed(7)
+    cache = PackedCache()
+    lens = [rows_per_head] * heads
+    head_positions = torch.arange(rows_per_head, dtype=torch.float32, device=device) * 4
+    for _ in range(layers):
+        keys = torch.randn(heads * rows_per_head, dim, generator=g, device=device).to(torch.bfloat16)
+        values = torch.randn(heads * rows_per_head, dim, generator=g, device=device).to(torch.bfloat16)
+        cache.add_layer(keys, values, head_positions.repeat(heads), lens, [0] * heads)
+    saved = [(layer.keys, layer.values, layer.positions, list(layer.head_lens), layer.cumulative)
+             for layer in cache.layers]
+    payload = torch.randn(recall_rows, 2, dim, generator=g, device=device).to(torch.bfloat16)
+    plans = []
+    for _ in range(events + 3):
+        picks = rng.choice(layers * heads * rows_per_head, recall_rows, replace=False)
+        plans.append(np.stack((picks // (heads * rows_per_head), picks // rows_per_head % heads,
+                               picks % rows_per_head * 4 + 2), axis=1))
+    result = {"rows": recall_rows, "layers": layers, "heads": heads, "rows_per_head": rows_per_head}
+    for plan in ("device", "host"):
+        times = []
+        for i, metadata in enumerate(plans):
+            for layer, state in zip(cache.layers, saved):
+                layer.keys, layer.values, layer.positions, lens_copy, layer.cumulative = state
+                layer.head_lens = list(lens_copy)
+            torch.cuda.synchronize()
+            start = time.perf_counter()
+            cache.insert_payload(payload, metadata, plan=plan)
+            torch.cuda.synchronize()
+            if i >= 3:
+                times.append((time.perf_counter() - start) * 1e6)
+        result[f"{plan}_plan_us"] = _median(times)
+    return result
 
 
 def measure_batch_append(device, requests: int = 8, layers: int = 32, heads: int = 8, dim: int = 128,

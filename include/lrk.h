@@ -394,7 +394,8 @@ typedef struct lrk_plan_layer {
   const float *positions;          /* [rows] the layer's positions, heads back to back */
   const int32_t *head_starts;      /* [heads + 1] the heads' row bounds (the layer's cu_seqlens) */
   const float *recalled_positions; /* [recalled] sorted by (head, position) */
-  const int64_t *recalled_index;   /* [recalled] each one's index among the layer's recalled rows */
+  const int64_t *recalled_index;   /* [recalled] each one's index among the layer's recalled rows
+                                      (NULL: entry e is recalled row e) */
   const int32_t *recalled_starts;  /* [heads + 1] each head's first entry in the two arrays above */
   int64_t rows, recalled;
   int64_t *mapping;                /* [rows + recalled] out: row i of the merged layer comes from

@@ -69,7 +69,8 @@ def test_device_plan_flags():
     lengths, positions, metadata = layer_case(rng, 4, 100, 20, 2000)
     assert device_plan([(lengths, positions, metadata)])[1] == 0
     resident = metadata.copy()
-    resident[0, 2] = positions[sum(lengths[:resident[0, 1]])]  # the head's first resident position
+    head = int(np.argmax(np.asarray(lengths) > 0))
+    resident[0] = (0, head, positions[sum(lengths[:head])])  # the head's first resident position
     assert device_plan([(lengths, positions, resident)])[1] == 1
     repeated = np.concatenate((metadata, metadata[:1]))
     assert device_plan([(lengths, positions, repeated)])[1] == 1
@@ -149,3 +150,38 @@ def test_insert_payload_unsorted_heads_and_refusals():
         np.testing.assert_array_equal(layer.positions.cpu().numpy().reshape(-1), merged.astype(np.float32))
         assert layer.head_lens == list(new_lengths)
         np.testing.assert_array_equal(layer.cumulative.cpu().numpy(), np.concatenate(([0], np.cumsum(new_lengths))))
+
+
+def test_insert_payload_device_plan_equals_host_plan():
+    """The same recall event through the device plan and the host plan leaves
+    two copies of a cache bit-identical (rows, positions, lengths, bounds)."""
+    import torch
+
+    from code_for_iclr27_b200.kvcache import PackedCache
+
+    rng = np.random.default_rng(21)
+    g = torch.Generator().manual_seed(21)
+    caches = [PackedCache(), PackedCache()]
+    metadata = []
+    for layer_index in range(6):
+        lengths, positions, meta = layer_case(rng, 8, 500, 40, 20000)
+        keys = torch.randn(sum(lengths), 64, generator=g).to(torch.bfloat16).cuda()
+        values = torch.randn(sum(lengths), 64, generator=g).to(torch.bfloat16).cuda()
+        for cache in caches:
+            cache.add_layer(keys.clone(), values.clone(), torch.as_tensor(positions, dtype=torch.float32).cuda(),
+                            lengths, [0] * 8)
+        if layer_index != 3:  # an untouched layer
+            meta[:, 0] = layer_index
+            metadata.append(meta)
+    metadata = np.concatenate(metadata)
+    payload = torch.randn(len(metadata), 2, 64, generator=g).to(torch.bfloat16).cuda()
+    assert caches[0].insert_payload(payload, metadata, plan="device") == len(metadata)
+    assert caches[1].insert_payload(payload, metadata, plan="host") == len(metadata)
+    for a, b in zip(caches[0].layers, caches[1].layers):
+        assert torch.equal(a.keys.view(torch.int16), b.keys.view(torch.int16))
+        assert torch.equal(a.values.view(torch.int16), b.values.view(torch.int16))
+        assert torch.equal(a.positions, b.positions)
+        assert a.head_lens == b.head_lens
+        assert torch.equal(a.cumulative, b.cumulative)
+    with pytest.raises(ValueError):
+        caches[0].insert_payload(payload, metadata, plan="neither")
