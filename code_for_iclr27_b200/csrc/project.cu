@@ -2,14 +2,15 @@
 // against its own KV head's query-head margin gradients.
 //
 // The reference forms g V^T per head with a float32 GEMM after converting V to
-// float32 (a [G, D] x [D, L] product per head).  Here one pass reads the V rows
-// once.  16-bit values in 16-byte aligned rows take rows_kernel: D/8 lanes
-// share a row, each loading its 8 channels with one 16-byte load and holding
-// its channels' gradients for the current head in registers; the G partial
-// dot products meet in a butterfly reduce-scatter (each exchange halves the
-// values a lane carries), so a row costs about log2(D/8) + G shuffles.  Other
-// shapes take project_kernel (a warp per row, gradients in shared memory).
-// Float32 accumulation; the order of the per-row sums is this file's own.
+// float32 (a [G, D] x [D, L] product per head); at the audit's head sizes that
+// GEMM accumulates each dot product in channel order with one fused
+// multiply-add per channel.  sequential_dim_kernel (16-bit values in 16-byte
+// aligned rows, D = 64 or 128) and sequential_kernel (any other D, or
+// unaligned rows) keep that order: a thread per row, G accumulators, the
+// gradients transposed in shared memory so that one read serves the G
+// products of a channel.  project_kernel (a warp per row) serves other group
+// counts, and rows_kernel (lanes sharing a row, butterfly reduce-scatter) is a
+// build option (LRK_PROJECT_LANES); both sum in their own order.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -248,9 +249,93 @@ __global__ void __launch_bounds__(kProjectThreads) sequential_kernel(const T *__
   }
 }
 
+// sequential_kernel for 16-bit rows of DIM channels in 16-byte aligned rows:
+// the same per-channel FMA order, with the loops unrolled at compile time.
+// A thread loads its whole row (DIM / 8 16-byte vectors) before the first
+// FMA, so a row's loads overlap one another, and reads a channel's G
+// gradients with one vector load from shared memory.
+template <typename T, int G, int DIM>
+__global__ void __launch_bounds__(kProjectThreads, 2) sequential_dim_kernel(const T *__restrict__ values, int64_t rows,
+                                                                           const float *__restrict__ gradients,
+                                                                           const int32_t *__restrict__ cumulative,
+                                                                           int heads, float *__restrict__ out) {
+  static_assert(DIM % 8 == 0, "16-byte rows");
+  constexpr int kVectors = DIM / 8;
+  extern __shared__ __align__(16) float transposed[];  // [heads][DIM][G]
+  __shared__ int32_t bounds[kMaxProjectHeads + 1];
+  for (int i = threadIdx.x; i < heads * G * DIM; i += kProjectThreads) {
+    const int h = i / (G * DIM), g = (i / DIM) % G, d = i % DIM;
+    transposed[(h * DIM + d) * G + g] = gradients[i];
+  }
+  for (int i = threadIdx.x; i <= heads; i += kProjectThreads) bounds[i] = cumulative[i];
+  __syncthreads();
+  const int64_t first = bounds[0], past = bounds[heads];
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kProjectThreads + threadIdx.x; r < rows;
+       r += static_cast<int64_t>(gridDim.x) * kProjectThreads) {
+    if (r < first || r >= past) continue;
+    const uint4 *vec = reinterpret_cast<const uint4 *>(values + r * DIM);
+    uint4 raw[kVectors];
+#pragma unroll
+    for (int c = 0; c < kVectors; ++c) raw[c] = __ldcs(vec + c);
+    int lo = 0, hi = heads;  // head h with bounds[h] <= r < bounds[h + 1]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) / 2;
+      if (bounds[mid] <= r) lo = mid; else hi = mid;
+    }
+    const float *grad = transposed + lo * DIM * G;
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+#pragma unroll
+    for (int d = 0; d < DIM; ++d) {
+      float2 pair = unpack_pair<T>(word_of(raw[d / 8], (d % 8) / 2));
+      const float x = d % 2 ? pair.y : pair.x;
+      float w[G];
+      if constexpr (G % 4 == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g += 4) {
+          const float4 q = *reinterpret_cast<const float4 *>(grad + d * G + g);
+          w[g] = q.x, w[g + 1] = q.y, w[g + 2] = q.z, w[g + 3] = q.w;
+        }
+      } else if constexpr (G == 2) {
+        const float2 q = *reinterpret_cast<const float2 *>(grad + d * G);
+        w[0] = q.x, w[1] = q.y;
+      } else {
+        w[0] = grad[d];
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] = __fmaf_rn(w[g], x, acc[g]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) out[static_cast<int64_t>(g) * rows + r] = acc[g];
+  }
+}
+
+template <typename T, int G, int DIM>
+int launch_sequential_dim(const void *values, int64_t rows, const float *gradients, const int32_t *cumulative,
+                          int heads, float *out, cudaStream_t stream) {
+  const size_t shared = static_cast<size_t>(heads) * G * DIM * sizeof(float);
+  auto kernel = sequential_dim_kernel<T, G, DIM>;
+  if (shared > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
+    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+  }
+  const int grid = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(rows, kProjectThreads), static_cast<int64_t>(sm_count()) * 2)));
+  kernel<<<grid, kProjectThreads, shared, stream>>>(static_cast<const T *>(values), rows, gradients, cumulative, heads,
+                                                    out);
+  return launch_status("lrk_project_values");
+}
+
 template <typename T, int G>
 int launch_sequential(const void *values, int64_t rows, int dim, const float *gradients, const int32_t *cumulative,
                       int heads, float *out, cudaStream_t stream) {
+  if constexpr (sizeof(T) == 2) {
+    if (aligned(values, 16)) {
+      if (dim == 128) return launch_sequential_dim<T, G, 128>(values, rows, gradients, cumulative, heads, out, stream);
+      if (dim == 64) return launch_sequential_dim<T, G, 64>(values, rows, gradients, cumulative, heads, out, stream);
+    }
+  }
   const size_t shared = static_cast<size_t>(heads) * G * dim * sizeof(float);
   auto kernel = sequential_kernel<T, G>;
   if (shared > 48 * 1024) {

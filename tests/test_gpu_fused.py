@@ -340,8 +340,8 @@ def test_fused_padded_logits_rows(C, cuda, length, gap, groups):
 PROJECT_CASES = [
     (4, "bf16", 128, 0), (8, "bf16", 128, 0), (1, "f32", 128, 0), (2, "f16", 128, 0),
     (1, "bf16", 64, 0), (8, "bf16", 64, 0), (4, "f16", 256, 0), (2, "bf16", 256, 0),
-    (4, "bf16", 72, 0),    # no lane-per-row layout for D = 72: warp-per-row kernel
-    (4, "bf16", 128, 1),   # values start 2 bytes past a 16-byte boundary: warp-per-row kernel
+    (4, "bf16", 72, 0),    # D = 72: the thread-per-row kernel with runtime D
+    (4, "bf16", 128, 1),   # values start 2 bytes past a 16-byte boundary: scalar loads
 ]
 
 
@@ -369,6 +369,29 @@ def test_project_values(C, cuda, groups, dtype_name, dim, offset):
         np.testing.assert_allclose(out[:, start:start + n].double().cpu().numpy(), expect.numpy(), rtol=1e-5,
                                    atol=1e-7 * dim)
         start += n
+
+
+@pytest.mark.parametrize("dim", [64, 128])
+@pytest.mark.parametrize("groups", [1, 2, 4, 8])
+def test_project_values_unrolled_equals_runtime_dim(C, cuda, groups, dim):
+    """16-byte aligned rows of D = 64 / 128 take the unrolled kernel; rows
+    2 bytes past a boundary take the runtime-D kernel with scalar loads.  Both
+    accumulate each dot product in channel order, so the same values give the
+    same bits."""
+    import torch
+
+    g = torch.Generator(device=cuda).manual_seed(groups + dim)
+    lengths = [3000, 0, 513, 7, 2048]
+    rows = sum(lengths)
+    storage = torch.randn(rows * dim + 1, generator=g, device=cuda).to(torch.bfloat16)
+    aligned = storage[:rows * dim].view(rows, dim).clone()
+    shifted = storage[1:].view(rows, dim)
+    shifted.copy_(aligned)
+    grads = torch.randn(len(lengths) * groups, dim, generator=g, device=cuda)
+    cumulative = torch.tensor(np.concatenate(([0], np.cumsum(lengths))), dtype=torch.int32, device=cuda)
+    a = C.project_values(aligned, grads, cumulative, groups)
+    b = C.project_values(shifted, grads, cumulative, groups)
+    assert torch.equal(a, b)
 
 
 def test_project_values_equal_float32_gemm_at_configs1_shape(C, cuda):
