@@ -251,32 +251,64 @@ __global__ void __launch_bounds__(kProjectThreads) sequential_kernel(const T *__
 
 // sequential_kernel for 16-bit rows of DIM channels in 16-byte aligned rows:
 // the same per-channel FMA order, with the loops unrolled at compile time.
-// A thread loads its whole row (DIM / 8 16-byte vectors) before the first
-// FMA, so a row's loads overlap one another, and reads a channel's G
-// gradients with one vector load from shared memory.
+// A CTA stages tiles of 256 consecutive rows (one contiguous block of
+// 256 * DIM * 2 bytes) in shared memory with coalesced 16-byte loads, 16-byte
+// chunk c of row r at chunk c ^ (r & 7) of the row (so the 8 threads of a
+// quarter-warp, each reading the same chunk of its own row, touch 8
+// distinct bank groups); then each thread takes one row of the tile.  A
+// channel's G gradients are one vector read from shared memory.
+constexpr int kTileRows = kProjectThreads;
+
+template <int DIM>
+__host__ __device__ constexpr size_t sequential_tile_bytes() {
+  return static_cast<size_t>(kTileRows) * DIM * 2;
+}
+
 template <typename T, int G, int DIM>
 __global__ void __launch_bounds__(kProjectThreads, 2) sequential_dim_kernel(const T *__restrict__ values, int64_t rows,
                                                                            const float *__restrict__ gradients,
                                                                            const int32_t *__restrict__ cumulative,
                                                                            int heads, float *__restrict__ out) {
-  static_assert(DIM % 8 == 0, "16-byte rows");
-  constexpr int kVectors = DIM / 8;
-  extern __shared__ __align__(16) float transposed[];  // [heads][DIM][G]
+  static_assert(DIM % 64 == 0, "at least 8 16-byte chunks per row");
+  constexpr int kChunks = DIM / 8;
+  extern __shared__ __align__(16) unsigned char project_shared[];
+  uint4 *tile = reinterpret_cast<uint4 *>(project_shared);                                  // [kTileRows][kChunks]
+  float *transposed = reinterpret_cast<float *>(project_shared + sequential_tile_bytes<DIM>());  // [heads][DIM][G]
   __shared__ int32_t bounds[kMaxProjectHeads + 1];
   for (int i = threadIdx.x; i < heads * G * DIM; i += kProjectThreads) {
     const int h = i / (G * DIM), g = (i / DIM) % G, d = i % DIM;
     transposed[(h * DIM + d) * G + g] = gradients[i];
   }
   for (int i = threadIdx.x; i <= heads; i += kProjectThreads) bounds[i] = cumulative[i];
-  __syncthreads();
-  const int64_t first = bounds[0], past = bounds[heads];
-  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kProjectThreads + threadIdx.x; r < rows;
-       r += static_cast<int64_t>(gridDim.x) * kProjectThreads) {
-    if (r < first || r >= past) continue;
-    const uint4 *vec = reinterpret_cast<const uint4 *>(values + r * DIM);
-    uint4 raw[kVectors];
+  const uint4 *source = reinterpret_cast<const uint4 *>(values);
+  const int64_t tiles = (rows + kTileRows - 1) / kTileRows;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t r0 = t * kTileRows;
+    const int in_tile = static_cast<int>(lmin(kTileRows, rows - r0));
+    __syncthreads();  // the previous tile's reads (and the set-up above) are done
+    const uint4 *block = source + r0 * kChunks;
+    if (in_tile == kTileRows) {
+      // All of the thread's kChunks loads in flight at once, then the stores.
+      uint4 staged[kChunks];
 #pragma unroll
-    for (int c = 0; c < kVectors; ++c) raw[c] = __ldcs(vec + c);
+      for (int u = 0; u < kChunks; ++u) staged[u] = __ldcs(block + threadIdx.x + u * kProjectThreads);
+#pragma unroll
+      for (int u = 0; u < kChunks; ++u) {
+        const int v = threadIdx.x + u * kProjectThreads, row = v / kChunks, c = v % kChunks;
+        tile[row * kChunks + (c ^ (row & 7))] = staged[u];
+      }
+    } else {
+      for (int v = threadIdx.x; v < in_tile * kChunks; v += kProjectThreads) {
+        const int row = v / kChunks, c = v % kChunks;
+        tile[row * kChunks + (c ^ (row & 7))] = __ldcs(block + v);
+      }
+    }
+    __syncthreads();
+    const int64_t r = r0 + threadIdx.x;
+    if (threadIdx.x >= in_tile || r < bounds[0] || r >= bounds[heads]) continue;
+    uint4 raw[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) raw[c] = tile[threadIdx.x * kChunks + (c ^ (threadIdx.x & 7))];
     int lo = 0, hi = heads;  // head h with bounds[h] <= r < bounds[h + 1]
     while (hi - lo > 1) {
       const int mid = (lo + hi) / 2;
@@ -288,7 +320,7 @@ __global__ void __launch_bounds__(kProjectThreads, 2) sequential_dim_kernel(cons
     for (int g = 0; g < G; ++g) acc[g] = 0.0f;
 #pragma unroll
     for (int d = 0; d < DIM; ++d) {
-      float2 pair = unpack_pair<T>(word_of(raw[d / 8], (d % 8) / 2));
+      const float2 pair = unpack_pair<T>(word_of(raw[d / 8], (d % 8) / 2));
       const float x = d % 2 ? pair.y : pair.x;
       float w[G];
       if constexpr (G % 4 == 0) {
@@ -314,14 +346,14 @@ __global__ void __launch_bounds__(kProjectThreads, 2) sequential_dim_kernel(cons
 template <typename T, int G, int DIM>
 int launch_sequential_dim(const void *values, int64_t rows, const float *gradients, const int32_t *cumulative,
                           int heads, float *out, cudaStream_t stream) {
-  const size_t shared = static_cast<size_t>(heads) * G * DIM * sizeof(float);
+  const size_t shared = sequential_tile_bytes<DIM>() + static_cast<size_t>(heads) * G * DIM * sizeof(float);
   auto kernel = sequential_dim_kernel<T, G, DIM>;
   if (shared > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
     if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
   const int grid = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(rows, kProjectThreads), static_cast<int64_t>(sm_count()) * 2)));
+      1, std::min<int64_t>(ceil_div(rows, kTileRows), static_cast<int64_t>(sm_count()) * 2)));
   kernel<<<grid, kProjectThreads, shared, stream>>>(static_cast<const T *>(values), rows, gradients, cumulative, heads,
                                                     out);
   return launch_status("lrk_project_values");
@@ -331,7 +363,9 @@ template <typename T, int G>
 int launch_sequential(const void *values, int64_t rows, int dim, const float *gradients, const int32_t *cumulative,
                       int heads, float *out, cudaStream_t stream) {
   if constexpr (sizeof(T) == 2) {
-    if (aligned(values, 16)) {
+    // The staged tile and the gradients must fit one CTA's shared memory.
+    const bool fits = static_cast<size_t>(heads) * G * dim * sizeof(float) + kTileRows * dim * 2 <= 200 * 1024;
+    if (aligned(values, 16) && fits) {
       if (dim == 128) return launch_sequential_dim<T, G, 128>(values, rows, gradients, cumulative, heads, out, stream);
       if (dim == 64) return launch_sequential_dim<T, G, 64>(values, rows, gradients, cumulative, heads, out, stream);
     }

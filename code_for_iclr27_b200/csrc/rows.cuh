@@ -82,6 +82,28 @@ __device__ __forceinline__ float block_max(float v, float *scratch) {
   return r;
 }
 
+// block_max of two values at once (one pair of barriers).
+__device__ __forceinline__ float2 block_max2(float a, float b, float *scratch) {
+  a = warp_max(a);
+  b = warp_max(b);
+  if ((threadIdx.x & 31) == 0) {
+    scratch[threadIdx.x >> 5] = a;
+    scratch[32 + (threadIdx.x >> 5)] = b;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float ra = threadIdx.x < kLanes / 32 ? scratch[threadIdx.x] : -INFINITY;
+    float rb = threadIdx.x < kLanes / 32 ? scratch[32 + threadIdx.x] : -INFINITY;
+    ra = warp_max(ra);
+    rb = warp_max(rb);
+    if (threadIdx.x == 0) scratch[64] = ra, scratch[65] = rb;
+  }
+  __syncthreads();
+  const float2 r = make_float2(scratch[64], scratch[65]);
+  __syncthreads();
+  return r;
+}
+
 // The reference's 256-wide pairwise tree: partial[t] += partial[t + s] for
 // s = 128 .. 1.  Lanes are threads 0..255; all threads of the CTA call.  tree
 // holds 256 floats.
@@ -360,6 +382,7 @@ __device__ __forceinline__ float2 fma2_rn(float2 a, float2 b, float2 c) {
 template <typename T> struct Packed;
 template <> struct Packed<__nv_bfloat16> {
   static constexpr uint32_t kMinusInfinity = 0xff80ff80u;
+  static constexpr uint32_t kPlusInfinity = 0x7f807f80u;
   static __device__ __forceinline__ float2 unpack(uint32_t w) {
     return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
   }
@@ -380,6 +403,7 @@ template <> struct Packed<__nv_bfloat16> {
 };
 template <> struct Packed<__half> {
   static constexpr uint32_t kMinusInfinity = 0xfc00fc00u;
+  static constexpr uint32_t kPlusInfinity = 0x7c007c00u;
   static __device__ __forceinline__ float2 unpack(uint32_t w) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&w));
   }
@@ -439,8 +463,11 @@ __device__ __forceinline__ int chunk_slot(int lane) { return lane ^ ((lane >> 3)
 // Pass C of the packed stage for one 8-element chunk of one lane (k-block
 // kb): x - max, expf, the division, the optional outputs, and the projection
 // sum in lane order.  STORE compiles in the store of every probability (the
-// drop-in probabilities operator), STASH the candidate stash.
-template <typename P, bool STORE, bool STASH>
+// drop-in probabilities operator), STASH the candidate stash.  CHECK tests the
+// chunk's operands for the fast division; without it the caller has shown
+// that every weight of the row is 0 or in [2^-60, 1] (a zero weight divides
+// to +0 in the residual form too: every product and residual is +0).
+template <typename P, bool STORE, bool STASH, bool CHECK>
 __device__ __forceinline__ void packed_chunk(const uint4 chunk, int64_t kb, const float2 minus_max,
                                              const Divider &divider, const float (&current)[8],
                                              float *__restrict__ probabilities_out, const CandidateOut &candidates,
@@ -448,10 +475,13 @@ __device__ __forceinline__ void packed_chunk(const uint4 chunk, int64_t kb, cons
   // One operand test for the chunk's 8 divisions: its smallest x (NaN if
   // any is NaN) minus max at or above kFastExponentFloor puts every weight
   // in [2^-60, 1] (x - max rounds monotonically in x, and x <= max).
-  const uint32_t lowest = P::min_nan(P::min_nan(word(chunk, 0), word(chunk, 1)),
-                                     P::min_nan(word(chunk, 2), word(chunk, 3)));
-  const float2 lowest_d = add2_rn(P::unpack(lowest), minus_max);
-  const bool fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
+  bool fast = true;
+  if constexpr (CHECK) {
+    const uint32_t lowest = P::min_nan(P::min_nan(word(chunk, 0), word(chunk, 1)),
+                                       P::min_nan(word(chunk, 2), word(chunk, 3)));
+    const float2 lowest_d = add2_rn(P::unpack(lowest), minus_max);
+    fast = divider.fast && lowest_d.x >= kFastExponentFloor && lowest_d.y >= kFastExponentFloor;
+  }
 #pragma unroll
   for (int v = 0; v < 4; ++v) {
     const float2 d = add2_rn(P::unpack(word(chunk, v)), minus_max);
@@ -497,12 +527,16 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   const float2 scale2 = make_float2(scale, scale);
   const unsigned short neg_inf = minus_infinity<T>();
   uint32_t max_pair = P::kMinusInfinity;
+  uint32_t min_pair = P::kPlusInfinity;  // before the mask; NaN wins
   float local_max = -INFINITY;
 
   // dtype(x * scale), masked, for the 8 elements from p0 (one vector).
   auto prepare = [&](int64_t p0, uint4 raw) -> uint4 {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) word(raw, i) = P::round(mul2_rn(P::unpack(word(raw, i)), scale2));
+    for (int i = 0; i < 4; ++i) {
+      word(raw, i) = P::round(mul2_rn(P::unpack(word(raw, i)), scale2));
+      min_pair = P::min_nan(min_pair, word(raw, i));
+    }
     if (!sees.all(p0, 8)) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -550,7 +584,13 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   }
   const float2 pair_max = P::unpack(max_pair);
   local_max = fmaxf(local_max, fmaxf(pair_max.x, pair_max.y));
-  const float maximum = block_max(local_max, scratch);
+  // The row's smallest k-block value, negated for the max reduction (+inf
+  // when a NaN is present, which turns the row-wide fast division off).
+  const float2 pair_min = P::unpack(min_pair);
+  const float lowest = fminf(pair_min.x, pair_min.y);
+  const float2 extremes =
+      block_max2(local_max, isnan(pair_min.x) || isnan(pair_min.y) ? INFINITY : -lowest, scratch);
+  const float maximum = extremes.x;
 
   // Pass B: x - max as x + (-max) (the same IEEE operation), lane order.
   const float2 minus_max = make_float2(-maximum, -maximum);
@@ -583,33 +623,54 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
 #pragma unroll
     for (int m = 0; m < 8; ++m) next[m] = __ldg(values + m * kLanes);
   }
-  auto run = [&](int64_t kb_begin, int64_t kb_end, auto store, auto stash) {
+  // Row-wide operand test: the smallest k-block x minus max at or above
+  // kFastExponentFloor puts every k-block weight in [2^-60, 1], or at 0 for
+  // a masked element; then no chunk tests its own.
+  const bool row_fast = divider.fast && __fadd_rn(-extremes.y, -maximum) >= kFastExponentFloor;
+  auto load_values = [&](int64_t kb, float (&into)[8]) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) into[m] = __ldg(values + (kb * 8 + m) * kLanes);
+  };
+  // Two k-blocks per iteration, their projected values in two buffers, so no
+  // buffer is copied; `next` holds the values of k-block kb on entry.
+  auto run = [&](int64_t kb_begin, int64_t kb_end, auto store, auto stash, auto check) {
     constexpr bool kStore = decltype(store)::value, kStash = decltype(stash)::value;
-    for (int64_t kb = kb_begin; kb < kb_end; ++kb) {
+    constexpr bool kCheck = decltype(check)::value;
+    int64_t kb = kb_begin;
+    for (; kb + 1 < kb_end; kb += 2) {
+      float second[8];
+      load_values(kb + 1, second);
+      packed_chunk<P, kStore, kStash, kCheck>(chunks[kb * kLanes + slot], kb, minus_max, divider, next,
+                                              probabilities_out, candidates, projection);
+      if (kb + 2 < blocks) load_values(kb + 2, next);
+      packed_chunk<P, kStore, kStash, kCheck>(chunks[(kb + 1) * kLanes + slot], kb + 1, minus_max, divider,
+                                              second, probabilities_out, candidates, projection);
+    }
+    if (kb < kb_end) {
       float current[8];
 #pragma unroll
       for (int m = 0; m < 8; ++m) current[m] = next[m];
-      if (kb + 1 < blocks) {
-#pragma unroll
-        for (int m = 0; m < 8; ++m) next[m] = __ldg(values + ((kb + 1) * 8 + m) * kLanes);
-      }
-      packed_chunk<P, kStore, kStash>(chunks[kb * kLanes + slot], kb, minus_max, divider, current,
-                                      probabilities_out, candidates, projection);
+      if (kb + 1 < blocks) load_values(kb + 1, next);
+      packed_chunk<P, kStore, kStash, kCheck>(chunks[kb * kLanes + slot], kb, minus_max, divider, current,
+                                              probabilities_out, candidates, projection);
     }
   };
   using yes = std::true_type;
   using no = std::false_type;
-  if (probabilities_out != nullptr) {
-    run(0, blocks, yes{}, no{});
-  } else if (candidates.out != nullptr) {
-    const int64_t lo = lmin(blocks, lmax(0, candidates.first / kBlock));
-    const int64_t hi = lmin(blocks, lmax(lo, (candidates.last + kBlock - 1) / kBlock));
-    run(0, lo, no{}, no{});
-    run(lo, hi, no{}, yes{});
-    run(hi, blocks, no{}, no{});
-  } else {
-    run(0, blocks, no{}, no{});
-  }
+  auto pass_c = [&](auto check) {
+    if (probabilities_out != nullptr) {
+      run(0, blocks, yes{}, no{}, check);
+    } else if (candidates.out != nullptr) {
+      const int64_t lo = lmin(blocks, lmax(0, candidates.first / kBlock));
+      const int64_t hi = lmin(blocks, lmax(lo, (candidates.last + kBlock - 1) / kBlock));
+      run(0, lo, no{}, no{}, check);
+      run(lo, hi, no{}, yes{}, check);
+      run(hi, blocks, no{}, no{}, check);
+    } else {
+      run(0, blocks, no{}, no{}, check);
+    }
+  };
+  if (row_fast) pass_c(no{}); else pass_c(yes{});
   for (int64_t p = body + threadIdx.x; p < length; p += kLanes) {
     const float probability = divide(divider, expf(__fsub_rn(D::to_float(tail[p - body]), maximum)));
     if (probabilities_out != nullptr) __stcs(probabilities_out + p, probability);
