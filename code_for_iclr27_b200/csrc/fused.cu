@@ -518,13 +518,12 @@ __global__ void __launch_bounds__(kRiskThreads, 4) risk_vec_kernel(ScoreTablePar
 // -- then the drop range of each query chunk, its fp64 risk and the running
 // maximum, exactly as risk_vec_kernel folds them.  This skips risk_vec's
 // logits load, scale, rounding, mask, expf and first division per element.
-// A CTA covers kStashTile candidates; thread (tx, ty) owns C consecutive
+// A CTA covers TILE candidates; thread (tx, ty) owns C consecutive
 // candidates (one 4C-byte load per stashed row; C = 4, or 2 for 8 groups to
 // keep the registers in check) and walks queries ty, ty + TY, ..., loading
-// the next query's rows while the current one computes.
-constexpr int kStashTile = 32;
-
-template <int G, int C>
+// the next query's rows while the current one computes.  The launch picks
+// TILE (32, 16 or 8) for the fewest waves of CTAs weighted by their length.
+template <int G, int C, int TILE>
 __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableParam table,
                                                                   const float *__restrict__ stash, int window,
                                                                   const float3 *__restrict__ stats,
@@ -532,13 +531,13 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
                                                                   const float *__restrict__ margin,
                                                                   float epsilon) {
   using Vec = typename std::conditional<C == 4, float4, float2>::type;
-  constexpr int TX = kStashTile / C, TY = kRiskThreads / TX;
+  constexpr int TX = TILE / C, TY = kRiskThreads / TX;
   extern __shared__ float projection[];  // [window * G]
-  __shared__ int cell_min[kRiskChunks][kStashTile], cell_max[kRiskChunks][kStashTile];
-  __shared__ int cell_bad[kRiskChunks][kStashTile];
+  __shared__ int cell_min[kRiskChunks][TILE], cell_max[kRiskChunks][TILE];
+  __shared__ int cell_bad[kRiskChunks][TILE];
   const lrk_score_segment &seg = table.segment[blockIdx.y];
   const int64_t count = seg.last - seg.first;
-  const int64_t tile = static_cast<int64_t>(blockIdx.x) * kStashTile;
+  const int64_t tile = static_cast<int64_t>(blockIdx.x) * TILE;
   if (tile >= count) return;  // the whole CTA: nothing of this segment here
   for (int i = threadIdx.x; i < window * G; i += kRiskThreads)
     projection[i] = stats[(segment_base + blockIdx.y) * window * G + i].z;
@@ -562,14 +561,14 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
   };
   const int chunk = chunk_queries(seg, window);
   const int chunks = (window + chunk - 1) / chunk;
-  const bool leader = threadIdx.x < kStashTile;
+  const bool leader = threadIdx.x < TILE;
   float result = 0.0f;
   for (int c_first = 0; c_first < chunks; c_first += kRiskChunks) {
     const int c_last = min(chunks, c_first + kRiskChunks);
-    for (int i = threadIdx.x; i < (c_last - c_first) * kStashTile; i += kRiskThreads) {
-      cell_min[i / kStashTile][i % kStashTile] = ordered_key(INFINITY);
-      cell_max[i / kStashTile][i % kStashTile] = ordered_key(-INFINITY);
-      cell_bad[i / kStashTile][i % kStashTile] = 0;
+    for (int i = threadIdx.x; i < (c_last - c_first) * TILE; i += kRiskThreads) {
+      cell_min[i / TILE][i % TILE] = ordered_key(INFINITY);
+      cell_max[i / TILE][i % TILE] = ordered_key(-INFINITY);
+      cell_bad[i / TILE][i % TILE] = 0;
     }
     __syncthreads();
     const int q_begin = c_first * chunk, q_end = min(window, c_last * chunk);
@@ -651,18 +650,52 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
   if (candidate < count) seg.scores[candidate] = result;
 }
 
-template <int G>
-int launch_risk_stash(const ScoreTableParam &table, int n, const float *stash, int window, const float3 *stats,
-                      int64_t s0, const float *margin, float epsilon, int64_t max_candidates, cudaStream_t stream) {
+template <int G, int TILE>
+int launch_risk_stash_tile(const ScoreTableParam &table, int n, const float *stash, int window, const float3 *stats,
+                           int64_t s0, const float *margin, float epsilon, int64_t max_candidates,
+                           cudaStream_t stream) {
   const size_t shared = static_cast<size_t>(window) * G * sizeof(float);
-  auto kernel = risk_stash_kernel<G, (G >= 8 ? 2 : 4)>;
+  auto kernel = risk_stash_kernel<G, (G >= 8 ? 2 : 4), TILE>;
   if (shared > 16 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
     if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
-  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, kStashTile))), n);
+  const dim3 grid(static_cast<unsigned>(std::max<int64_t>(1, ceil_div(max_candidates, TILE))), n);
   kernel<<<grid, kRiskThreads, shared, stream>>>(table, stash, window, stats, s0, margin, epsilon);
   return launch_status("lrk_temporal_scores risk from stashed probabilities");
+}
+
+// Candidates per CTA: a CTA's length grows with its tile plus a fixed part
+// (the projections it stages, the cells, the fp64 scores of its leaders),
+// taken as 8 candidates' worth; the tile with the fewest waves x length wins
+// (3 CTAs per SM).  A configs[1] layer (8 x 2080 candidates) takes 16: 3
+// waves of 1040 CTAs instead of 2 of 520 with the second one 17 % full.
+inline int stash_tile(int64_t max_candidates, int n) {
+#ifdef LRK_STASH_TILE
+  return LRK_STASH_TILE;
+#endif
+  const int64_t slots = 3 * static_cast<int64_t>(sm_count());
+  int best = 32;
+  int64_t best_cost = INT64_MAX;
+  for (int tile : {32, 16, 8}) {
+    const int64_t waves = ceil_div(ceil_div(max_candidates, tile) * n, slots);
+    const int64_t cost = waves * (tile + 8);
+    if (cost < best_cost) best = tile, best_cost = cost;
+  }
+  return best;
+}
+
+template <int G>
+int launch_risk_stash(const ScoreTableParam &table, int n, const float *stash, int window, const float3 *stats,
+                      int64_t s0, const float *margin, float epsilon, int64_t max_candidates, cudaStream_t stream) {
+  switch (stash_tile(max_candidates, n)) {
+    case 8: return launch_risk_stash_tile<G, 8>(table, n, stash, window, stats, s0, margin, epsilon, max_candidates,
+                                                stream);
+    case 16: return launch_risk_stash_tile<G, 16>(table, n, stash, window, stats, s0, margin, epsilon, max_candidates,
+                                                  stream);
+    default: return launch_risk_stash_tile<G, 32>(table, n, stash, window, stats, s0, margin, epsilon,
+                                                  max_candidates, stream);
+  }
 }
 
 template <typename T, int G, int C>

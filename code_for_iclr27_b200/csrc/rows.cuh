@@ -216,7 +216,7 @@ struct Visibility {
     return visible >= 0 ? p < visible : __ldg(key_positions + p) <= query_position;
   }
   // Every key of [p, p + n) is visible (index test only).
-  __device__ __forceinline__ bool all(int64_t p, int n) const { return visible >= 0 && p + n <= visible; }
+  __device__ __forceinline__ bool all(int64_t p, int64_t n) const { return visible >= 0 && p + n <= visible; }
 };
 
 // Optional output of pass C: the probability of every candidate column
@@ -531,13 +531,14 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   float local_max = -INFINITY;
 
   // dtype(x * scale), masked, for the 8 elements from p0 (one vector).
-  auto prepare = [&](int64_t p0, uint4 raw) -> uint4 {
+  // CHECK tests the mask; without it the caller knows all 8 keys are visible.
+  auto prepare = [&](int64_t p0, uint4 raw, auto check) -> uint4 {
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       word(raw, i) = P::round(mul2_rn(P::unpack(word(raw, i)), scale2));
       min_pair = P::min_nan(min_pair, word(raw, i));
     }
-    if (!sees.all(p0, 8)) {
+    if (decltype(check)::value && !sees.all(p0, 8)) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint32_t keep = (sees(p0 + 2 * i) ? 0x0000ffffu : 0u) | (sees(p0 + 2 * i + 1) ? 0xffff0000u : 0u);
@@ -550,6 +551,9 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
   };
 
   // Pass A, k-blocks: thread item i = (kb, c) covers lanes 8c .. 8c + 7.
+  // A row whose k-blocks are all visible (the usual case) skips the mask
+  // tests.
+  auto k_blocks = [&](auto check) {
   for (int64_t i = threadIdx.x; i < blocks * 32; i += kLanes) {
     const int64_t kb = i >> 5;
     const int c = static_cast<int>(i & 31);
@@ -557,7 +561,7 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
 #pragma unroll
     for (int m = 0; m < 8; ++m) raw[m] = __ldcs(in + (kb * 8 + m) * 32 + c);
 #pragma unroll
-    for (int m = 0; m < 8; ++m) raw[m] = prepare((kb * 8 + m) * kLanes + c * 8, raw[m]);
+    for (int m = 0; m < 8; ++m) raw[m] = prepare((kb * 8 + m) * kLanes + c * 8, raw[m], check);
     uint4 *dst = chunks + kb * kLanes;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
@@ -572,10 +576,13 @@ __device__ RowResult row_statistics_packed(const T *__restrict__ row, int64_t le
       dst[chunk_slot(c * 8 + 2 * w + 1)] = odd;
     }
   }
+  };
+  if (sees.all(0, body)) k_blocks(std::false_type{});
+  else k_blocks(std::true_type{});
   // Pass A, tail: whole vectors, then single elements, in row order.
   const int64_t tail_vectors = (length - body) / 8;
   for (int64_t v = threadIdx.x; v < tail_vectors; v += kLanes)
-    reinterpret_cast<uint4 *>(tail)[v] = prepare(body + v * 8, __ldcs(in + body / 8 + v));
+    reinterpret_cast<uint4 *>(tail)[v] = prepare(body + v * 8, __ldcs(in + body / 8 + v), std::true_type{});
   for (int64_t p = body + tail_vectors * 8 + threadIdx.x; p < length; p += kLanes) {
     const unsigned short raw = reinterpret_cast<const unsigned short *>(row)[p];
     const unsigned short b = sees(p) ? D::round(D::to_float(raw), scale) : neg_inf;
