@@ -154,6 +154,55 @@ def tensor_core_order_matches(length: int, window: int, groups: int, chunk: int)
     return not (batches & exceptions)
 
 
+# Runtime check of the step-order rule: the first head of each (groups, key
+# count parity, query batches) class this process scores through lrk_logits is
+# also computed by the reference's GEMM and compared bit for bit.  A class
+# that differs (a cuBLAS whose heuristics moved) takes the reference's GEMM
+# from then on, and that head's logits are replaced by the reference's.
+_ORDER_VERIFIED = {}
+
+
+def _order_class(length: int, window: int, groups: int, chunk: int):
+    return groups, length % 2, tuple(sorted({min(chunk, window - a) for a in range(0, window, chunk)}))
+
+
+def order_verified(length: int, window: int, groups: int, chunk: int) -> bool:
+    """False once the class of this head failed the runtime check."""
+    return _ORDER_VERIFIED.get(_order_class(length, window, groups, chunk), True)
+
+
+def _reference_head_logits(per_head_queries, keys, start: int, end: int, chunk: int):
+    import torch
+
+    window = per_head_queries.shape[0]
+    mapped = reference_query_view(per_head_queries)
+    head_keys = keys[start:end]
+    return torch.cat([torch.matmul(mapped[a:a + chunk].to(keys.dtype), head_keys.transpose(0, 1))
+                      for a in range(0, window, chunk)])
+
+
+def _check_order(per_head_queries, keys, start: int, end: int, chunk: int, logits):
+    """The runtime check for one head computed by lrk_logits: returns the
+    logits to use (the reference's when the class fails)."""
+    import torch
+
+    window, groups, _ = per_head_queries.shape
+    key = _order_class(end - start, window, groups, chunk)
+    if key in _ORDER_VERIFIED:
+        return logits
+    reference = _reference_head_logits(per_head_queries, keys, start, end, chunk)
+    same = bool(torch.equal(reference.view(torch.int16), logits.contiguous().view(torch.int16)))
+    _ORDER_VERIFIED[key] = same
+    if not same:
+        import warnings
+
+        warnings.warn(f"lrk_logits' step order differs from this cuBLAS for groups={groups}, "
+                      f"{'odd' if (end - start) % 2 else 'even'} key counts, query batches {key[2]}: "
+                      "those heads take the reference's GEMM")
+        return reference
+    return logits
+
+
 def head_logits(per_head_queries, keys, start: int, end: int, chunk: int):
     """bf16 logits [W, G, L] of one head, equal bit for bit to the logits the
     reference computes per query chunk with torch.matmul (scoring.py:184), as
@@ -165,14 +214,13 @@ def head_logits(per_head_queries, keys, start: int, end: int, chunk: int):
     window, groups, dim = per_head_queries.shape
     length = end - start
     if (keys.dtype == torch.bfloat16 and per_head_queries.dtype == torch.bfloat16 and dim in (64, 128)
-            and tensor_core_order_matches(length, window, groups, chunk)):
+            and tensor_core_order_matches(length, window, groups, chunk)
+            and order_verified(length, window, groups, chunk)):
         flat = per_head_queries.contiguous().view(window * groups, dim)
         padded = operators().logits(flat, keys[start:end], 8 if length % 2 else 16, (length + 7) // 8 * 8)
-        return padded.view(window, groups, -1)[:, :, :length]
-    mapped = reference_query_view(per_head_queries)
-    head_keys = keys[start:end]
-    return torch.cat([torch.matmul(mapped[a:a + chunk].to(keys.dtype), head_keys.transpose(0, 1))
-                      for a in range(0, window, chunk)])
+        return _check_order(per_head_queries, keys, start, end, chunk,
+                            padded.view(window, groups, -1)[:, :, :length])
+    return _reference_head_logits(per_head_queries, keys, start, end, chunk)
 
 
 def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stream=None):
@@ -190,7 +238,8 @@ def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stre
     fast, slow = [], []
     for i, (head, start, end, chunk) in enumerate(spans):
         if (keys.dtype == torch.bfloat16 and dim in (64, 128) and per_head.dtype == torch.bfloat16
-                and tensor_core_order_matches(end - start, window, groups, chunk)):
+                and tensor_core_order_matches(end - start, window, groups, chunk)
+                and order_verified(end - start, window, groups, chunk)):
             fast.append(i)
         else:
             slow.append(i)
@@ -210,7 +259,9 @@ def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stre
         steps = [8 if (e - b) % 2 else 16 for b, e in zip(starts, ends)]
         views = operators().logits_heads(per_head, keys, heads, starts, ends, steps)
         for i, view, b, e in zip(fast, views, starts, ends):
-            out[i] = view.view(window, groups, -1)[:, :, :e - b]
+            head, _, _, chunk = spans[i]
+            out[i] = _check_order(per_head[head].view(window, groups, dim), keys, b, e, chunk,
+                                  view.view(window, groups, -1)[:, :, :e - b])
     return out
 
 

@@ -577,6 +577,43 @@ def test_layer_logits_equal_reference_chunks(C, cuda, window, groups):
         assert torch.equal(logits, expect), f"head {h} ({end - start} keys, chunk {chunk})"
 
 
+def test_layer_logits_runtime_order_check(C, cuda, monkeypatch):
+    """The first head of each (groups, parity, query batches) class goes
+    through lrk_logits and is checked against the reference GEMM; a class
+    marked as failed takes the reference GEMM for all its heads (no
+    lrk_logits_heads launch for them) and the logits still equal the
+    reference's."""
+    import torch
+
+    from code_for_iclr27_b200 import audit
+
+    monkeypatch.setattr(audit, "_ORDER_VERIFIED", {})
+    g = torch.Generator(device=cuda).manual_seed(77)
+    window, groups, lens = 250, 4, [4096, 4097, 4098]
+    bounds = [0, 4096, 8193, 12291]
+    keys = torch.randn(bounds[-1], 128, generator=g, device=cuda).to(torch.bfloat16)
+    per_head = (torch.randn(len(lens), window, groups, 128, generator=g, device=cuda) * 2).to(torch.bfloat16)
+    spans = [(h, bounds[h], bounds[h + 1], audit.query_chunk(250, groups, n, 2)) for h, n in enumerate(lens)]
+    flat = per_head.view(len(lens), window * groups, 128)
+    audit.layer_logits(flat, keys, spans, window, groups)
+    even = audit._order_class(4096, window, groups, spans[0][3])
+    odd = audit._order_class(4097, window, groups, spans[1][3])
+    assert audit._ORDER_VERIFIED == {even: True, odd: True}
+    audit._ORDER_VERIFIED[even] = False  # as if this cuBLAS took another order for even counts
+    launched = []
+    original = C.logits_heads
+
+    def counting(per_head_arg, keys_arg, heads, *rest):
+        launched.extend(heads)
+        return original(per_head_arg, keys_arg, heads, *rest)
+
+    monkeypatch.setattr(audit, "operators", lambda: type("Ops", (), {"logits_heads": staticmethod(counting)})())
+    got = audit.layer_logits(flat, keys, spans, window, groups)
+    assert launched == [1]  # only the odd head
+    for (h, start, end, chunk), logits in zip(spans, got):
+        assert torch.equal(logits, reference_chunks(per_head[h], keys[start:end], chunk))
+
+
 def test_logits_heads_rejects_bad_arguments(C, cuda):
     """lrk_logits_heads checks every head like lrk_logits (step, stride,
     alignment) before anything runs."""
