@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace lrk {
 namespace {
@@ -496,6 +497,107 @@ int launch_gather(const Plan &plan, GatherOut out, int vb, cudaStream_t stream, 
   return launch_status(what);
 }
 
+// lrk_compact by bulk copies, for 16-byte aligned rows of 16-byte multiples
+// up to 512 bytes.  A CTA owns kBulkRows output rows.  Output row o comes from
+// source row o + lower(o) (CompactPlan), so the tile's rows fall into runs of
+// consecutive source rows, one per stretch between removed rows: thread 0
+// finds each run with one binary search, checks that it lies inside the
+// source, and moves it with one `cp.async.bulk` load per tensor (K and V)
+// into shared memory, completing on an mbarrier; the other threads copy the
+// positions meanwhile.  The tile then leaves with one bulk store per tensor.
+// Measured on a configs[1] layer (279k rows of 256 bytes, 64 removed):
+// 42.9 us against 49.0 us for gather_kernel<CompactPlan>, with a fifth of the
+// instructions.  A tile with a run outside the source (an invalid removal
+// list), or whose loads do not land within the bounded wait (the wait is then
+// repeated, also bounded, for the copies in flight), is copied row by row
+// with 16-byte vectors instead, rows without a valid source skipped as in
+// gather_kernel.
+constexpr int kBulkRows = 64;
+constexpr int kBulkThreads = 128;
+constexpr int64_t kBulkMaxRowBytes = 512;
+
+__global__ void __launch_bounds__(kBulkThreads) compact_bulk_kernel(CompactPlan plan, char *__restrict__ out_k,
+                                                                  char *__restrict__ out_v,
+                                                                  float *__restrict__ out_positions,
+                                                                  int64_t out_rows) {
+  extern __shared__ __align__(128) unsigned char bulk_stage[];  // K rows, then V rows
+  __shared__ __align__(8) uint64_t loaded_storage;
+  __shared__ int landed;
+  const int64_t rb = plan.row_bytes;
+  const int64_t o0 = static_cast<int64_t>(blockIdx.x) * kBulkRows;
+  const int n = static_cast<int>(lmin(kBulkRows, out_rows - o0));
+  const uint32_t loaded = static_cast<uint32_t>(__cvta_generic_to_shared(&loaded_storage));
+  const uint32_t stage_k = static_cast<uint32_t>(__cvta_generic_to_shared(bulk_stage));
+  const uint32_t stage_v = stage_k + static_cast<uint32_t>(kBulkRows * rb);
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    tc::init_barrier(loaded, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    // Validate every run first: nothing is issued for a tile with a bad one.
+    for (int64_t o = o0; o < o0 + n && ok;) {
+      const int64_t c = plan.lower(o);
+      const int64_t end = c < plan.removed_count ? lmin(o0 + n, plan.removed[c] - c) : o0 + n;
+      ok = end > o && o + c >= 0 && end + c <= plan.rows;
+      o = end;
+    }
+    if (ok) {
+      tc::expect_bytes(loaded, static_cast<uint32_t>(2 * n * rb));
+      for (int64_t o = o0; o < o0 + n;) {
+        const int64_t c = plan.lower(o);
+        const int64_t end = c < plan.removed_count ? lmin(o0 + n, plan.removed[c] - c) : o0 + n;
+        const uint32_t size = static_cast<uint32_t>((end - o) * rb), offset = static_cast<uint32_t>((o - o0) * rb);
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                         stage_k + offset),
+                     "l"(plan.k + (o + c) * rb), "r"(size), "r"(loaded)
+                     : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                         stage_v + offset),
+                     "l"(plan.v + (o + c) * rb), "r"(size), "r"(loaded)
+                     : "memory");
+        o = end;
+      }
+    }
+    landed = ok;
+  }
+  __syncthreads();
+  // Positions while the loads are in flight; the source of each row again
+  // by lower(), rows without a valid source skipped.
+  for (int i = threadIdx.x; i < n; i += kBulkThreads) {
+    const int64_t o = o0 + i, source = o + plan.lower(o);
+    if (source >= 0 && source < plan.rows) out_positions[o] = plan.positions[source];
+  }
+  if (threadIdx.x == 0 && landed) {
+    if (tc::wait_phase(loaded, 0, nullptr)) {
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      const uint32_t size = static_cast<uint32_t>(n * rb);
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_k + o0 * rb),
+                   "r"(stage_k), "r"(size)
+                   : "memory");
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_v + o0 * rb),
+                   "r"(stage_v), "r"(size)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+    } else {
+      tc::wait_phase(loaded, 0, nullptr);  // the copies in flight, bounded once more
+      landed = 0;
+    }
+  }
+  __syncthreads();
+  if (landed) return;
+  // Row by row: 16-byte vectors, rows without a valid source skipped.
+  const int units = static_cast<int>(rb / 16);
+  for (int item = threadIdx.x; item < n * units; item += kBulkThreads) {
+    const int row = item / units, unit = item - row * units;
+    const int64_t o = o0 + row, source = o + plan.lower(o);
+    if (source < 0 || source >= plan.rows) continue;
+    const uint4 kv = __ldcs(reinterpret_cast<const uint4 *>(plan.k + source * rb) + unit);
+    const uint4 vv = __ldcs(reinterpret_cast<const uint4 *>(plan.v + source * rb) + unit);
+    __stcs(reinterpret_cast<uint4 *>(out_k + o * rb) + unit, kv);
+    __stcs(reinterpret_cast<uint4 *>(out_v + o * rb) + unit, vv);
+  }
+}
+
 int element_bytes(int dtype) { return lrk_dtype_size(dtype); }
 
 }  // namespace
@@ -518,6 +620,15 @@ extern "C" int lrk_compact(const void *keys, const void *values, const float *po
   const int vb = pick_vector(rb, {keys, values, out_keys, out_values}, {});
   CompactPlan plan{static_cast<const char *>(keys), static_cast<const char *>(values), positions, rows, rb,
                    removed, removed_count};
+  const int64_t tiles = ceil_div(out_rows, kBulkRows);
+  if (vb == 16 && rb % 16 == 0 && rb <= kBulkMaxRowBytes && tiles >= 2 * sm_count()) {
+    const int shared = static_cast<int>(2 * kBulkRows * rb);
+    cudaError_t e = cudaFuncSetAttribute(compact_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shared);
+    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+    compact_bulk_kernel<<<static_cast<unsigned>(tiles), kBulkThreads, shared, reinterpret_cast<cudaStream_t>(stream)>>>(
+        plan, static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, out_rows);
+    return launch_status("lrk_compact");
+  }
   GatherOut out{static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, rb, rb,
                 out_rows, rb, {}};
   return launch_gather(plan, out, vb, reinterpret_cast<cudaStream_t>(stream), "lrk_compact");
