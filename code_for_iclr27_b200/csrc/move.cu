@@ -228,36 +228,39 @@ struct AppendPlan {
     }
     __syncthreads();
   }
+  // Last head whose start is <= o.
+  __device__ int64_t head_of(int64_t o, const Shared &s) const {
+    int64_t lo = 0, hi = heads;  // answer in [0, heads)
+    while (hi - lo > 1) {
+      const int64_t mid = (lo + hi) / 2;
+      if (start_of(s, mid) <= o) lo = mid; else hi = mid;
+    }
+    return lo;
+  }
+  __device__ RowSource source(int64_t o, const Shared &s) const {
+    const int64_t h = head_of(o, s);
+    const int64_t local = o - start_of(s, h);
+    const int64_t old = old_length(h);
+    RowSource out{nullptr, nullptr, 0.0f};
+    if (local >= 0 && local < old) {
+      const int64_t source = cumulative[h] + local;
+      if (source >= 0 && source < rows) {
+        out.k = k + source * row_bytes;
+        out.v = v != nullptr ? v + source * row_bytes : nullptr;
+        out.position = positions != nullptr ? positions[source] : 0.0f;
+      }
+    } else if (local >= old && local < old + added) {
+      const int64_t j = local - old;
+      const int64_t source = h * added + j;
+      out.k = new_k + source * row_bytes;
+      out.v = new_v != nullptr ? new_v + source * row_bytes : nullptr;
+      out.position = static_cast<float>(logical_start + j);
+    }
+    return out;
+  }
   template <int TR>
   __device__ void fill(int64_t first, int nrows, RowSource *sources, Shared &s) const {
-    for (int i = threadIdx.x; i < nrows; i += kThreads) {
-      const int64_t o = first + i;
-      // Last head whose start is <= o.
-      int64_t lo = 0, hi = heads;  // answer in [0, heads)
-      while (hi - lo > 1) {
-        const int64_t mid = (lo + hi) / 2;
-        if (start_of(s, mid) <= o) lo = mid; else hi = mid;
-      }
-      const int64_t h = lo;
-      const int64_t local = o - start_of(s, h);
-      const int64_t old = old_length(h);
-      RowSource out{nullptr, nullptr, 0.0f};
-      if (local >= 0 && local < old) {
-        const int64_t source = cumulative[h] + local;
-        if (source >= 0 && source < rows) {
-          out.k = k + source * row_bytes;
-          out.v = v != nullptr ? v + source * row_bytes : nullptr;
-          out.position = positions != nullptr ? positions[source] : 0.0f;
-        }
-      } else if (local >= old && local < old + added) {
-        const int64_t j = local - old;
-        const int64_t source = h * added + j;
-        out.k = new_k + source * row_bytes;
-        out.v = new_v != nullptr ? new_v + source * row_bytes : nullptr;
-        out.position = static_cast<float>(logical_start + j);
-      }
-      sources[i] = out;
-    }
+    for (int i = threadIdx.x; i < nrows; i += kThreads) sources[i] = source(first + i, s);
   }
 };
 
@@ -598,6 +601,124 @@ __global__ void __launch_bounds__(kBulkThreads) compact_bulk_kernel(CompactPlan 
   }
 }
 
+// lrk_append by bulk copies (the decode step of the packed layout), same
+// engine as compact_bulk_kernel: a head's rows in a tile are one run of
+// consecutive cache rows followed by one run of its new rows (new_keys is
+// [heads, added, row]), so thread 0 walks the heads the tile overlaps, checks
+// every run against the source sizes, then issues one bulk load per run and
+// tensor; the tile leaves with one bulk store per tensor.  Positions and the
+// new cumulative lengths are written by plain stores; an invalid run or a
+// timed-out wait copies the tile row by row (AppendPlan::source).
+__global__ void __launch_bounds__(kBulkThreads) append_bulk_kernel(AppendPlan plan, char *__restrict__ out_k,
+                                                                 char *__restrict__ out_v,
+                                                                 float *__restrict__ out_positions,
+                                                                 int64_t out_rows) {
+  extern __shared__ __align__(128) unsigned char bulk_stage[];  // K rows, then V rows
+  __shared__ AppendPlan::Shared shared;
+  __shared__ __align__(8) uint64_t loaded_storage;
+  __shared__ int landed;
+  if (plan.heads <= kMaxSharedHeads)
+    for (int64_t h = threadIdx.x; h <= plan.heads; h += kBulkThreads)
+      shared.start[h] = plan.cumulative[h] + h * plan.added;
+  if (blockIdx.x == 0 && plan.out_cumulative != nullptr) {
+    for (int64_t h = threadIdx.x; h < plan.heads; h += kBulkThreads) {
+      plan.out_cumulative[h] = static_cast<int32_t>(plan.cumulative[h] + h * plan.added);
+      plan.out_lengths[h] = static_cast<int32_t>(plan.old_length(h) + plan.added);
+    }
+    if (threadIdx.x == 0)
+      plan.out_cumulative[plan.heads] = static_cast<int32_t>(plan.cumulative[plan.heads] + plan.heads * plan.added);
+  }
+  __syncthreads();
+  const int64_t rb = plan.row_bytes;
+  const int64_t o0 = static_cast<int64_t>(blockIdx.x) * kBulkRows;
+  const int n = static_cast<int>(lmin(kBulkRows, out_rows - o0));
+  const uint32_t loaded = static_cast<uint32_t>(__cvta_generic_to_shared(&loaded_storage));
+  const uint32_t stage_k = static_cast<uint32_t>(__cvta_generic_to_shared(bulk_stage));
+  const uint32_t stage_v = stage_k + static_cast<uint32_t>(kBulkRows * rb);
+  if (threadIdx.x == 0) {
+    tc::init_barrier(loaded, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    // pass 0 checks every run, pass 1 issues the loads.
+    bool ok = true;
+    for (int pass = 0; pass < 2 && ok; ++pass) {
+      if (pass == 1) tc::expect_bytes(loaded, static_cast<uint32_t>(2 * n * rb));
+      int64_t h = plan.head_of(o0, shared), o = o0;
+      while (o < o0 + n && ok) {
+        if (h >= plan.heads) {
+          ok = false;
+          break;
+        }
+        const int64_t start = plan.start_of(shared, h), old = plan.old_length(h), local = o - start;
+        const char *k_src, *v_src;
+        int64_t end;
+        if (local >= 0 && local < old) {
+          end = lmin(o0 + n, start + old);
+          const int64_t source = plan.cumulative[h] + local;
+          ok = source >= 0 && source + (end - o) <= plan.rows;
+          k_src = plan.k + source * rb;
+          v_src = plan.v + source * rb;
+        } else if (local >= old && local < old + plan.added) {
+          end = lmin(o0 + n, start + old + plan.added);
+          const int64_t source = h * plan.added + (local - old);
+          k_src = plan.new_k + source * rb;
+          v_src = plan.new_v + source * rb;
+        } else {
+          ok = local >= old + plan.added;  // past this head: the next one
+          ++h;
+          continue;
+        }
+        if (pass == 1) {
+          const uint32_t size = static_cast<uint32_t>((end - o) * rb), offset = static_cast<uint32_t>((o - o0) * rb);
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                  stage_k + offset),
+              "l"(k_src), "r"(size), "r"(loaded)
+              : "memory");
+          asm volatile(
+              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                  stage_v + offset),
+              "l"(v_src), "r"(size), "r"(loaded)
+              : "memory");
+        }
+        o = end;
+      }
+    }
+    landed = ok;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += kBulkThreads) {
+    const RowSource src = plan.source(o0 + i, shared);
+    if (src.k != nullptr) out_positions[o0 + i] = src.position;
+  }
+  if (threadIdx.x == 0 && landed) {
+    if (tc::wait_phase(loaded, 0, nullptr)) {
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      const uint32_t size = static_cast<uint32_t>(n * rb);
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_k + o0 * rb),
+                   "r"(stage_k), "r"(size)
+                   : "memory");
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_v + o0 * rb),
+                   "r"(stage_v), "r"(size)
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+    } else {
+      tc::wait_phase(loaded, 0, nullptr);  // the copies in flight, bounded once more
+      landed = 0;
+    }
+  }
+  __syncthreads();
+  if (landed) return;
+  const int units = static_cast<int>(rb / 16);
+  for (int item = threadIdx.x; item < n * units; item += kBulkThreads) {
+    const int row = item / units, unit = item - row * units;
+    const RowSource src = plan.source(o0 + row, shared);
+    if (src.k == nullptr) continue;
+    __stcs(reinterpret_cast<uint4 *>(out_k + (o0 + row) * rb) + unit, __ldcs(reinterpret_cast<const uint4 *>(src.k) + unit));
+    __stcs(reinterpret_cast<uint4 *>(out_v + (o0 + row) * rb) + unit, __ldcs(reinterpret_cast<const uint4 *>(src.v) + unit));
+  }
+}
+
 int element_bytes(int dtype) { return lrk_dtype_size(dtype); }
 
 }  // namespace
@@ -652,8 +773,18 @@ extern "C" int lrk_append(const void *keys, const void *values, const float *pos
   AppendPlan plan{static_cast<const char *>(keys), static_cast<const char *>(values), positions, rows, rb,
                   static_cast<const char *>(new_keys), static_cast<const char *>(new_values), cumulative,
                   nullptr, heads, added, logical_start, out_cumulative, out_lengths};
+  const int64_t out_rows = rows + heads * added;
+  const int64_t tiles = ceil_div(out_rows, kBulkRows);
+  if (vb == 16 && rb % 16 == 0 && rb <= kBulkMaxRowBytes && rows > 0 && tiles >= 2 * sm_count()) {
+    const int shared = static_cast<int>(2 * kBulkRows * rb);
+    cudaError_t e = cudaFuncSetAttribute(append_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shared);
+    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+    append_bulk_kernel<<<static_cast<unsigned>(tiles), kBulkThreads, shared, reinterpret_cast<cudaStream_t>(stream)>>>(
+        plan, static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, out_rows);
+    return launch_status("lrk_append");
+  }
   GatherOut out{static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, rb, rb,
-                rows + heads * added, rb, {}};
+                out_rows, rb, {}};
   return launch_gather(plan, out, vb, reinterpret_cast<cudaStream_t>(stream), "lrk_append");
 }
 
