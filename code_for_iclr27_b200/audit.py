@@ -155,15 +155,16 @@ def tensor_core_order_matches(length: int, window: int, groups: int, chunk: int)
 
 
 # Runtime check of the step-order rule: the first head of each (groups, key
-# count parity, query batches) class this process scores through lrk_logits is
-# also computed by the reference's GEMM and compared bit for bit.  A class
-# that differs (a cuBLAS whose heuristics moved) takes the reference's GEMM
-# from then on, and that head's logits are replaced by the reference's.
+# count parity, window, query chunk) class this process scores through
+# lrk_logits is also computed by the reference's GEMM and compared bit for
+# bit.  A class that differs (a cuBLAS whose heuristics moved) takes the
+# reference's GEMM from then on, and that head's logits are replaced by the
+# reference's.  (The key is cheap to form: the audit asks it for every head.)
 _ORDER_VERIFIED = {}
 
 
 def _order_class(length: int, window: int, groups: int, chunk: int):
-    return groups, length % 2, tuple(sorted({min(chunk, window - a) for a in range(0, window, chunk)}))
+    return groups, length % 2, window, chunk
 
 
 def order_verified(length: int, window: int, groups: int, chunk: int) -> bool:
@@ -197,7 +198,7 @@ def _check_order(per_head_queries, keys, start: int, end: int, chunk: int, logit
         import warnings
 
         warnings.warn(f"lrk_logits' step order differs from this cuBLAS for groups={groups}, "
-                      f"{'odd' if (end - start) % 2 else 'even'} key counts, query batches {key[2]}: "
+                      f"{'odd' if (end - start) % 2 else 'even'} key counts, window {window}, query chunk {chunk}: "
                       "those heads take the reference's GEMM")
         return reference
     return logits

@@ -415,30 +415,35 @@ struct BatchAppendPlan {
   int64_t row_bytes;
   using Shared = NoShared;
   __device__ void prologue(Shared &) const {}
+  // Last segment whose destination is <= o.
+  __device__ int segment_of(int64_t o) const {
+    int lo = 0, hi = table.count;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) / 2;
+      if (table.segment[mid].destination_row <= o) lo = mid; else hi = mid;
+    }
+    return lo;
+  }
+  __device__ RowSource source(int64_t o) const {
+    const int lo = segment_of(o);
+    const lrk_segment &seg = table.segment[lo];
+    const int64_t local = o - seg.destination_row;
+    RowSource out{nullptr, nullptr, 0.0f};
+    if (local >= 0 && local < seg.length) {
+      const int64_t source = seg.source_row + local;
+      out.k = static_cast<const char *>(seg.keys) + source * row_bytes;
+      out.v = static_cast<const char *>(seg.values) + source * row_bytes;
+      out.position = seg.positions[source];
+    } else if (local == seg.length) {
+      out.k = new_k + (segment_base + lo) * row_bytes;
+      out.v = new_v + (segment_base + lo) * row_bytes;
+      out.position = static_cast<float>(seg.logical_position);
+    }
+    return out;
+  }
   template <int TR>
   __device__ void fill(int64_t first, int nrows, RowSource *sources, Shared &) const {
-    for (int i = threadIdx.x; i < nrows; i += kThreads) {
-      const int64_t o = first + i;
-      int lo = 0, hi = table.count;
-      while (hi - lo > 1) {
-        const int mid = (lo + hi) / 2;
-        if (table.segment[mid].destination_row <= o) lo = mid; else hi = mid;
-      }
-      const lrk_segment &seg = table.segment[lo];
-      const int64_t local = o - seg.destination_row;
-      RowSource out{nullptr, nullptr, 0.0f};
-      if (local >= 0 && local < seg.length) {
-        const int64_t source = seg.source_row + local;
-        out.k = static_cast<const char *>(seg.keys) + source * row_bytes;
-        out.v = static_cast<const char *>(seg.values) + source * row_bytes;
-        out.position = seg.positions[source];
-      } else if (local == seg.length) {
-        out.k = new_k + (segment_base + lo) * row_bytes;
-        out.v = new_v + (segment_base + lo) * row_bytes;
-        out.position = static_cast<float>(seg.logical_position);
-      }
-      sources[i] = out;
-    }
+    for (int i = threadIdx.x; i < nrows; i += kThreads) sources[i] = source(first + i);
   }
 };
 
@@ -500,194 +505,163 @@ int launch_gather(const Plan &plan, GatherOut out, int vb, cudaStream_t stream, 
   return launch_status(what);
 }
 
-// lrk_compact by bulk copies, for 16-byte aligned rows of 16-byte multiples
-// up to 512 bytes.  A CTA owns kBulkRows output rows.  Output row o comes from
-// source row o + lower(o) (CompactPlan), so the tile's rows fall into runs of
-// consecutive source rows, one per stretch between removed rows: thread 0
-// finds each run with one binary search, checks that it lies inside the
-// source, and moves it with one `cp.async.bulk` load per tensor (K and V)
-// into shared memory, completing on an mbarrier; the other threads copy the
-// positions meanwhile.  The tile then leaves with one bulk store per tensor.
-// Measured on a configs[1] layer (279k rows of 256 bytes, 64 removed):
-// 42.9 us against 49.0 us for gather_kernel<CompactPlan>, with a fifth of the
-// instructions.  A tile with a run outside the source (an invalid removal
-// list), or whose loads do not land within the bounded wait (the wait is then
-// repeated, also bounded, for the copies in flight), is copied row by row
-// with 16-byte vectors instead, rows without a valid source skipped as in
-// gather_kernel.
+// Bulk-copy engine for the operators whose output tiles are a few runs of
+// consecutive source rows (compaction, append, batch append), for 16-byte
+// aligned rows of 16-byte multiples up to 512 bytes.  A CTA owns kBulkRows
+// output rows.  Thread 0 walks the tile's runs twice (Runs::walk): first to
+// check each against the sizes it knows, then to move each with one
+// `cp.async.bulk` load per tensor (K and V) into shared memory, completing on
+// an mbarrier; the other threads copy the positions meanwhile.  The tile then
+// leaves with one bulk store per tensor.  A tile with an invalid run, or whose
+// loads do not land within the bounded wait (the wait is then repeated, also
+// bounded, for the copies in flight), is copied row by row with 16-byte
+// vectors (Runs::source), rows without a valid source skipped as in
+// gather_kernel.  A generic version (any gather plan's fill, then one thread
+// merging the filled rows into runs) measured 2.7 times slower than the
+// vector engine and was not kept.
 constexpr int kBulkRows = 64;
 constexpr int kBulkThreads = 128;
 constexpr int64_t kBulkMaxRowBytes = 512;
 
-__global__ void __launch_bounds__(kBulkThreads) compact_bulk_kernel(CompactPlan plan, char *__restrict__ out_k,
-                                                                  char *__restrict__ out_v,
-                                                                  float *__restrict__ out_positions,
-                                                                  int64_t out_rows) {
+// Runs of lrk_compact: output row o comes from o + lower(o), so a run ends
+// where the next removed row lands.
+struct CompactRuns {
+  CompactPlan plan;
+  struct Shared {};
+  __device__ void setup(Shared &) const {}
+  template <class Issue>
+  __device__ bool walk(int64_t o0, int n, const Shared &, Issue issue) const {
+    const int64_t rb = plan.row_bytes;
+    for (int64_t o = o0; o < o0 + n;) {
+      const int64_t c = plan.lower(o);
+      const int64_t end = c < plan.removed_count ? lmin(o0 + n, plan.removed[c] - c) : o0 + n;
+      if (!(end > o && o + c >= 0 && end + c <= plan.rows)) return false;
+      issue(o, plan.k + (o + c) * rb, plan.v + (o + c) * rb, end - o);
+      o = end;
+    }
+    return true;
+  }
+  __device__ RowSource source(int64_t o, const Shared &) const {
+    const int64_t source = o + plan.lower(o);
+    if (source < 0 || source >= plan.rows) return {nullptr, nullptr, 0.0f};
+    return {plan.k + source * plan.row_bytes, plan.v + source * plan.row_bytes, plan.positions[source]};
+  }
+};
+
+// Runs of lrk_append: per head the tile overlaps, its cache rows, then its
+// new rows (new_keys is [heads, added, row]).  CTA 0 also writes the new
+// cumulative lengths.
+struct AppendRuns {
+  AppendPlan plan;
+  using Shared = AppendPlan::Shared;
+  __device__ void setup(Shared &s) const {
+    if (plan.heads <= kMaxSharedHeads)
+      for (int64_t h = threadIdx.x; h <= plan.heads; h += kBulkThreads) s.start[h] = plan.cumulative[h] + h * plan.added;
+    if (blockIdx.x == 0 && plan.out_cumulative != nullptr) {
+      for (int64_t h = threadIdx.x; h < plan.heads; h += kBulkThreads) {
+        plan.out_cumulative[h] = static_cast<int32_t>(plan.cumulative[h] + h * plan.added);
+        plan.out_lengths[h] = static_cast<int32_t>(plan.old_length(h) + plan.added);
+      }
+      if (threadIdx.x == 0)
+        plan.out_cumulative[plan.heads] = static_cast<int32_t>(plan.cumulative[plan.heads] + plan.heads * plan.added);
+    }
+  }
+  template <class Issue>
+  __device__ bool walk(int64_t o0, int n, const Shared &s, Issue issue) const {
+    const int64_t rb = plan.row_bytes;
+    int64_t h = plan.head_of(o0, s), o = o0;
+    while (o < o0 + n) {
+      if (h >= plan.heads) return false;
+      const int64_t start = plan.start_of(s, h), old = plan.old_length(h), local = o - start;
+      if (local >= 0 && local < old) {
+        const int64_t end = lmin(o0 + n, start + old), source = plan.cumulative[h] + local;
+        if (source < 0 || source + (end - o) > plan.rows) return false;
+        issue(o, plan.k + source * rb, plan.v + source * rb, end - o);
+        o = end;
+      } else if (local >= old && local < old + plan.added) {
+        const int64_t end = lmin(o0 + n, start + old + plan.added), source = h * plan.added + (local - old);
+        issue(o, plan.new_k + source * rb, plan.new_v + source * rb, end - o);
+        o = end;
+      } else {
+        if (local < 0) return false;
+        ++h;  // past this head
+      }
+    }
+    return true;
+  }
+  __device__ RowSource source(int64_t o, const Shared &s) const { return plan.source(o, s); }
+};
+
+// Runs of lrk_batch_append: per (request, head) segment the tile overlaps,
+// its cache rows, then its one new row.
+struct BatchAppendRuns {
+  BatchAppendPlan plan;
+  struct Shared {};
+  __device__ void setup(Shared &) const {}
+  template <class Issue>
+  __device__ bool walk(int64_t o0, int n, const Shared &, Issue issue) const {
+    const int64_t rb = plan.row_bytes;
+    int i = plan.segment_of(o0);
+    for (int64_t o = o0; o < o0 + n;) {
+      if (i >= plan.table.count) return false;
+      const lrk_segment &seg = plan.table.segment[i];
+      const int64_t local = o - seg.destination_row;
+      if (local >= 0 && local < seg.length) {
+        const int64_t end = lmin(o0 + n, seg.destination_row + seg.length), source = seg.source_row + local;
+        issue(o, static_cast<const char *>(seg.keys) + source * rb, static_cast<const char *>(seg.values) + source * rb,
+              end - o);
+        o = end;
+      } else if (local == seg.length) {
+        issue(o, plan.new_k + (plan.segment_base + i) * rb, plan.new_v + (plan.segment_base + i) * rb, 1);
+        o += 1;
+      } else {
+        if (local < 0) return false;
+        ++i;
+      }
+    }
+    return true;
+  }
+  __device__ RowSource source(int64_t o, const Shared &) const { return plan.source(o); }
+};
+
+template <class Runs>
+__global__ void __launch_bounds__(kBulkThreads) bulk_kernel(Runs runs, char *__restrict__ out_k,
+                                                          char *__restrict__ out_v, float *__restrict__ out_positions,
+                                                          int64_t out_rows, int64_t rb) {
   extern __shared__ __align__(128) unsigned char bulk_stage[];  // K rows, then V rows
+  __shared__ typename Runs::Shared shared;
   __shared__ __align__(8) uint64_t loaded_storage;
   __shared__ int landed;
-  const int64_t rb = plan.row_bytes;
+  runs.setup(shared);
   const int64_t o0 = static_cast<int64_t>(blockIdx.x) * kBulkRows;
   const int n = static_cast<int>(lmin(kBulkRows, out_rows - o0));
   const uint32_t loaded = static_cast<uint32_t>(__cvta_generic_to_shared(&loaded_storage));
   const uint32_t stage_k = static_cast<uint32_t>(__cvta_generic_to_shared(bulk_stage));
   const uint32_t stage_v = stage_k + static_cast<uint32_t>(kBulkRows * rb);
+  __syncthreads();  // setup's shared state
   if (threadIdx.x == 0) {
-    bool ok = true;
     tc::init_barrier(loaded, 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    // Validate every run first: nothing is issued for a tile with a bad one.
-    for (int64_t o = o0; o < o0 + n && ok;) {
-      const int64_t c = plan.lower(o);
-      const int64_t end = c < plan.removed_count ? lmin(o0 + n, plan.removed[c] - c) : o0 + n;
-      ok = end > o && o + c >= 0 && end + c <= plan.rows;
-      o = end;
-    }
+    const bool ok = runs.walk(o0, n, shared, [](int64_t, const char *, const char *, int64_t) {});
     if (ok) {
       tc::expect_bytes(loaded, static_cast<uint32_t>(2 * n * rb));
-      for (int64_t o = o0; o < o0 + n;) {
-        const int64_t c = plan.lower(o);
-        const int64_t end = c < plan.removed_count ? lmin(o0 + n, plan.removed[c] - c) : o0 + n;
-        const uint32_t size = static_cast<uint32_t>((end - o) * rb), offset = static_cast<uint32_t>((o - o0) * rb);
+      runs.walk(o0, n, shared, [&](int64_t o, const char *k_src, const char *v_src, int64_t len) {
+        const uint32_t size = static_cast<uint32_t>(len * rb), offset = static_cast<uint32_t>((o - o0) * rb);
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                          stage_k + offset),
-                     "l"(plan.k + (o + c) * rb), "r"(size), "r"(loaded)
+                     "l"(k_src), "r"(size), "r"(loaded)
                      : "memory");
         asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                          stage_v + offset),
-                     "l"(plan.v + (o + c) * rb), "r"(size), "r"(loaded)
+                     "l"(v_src), "r"(size), "r"(loaded)
                      : "memory");
-        o = end;
-      }
-    }
-    landed = ok;
-  }
-  __syncthreads();
-  // Positions while the loads are in flight; the source of each row again
-  // by lower(), rows without a valid source skipped.
-  for (int i = threadIdx.x; i < n; i += kBulkThreads) {
-    const int64_t o = o0 + i, source = o + plan.lower(o);
-    if (source >= 0 && source < plan.rows) out_positions[o] = plan.positions[source];
-  }
-  if (threadIdx.x == 0 && landed) {
-    if (tc::wait_phase(loaded, 0, nullptr)) {
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      const uint32_t size = static_cast<uint32_t>(n * rb);
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_k + o0 * rb),
-                   "r"(stage_k), "r"(size)
-                   : "memory");
-      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(out_v + o0 * rb),
-                   "r"(stage_v), "r"(size)
-                   : "memory");
-      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
-      asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
-    } else {
-      tc::wait_phase(loaded, 0, nullptr);  // the copies in flight, bounded once more
-      landed = 0;
-    }
-  }
-  __syncthreads();
-  if (landed) return;
-  // Row by row: 16-byte vectors, rows without a valid source skipped.
-  const int units = static_cast<int>(rb / 16);
-  for (int item = threadIdx.x; item < n * units; item += kBulkThreads) {
-    const int row = item / units, unit = item - row * units;
-    const int64_t o = o0 + row, source = o + plan.lower(o);
-    if (source < 0 || source >= plan.rows) continue;
-    const uint4 kv = __ldcs(reinterpret_cast<const uint4 *>(plan.k + source * rb) + unit);
-    const uint4 vv = __ldcs(reinterpret_cast<const uint4 *>(plan.v + source * rb) + unit);
-    __stcs(reinterpret_cast<uint4 *>(out_k + o * rb) + unit, kv);
-    __stcs(reinterpret_cast<uint4 *>(out_v + o * rb) + unit, vv);
-  }
-}
-
-// lrk_append by bulk copies (the decode step of the packed layout), same
-// engine as compact_bulk_kernel: a head's rows in a tile are one run of
-// consecutive cache rows followed by one run of its new rows (new_keys is
-// [heads, added, row]), so thread 0 walks the heads the tile overlaps, checks
-// every run against the source sizes, then issues one bulk load per run and
-// tensor; the tile leaves with one bulk store per tensor.  Positions and the
-// new cumulative lengths are written by plain stores; an invalid run or a
-// timed-out wait copies the tile row by row (AppendPlan::source).
-__global__ void __launch_bounds__(kBulkThreads) append_bulk_kernel(AppendPlan plan, char *__restrict__ out_k,
-                                                                 char *__restrict__ out_v,
-                                                                 float *__restrict__ out_positions,
-                                                                 int64_t out_rows) {
-  extern __shared__ __align__(128) unsigned char bulk_stage[];  // K rows, then V rows
-  __shared__ AppendPlan::Shared shared;
-  __shared__ __align__(8) uint64_t loaded_storage;
-  __shared__ int landed;
-  if (plan.heads <= kMaxSharedHeads)
-    for (int64_t h = threadIdx.x; h <= plan.heads; h += kBulkThreads)
-      shared.start[h] = plan.cumulative[h] + h * plan.added;
-  if (blockIdx.x == 0 && plan.out_cumulative != nullptr) {
-    for (int64_t h = threadIdx.x; h < plan.heads; h += kBulkThreads) {
-      plan.out_cumulative[h] = static_cast<int32_t>(plan.cumulative[h] + h * plan.added);
-      plan.out_lengths[h] = static_cast<int32_t>(plan.old_length(h) + plan.added);
-    }
-    if (threadIdx.x == 0)
-      plan.out_cumulative[plan.heads] = static_cast<int32_t>(plan.cumulative[plan.heads] + plan.heads * plan.added);
-  }
-  __syncthreads();
-  const int64_t rb = plan.row_bytes;
-  const int64_t o0 = static_cast<int64_t>(blockIdx.x) * kBulkRows;
-  const int n = static_cast<int>(lmin(kBulkRows, out_rows - o0));
-  const uint32_t loaded = static_cast<uint32_t>(__cvta_generic_to_shared(&loaded_storage));
-  const uint32_t stage_k = static_cast<uint32_t>(__cvta_generic_to_shared(bulk_stage));
-  const uint32_t stage_v = stage_k + static_cast<uint32_t>(kBulkRows * rb);
-  if (threadIdx.x == 0) {
-    tc::init_barrier(loaded, 1);
-    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    // pass 0 checks every run, pass 1 issues the loads.
-    bool ok = true;
-    for (int pass = 0; pass < 2 && ok; ++pass) {
-      if (pass == 1) tc::expect_bytes(loaded, static_cast<uint32_t>(2 * n * rb));
-      int64_t h = plan.head_of(o0, shared), o = o0;
-      while (o < o0 + n && ok) {
-        if (h >= plan.heads) {
-          ok = false;
-          break;
-        }
-        const int64_t start = plan.start_of(shared, h), old = plan.old_length(h), local = o - start;
-        const char *k_src, *v_src;
-        int64_t end;
-        if (local >= 0 && local < old) {
-          end = lmin(o0 + n, start + old);
-          const int64_t source = plan.cumulative[h] + local;
-          ok = source >= 0 && source + (end - o) <= plan.rows;
-          k_src = plan.k + source * rb;
-          v_src = plan.v + source * rb;
-        } else if (local >= old && local < old + plan.added) {
-          end = lmin(o0 + n, start + old + plan.added);
-          const int64_t source = h * plan.added + (local - old);
-          k_src = plan.new_k + source * rb;
-          v_src = plan.new_v + source * rb;
-        } else {
-          ok = local >= old + plan.added;  // past this head: the next one
-          ++h;
-          continue;
-        }
-        if (pass == 1) {
-          const uint32_t size = static_cast<uint32_t>((end - o) * rb), offset = static_cast<uint32_t>((o - o0) * rb);
-          asm volatile(
-              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                  stage_k + offset),
-              "l"(k_src), "r"(size), "r"(loaded)
-              : "memory");
-          asm volatile(
-              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                  stage_v + offset),
-              "l"(v_src), "r"(size), "r"(loaded)
-              : "memory");
-        }
-        o = end;
-      }
+      });
     }
     landed = ok;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += kBulkThreads) {
-    const RowSource src = plan.source(o0 + i, shared);
+    const RowSource src = runs.source(o0 + i, shared);
     if (src.k != nullptr) out_positions[o0 + i] = src.position;
   }
   if (threadIdx.x == 0 && landed) {
@@ -712,11 +686,34 @@ __global__ void __launch_bounds__(kBulkThreads) append_bulk_kernel(AppendPlan pl
   const int units = static_cast<int>(rb / 16);
   for (int item = threadIdx.x; item < n * units; item += kBulkThreads) {
     const int row = item / units, unit = item - row * units;
-    const RowSource src = plan.source(o0 + row, shared);
+    const RowSource src = runs.source(o0 + row, shared);
     if (src.k == nullptr) continue;
-    __stcs(reinterpret_cast<uint4 *>(out_k + (o0 + row) * rb) + unit, __ldcs(reinterpret_cast<const uint4 *>(src.k) + unit));
-    __stcs(reinterpret_cast<uint4 *>(out_v + (o0 + row) * rb) + unit, __ldcs(reinterpret_cast<const uint4 *>(src.v) + unit));
+    __stcs(reinterpret_cast<uint4 *>(out_k + (o0 + row) * rb) + unit,
+           __ldcs(reinterpret_cast<const uint4 *>(src.k) + unit));
+    __stcs(reinterpret_cast<uint4 *>(out_v + (o0 + row) * rb) + unit,
+           __ldcs(reinterpret_cast<const uint4 *>(src.v) + unit));
   }
+}
+
+// Launches bulk_kernel when the rows qualify (vb: the common vector width of
+// every source and output pointer; breaks: how many places the output's runs
+// can end, at most one per tile on average, since a tile of many short runs
+// issues many small copies: an audit of configs[0] or [4] that evicts half or
+// more of the rows takes the vector engine); returns LRK_ERR_UNSUPPORTED
+// otherwise.
+template <class Runs>
+int launch_bulk(const Runs &runs, int vb, int64_t rb, char *out_k, char *out_v, float *out_positions,
+                int64_t out_rows, int64_t breaks, cudaStream_t stream, const char *what) {
+  const int64_t tiles = ceil_div(out_rows, kBulkRows);
+  if (vb != 16 || rb % 16 != 0 || rb > kBulkMaxRowBytes || tiles < 2 * sm_count() || breaks > tiles)
+    return LRK_ERR_UNSUPPORTED;
+  const int shared = static_cast<int>(2 * kBulkRows * rb);
+  auto kernel = bulk_kernel<Runs>;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shared);
+  if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
+  kernel<<<static_cast<unsigned>(tiles), kBulkThreads, shared, stream>>>(runs, out_k, out_v, out_positions, out_rows,
+                                                                       rb);
+  return launch_status(what);
 }
 
 int element_bytes(int dtype) { return lrk_dtype_size(dtype); }
@@ -741,15 +738,10 @@ extern "C" int lrk_compact(const void *keys, const void *values, const float *po
   const int vb = pick_vector(rb, {keys, values, out_keys, out_values}, {});
   CompactPlan plan{static_cast<const char *>(keys), static_cast<const char *>(values), positions, rows, rb,
                    removed, removed_count};
-  const int64_t tiles = ceil_div(out_rows, kBulkRows);
-  if (vb == 16 && rb % 16 == 0 && rb <= kBulkMaxRowBytes && tiles >= 2 * sm_count()) {
-    const int shared = static_cast<int>(2 * kBulkRows * rb);
-    cudaError_t e = cudaFuncSetAttribute(compact_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shared);
-    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-    compact_bulk_kernel<<<static_cast<unsigned>(tiles), kBulkThreads, shared, reinterpret_cast<cudaStream_t>(stream)>>>(
-        plan, static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, out_rows);
-    return launch_status("lrk_compact");
-  }
+  const int bulk = launch_bulk(CompactRuns{plan}, vb, rb, static_cast<char *>(out_keys), static_cast<char *>(out_values),
+                               out_positions, out_rows, removed_count, reinterpret_cast<cudaStream_t>(stream),
+                               "lrk_compact");
+  if (bulk != LRK_ERR_UNSUPPORTED) return bulk;
   GatherOut out{static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, rb, rb,
                 out_rows, rb, {}};
   return launch_gather(plan, out, vb, reinterpret_cast<cudaStream_t>(stream), "lrk_compact");
@@ -774,14 +766,11 @@ extern "C" int lrk_append(const void *keys, const void *values, const float *pos
                   static_cast<const char *>(new_keys), static_cast<const char *>(new_values), cumulative,
                   nullptr, heads, added, logical_start, out_cumulative, out_lengths};
   const int64_t out_rows = rows + heads * added;
-  const int64_t tiles = ceil_div(out_rows, kBulkRows);
-  if (vb == 16 && rb % 16 == 0 && rb <= kBulkMaxRowBytes && rows > 0 && tiles >= 2 * sm_count()) {
-    const int shared = static_cast<int>(2 * kBulkRows * rb);
-    cudaError_t e = cudaFuncSetAttribute(append_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, shared);
-    if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
-    append_bulk_kernel<<<static_cast<unsigned>(tiles), kBulkThreads, shared, reinterpret_cast<cudaStream_t>(stream)>>>(
-        plan, static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, out_rows);
-    return launch_status("lrk_append");
+  if (rows > 0) {
+    const int bulk = launch_bulk(AppendRuns{plan}, vb, rb, static_cast<char *>(out_keys),
+                                 static_cast<char *>(out_values), out_positions, out_rows, 2 * heads,
+                                 reinterpret_cast<cudaStream_t>(stream), "lrk_append");
+    if (bulk != LRK_ERR_UNSUPPORTED) return bulk;
   }
   GatherOut out{static_cast<char *>(out_keys), static_cast<char *>(out_values), out_positions, rb, rb,
                 out_rows, rb, {}};
@@ -948,9 +937,14 @@ extern "C" int lrk_batch_append(const lrk_segment *segments, int64_t segment_cou
     plan.new_v = static_cast<const char *>(new_values);
     plan.segment_base = s0;
     plan.row_bytes = rb;
-    GatherOut out{static_cast<char *>(out_keys) + first * rb, static_cast<char *>(out_values) + first * rb,
-                  out_positions + first, rb, rb, last - first, rb, {}};
-    const int status = launch_gather(plan, out, vb, cs, "lrk_batch_append");
+    int status = launch_bulk(BatchAppendRuns{plan}, vb, rb, static_cast<char *>(out_keys) + first * rb,
+                             static_cast<char *>(out_values) + first * rb, out_positions + first, last - first, 2 * n,
+                             cs, "lrk_batch_append");
+    if (status == LRK_ERR_UNSUPPORTED) {
+      GatherOut out{static_cast<char *>(out_keys) + first * rb, static_cast<char *>(out_values) + first * rb,
+                    out_positions + first, rb, rb, last - first, rb, {}};
+      status = launch_gather(plan, out, vb, cs, "lrk_batch_append");
+    }
     if (status != LRK_OK) return status;
   }
   return LRK_OK;

@@ -1,9 +1,10 @@
 """The data-movement operators at sizes of whole layers (48k+ rows) against
-the oracle.  lrk_compact takes its bulk-copy kernel (compact_bulk_kernel in
-csrc/move.cu: outputs of at least 2 x SMs x 64 rows, 16-byte aligned rows of
-16-byte multiples up to 512 bytes) in the aligned cases and the vector gather
-engine in the misaligned twin; append, merge, merge_layers, batch_append and
-the legacy flattened append / compact run the vector engine at the same sizes.
+the oracle.  lrk_compact, lrk_append and lrk_batch_append take the bulk-copy
+kernel (bulk_kernel in csrc/move.cu: outputs of at least 2 x SMs x 64 rows,
+16-byte aligned rows of 16-byte multiples up to 512 bytes, at most one run
+break per tile on average) in the aligned cases and the vector gather engine
+in the misaligned twins and heavy compactions; merge, merge_layers and the
+legacy flattened append / compact run the vector engine at the same sizes.
 Row widths 128, 256 and 512 bytes; runs of every length (compactions remove
 runs and isolated rows; merges interleave single recalled rows)."""
 import numpy as np
@@ -65,7 +66,10 @@ def test_compact_bulk(C, cuda, d, misaligned):
     rows = ROWS + 777
     keys, values = kv(rows, d, g, cuda, misaligned), kv(rows, d, g, cuda, misaligned)
     positions = (torch.arange(rows, dtype=torch.float32) * 2).reshape(-1, 1).to(cuda)
-    for removed in (torch.randperm(rows, generator=g)[:rows // 7].sort().values,
+    # At most one removed row per 64-row tile on average takes the bulk kernel
+    # (runs of every length, several per tile in places); more, the vector engine.
+    for removed in (torch.randperm(rows, generator=g)[:500].sort().values,
+                    torch.randperm(rows, generator=g)[:rows // 7].sort().values,
                     torch.cat([torch.arange(5, 70), torch.arange(1000, 1001), torch.arange(rows - 130, rows)]),
                     torch.zeros(0, dtype=torch.int64)):
         out = C.compact(keys, values, positions, removed.to(cuda))

@@ -578,7 +578,7 @@ def test_layer_logits_equal_reference_chunks(C, cuda, window, groups):
 
 
 def test_layer_logits_runtime_order_check(C, cuda, monkeypatch):
-    """The first head of each (groups, parity, query batches) class goes
+    """The first head of each (groups, parity, window, chunk) class goes
     through lrk_logits and is checked against the reference GEMM; a class
     marked as failed takes the reference GEMM for all its heads (no
     lrk_logits_heads launch for them) and the logits still equal the
