@@ -258,11 +258,12 @@ def layer_logits(per_head, keys, spans, window: int, groups: int, reference_stre
         starts = [spans[i][1] for i in fast]
         ends = [spans[i][2] for i in fast]
         steps = [8 if (e - b) % 2 else 16 for b, e in zip(starts, ends)]
-        views = operators().logits_heads(per_head, keys, heads, starts, ends, steps)
+        views = operators().logits_heads(per_head, keys, heads, starts, ends, steps, groups)
         for i, view, b, e in zip(fast, views, starts, ends):
             head, _, _, chunk = spans[i]
-            out[i] = _check_order(per_head[head].view(window, groups, dim), keys, b, e, chunk,
-                                  view.view(window, groups, -1)[:, :, :e - b])
+            out[i] = view  # [window, groups, e - b]
+            if _order_class(e - b, window, groups, chunk) not in _ORDER_VERIFIED:
+                out[i] = _check_order(per_head[head].view(window, groups, dim), keys, b, e, chunk, out[i])
     return out
 
 
@@ -288,6 +289,22 @@ def _audit_streams(device):
         highest = torch.cuda.Stream.priority_range()[1] if hasattr(torch.cuda.Stream, "priority_range") else -1
         _STREAMS[key] = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device, priority=highest))
     return _STREAMS[key]
+
+
+def _head_pieces(spans, total: int):
+    """Split sizes that cut [0, total) at every head's (start, end) -- heads
+    ascending and disjoint, with or without gaps between them -- and each
+    head's piece index."""
+    pieces, at, cursor = [], [], 0
+    for start, end in spans:
+        if start > cursor:
+            pieces.append(start - cursor)
+        at.append(len(pieces))
+        pieces.append(end - start)
+        cursor = end
+    if cursor < total:
+        pieces.append(total - cursor)
+    return pieces, at
 
 
 def score_table_fused(cache, queries, query_positions, gradients, base_margin, protect_recent=32,
@@ -355,9 +372,13 @@ def score_table_fused(cache, queries, query_positions, gradients, base_margin, p
         scoring.wait_event(ready)
         held.append((projected, per_head, logits))
         pvs, kpos, firsts, lasts, chunks = [], [], [], [], []
+        # Every head's projected values and positions as views, two calls per
+        # layer (the pieces between heads of a gapped layout are split off too).
+        pieces, at = _head_pieces(spans, positions.shape[0])
+        pv_views, kpos_views = projected.split(pieces, dim=1), positions.split(pieces)
         for head, start, end, candidate_start, candidate_end, chunk in heads_kept:
-            pvs.append(projected[:, start:end])
-            kpos.append(positions[start:end])
+            pvs.append(pv_views[at[head]])
+            kpos.append(kpos_views[at[head]])
             firsts.append(candidate_start)
             lasts.append(candidate_end)
             chunks.append(chunk)

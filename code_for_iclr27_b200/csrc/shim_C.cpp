@@ -516,7 +516,7 @@ torch::Tensor logits(torch::Tensor queries, torch::Tensor keys, int64_t k_step, 
 // configs[1] layer with a stride rounded to 8).
 std::vector<torch::Tensor> logits_heads(torch::Tensor queries, torch::Tensor keys, std::vector<int64_t> heads,
                                         std::vector<int64_t> starts, std::vector<int64_t> ends,
-                                        std::vector<int64_t> k_steps) {
+                                        std::vector<int64_t> k_steps, int64_t groups) {
   check_cuda(queries, queries);
   check_cuda(keys, queries);
   TORCH_CHECK(queries.dim() == 3 && keys.dim() == 2 && queries.size(2) == keys.size(1) &&
@@ -527,6 +527,7 @@ std::vector<torch::Tensor> logits_heads(torch::Tensor queries, torch::Tensor key
   TORCH_CHECK(starts.size() == n && ends.size() == n && k_steps.size() == n,
               "heads, starts, ends and k_steps must have one entry per head");
   const int64_t rows = queries.size(1), dim = queries.size(2);
+  TORCH_CHECK(groups >= 0 && (groups == 0 || rows % groups == 0), "groups must divide the query rows");
   std::vector<int64_t> offsets(n + 1, 0);
   for (size_t i = 0; i < n; ++i) {
     TORCH_CHECK(heads[i] >= 0 && heads[i] < queries.size(0), "head index out of range");
@@ -548,7 +549,9 @@ std::vector<torch::Tensor> logits_heads(torch::Tensor queries, torch::Tensor key
     h.k_step = k_steps[i];
     h.out = static_cast<char *>(flat.data_ptr()) + offsets[i] * element;
     h.out_stride = stride;
-    out.push_back(flat.narrow(0, offsets[i], rows * stride).view({rows, stride}));
+    auto head_logits = flat.narrow(0, offsets[i], rows * stride).view({rows, stride});
+    // groups > 0: the head's [window, groups, count] view (rows = window * groups).
+    out.push_back(groups > 0 ? head_logits.view({rows / groups, groups, stride}).narrow(2, 0, count) : head_logits);
   }
   check_status(lrk_logits_heads(table.data(), static_cast<int64_t>(n), rows, dim, current_stream()));
   return out;
@@ -932,7 +935,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("topk_smallest", &topk_smallest);
   module.def("logits", &logits);
   module.def("logits_heads", &logits_heads, pybind11::arg("queries"), pybind11::arg("keys"), pybind11::arg("heads"),
-             pybind11::arg("starts"), pybind11::arg("ends"), pybind11::arg("k_steps"));
+             pybind11::arg("starts"), pybind11::arg("ends"), pybind11::arg("k_steps"), pybind11::arg("groups") = 0);
   module.def("temporal_scores", &temporal_scores, pybind11::arg("logits"), pybind11::arg("projected_values"),
              pybind11::arg("key_positions"), pybind11::arg("first"), pybind11::arg("last"),
              pybind11::arg("query_positions"), pybind11::arg("margin"), pybind11::arg("scale"),
