@@ -5,6 +5,9 @@
 CASE is one of:
   scores         lrk_temporal_scores over one layer (8 heads x [250, 4, 34880]
                  bf16 logits, 558 MB, larger than L2)
+  scores_large   lrk_temporal_scores over one configs[4] layer (8 heads x
+                 [250, 8, 32768] bf16 logits, 1 GB; every row but the last 32
+                 a candidate, so the probability stash is 2.1 GB)
   probabilities  temporal_probabilities on one query chunk [79, 4, 35026]
   risk           temporal_risk over 2226 candidates of that chunk
   compact        compaction of one layer (279k rows of D=128 bf16) removing 64 rows
@@ -36,7 +39,7 @@ LAYER_ROWS = 8 * 34880
 
 def main(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    parser.add_argument("case", choices=["scores", "probabilities", "risk", "compact", "append", "refine",
+    parser.add_argument("case", choices=["scores", "scores_large", "probabilities", "risk", "compact", "append", "refine",
                                            "project", "logits", "logits_odd", "logits_layer", "from_keys",
                                            "table_fused", "large_pass", "arena_evict", "select"])
     parser.add_argument("--iters", type=int, default=3)
@@ -58,6 +61,16 @@ def main(argv=None):
         qpos = torch.arange(length - window, length, dtype=torch.int64, device=dev)
         margin = torch.tensor([1.0], device=dev)
         run = lambda: C.temporal_scores(logits, pv, kpos, [32768] * 8, [length - 32] * 8, qpos, margin,
+                                        1 / math.sqrt(128), 1e-6)
+    elif args.case == "scores_large":
+        length, window, groups = 32768, 250, 8
+        logits = [(torch.randn(window, groups, length, generator=g, device=dev) * 2 * math.sqrt(128)).to(torch.bfloat16)
+                  for _ in range(8)]
+        pv = [torch.randn(groups, length, generator=g, device=dev) for _ in range(8)]
+        kpos = [torch.arange(length, dtype=torch.float32, device=dev) for _ in range(8)]
+        qpos = torch.arange(length - window, length, dtype=torch.int64, device=dev)
+        margin = torch.tensor([1.0], device=dev)
+        run = lambda: C.temporal_scores(logits, pv, kpos, [0] * 8, [length - 32] * 8, qpos, margin,
                                         1 / math.sqrt(128), 1e-6)
     elif args.case in ("probabilities", "risk"):
         window, groups, length = 79, 4, 35026
