@@ -80,11 +80,12 @@ class PackedCache:
         import torch
 
         coordinates = np.asarray(coordinates, dtype=np.int64).reshape(-1, 2)
-        bounds = {int(l): self.layers[int(l)].bounds() for l in np.unique(coordinates[:, 0])}
-        table = np.empty((4, coordinates.shape[0]), dtype=np.int64)
-        for i, (l, h) in enumerate(coordinates.tolist()):
-            layer = self.layers[l]
-            table[:, i] = (l, bounds[l][h], layer.prompt_lens[h], layer.head_lens[h])
+        used = np.unique(coordinates[:, 0])
+        lens = np.asarray([self.layers[int(l)].head_lens for l in used], dtype=np.int64)
+        prompts = np.asarray([self.layers[int(l)].prompt_lens for l in used], dtype=np.int64)
+        starts = np.cumsum(lens, axis=1) - lens
+        row, head = np.searchsorted(used, coordinates[:, 0]), coordinates[:, 1]
+        table = np.stack((coordinates[:, 0], starts[row, head], prompts[row, head], lens[row, head]))
         return upload(table, self.layers[0].keys.device)
 
     def remove_selected(self, coordinates: Sequence[Tuple[int, int]], segment_ids, positions, table=None) -> int:
