@@ -65,18 +65,42 @@ constexpr int kVisibilityThreads = 1024;
 // One CTA per segment.  If key_positions[0 .. length) is non-decreasing (and
 // free of NaN), visible[(segment * window) + q] = the number of keys with
 // position <= the query's position (they are a prefix); otherwise -1.
+// Every kVisibilitySample-th key position sits in shared memory, so a query's
+// search takes a few shared-memory steps and one short search of global
+// memory (the sortedness check's loads left the positions in L2).
+constexpr int kVisibilitySample = 64;
+constexpr int kVisibilitySamples = 2048;  // rows up to 131,072 keys use the samples
+
 __global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTableParam table,
                                                                         const int64_t *__restrict__ qpos, int window,
                                                                         int32_t *__restrict__ visible,
                                                                         int64_t segment_base) {
+  __shared__ float samples[kVisibilitySamples];
   const lrk_score_segment &seg = table.segment[blockIdx.x];
   const float *kpos = seg.key_positions;
   const int64_t n = seg.length;
+  // Non-decreasing and free of NaN; eight elements per thread per round, all
+  // loads of a round issued before the comparisons.
   int ordered = 1;
-  for (int64_t p = threadIdx.x; p < n; p += kVisibilityThreads) {
-    const float here = __ldg(kpos + p);
-    if (!(here == here) || (p + 1 < n && !(here <= __ldg(kpos + p + 1)))) ordered = 0;
+  constexpr int kUnroll = 8;
+  for (int64_t base = threadIdx.x; base < n; base += static_cast<int64_t>(kVisibilityThreads) * kUnroll) {
+    float here[kUnroll], next[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t p = base + static_cast<int64_t>(u) * kVisibilityThreads;
+      here[u] = p < n ? __ldg(kpos + p) : 0.0f;
+      next[u] = p + 1 < n ? __ldg(kpos + p + 1) : INFINITY;
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t p = base + static_cast<int64_t>(u) * kVisibilityThreads;
+      if (p < n && (!(here[u] == here[u]) || !(here[u] <= next[u]))) ordered = 0;
+    }
   }
+  const int64_t sampled = (n + kVisibilitySample - 1) / kVisibilitySample;
+  const bool use_samples = sampled <= kVisibilitySamples;
+  if (use_samples)
+    for (int64_t j = threadIdx.x; j < sampled; j += kVisibilityThreads) samples[j] = __ldg(kpos + j * kVisibilitySample);
   ordered = __syncthreads_and(ordered);
   int32_t *out = visible + (segment_base + blockIdx.x) * window;
   for (int q = threadIdx.x; q < window; q += kVisibilityThreads) {
@@ -84,6 +108,20 @@ __global__ void __launch_bounds__(kVisibilityThreads) visibility_kernel(ScoreTab
     if (ordered) {
       const float position = static_cast<float>(qpos[q]);
       int64_t lo = 0, hi = n;  // first key with position > the query's
+      if (use_samples && sampled > 0) {
+        // The last sample at or below the position bounds the search window.
+        int slo = 0, shi = static_cast<int>(sampled);  // first sample > position
+        while (slo < shi) {
+          const int mid = (slo + shi) / 2;
+          if (samples[mid] <= position) slo = mid + 1; else shi = mid;
+        }
+        if (slo == 0) {
+          hi = 0;
+        } else {
+          lo = static_cast<int64_t>(slo - 1) * kVisibilitySample + 1;
+          hi = lmin(n, static_cast<int64_t>(slo) * kVisibilitySample);
+        }
+      }
       while (lo < hi) {
         const int64_t mid = (lo + hi) / 2;
         if (__ldg(kpos + mid) <= position) lo = mid + 1; else hi = mid;

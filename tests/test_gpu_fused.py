@@ -93,7 +93,7 @@ CASES = [
     ("bf16", 7, 4, 20008, 100, 20000),
     ("f16", 5, 2, 40000, 0, 40000),
     ("bf16", 3, 4, 100000, 99000, 100000),
-    # aligned rows of 18,433 .. 36,864 keys: the two-CTA cluster statistics
+    # aligned rows just above the fp32-weight stage: the packed stage
     ("bf16", 5, 4, 36864, 100, 36000),
     ("bf16", 6, 8, 18440, 0, 18440),
     ("f16", 4, 2, 25600, 25000, 25600),
@@ -127,13 +127,15 @@ def test_fused_matches_dropin_and_oracle(C, cuda, dtype_name, window, groups, le
 KEY_LAYOUTS = ["sorted_ties", "shuffled", "sorted_nan", "sorted_inf", "descending"]
 
 
-@pytest.mark.parametrize("length", [3001, 20011, 24576])
+@pytest.mark.parametrize("length", [3001, 20011, 24576, 140001])
 @pytest.mark.parametrize("layout", KEY_LAYOUTS)
 def test_fused_key_position_layouts(C, cuda, layout, length):
     """Masks from every kind of key-position vector: non-decreasing ones take
-    the visible-prefix path, the others compare positions per key.  Queries sit
-    inside the key range, so each row sees a different prefix (some none).
-    The fused scores must equal the drop-in composition bit for bit."""
+    the visible-prefix path (its search through sampled positions up to
+    131,072 keys, a plain binary search above), the others compare positions
+    per key.  Queries sit inside the key range, so each row sees a different
+    prefix (some none).  The fused scores must equal the drop-in composition
+    bit for bit."""
     import torch
 
     g = torch.Generator().manual_seed(KEY_LAYOUTS.index(layout) * 7919 + length)
