@@ -119,6 +119,7 @@ SIGNATURES = {
     "lrk_arena_compact_positions": (I32, [ctypes.POINTER(Arena), P, I64, P, P, P]),
     "lrk_arena_evict": (I32, [ctypes.POINTER(Arena), P, P, I64, P, P]),
     "lrk_merge_plan": (I32, [ctypes.POINTER(PlanLayer), I64, I64, P, P]),
+    "lrk_arena_insert": (I32, [ctypes.POINTER(Arena), P, I64, P, P, I32, P, P]),
 }
 
 _library = None

@@ -303,6 +303,79 @@ class ArenaCache:
                                 logical.contiguous(), self.flags[1:2])
         self._stale = True
 
+    # -------------------------------------------------------------- recall
+
+    # Entries one lrk_arena_insert launch takes per head; a larger event goes
+    # in rounds (merging in rounds gives the same rows: the order is by position).
+    INSERT_MAX = 2048
+
+    def insert_payload(self, payload, metadata) -> int:
+        """Recall reinsertion in place (cache.py:201-253): payload [n, 2, D]
+        (K, V rows on the arena's device), metadata [n, 3] of (layer, head,
+        position).  Each touched head's rows above its first recalled
+        position move up inside its slot and the recalled rows land in
+        position order -- the rows and positions the reference's merge gives
+        the head -- with no layer copied.  A check launch runs first and its
+        flag is read before anything moves: a position recalled twice or
+        recalled while resident raises ValueError (cache unchanged, as the
+        reference refuses the merge); a head whose positions do not ascend
+        raises ValueError too (the arena keeps heads in position order; a
+        caller-built arena may not).  A head without room grows every slot
+        first.  Returns the number of rows inserted."""
+        import torch
+
+        metadata = np.asarray(metadata, dtype=np.int64).reshape(-1, 3)
+        if payload.shape[:2] != (len(metadata), 2):
+            raise ValueError("Recall payload/identity shape mismatch")
+        if not len(metadata):
+            return 0
+        layers = len(self.head_lens)
+        if ((metadata[:, 1] < 0) | (metadata[:, 1] >= self.heads) | (metadata[:, 0] < 0)
+                | (metadata[:, 0] >= layers)).any():
+            raise AssertionError("Recall changed logical time or inserted an incorrect slot count")
+        flat = metadata[:, 0] * self.heads + metadata[:, 1]
+        order = np.lexsort((metadata[:, 2], flat))
+        flat_sorted = flat[order]
+        heads, first, counts = np.unique(flat_sorted, return_index=True, return_counts=True)
+        lens = self.head_lens.reshape(-1)
+        need = int((lens[heads] + counts).max())
+        if need > self.capacity:
+            self._grow(max(need - self.capacity, 256, self.capacity // 8))
+        rank = np.arange(len(order)) - np.repeat(first, counts)  # each entry's place within its head
+        positions_sorted = metadata[order, 2]
+        if ((flat_sorted[1:] == flat_sorted[:-1]) & (positions_sorted[1:] == positions_sorted[:-1])).any():
+            raise ValueError("Cannot merge duplicate physical KV identities")
+        rounds = int((counts.max() + self.INSERT_MAX - 1) // self.INSERT_MAX)
+        rows_all = upload(order, self.device)
+        recalled_all = payload.index_select(0, rows_all).contiguous()
+        positions_all = upload(positions_sorted.astype(np.float32), self.device)
+        batches = []
+        for r in range(rounds):
+            picked = np.flatnonzero((rank >= r * self.INSERT_MAX) & (rank < (r + 1) * self.INSERT_MAX))
+            part_heads, part_first, part_counts = np.unique(flat_sorted[picked], return_index=True,
+                                                            return_counts=True)
+            plan = upload(np.stack([part_heads, part_first, part_counts], axis=1).astype(np.int64), self.device)
+            if rounds > 1:
+                index = upload(picked.astype(np.int64), self.device)
+                recalled = recalled_all.index_select(0, index).contiguous()
+                positions = positions_all.index_select(0, index).contiguous()
+            else:
+                recalled, positions = recalled_all, positions_all
+            batches.append(((self.keys, self.values, self.positions, self.lengths, plan, recalled, positions),
+                            part_heads, part_counts))
+        # Every round is checked against the rows resident now before any
+        # moves (the rounds' entries were checked against each other above).
+        for args, _, _ in batches:
+            state = int(operators().arena_insert(*args, True).item())
+            if state & 1:
+                raise ValueError("Cannot merge duplicate physical KV identities")
+            if state:
+                raise ValueError(f"arena recall refused (flag {state}): positions must ascend in every head")
+        for args, part_heads, part_counts in batches:
+            operators().arena_insert(*args, False)
+            self._head_lens.reshape(-1)[part_heads] += part_counts
+        return int(len(metadata))
+
     def check_flags(self) -> None:
         """Raise if a kernel flagged a full slot or a bad removal list (reads
         the device flags: a synchronisation)."""

@@ -286,6 +286,110 @@ __global__ void __launch_bounds__(kCompactThreads, 2) arena_evict_kernel(ArenaPa
   }
 }
 
+// Recall reinsertion in place (lrk_arena_insert).  One CTA per touched head.
+// The head's recalled entries (ascending positions, at most kInsertMax) sit
+// in shared memory.  CHECK: only flags (1: a position recalled twice or
+// recalled while resident; 2: resident positions not ascending; 4: the head
+// would pass its capacity; 8: more than kInsertMax entries).  Otherwise a
+// resident row i moves up by k(i) = the entries below its position, which
+// never decreases with i: chunks of rows go from the top of the head down
+// (loads, barrier, stores), so no store reaches a row still to be loaded and
+// no chunk writes where a higher chunk wrote; only the rows above the first
+// entry's place move.  Then entry e lands in row e + (resident rows below
+// it), a slot the moves have emptied, and the length grows by the count.
+constexpr int kInsertMax = 2048;
+
+template <bool CHECK>
+__global__ void __launch_bounds__(kCompactThreads) arena_insert_kernel(ArenaParam a, const int64_t *__restrict__ plan,
+                                                                       int64_t touched,
+                                                                       const char *__restrict__ recalled,
+                                                                       const float *__restrict__ recalled_positions,
+                                                                       unsigned int *__restrict__ flag) {
+  __shared__ float entries[kInsertMax];
+  __shared__ int32_t landing[kInsertMax];
+  __shared__ int32_t shift[kCompactThreads];
+  const int64_t vectors = a.row_bytes / 16;
+  const int64_t chunk_rows = chunk_rows_for(vectors);
+  for (int64_t t = blockIdx.x; t < touched; t += gridDim.x) {
+    const int64_t head = plan[3 * t], first = plan[3 * t + 1], count = plan[3 * t + 2];
+    if (head < 0 || head >= a.heads_total || count <= 0) continue;
+    const int64_t length = a.lengths[head];
+    char *keys = a.keys + head * a.capacity * a.row_bytes;
+    char *values = a.values + head * a.capacity * a.row_bytes;
+    float *positions = a.positions + head * a.capacity;
+    const float *wanted = recalled_positions + first;
+    if (CHECK) {
+      if (threadIdx.x == 0) {
+        if (length < 0 || length + count > a.capacity) atomicOr(flag, 4u);
+        if (count > kInsertMax) atomicOr(flag, 8u);
+      }
+      const int64_t rows = lmin(lmax(length, 0), a.capacity);
+      for (int64_t i = threadIdx.x; i < rows; i += kCompactThreads) {
+        const float p = positions[i];
+        if (i > 0 && !(positions[i - 1] < p)) atomicOr(flag, 2u);
+        const int64_t k = count_below(wanted, count, p);
+        if (k < count && wanted[k] == p) atomicOr(flag, 1u);
+      }
+      for (int64_t e = threadIdx.x; e < count; e += kCompactThreads)
+        if (e > 0 && !(wanted[e - 1] < wanted[e])) atomicOr(flag, 1u);
+      continue;
+    }
+    if (length < 0 || length + count > a.capacity || count > kInsertMax) {  // the check refused it
+      if (threadIdx.x == 0) atomicOr(flag, 4u);
+      continue;
+    }
+    __syncthreads();  // the previous head's shared arrays are free
+    for (int64_t e = threadIdx.x; e < count; e += kCompactThreads) {
+      entries[e] = wanted[e];
+      landing[e] = static_cast<int32_t>(e + count_below(positions, length, wanted[e]));
+    }
+    __syncthreads();
+    const int64_t lowest = landing[0];  // resident rows below the first entry stay
+    for (int64_t end = length; end > lowest;) {
+      const int64_t start = lmax(lowest, end - chunk_rows), rows_here = end - start;
+      uint4 k[kCompactVectors], v[kCompactVectors];
+#pragma unroll
+      for (int j = 0; j < kCompactVectors; ++j) {
+        const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
+        const int64_t r = item / vectors, c = item % vectors;
+        if (r < rows_here) {
+          k[j] = reinterpret_cast<const uint4 *>(keys + (start + r) * a.row_bytes)[c];
+          v[j] = reinterpret_cast<const uint4 *>(values + (start + r) * a.row_bytes)[c];
+        }
+      }
+      float p = 0.0f;
+      if (threadIdx.x < rows_here) {
+        p = positions[start + threadIdx.x];
+        shift[threadIdx.x] = static_cast<int32_t>(count_below(entries, count, p));
+      }
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < kCompactVectors; ++j) {
+        const int64_t item = threadIdx.x + static_cast<int64_t>(j) * kCompactThreads;
+        const int64_t r = item / vectors, c = item % vectors;
+        if (r < rows_here) {
+          const int64_t to = start + r + shift[r];
+          reinterpret_cast<uint4 *>(keys + to * a.row_bytes)[c] = k[j];
+          reinterpret_cast<uint4 *>(values + to * a.row_bytes)[c] = v[j];
+        }
+      }
+      if (threadIdx.x < rows_here) positions[start + threadIdx.x + shift[threadIdx.x]] = p;
+      __syncthreads();  // shift[] and this chunk's stores before the next chunk
+      end = start;
+    }
+    const char *rows = recalled + first * 2 * a.row_bytes;
+    for (int64_t item = threadIdx.x; item < count * vectors; item += kCompactThreads) {
+      const int64_t e = item / vectors, c = item % vectors, to = landing[e];
+      reinterpret_cast<uint4 *>(keys + to * a.row_bytes)[c] =
+          reinterpret_cast<const uint4 *>(rows + 2 * e * a.row_bytes)[c];
+      reinterpret_cast<uint4 *>(values + to * a.row_bytes)[c] =
+          reinterpret_cast<const uint4 *>(rows + (2 * e + 1) * a.row_bytes)[c];
+    }
+    for (int64_t e = threadIdx.x; e < count; e += kCompactThreads) positions[landing[e]] = entries[e];
+    if (threadIdx.x == 0) a.lengths[head] = static_cast<int32_t>(length + count);
+  }
+}
+
 int check_arena(const lrk_arena *arena, int64_t *element) {
   LRK_REQUIRE(arena != nullptr, "null arena");
   LRK_REQUIRE(arena->heads_total >= 0 && arena->capacity > 0 && arena->dimension > 0, "invalid arena sizes");
@@ -362,4 +466,27 @@ extern "C" int lrk_arena_evict(const lrk_arena *arena, const int64_t *heads, con
   arena_evict_kernel<<<blocks, kCompactThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       param(*arena, element), heads, removed_positions, count, error);
   return launch_status("lrk_arena_evict");
+}
+
+extern "C" int lrk_arena_insert(const lrk_arena *arena, const int64_t *plan, int64_t touched, const void *recalled,
+                                const float *recalled_positions, int check, unsigned int *flag, lrk_stream_t stream) {
+  clear_error();
+  int64_t element = 0;
+  int status = check_arena(arena, &element);
+  if (status != LRK_OK) return status;
+  LRK_REQUIRE(touched >= 0, "invalid plan size");
+  if (touched == 0) return LRK_OK;
+  LRK_REQUIRE(plan && recalled && recalled_positions && flag, "null pointer");
+  LRK_REQUIRE(aligned(recalled, 16), "recalled rows must be 16-byte aligned");
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>(touched, 65535));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (check)
+    arena_insert_kernel<true><<<blocks, kCompactThreads, 0, s>>>(param(*arena, element), plan, touched,
+                                                                 static_cast<const char *>(recalled),
+                                                                 recalled_positions, flag);
+  else
+    arena_insert_kernel<false><<<blocks, kCompactThreads, 0, s>>>(param(*arena, element), plan, touched,
+                                                                  static_cast<const char *>(recalled),
+                                                                  recalled_positions, flag);
+  return launch_status("lrk_arena_insert");
 }

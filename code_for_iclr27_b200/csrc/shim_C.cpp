@@ -700,6 +700,27 @@ lrk_arena arena_of(const torch::Tensor &keys, const torch::Tensor &values, const
   return a;
 }
 
+// Recall rows into the arena in place (lrk_arena_insert): plan int64 [touched,
+// 3] (head, first entry, count), recalled [entries, 2, D], recalled_positions
+// float32 [entries].  check: only the checks.  Returns the device flag (int32 [1]).
+torch::Tensor arena_insert(torch::Tensor keys, torch::Tensor values, torch::Tensor positions, torch::Tensor lengths,
+                           torch::Tensor plan, torch::Tensor recalled, torch::Tensor recalled_positions, bool check) {
+  const lrk_arena a = arena_of(keys, values, positions, lengths);
+  for (const auto &t : {plan, recalled, recalled_positions}) check_cuda(t, keys);
+  TORCH_CHECK(plan.scalar_type() == at::kLong && plan.dim() == 2 && plan.size(1) == 3, "plan must be int64 [touched, 3]");
+  TORCH_CHECK(recalled.scalar_type() == keys.scalar_type() && recalled.dim() == 3 && recalled.size(1) == 2 &&
+                  recalled.size(2) == keys.size(2),
+              "recalled rows must be [entries, 2, dimension] of the arena dtype");
+  TORCH_CHECK(recalled_positions.scalar_type() == at::kFloat && recalled_positions.numel() == recalled.size(0),
+              "recalled positions must be float32, one per recalled row");
+  c10::cuda::CUDAGuard guard(keys.device());
+  auto flag = torch::zeros({1}, lengths.options());
+  check_status(lrk_arena_insert(&a, plan.data_ptr<int64_t>(), plan.size(0), recalled.data_ptr(),
+                                recalled_positions.data_ptr<float>(), check ? 1 : 0,
+                                reinterpret_cast<unsigned int *>(flag.data_ptr<int32_t>()), current_stream()));
+  return flag;
+}
+
 // Append one row per head to heads [first_head, first_head + new_keys.size(0))
 // in place; returns the device overflow flag (int32 [1], nonzero if a head
 // was full).
@@ -946,6 +967,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("select_pick", &select_pick);
   module.def("arena_append", &arena_append);
   module.def("arena_compact", &arena_compact);
+  module.def("arena_insert", &arena_insert);
   module.def("arena_compact_positions", &arena_compact_positions);
   module.def("arena_evict", &arena_evict);
   module.def("arena_append_into", &arena_append_into);

@@ -283,7 +283,7 @@ def measure_reinsert(device, layers, heads, dim, rows_per_head, recall_rows, eve
     the merge plan on the device and with the host plan (the resident
     positions of the touched layers copied to the host, numpy's stable
     argsort per head, recall/planning.py:34-52); the cache is restored
-    between events."""
+    between events; and the same events into a KV arena (in place)."""
     import torch
 
     from .kvcache import PackedCache
@@ -305,6 +305,26 @@ def measure_reinsert(device, layers, heads, dim, rows_per_head, recall_rows, eve
         plans.append(np.stack((picks // (heads * rows_per_head), picks // rows_per_head % heads,
                                picks % rows_per_head * 4 + 2), axis=1))
     result = {"rows": recall_rows, "layers": layers, "heads": heads, "rows_per_head": rows_per_head}
+    # The same events into a KV arena holding the same rows (in place,
+    # lrk_arena_insert), its tensors copied back between events.
+    from .arena import ArenaCache
+
+    arena = ArenaCache.from_packed(cache, margin=512)
+    kept = (arena.keys.clone(), arena.values.clone(), arena.positions.clone(), arena.lengths.clone(),
+            arena.head_lens.copy())
+    times = []
+    for i, metadata in enumerate(plans):
+        arena.keys.copy_(kept[0]), arena.values.copy_(kept[1]), arena.positions.copy_(kept[2])
+        arena.lengths.copy_(kept[3])
+        arena.head_lens[:] = kept[4]
+        torch.cuda.synchronize()
+        start = time.perf_counter()
+        arena.insert_payload(payload, metadata)
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append((time.perf_counter() - start) * 1e6)
+    result["arena_in_place_us"] = _median(times)
+    del arena, kept
     for plan in ("device", "host"):
         times = []
         for i, metadata in enumerate(plans):

@@ -470,6 +470,22 @@ int lrk_arena_compact(const lrk_arena *arena, const int64_t *plan, int64_t touch
 int lrk_arena_compact_positions(const lrk_arena *arena, const int64_t *plan, int64_t touched,
                                 const float *removed_positions, unsigned int *error, lrk_stream_t stream);
 
+/* Recall reinsertion into the arena in place: no reference counterpart (the
+ * reference rebuilds every touched layer, src/lazy_recall/cache.py:201-253,
+ * csrc/recall.cu:54-84; the rows and positions that result are the same as
+ * that merge's for each head).  plan [touched, 3] i64 = (head, first entry,
+ * count), device memory; recalled [entries, 2, dimension] (K then V, 16-byte
+ * aligned) and recalled_positions [entries] (f32), each head's entries in
+ * ascending position order.  check != 0 only sets *flag: bit 1 a position
+ * recalled twice or recalled while resident, bit 2 resident positions that
+ * do not ascend, bit 4 a head that would pass its capacity, bit 8 more than
+ * 2048 entries for one head; nothing changes.  check == 0 merges: a head's
+ * rows above its first entry's place move up in place and the entries land
+ * in position order; lengths[head] += count.  Run the check first and merge
+ * only when *flag is 0. */
+int lrk_arena_insert(const lrk_arena *arena, const int64_t *plan, int64_t touched, const void *recalled,
+                     const float *recalled_positions, int check, unsigned int *flag, lrk_stream_t stream);
+
 /* A lazy eviction batch as it leaves the queue: heads [count] (i64: layer x
  * heads + head) and removed_positions [count] (f32 logical positions), in any
  * order, device memory.  Each head collects, sorts and removes its own

@@ -5,7 +5,9 @@ appends (one launch for all layers, and per layer), removals from the host
 (remove_positions) and from a device queue (remove_selected), a whole audit
 pass -- and after each, every layer of the arena read back in the packed
 layout (packed_layer) equals the packed cache bit for bit: the same rows in
-the same order.  FlashAttention's cache kernel over the arena gives the
+the same order; recall reinsertion (insert_payload, in place in the arena, a
+whole-layer merge in the packed cache) keeps them equal.  FlashAttention's
+cache kernel over the arena gives the
 reference's decode attention (flash_attn_varlen_func over the packed layer,
 attention.py:15-35) within bf16 rounding.  Malformed compaction plans set the
 error flag and leave the heads unchanged.
@@ -278,3 +280,51 @@ def test_arena_evict_unsorted_batch_c_abi(cuda):
                                       flag.data_ptr(), stream))
         torch.cuda.synchronize()
         assert int(flag) == 1 and l1.tolist() == [58, 9, 0, 61] and torch.equal(k1, before)
+
+
+def test_arena_recall_insert_equals_packed_merge(cuda):
+    """Rows evicted from both caches and recalled into both (the arena in
+    place: lrk_arena_insert; the packed cache: the merge plan and
+    merge_layers), plus rows never resident (positions above a head's last
+    one): the caches stay equal.  One head receives more than one launch's
+    2048 entries (two rounds), some heads none; a small margin makes the
+    slots grow first.  A recalled position that is resident raises
+    ValueError before either cache changes."""
+    import torch
+
+    from code_for_iclr27_b200.arena import ArenaCache
+
+    packed = make_packed(cuda, seed=5, prompt=3000)
+    arena = ArenaCache.from_packed(packed, margin=16)
+    rng = np.random.default_rng(5)
+    removals, payload, metadata = {}, [], []
+    for l, layer in enumerate(packed.layers):
+        bounds = layer.bounds()
+        for h in range(packed.heads):
+            if (l, h) == (1, 2):
+                continue  # an untouched head
+            count = 2600 if (l, h) == (0, 1) else int(rng.integers(1, 40))
+            picks = np.sort(rng.choice(layer.head_lens[h], count, replace=False))
+            removals[(l, h)] = picks
+            rows = torch.as_tensor(bounds[h] + picks, device=cuda)
+            payload.append(torch.stack([layer.keys[rows], layer.values[rows]], dim=1))
+            metadata.extend((l, h, int(p)) for p in layer.positions.reshape(-1)[rows].cpu().numpy())
+    for cache in (packed, arena):
+        cache.remove_positions(removals)
+    assert_same(arena, packed)
+    # Rows never resident: positions above a head's last one.
+    top = int(packed.layers[2].head_lens[3]) + int(len(removals.get((2, 3), ())))
+    payload.append(torch.randn(50, 2, 128).to(torch.bfloat16).to(cuda))
+    metadata.extend((2, 3, top + 10 + 7 * i) for i in range(50))
+    payload = torch.cat(payload)
+    metadata = np.asarray(metadata, dtype=np.int64)
+    order = rng.permutation(len(metadata))  # any payload order
+    payload, metadata = payload[torch.as_tensor(order, device=cuda)], metadata[order]
+    bad = metadata[:3].copy()
+    bad[0] = (0, 0, int(packed.layers[0].positions.reshape(-1)[0].item()))  # resident
+    with pytest.raises(ValueError):
+        arena.insert_payload(payload[:3], bad)
+    assert_same(arena, packed)  # nothing changed
+    assert arena.insert_payload(payload, metadata) == len(metadata)
+    assert packed.insert_payload(payload, metadata) == len(metadata)
+    assert_same(arena, packed)
