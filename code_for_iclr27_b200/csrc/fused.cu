@@ -56,9 +56,10 @@ struct ScoreTableParam {
   int count;
 };
 
-// Floats per stashed row: the candidate count rounded up to 16 (64-byte rows,
-// so every row starts 16-byte aligned for 4-candidate vector loads).
-__host__ __device__ __forceinline__ int64_t stash_stride(int64_t candidates) { return (candidates + 15) & ~int64_t{15}; }
+// Floats per stashed row: the candidate count rounded up to 32 (128-byte
+// rows: every row starts 16-byte aligned for 4-candidate vector copies, and
+// the last tile of up to 32 candidates ends inside its row).
+__host__ __device__ __forceinline__ int64_t stash_stride(int64_t candidates) { return (candidates + 31) & ~int64_t{31}; }
 
 constexpr int kVisibilityThreads = 1024;
 
@@ -557,10 +558,40 @@ __global__ void __launch_bounds__(kRiskThreads, 4) risk_vec_kernel(ScoreTablePar
 // maximum, exactly as risk_vec_kernel folds them.  This skips risk_vec's
 // logits load, scale, rounding, mask, expf and first division per element.
 // A CTA covers TILE candidates; thread (tx, ty) owns C consecutive
-// candidates (one 4C-byte load per stashed row; C = 4, or 2 for 8 groups to
-// keep the registers in check) and walks queries ty, ty + TY, ..., loading
-// the next query's rows while the current one computes.  The launch picks
-// TILE (32, 16 or 8) for the fewest waves of CTAs weighted by their length.
+// candidates (one 4C-byte copy per stashed row; C = 4, or 2 for 8 groups to
+// keep the registers in check) and walks queries ty, ty + TY, ...  Each
+// thread streams its rows through its own kStashStages-slot ring in shared
+// memory with cp.async, kStashStages - 1 queries ahead of the one it
+// computes: the copies in flight hold no registers, so a CTA keeps
+// 3 x 64 bytes per thread on the way from HBM (one query ahead in registers
+// covered about one memory latency and left the kernel latency-bound); 2 x 64
+// for 8 groups, whose projections take twice the shared memory, so that
+// 3 CTAs still fit an SM at a 250-query window.  The launch picks TILE (32,
+// 16 or 8) for the fewest waves of CTAs weighted by their length.
+template <int G>
+__host__ __device__ constexpr int stash_stages() {
+  return G >= 8 ? 3 : 4;
+}
+
+template <int BYTES>
+__device__ __forceinline__ void stage_async(void *dst, const void *src) {
+  const auto to = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+  if constexpr (BYTES == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(to), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;\n" ::"r"(to), "l"(src), "n"(BYTES) : "memory");
+}
+__device__ __forceinline__ void stage_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int PENDING>
+__device__ __forceinline__ void stage_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(PENDING) : "memory");
+}
+
+template <int G, int C>
+__host__ __device__ constexpr size_t stash_ring_bytes() {
+  return static_cast<size_t>(stash_stages<G>()) * G * kRiskThreads * C * sizeof(float);
+}
+
 template <int G, int C, int TILE>
 __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableParam table,
                                                                   const float *__restrict__ stash, int window,
@@ -569,20 +600,60 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
                                                                   const float *__restrict__ margin,
                                                                   float epsilon) {
   using Vec = typename std::conditional<C == 4, float4, float2>::type;
-  constexpr int TX = TILE / C, TY = kRiskThreads / TX;
-  extern __shared__ float projection[];  // [window * G]
+  constexpr int TX = TILE / C, TY = kRiskThreads / TX, kStashStages = stash_stages<G>();
+  // [kStashStages][G][kRiskThreads] vectors, then the projections [window * G].
+  extern __shared__ __align__(16) unsigned char risk_shared[];
+  Vec *ring = reinterpret_cast<Vec *>(risk_shared);
+  float *projection = reinterpret_cast<float *>(risk_shared + stash_ring_bytes<G, C>());
   __shared__ int cell_min[kRiskChunks][TILE], cell_max[kRiskChunks][TILE];
   __shared__ int cell_bad[kRiskChunks][TILE];
+  __shared__ float cell_risk[kRiskChunks][TILE][2];
   const lrk_score_segment &seg = table.segment[blockIdx.y];
   const int64_t count = seg.last - seg.first;
   const int64_t tile = static_cast<int64_t>(blockIdx.x) * TILE;
   if (tile >= count) return;  // the whole CTA: nothing of this segment here
-  for (int i = threadIdx.x; i < window * G; i += kRiskThreads)
-    projection[i] = stats[(segment_base + blockIdx.y) * window * G + i].z;
-  __syncthreads();
   const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
   const int64_t col0 = tile + tx * C;  // candidate index of this thread's first candidate
   const int64_t stride = stash_stride(count);
+  // Rows are padded to `stride` floats (a multiple of 32 >= the last tile's
+  // end), so a vector past the last candidate stays inside the row (its
+  // lanes are never scored).
+  const float *base = stash + table.stash_offset[blockIdx.y] + col0;
+  Vec *mine = ring + threadIdx.x;  // slot (s, g) at mine[(s * G + g) * kRiskThreads]
+  const int chunk = chunk_queries(seg, window);
+  const int chunks = (window + chunk - 1) / chunk;
+  const bool leader = threadIdx.x < TILE;
+  // A pass folds up to kRiskChunks query chunks; this thread walks its
+  // queries q_first, q_first + TY, ... of the pass, `steps` of them.  One
+  // commit group per step (empty past the last one), so group i is complete
+  // once at most kStashStages - 2 later groups are pending.
+  int q_first = 0, steps = 0;
+  auto issue = [&](int step) {
+    if (step < steps) {
+      const int64_t row = static_cast<int64_t>(q_first + step * TY) * G;
+      Vec *slot = mine + (step % kStashStages) * G * kRiskThreads;
+#pragma unroll
+      for (int g = 0; g < G; ++g) stage_async<sizeof(Vec)>(slot + g * kRiskThreads, base + (row + g) * stride);
+    }
+    stage_commit();
+  };
+  // The pass's first copies and its cells; the caller synchronises.
+  auto start_pass = [&](int c_first) {
+    const int c_last = min(chunks, c_first + kRiskChunks);
+    const int q_end = min(window, c_last * chunk);
+    q_first = c_first * chunk + ty;
+    steps = q_first < q_end ? (q_end - q_first + TY - 1) / TY : 0;
+#pragma unroll
+    for (int s = 0; s < kStashStages - 1; ++s) issue(s);
+    for (int i = threadIdx.x; i < (c_last - c_first) * TILE; i += kRiskThreads) {
+      cell_min[i / TILE][i % TILE] = ordered_key(INFINITY);
+      cell_max[i / TILE][i % TILE] = ordered_key(-INFINITY);
+      cell_bad[i / TILE][i % TILE] = 0;
+    }
+  };
+  // The first pass's copies are on their way while the projections and this
+  // thread's projected values load.
+  start_pass(0);
   float pv[G][C];
 #pragma unroll
   for (int j = 0; j < C; ++j) {
@@ -591,25 +662,16 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
       pv[g][j] = col0 + j < count ? __ldg(seg.projected_values + g * seg.projected_stride + seg.first + col0 + j)
                                   : 0.0f;
   }
-  // Rows are padded to `stride` floats, so a vector past the last candidate
-  // stays inside the row (its lanes are never scored).
-  const float *base = stash + table.stash_offset[blockIdx.y] + col0;
-  auto load = [&](int q, int g) -> Vec {
-    return __ldcs(reinterpret_cast<const Vec *>(base + (static_cast<int64_t>(q) * G + g) * stride));
-  };
-  const int chunk = chunk_queries(seg, window);
-  const int chunks = (window + chunk - 1) / chunk;
-  const bool leader = threadIdx.x < TILE;
+  for (int i = threadIdx.x; i < window * G; i += kRiskThreads)
+    projection[i] = stats[(segment_base + blockIdx.y) * window * G + i].z;
+  __syncthreads();
   float result = 0.0f;
   for (int c_first = 0; c_first < chunks; c_first += kRiskChunks) {
     const int c_last = min(chunks, c_first + kRiskChunks);
-    for (int i = threadIdx.x; i < (c_last - c_first) * TILE; i += kRiskThreads) {
-      cell_min[i / TILE][i % TILE] = ordered_key(INFINITY);
-      cell_max[i / TILE][i % TILE] = ordered_key(-INFINITY);
-      cell_bad[i / TILE][i % TILE] = 0;
+    if (c_first > 0) {
+      start_pass(c_first);
+      __syncthreads();
     }
-    __syncthreads();
-    const int q_begin = c_first * chunk, q_end = min(window, c_last * chunk);
     float lo[C], hi[C];
     uint32_t bad = 0;
 #pragma unroll
@@ -633,16 +695,16 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
       bad = 0;
     };
     int current_chunk = -1;
-    Vec current[G], next[G];
-    if (q_begin + ty < q_end) {
+    for (int step = 0; step < steps; ++step) {
+      stage_wait<kStashStages - 2>();
+      // A thread reads only the slots its own copies filled; the slot the
+      // next issue refills was read (and its values used) one step earlier.
+      const Vec *slot = mine + (step % kStashStages) * G * kRiskThreads;
+      Vec current[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) current[g] = load(q_begin + ty, g);
-    }
-    for (int q = q_begin + ty; q < q_end; q += TY) {
-      if (q + TY < q_end) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) next[g] = load(q + TY, g);
-      }
+      for (int g = 0; g < G; ++g) current[g] = slot[g * kRiskThreads];
+      issue(step + kStashStages - 1);
+      const int q = q_first + step * TY;
       const int c = q / chunk;
       if (c != current_chunk) {
         if (current_chunk >= 0) flush(current_chunk);
@@ -667,21 +729,32 @@ __global__ void __launch_bounds__(kRiskThreads, 3) risk_stash_kernel(ScoreTableP
         lo[j] = fminf(lo[j], drop[j]);
         hi[j] = fmaxf(hi[j], drop[j]);
       }
-#pragma unroll
-      for (int g = 0; g < G; ++g) current[g] = next[g];
     }
     if (current_chunk >= 0) flush(current_chunk);
     __syncthreads();
-    if (leader) {
+    // The fp64 risk of each end of each (chunk, candidate) drop range on its
+    // own thread, rounded to float: rounding is monotonic, so the larger of
+    // the two rounded risks is chunk_score's rounded larger risk.
+    const int jobs = (c_last - c_first) * TILE * 2;
+    if (threadIdx.x < jobs) {
       const MarginTerms terms = margin_terms(margin);
+      for (int i = threadIdx.x; i < jobs; i += kRiskThreads) {
+        const int c = i / (2 * TILE), k = (i >> 1) % TILE;
+        const int key = (i & 1) ? cell_max[c][k] : cell_min[c][k];
+        cell_risk[c][k][i & 1] =
+            static_cast<float>(risk64(terms.m, terms.probability, terms.base_softplus, from_ordered_key(key)));
+      }
+    }
+    __syncthreads();
+    if (leader) {
       for (int c = c_first; c < c_last; ++c) {
-        const float score = chunk_score(terms, cell_bad[c - c_first][threadIdx.x] != 0,
-                                        from_ordered_key(cell_min[c - c_first][threadIdx.x]),
-                                        from_ordered_key(cell_max[c - c_first][threadIdx.x]));
+        const float score = cell_bad[c - c_first][threadIdx.x] != 0
+                                ? NAN
+                                : fmaxf(cell_risk[c - c_first][threadIdx.x][0], cell_risk[c - c_first][threadIdx.x][1]);
         result = c == 0 ? score : running_max(result, score);
       }
     }
-    __syncthreads();  // cells free for the next pass
+    if (c_last < chunks) __syncthreads();  // cells free for the next pass
   }
   if (!leader) return;
   const int64_t candidate = tile + threadIdx.x;
@@ -692,9 +765,10 @@ template <int G, int TILE>
 int launch_risk_stash_tile(const ScoreTableParam &table, int n, const float *stash, int window, const float3 *stats,
                            int64_t s0, const float *margin, float epsilon, int64_t max_candidates,
                            cudaStream_t stream) {
-  const size_t shared = static_cast<size_t>(window) * G * sizeof(float);
-  auto kernel = risk_stash_kernel<G, (G >= 8 ? 2 : 4), TILE>;
-  if (shared > 16 * 1024) {
+  constexpr int C = G >= 8 ? 2 : 4;
+  const size_t shared = stash_ring_bytes<G, C>() + static_cast<size_t>(window) * G * sizeof(float);
+  auto kernel = risk_stash_kernel<G, C, TILE>;
+  if (shared > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(shared));
     if (e != cudaSuccess) return fail(LRK_ERR_CUDA, cudaGetErrorString(e));
   }
@@ -812,8 +886,16 @@ int64_t stash_layout(ScoreTableParam &table, int n, int64_t rows_per_segment) {
   return total;
 }
 
-// The stash path serves 1, 2, 4 or 8 groups.
-bool stash_supported(int groups) { return groups == 1 || groups == 2 || groups == 4 || groups == 8; }
+// The stash path serves 1, 2, 4 or 8 groups, with the risk kernel's ring
+// and projections within 200 KB of shared memory.
+bool stash_supported(int groups, int window) {
+  const size_t ring = groups == 1   ? stash_ring_bytes<1, 4>()
+                      : groups == 2 ? stash_ring_bytes<2, 4>()
+                      : groups == 4 ? stash_ring_bytes<4, 4>()
+                                    : stash_ring_bytes<8, 2>();
+  return (groups == 1 || groups == 2 || groups == 4 || groups == 8) &&
+         ring + static_cast<size_t>(window) * groups * sizeof(float) <= 200 * 1024;
+}
 
 template <typename T>
 int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_t *qpos, int window, int groups,
@@ -827,7 +909,7 @@ int launch_scores(const lrk_score_segment *segments, int64_t count, const int64_
       max_length = std::max<int64_t>(max_length, table.segment[i].length);
       max_candidates = std::max<int64_t>(max_candidates, table.segment[i].last - table.segment[i].first);
     }
-    float *table_stash = stash != nullptr && stash_supported(groups) ? stash : nullptr;
+    float *table_stash = stash != nullptr && stash_supported(groups, window) ? stash : nullptr;
     if (table_stash != nullptr) stash_layout(table, n, static_cast<int64_t>(window) * groups);
     int status = launch_stats<T>(table, n, qpos, window, groups, scale, stats, visible, s0, max_length, table_stash,
                                  stream);

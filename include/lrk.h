@@ -125,7 +125,7 @@ int lrk_temporal_scores(const lrk_score_segment *segments, int64_t count, int lo
  * and the risk step (csrc/scoring.cu:68-128) reads p instead of recomputing
  * it from the logits (scale, round, mask, expf, division).  The scores are
  * the same bit for bit either way.  Per segment: window x groups rows of the
- * candidate count rounded up to 16 floats. */
+ * candidate count rounded up to 32 floats. */
 size_t lrk_temporal_scores_stash_bytes(const lrk_score_segment *segments, int64_t count, int64_t window,
                                        int64_t groups);
 
